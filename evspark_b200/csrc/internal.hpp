@@ -1,0 +1,133 @@
+// Internal structures of libevspark_sm100 (not part of the C ABI).
+#pragma once
+
+#include <vector>
+
+#include "common.cuh"
+
+// GEMM tile geometry (tcgen05 path): 128 weight rows x 64 K per stage, tokens per MMA = NT
+constexpr int GEMM_BM = 128;
+constexpr int GEMM_BK = 64;
+constexpr int TOK_TILE = 16;  // token rows per decode tile (MMA N)
+constexpr int ATTN_BLOCK = 256;  // keys per attention partial (aligned at absolute positions)
+
+// HBM layout of the per-sequence state ------------------------------------
+//   outer FIR history ring   [B][cap_outer][3d]   data dtype  (positions mod cap_outer)
+//   inner FIR history ring   [B][cap_inner][d]    data dtype  (SE / MR layers)
+//   IIR per-position states  [B][iir_slots][d][S] fp32        (slot = block index)
+//   KV cache                 [B][Lmax][2][H][Dh]  data dtype
+//   capture ring             [B][ring_len][d]     fp32        (injection-layer outputs)
+struct LayerDev {
+  int kind = 0;
+  const void* pre_norm = nullptr;
+  const void* post_norm = nullptr;
+  const void* w_in = nullptr;
+  const void* short_w = nullptr;
+  const void* inner_w = nullptr;
+  const void* D = nullptr;
+  const void* log_poles = nullptr;
+  const void* residues = nullptr;
+  const void* w_out = nullptr;
+  const void* w_qkv = nullptr;
+  const void* w_o = nullptr;
+  const void* w1 = nullptr;
+  const void* w2 = nullptr;
+  const void* w3 = nullptr;
+  float* poles = nullptr;  // owned: exp(log_poles) fp32 [d, S]
+  CUtensorMap tm_in, tm_out, tm_qkv, tm_o, tm_w1, tm_w2, tm_w3;
+  int64_t numel[EVS_W_NUM_SLOTS] = {0};
+};
+
+struct evs_model {
+  evs_model_config cfg;
+  int device = 0;
+  bool finalized = false;
+  const void* embed = nullptr;
+  const void* final_norm = nullptr;
+  int64_t embed_numel = 0, final_norm_numel = 0;
+  CUtensorMap tm_embed;
+  LayerDev L[EVS_MAX_LAYERS];
+  int n_capture = 0;
+  int capture_layer[4] = {-1, -1, -1, -1};
+  size_t elem() const { return cfg.dtype == EVS_DTYPE_BF16 ? 2 : 4; }
+  int capture_slot(int layer) const {
+    for (int c = 0; c < n_capture; ++c)
+      if (capture_layer[c] == layer) return c;
+    return -1;
+  }
+};
+
+struct HyenaDev {
+  void* outer_ring = nullptr;
+  void* inner_ring = nullptr;
+  float* s_all = nullptr;
+};
+
+struct evs_state {
+  const evs_model* m = nullptr;
+  int max_batch = 0, max_seqlen = 0, max_chunk = 0;
+  int cap_outer = 0, cap_hcs = 0, cap_hcm = 0, iir_slots = 0, ring_len = 0;
+  int m_cap = 0;      // max token rows per call = max_batch * max_chunk (padded to TOK_TILE)
+  int ld_act = 0;     // row stride (elements) of the activation buffer = max(d, F)
+  size_t ws_floats = 0;  // capacity of the split-K workspace
+  int attn_blocks = 0;   // ceil(max_seqlen / ATTN_BLOCK)
+  // per-row bookkeeping (device truth) and a host upper bound of the lengths
+  int32_t* d_len = nullptr;      // [B] tokens consumed
+  int32_t* d_len0 = nullptr;     // [B] lengths before the last retained forward
+  int32_t* d_iir_cur = nullptr;  // [B] IIR slot holding the current state
+  int32_t* d_chunk = nullptr;    // [1] length of the last retained chunk (0: no stash)
+  std::vector<int32_t> h_len;    // host upper bound of d_len
+  int h_chunk = 0;               // host copy of the last retained chunk length
+  HyenaDev hy[EVS_MAX_LAYERS];
+  void* kv[EVS_MAX_LAYERS] = {nullptr};
+  float* cap_ring[4] = {nullptr, nullptr, nullptr, nullptr};
+  // scratch
+  float* resid = nullptr;      // [m_cap][d] fp32 residual stream
+  void* act = nullptr;         // [m_cap][ld_act] data dtype: GEMM B operand
+  float* ws = nullptr;         // split-K partials [splits][m][n] fp32
+  void* qrot = nullptr;        // [m_cap][d] data dtype rotated queries
+  float* attn_part = nullptr;  // [B][H][attn_blocks][max_chunk][Dh+2] fp32
+  EvsDevErr* d_err = nullptr;
+  CUtensorMap tm_act_d, tm_act_f;  // activation buffer viewed with K = d and K = F
+  std::vector<void*> owned;
+};
+
+// ---- launchers (stream-ordered; return EVS_* status) ----
+// GEMM partial sums ws[split][tok][n] over the weight rows; dual: w1/w2 interleaved per 64 rows
+struct GemmPlan {
+  int N, K, M, splits, dual;
+};
+GemmPlan gemm_plan(const evs_model* m, int N, int K, int M, int dual);
+int launch_gemm_tc(const CUtensorMap* tmA, const CUtensorMap* tmA2, const CUtensorMap* tmB, const GemmPlan& p,
+                   float* ws, EvsDevErr* err, cudaStream_t st);
+int launch_gemm_simt(const void* W, const void* W2, const void* X, int ldx, int dtype, const GemmPlan& p, float* ws,
+                     cudaStream_t st);
+int make_tmap_2d_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t row_stride_bytes,
+                      uint32_t box_inner, uint32_t box_outer);
+
+// row kernels
+int launch_embed_norm(const evs_model* m, evs_state* s, const int64_t* ids, int M, const float* scale,
+                      cudaStream_t st);
+int launch_res_add_norm(const evs_model* m, evs_state* s, int M, int splits, const float* scale, int capture_slot,
+                        int T, cudaStream_t st);
+int launch_swiglu(const evs_model* m, evs_state* s, int M, int splits, cudaStream_t st);
+int launch_logits(const evs_model* m, evs_state* s, int M, int T, int splits, float* logits, int last_only,
+                  cudaStream_t st);
+int launch_bookkeeping(evs_state* s, int B, int T, int retain, cudaStream_t st);
+int launch_poles(const float* log_poles, float* poles, int n, cudaStream_t st);
+
+// Hyena mixer (outer FIR + inner FIR / IIR), reads in-projection partials from s->ws
+int launch_hyena(const evs_model* m, evs_state* s, int layer, int B, int T, int splits, int prefill, int retain,
+                 cudaStream_t st);
+int launch_rollback(evs_state* s, const int32_t* k, int B, cudaStream_t st);
+int launch_state_export(const evs_state* s, int layer, int which, int row, int width, void* dst, cudaStream_t st);
+
+// attention: rope + KV append + split-KV partials + ordered combine (output into s->act)
+int launch_attention(const evs_model* m, evs_state* s, int layer, int B, int T, int splits, int kv_blocks,
+                     cudaStream_t st);
+
+// verification
+int launch_transform(const float* logits, int rows, int V, float temperature, int top_k, double* probs,
+                     cudaStream_t st);
+int launch_verify(const double* p, const double* q, const int64_t* x, const double* u, int B, int gamma, int V,
+                  int greedy, int32_t* accepted, int64_t* tokens, int32_t* info, cudaStream_t st);
