@@ -87,9 +87,11 @@ struct evs_state {
   float* ws = nullptr;         // split-K partials [splits][m][n] fp32
   void* qrot = nullptr;        // [m_cap][d] data dtype rotated queries
   float* attn_part = nullptr;  // [B][H][attn_blocks][max_chunk][Dh+2] fp32
+  int64_t* ids_scratch = nullptr;  // [m_cap] chunk ids of a strided prefill
   EvsDevErr* d_err = nullptr;
   CUtensorMap tm_act_d, tm_act_f;  // activation buffer viewed with K = d and K = F
-  std::vector<void*> owned;
+  std::vector<void*> owned;        // [0] persistent arenas, [1] scratch
+  std::vector<size_t> owned_bytes;
 };
 
 // ---- launchers (stream-ordered; return EVS_* status) ----
@@ -111,8 +113,9 @@ int launch_embed_norm(const evs_model* m, evs_state* s, const int64_t* ids, int 
 int launch_res_add_norm(const evs_model* m, evs_state* s, int M, int splits, const float* scale, int capture_slot,
                         int T, cudaStream_t st);
 int launch_swiglu(const evs_model* m, evs_state* s, int M, int splits, cudaStream_t st);
-int launch_logits(const evs_model* m, evs_state* s, int M, int T, int splits, float* logits, int last_only,
-                  cudaStream_t st);
+// logits rows go to out[(b * out_T + t0 + t) * V] (or out[b * V] for the last row when last_only)
+int launch_logits(const evs_model* m, evs_state* s, int M, int T, int splits, float* logits, int out_T, int t0,
+                  int last_only, cudaStream_t st);
 int launch_bookkeeping(evs_state* s, int B, int T, int retain, cudaStream_t st);
 int launch_poles(const float* log_poles, float* poles, int n, cudaStream_t st);
 
@@ -127,7 +130,8 @@ int launch_attention(const evs_model* m, evs_state* s, int layer, int B, int T, 
                      cudaStream_t st);
 
 // verification
-int launch_transform(const float* logits, int rows, int V, float temperature, int top_k, double* probs,
-                     cudaStream_t st);
+int launch_transform(const void* logits, int logits_fp64, int rows, int V, double temperature, int top_k,
+                     double* probs, cudaStream_t st);
+int launch_sample(const double* rows, int n, int V, const double* u, int64_t* out, cudaStream_t st);
 int launch_verify(const double* p, const double* q, const int64_t* x, const double* u, int B, int gamma, int V,
                   int greedy, int32_t* accepted, int64_t* tokens, int32_t* info, cudaStream_t st);

@@ -101,8 +101,8 @@ __global__ void __launch_bounds__(ROW_THREADS) swiglu_kernel(const float* __rest
   act[static_cast<size_t>(row) * ld_act + f] = from_f32<TD>(g1 * sig * g2);
 }
 
-__global__ void logits_kernel(const float* __restrict__ ws, int splits, int M, int V, int T, int last_only,
-                              float* __restrict__ out) {
+__global__ void logits_kernel(const float* __restrict__ ws, int splits, int M, int V, int T, int out_T, int t0,
+                              int last_only, float* __restrict__ out) {
   const int row = blockIdx.y;
   const int v = blockIdx.x * blockDim.x + threadIdx.x;
   if (v >= V) return;
@@ -110,7 +110,8 @@ __global__ void logits_kernel(const float* __restrict__ ws, int splits, int M, i
   if (last_only && t != T - 1) return;
   float acc = 0.f;
   for (int sp = 0; sp < splits; ++sp) acc += ws[(static_cast<size_t>(sp) * M + row) * V + v];
-  const size_t orow = last_only ? static_cast<size_t>(row / T) : static_cast<size_t>(row);
+  const int b = row / T;
+  const size_t orow = last_only ? static_cast<size_t>(b) : static_cast<size_t>(b) * out_T + t0 + t;
   out[orow * V + v] = acc;
 }
 
@@ -176,11 +177,11 @@ int launch_swiglu(const evs_model* m, evs_state* s, int M, int splits, cudaStrea
   return EVS_OK;
 }
 
-int launch_logits(const evs_model* m, evs_state* s, int M, int T, int splits, float* logits, int last_only,
-                  cudaStream_t st) {
+int launch_logits(const evs_model* m, evs_state* s, int M, int T, int splits, float* logits, int out_T, int t0,
+                  int last_only, cudaStream_t st) {
   const int V = m->cfg.vocab_size;
   dim3 grid((V + 255) / 256, M);
-  logits_kernel<<<grid, 256, 0, st>>>(s->ws, splits, M, V, T, last_only, logits);
+  logits_kernel<<<grid, 256, 0, st>>>(s->ws, splits, M, V, T, out_T, t0, last_only, logits);
   EVS_CUDA_TRY(cudaGetLastError());
   return EVS_OK;
 }

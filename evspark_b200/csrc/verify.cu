@@ -1,0 +1,169 @@
+// Sampling transform and Leviathan verification on the device, fp64 decision math.
+//
+// apply_transform (evspark/specdec/transforms.py:18-64): logits/T, max-subtracted exp,
+//   normalise, keep the top-k by (-p, index), renormalise; T <= 0 -> one-hot argmax.
+// verify_round (evspark/specdec/verifier.py:54-123): for each draft position draw r and accept
+//   iff r < min(1, p(x)/q(x)); on the first rejection sample norm(max(0, p - q)) (p itself when
+//   that mass underflows); if everything is accepted sample the bonus token from p_{γ+1}.
+// verify_round_greedy (verifier.py:126-176): accept iff x == argmax p (lowest index on ties).
+// sample_categorical (verifier.py:28-40): clip at 0, normalise (uniform when the mass is 0 or
+//   not finite), inverse CDF with one uniform: the first index whose cumulative sum / total > u.
+//
+// All fp64 row sums use pairwise summation (blocks of 128 with eight running partials, halves
+// split at a multiple of 8) and cumulative sums run left to right, so that for the same inputs
+// the normalised rows are the ones numpy produces.
+#include "internal.hpp"
+#include "sampling.cuh"
+
+namespace {
+
+using namespace evs_sampling;
+
+// one CTA per row
+__global__ void __launch_bounds__(256) transform_kernel(const void* __restrict__ logits, int f64, int V,
+                                                        double temperature, int top_k, double* __restrict__ probs) {
+  __shared__ double e[VMAX], masked[VMAX], sv[256], scal[1];
+  __shared__ int keep[VMAX], si[256];
+  const int r = blockIdx.x;
+  if (f64) {
+    const double* lg = static_cast<const double*>(logits) + static_cast<size_t>(r) * V;
+    for (int i = threadIdx.x; i < V; i += blockDim.x) e[i] = lg[i];
+  } else {
+    const float* lg = static_cast<const float*>(logits) + static_cast<size_t>(r) * V;
+    for (int i = threadIdx.x; i < V; i += blockDim.x) e[i] = static_cast<double>(lg[i]);
+  }
+  __syncthreads();
+  transform_row(e, V, temperature, top_k, probs + static_cast<size_t>(r) * V, keep, masked, sv, si, scal);
+}
+
+// one CTA per row b
+__global__ void __launch_bounds__(256) verify_kernel(const double* __restrict__ p, const double* __restrict__ q,
+                                                     const int64_t* __restrict__ x, const double* __restrict__ u,
+                                                     int gamma, int V, int greedy, int32_t* __restrict__ accepted,
+                                                     int64_t* __restrict__ tokens, int32_t* __restrict__ info) {
+  __shared__ double w[VMAX];
+  __shared__ double sv[256];
+  __shared__ int si[256];
+  __shared__ int s_done, s_acc, s_tok, s_ui, s_res, s_fb;
+  const int b = blockIdx.x;
+  const double* pb = p + static_cast<size_t>(b) * (gamma + 1) * V;
+  const double* qb = q ? q + static_cast<size_t>(b) * gamma * V : nullptr;
+  const int64_t* xb = x + static_cast<size_t>(b) * gamma;
+  const double* ub = u ? u + static_cast<size_t>(b) * (gamma + 1) : nullptr;
+  int64_t* tb = tokens + static_cast<size_t>(b) * (gamma + 1);
+  if (threadIdx.x == 0) {
+    s_done = 0;
+    s_acc = 0;
+    s_ui = 0;
+    s_res = 0;
+    s_fb = 0;
+    s_tok = -1;
+  }
+  for (int i = threadIdx.x; i <= gamma; i += blockDim.x) tb[i] = -1;
+  __syncthreads();
+  for (int i = 0; i < gamma; ++i) {
+    const double* pi = pb + static_cast<size_t>(i) * V;
+    const int64_t xi = xb[i];
+    if (greedy) {
+      const int am = block_argmax(pi, V, sv, si);
+      if (threadIdx.x == 0) {
+        if (xi == am) {
+          tb[i] = am;
+          s_acc = i + 1;
+        } else {
+          s_tok = am;
+          s_res = 1;
+          s_done = 1;
+        }
+      }
+      __syncthreads();
+    } else {
+      const double* qi = qb + static_cast<size_t>(i) * V;
+      if (threadIdx.x == 0) {
+        const double r = ub[s_ui++];
+        const bool ok = xi >= 0 && xi < V && r < accept_prob(pi[xi], qi[xi]);
+        if (ok) {
+          tb[i] = xi;
+          s_acc = i + 1;
+        } else {
+          s_done = 1;
+        }
+      }
+      __syncthreads();
+      if (s_done) {
+        for (int v = threadIdx.x; v < V; v += blockDim.x) w[v] = fmax(pi[v] - qi[v], 0.0);
+        __syncthreads();
+        if (threadIdx.x == 0) {
+          const double mass = pairwise_sum(w, V);
+          const bool fb = !(mass > 0.0) || !isfinite(mass);
+          if (fb)
+            for (int v = 0; v < V; ++v) w[v] = fmax(pi[v], 0.0);
+          s_fb = fb ? 1 : 0;
+          s_res = 1;
+          s_tok = sample_clipped(w, V, ub[s_ui++]);
+        }
+        __syncthreads();
+      }
+    }
+    if (s_done) break;
+  }
+  if (!s_done) {
+    const double* pg = pb + static_cast<size_t>(gamma) * V;
+    if (greedy) {
+      const int am = block_argmax(pg, V, sv, si);
+      if (threadIdx.x == 0) s_tok = am;
+    } else {
+      for (int v = threadIdx.x; v < V; v += blockDim.x) w[v] = fmax(pg[v], 0.0);
+      __syncthreads();
+      if (threadIdx.x == 0) s_tok = sample_clipped(w, V, ub[s_ui++]);
+    }
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    tb[s_acc] = s_tok;
+    accepted[b] = s_acc;
+    info[3 * b + 0] = s_res;
+    info[3 * b + 1] = s_fb;
+    info[3 * b + 2] = s_ui;
+  }
+}
+
+__global__ void __launch_bounds__(256) sample_kernel(const double* __restrict__ rows, int V,
+                                                     const double* __restrict__ u, int64_t* __restrict__ out) {
+  __shared__ double w[VMAX];
+  const int r = blockIdx.x;
+  const double* row = rows + static_cast<size_t>(r) * V;
+  for (int v = threadIdx.x; v < V; v += blockDim.x) w[v] = fmax(row[v], 0.0);
+  __syncthreads();
+  if (threadIdx.x == 0) out[r] = sample_clipped(w, V, u[r]);
+}
+
+}  // namespace
+
+int launch_transform(const void* logits, int logits_fp64, int rows, int V, double temperature, int top_k,
+                     double* probs, cudaStream_t st) {
+  EVS_CHECK_ARG(V > 0 && V <= VMAX, "vocabulary must be in [1, 1024]");
+  if (rows <= 0) return EVS_OK;
+  transform_kernel<<<rows, 256, 0, st>>>(logits, logits_fp64, V, temperature, top_k, probs);
+  EVS_CUDA_TRY(cudaGetLastError());
+  return EVS_OK;
+}
+
+int launch_verify(const double* p, const double* q, const int64_t* x, const double* u, int B, int gamma, int V,
+                  int greedy, int32_t* accepted, int64_t* tokens, int32_t* info, cudaStream_t st) {
+  EVS_CHECK_ARG(V > 0 && V <= VMAX, "vocabulary must be in [1, 1024]");
+  EVS_CHECK_ARG(gamma >= 1, "gamma must be >= 1");
+  EVS_CHECK_ARG(greedy || (q != nullptr && u != nullptr), "sampling verification needs q and uniforms");
+  if (B <= 0) return EVS_OK;
+  verify_kernel<<<B, 256, 0, st>>>(p, q, x, u, gamma, V, greedy, accepted, tokens, info);
+  EVS_CUDA_TRY(cudaGetLastError());
+  return EVS_OK;
+}
+
+int launch_sample(const double* rows, int n, int V, const double* u, int64_t* out, cudaStream_t st) {
+  EVS_CHECK_ARG(V > 0 && V <= VMAX, "vocabulary must be in [1, 1024]");
+  if (n <= 0) return EVS_OK;
+  sample_kernel<<<n, 256, 0, st>>>(rows, V, u, out);
+  EVS_CUDA_TRY(cudaGetLastError());
+  return EVS_OK;
+}

@@ -26,6 +26,12 @@
 #include <stdint.h>
 #include <cuda_runtime.h>
 
+#if defined(__GNUC__)
+#define EVS_API __attribute__((visibility("default")))
+#else
+#define EVS_API
+#endif
+
 #ifdef __cplusplus
 extern "C" {
 #endif
@@ -86,44 +92,44 @@ typedef struct evs_state evs_state;
 typedef struct evs_drafter evs_drafter;
 
 /* ---- library ---- */
-int evs_version(void);
-const char* evs_last_error(void);
+EVS_API int evs_version(void);
+EVS_API const char* evs_last_error(void);
 /* EVS_OK when the current device is sm_100 (B200); EVS_ENODEV otherwise */
-int evs_device_check(void);
+EVS_API int evs_device_check(void);
 
 /* ---- target model (weights are caller-owned device memory, never copied) ----
  * replaces vortex StripedHyena construction + Evo2 weight loading (evspark/api.py:94-98) */
-int evs_model_create(const evs_model_config* cfg, evs_model** out);
-int evs_model_set_tensor(evs_model* m, int layer, int slot, const void* dev_ptr, int64_t numel);
+EVS_API int evs_model_create(const evs_model_config* cfg, evs_model** out);
+EVS_API int evs_model_set_tensor(evs_model* m, int layer, int slot, const void* dev_ptr, int64_t numel);
 /* validates every slot, builds TMA tensor maps and derived constants (poles = exp(log_poles)) */
-int evs_model_finalize(evs_model* m);
-void evs_model_destroy(evs_model* m);
+EVS_API int evs_model_finalize(evs_model* m);
+EVS_API void evs_model_destroy(evs_model* m);
 
 /* ---- per-sequence state: FIR history rings, per-position IIR states, KV cache, lengths ----
  * replaces model.initialize_inference_params (evspark/specdec/block/loop.py:341).
  * max_chunk bounds the tokens of one evs_forward call (prefill is chunked internally). */
-int evs_state_create(const evs_model* m, int max_batch, int max_seqlen, int max_chunk, evs_state** out);
-void evs_state_destroy(evs_state* s);
+EVS_API int evs_state_create(const evs_model* m, int max_batch, int max_seqlen, int max_chunk, evs_state** out);
+EVS_API void evs_state_destroy(evs_state* s);
 /* zero the lengths of every row (an empty cache; prefill may follow) */
-int evs_state_reset(evs_state* s, cudaStream_t stream);
+EVS_API int evs_state_reset(evs_state* s, cudaStream_t stream);
 /* full copy of every arena (clone_inference_params, driver.py:40-46) */
-int evs_state_copy(evs_state* dst, const evs_state* src, cudaStream_t stream);
+EVS_API int evs_state_copy(evs_state* dst, const evs_state* src, cudaStream_t stream);
 /* per-row consumed lengths (device-resident truth) -> host, and host -> device */
-int evs_state_get_lengths(const evs_state* s, int32_t* host_lengths, int batch, cudaStream_t stream);
-int evs_state_set_lengths(evs_state* s, const int32_t* host_lengths, int batch, cudaStream_t stream);
+EVS_API int evs_state_get_lengths(const evs_state* s, int32_t* host_lengths, int batch, cudaStream_t stream);
+EVS_API int evs_state_set_lengths(evs_state* s, const int32_t* host_lengths, int batch, cudaStream_t stream);
 /* replicate row 0 into rows [1, batch) (expand_inference_params, driver.py:96-142) */
-int evs_state_expand(evs_state* s, int batch, cudaStream_t stream);
+EVS_API int evs_state_expand(evs_state* s, int batch, cudaStream_t stream);
 /* move row idx into row 0 (collapse_inference_params, driver.py:145-176) */
-int evs_state_collapse(evs_state* s, int idx, cudaStream_t stream);
+EVS_API int evs_state_collapse(evs_state* s, int idx, cudaStream_t stream);
 /* vortex-layout export for tests/snapshots (snapshot_states, driver.py:243-278):
  * which = 0 outer FIR state [3d, width] fp32, 1 inner FIR state [d, width] fp32,
  *         2 IIR state [d, state_size] fp32, 3 KV rows [width, 2, H, Dh] in the data dtype;
  * dst is device memory */
-int evs_state_export(const evs_state* s, int layer, int which, int row, int width, void* dst,
+EVS_API int evs_state_export(const evs_state* s, int layer, int which, int row, int width, void* dst,
                      cudaStream_t stream);
 /* device address of the drafter-context ring of capture slot c: [max_batch, ring_len, d] fp32,
  * row P mod ring_len holds the injection-layer output at absolute position P */
-int evs_state_capture_ring(const evs_state* s, int c, float** dev_ptr, int* ring_len);
+EVS_API int evs_state_capture_ring(const evs_state* s, int c, float** dev_ptr, int* ring_len);
 
 /* ---- forward passes ----
  * ids: device int64 [batch, T] (row-major).  logits: device fp32 [batch, T, V] or NULL.
@@ -132,28 +138,39 @@ int evs_state_capture_ring(const evs_state* s, int c, float** dev_ptr, int* ring
  * evs_forward (driver.py:179-226 / 229-240): continue from the current state (block verify when
  *   T = γ+1, native step when T = 1).  retain != 0 keeps every per-position state so that
  *   evs_rollback is a pure slice (ChunkStash, slice.py:33-52). */
-int evs_prefill(const evs_model* m, evs_state* s, const int64_t* ids, int batch, int T, float* logits,
+EVS_API int evs_prefill(const evs_model* m, evs_state* s, const int64_t* ids, int batch, int T, float* logits,
                 int last_only, cudaStream_t stream);
-int evs_forward(const evs_model* m, evs_state* s, const int64_t* ids, int batch, int T, int retain,
+EVS_API int evs_forward(const evs_model* m, evs_state* s, const int64_t* ids, int batch, int T, int retain,
                 float* logits, cudaStream_t stream);
 /* roll every row back to block index k[b] of the last retained evs_forward (device int32 [batch])
  * (slice_states_to_accept, slice.py:117-191); zero data movement: per-row ring heads, IIR slot
  * index and KV length are updated */
-int evs_rollback(evs_state* s, const int32_t* k, int batch, cudaStream_t stream);
+EVS_API int evs_rollback(evs_state* s, const int32_t* k, int batch, cudaStream_t stream);
 
 /* ---- sampling transform and verification (fp64 decision math) ---- */
 /* probs[r] = apply_transform(logits[r], temperature, top_k) for r < rows; probs fp64 [rows, V]
- * (transforms.py:18-64) */
-int evs_transform(const float* logits, int rows, int V, float temperature, int top_k, double* probs,
-                  cudaStream_t stream);
+ * (transforms.py:18-64).  logits [rows, V] are fp32 (logits_fp64 == 0) or fp64 (!= 0, may hold -inf). */
+EVS_API int evs_transform(const void* logits, int logits_fp64, int rows, int V, double temperature, int top_k,
+                          double* probs, cudaStream_t stream);
 /* Leviathan verification of `batch` independent rounds (verifier.py:54-176).
  * p fp64 [batch, γ+1, V] target rows (transformed probabilities, or raw logits when greedy),
  * q fp64 [batch, γ, V] draft rows (unused when greedy), x int64 [batch, γ] draft tokens,
  * u fp64 [batch, γ+1] uniforms in draw order (a round consumes a prefix of them).
  * Outputs: accepted int32 [batch], tokens int64 [batch, γ+1] (-1 padded),
  * info int32 [batch, 3] = {from_residual, fallback, uniforms consumed}. */
-int evs_verify(const double* p, const double* q, const int64_t* x, const double* u, int batch, int gamma, int V,
+EVS_API int evs_verify(const double* p, const double* q, const int64_t* x, const double* u, int batch, int gamma, int V,
                int greedy, int32_t* accepted, int64_t* tokens, int32_t* info, cudaStream_t stream);
+
+/* sample_categorical (verifier.py:37-40) for n rows: clip at 0, normalise, inverse CDF with u[r];
+ * rows fp64 [n, V], u fp64 [n], out int64 [n] */
+EVS_API int evs_sample(const double* rows, int n, int V, const double* u, int64_t* out, cudaStream_t stream);
+
+/* Dense projection used inside evs_forward, exposed for tests and benchmarks:
+ * out[m][n] = sum_k X[m][k] * W[n][k], bf16 inputs, fp32 accumulate/output, tcgen05 path.
+ * W [N, K], X [M, K] row-major device bf16 (16-byte aligned, N % 128 == 0, K % 64 == 0,
+ * M <= 4096); out fp32 [M, N].  splits <= 0 picks the same K split as evs_forward. */
+EVS_API int evs_gemm_bf16(const void* W, const void* X, float* out, int N, int K, int M, int splits,
+                  cudaStream_t stream);
 
 /* ---- γ-parallel drafter (fp32; evspark/train/drafter.py Drafter parameters) ---- */
 typedef struct evs_drafter_config {
@@ -161,25 +178,47 @@ typedef struct evs_drafter_config {
       mlp_mult;
 } evs_drafter_config;
 
-/* drafter tensor ids follow evspark_b200.weights.drafter_weight_specs order
- * (NeuralDraftModel.from_checkpoint, neural_draft.py:285-303) */
-int evs_drafter_create(const evs_drafter_config* cfg, int max_batch, evs_drafter** out);
-int evs_drafter_set_tensor(evs_drafter* d, int tensor_id, const void* dev_ptr, int64_t numel);
-int evs_drafter_finalize(evs_drafter* d);
-void evs_drafter_destroy(evs_drafter* d);
+/* drafter tensor ids (parameter names of the reference Drafter, evspark/train/drafter.py:274-336);
+ * layer l tensors are EVS_D_LAYER0 + l * EVS_D_PER_LAYER + {LN1, Q, K, V, O, LN2, MLP0_W, MLP0_B,
+ * MLP2_W, MLP2_B} */
+enum evs_drafter_tensor {
+  EVS_D_EMBED = 0,    /* embed.weight     [V, H]   (frozen target embedding, fp32) */
+  EVS_D_IN_W = 1,     /* in_proj.weight   [d, H] */
+  EVS_D_IN_B = 2,     /* in_proj.bias     [d] */
+  EVS_D_OUT_W = 3,    /* out_proj.weight  [H, d] */
+  EVS_D_OUT_B = 4,    /* out_proj.bias    [H] */
+  EVS_D_POS = 5,      /* pos.weight       [gamma, d] */
+  EVS_D_CTX_W = 6,    /* ctx_proj.weight  [d, n_inject*H] */
+  EVS_D_CTX_B = 7,    /* ctx_proj.bias    [d] */
+  EVS_D_CTX_NORM = 8, /* ctx_norm.scale   [d] */
+  EVS_D_FINAL_LN = 9, /* final_ln.scale   [d] */
+  EVS_D_MARKOV = 10,  /* markov           [V, V] */
+  EVS_D_CONF_W = 11,  /* conf_w.weight    [1, 2d] */
+  EVS_D_CONF_B = 12,  /* conf_w.bias      [1] */
+  EVS_D_LAYER0 = 16,
+  EVS_D_PER_LAYER = 10,
+  EVS_D_LN1 = 0, EVS_D_Q = 1, EVS_D_K = 2, EVS_D_V = 3, EVS_D_O = 4, EVS_D_LN2 = 5,
+  EVS_D_MLP0_W = 6, EVS_D_MLP0_B = 7, EVS_D_MLP2_W = 8, EVS_D_MLP2_B = 9
+};
+#define EVS_D_MAX_LAYERS 8
+/* (NeuralDraftModel.from_checkpoint, neural_draft.py:285-303) */
+EVS_API int evs_drafter_create(const evs_drafter_config* cfg, int max_batch, evs_drafter** out);
+EVS_API int evs_drafter_set_tensor(evs_drafter* d, int tensor_id, const void* dev_ptr, int64_t numel);
+EVS_API int evs_drafter_finalize(evs_drafter* d);
+EVS_API void evs_drafter_destroy(evs_drafter* d);
 /* One drafting round per row (propose_block, neural_draft.py:323-363): context = the last
  * min(ctx_window, len) captured rows of the state, trunk over [anchor, MASK x (γ'-1)], then the
  * serial Markov head.  anchor int64 [batch]; u fp64 [batch, γ'] uniforms (sampling);
  * forced int64 [batch, γ'] or NULL.  Outputs: tokens int64 [batch, γ'], q fp64 [batch, γ', V]
  * (q' rows when sampling, raw q when greedy), conf fp32 [batch, γ'], U fp32 [batch, γ', V]
  * trunk logits (may be NULL). */
-int evs_draft_propose(evs_drafter* d, const evs_state* s, const int64_t* anchor, int batch, int gamma,
-                      int greedy, float temperature, int top_k, const double* u, const int64_t* forced,
+EVS_API int evs_draft_propose(evs_drafter* d, const evs_state* s, const int64_t* anchor, int batch, int gamma,
+                      int greedy, double temperature, int top_k, const double* u, const int64_t* forced,
                       int64_t* tokens, double* q, float* conf, float* U, cudaStream_t stream);
 
 /* ---- device error word ---- */
-int evs_get_device_error(const evs_state* s, int32_t* code, int32_t* where, int32_t* info);
-int evs_clear_device_error(evs_state* s, cudaStream_t stream);
+EVS_API int evs_get_device_error(const evs_state* s, int32_t* code, int32_t* where, int32_t* info);
+EVS_API int evs_clear_device_error(evs_state* s, cudaStream_t stream);
 
 #ifdef __cplusplus
 }
