@@ -88,6 +88,9 @@ _PROTOS = {
     "evs_drafter_finalize": (_I, [_P]),
     "evs_drafter_destroy": (None, [_P]),
     "evs_draft_propose": (_I, [_P, _P, _P, _I, _I, _I, C.c_double, _I, _P, _P, _P, _P, _P, _P, _P]),
+    "evs_profile_start": (_I, [_P]),
+    "evs_profile_stop": (_I, [_P, _P, _P, _P]),
+    "evs_launch_count": (C.c_int64, []),
     "evs_get_device_error": (_I, [_P, C.POINTER(C.c_int32), C.POINTER(C.c_int32), C.POINTER(C.c_int32)]),
     "evs_clear_device_error": (_I, [_P, _P]),
 }

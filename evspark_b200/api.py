@@ -1,0 +1,171 @@
+"""Public facade, same names and defaults as evspark/api.py:31-216.
+
+    from evspark_b200 import EvSpark
+    es = EvSpark.load(model_name="evo2_7b")            # random-init target + drafter of that shape
+    res = es.generate("ACGT..." * 16, n_tokens=1024)   # sampling, T=1.0, top_k=4
+    g = es.generate(prompt, greedy=True)
+    nat = es.generate_native(prompt, greedy=True)
+    assert g.ids.tolist() == nat.ids.tolist()
+
+Real Evo2 weights and trained drafter checkpoints are not available offline: the target is a
+seeded random-init StripedHyena2 of the named shape, and the drafter is loaded from a local
+checkpoint of the reference's .pt schema when ``ckpt`` is a file, else seeded random-init.
+"""
+
+from __future__ import annotations
+
+import time
+from dataclasses import dataclass, field
+from pathlib import Path
+
+import numpy as np
+
+DEFAULT_CKPT = "L27_g12_150M_s1"
+
+
+def clean_prompt(seq: str) -> str:
+    """Upper-case and validate ACGTN; reject short prompts (evspark/api.py:31-39)."""
+    seq = "".join(seq.split()).upper()
+    bad = sorted(set(seq) - set("ACGTN"))
+    if bad:
+        raise ValueError(f"prompt contains non-ACGTN characters: {bad}")
+    if len(seq) < 64:
+        raise ValueError("prompt too short (<64 bp); give the model some context")
+    return seq
+
+
+def ids_to_text(ids) -> str:
+    """token id = ASCII byte (CharLevelTokenizer convention)."""
+    arr = np.clip(np.asarray(ids, dtype=np.int64).ravel(), 0, 255)
+    return bytes(arr.tolist()).decode("ascii", errors="replace")
+
+
+def tokenize(seq: str) -> np.ndarray:
+    return np.frombuffer(seq.encode("ascii"), dtype=np.uint8).astype(np.int64)
+
+
+@dataclass
+class GenerateResult:
+    text: str
+    ids: np.ndarray
+    mode: str
+    speculative: bool
+    n_tokens: int
+    wall_s: float
+    tok_s: float
+    mean_tau: float | None = None
+    n_rounds: int | None = None
+    extra: dict = field(default_factory=dict)
+
+
+class EvSpark:
+    def __init__(self, model, nd, device: str = "cuda:0"):
+        self.model = model
+        self._nd = nd
+        self.device = device
+
+    @classmethod
+    def load(cls, ckpt: str | None = DEFAULT_CKPT, model_name: str = "evo2_7b", device: str = "cuda:0",
+             use_kernels: bool = True, *, seed: int = 20260820, drafter_seed: int = 20260830,
+             max_chunk: int = 32) -> "EvSpark":
+        import torch
+
+        from evspark_b200.config import DRAFTERS, target_config
+        from evspark_b200.drafter import DeviceDrafter, load_checkpoint, layer_index
+        from evspark_b200.model import TargetModel, require_device
+        from evspark_b200.specdec.block.neural_draft import NeuralDraftModel
+
+        if not use_kernels:
+            raise ValueError("evspark_b200 has one compute path: the sm_100a kernels (use_kernels=True)")
+        require_device(device)
+        cfg = target_config(model_name)
+        path = Path(str(ckpt)) if ckpt else None
+        if path is not None and path.is_file():
+            dcfg_layers = torch.load(path, map_location="cpu")["scheme"]
+            from evspark_b200.drafter import SCHEME_LAYERS
+
+            layers = SCHEME_LAYERS[dcfg_layers]
+        else:
+            layers = DRAFTERS[model_name].inject_layers
+        init_on = "cuda" if cfg.d_model >= 1024 else "cpu"
+        model = TargetModel.random(cfg, seed=seed, device=device, init_on=init_on,
+                                   capture_layers=tuple(layer_index(n) for n in layers), max_chunk=max_chunk)
+        if path is not None and path.is_file():
+            drafter, layers, meta = load_checkpoint(str(path), cfg.d_model, device=device)
+        else:
+            dcfg = DRAFTERS[model_name]
+            drafter = DeviceDrafter.random(dcfg, seed=drafter_seed, embed=model.weights["embed"], device=device,
+                                           init_on=init_on)
+        nd = NeuralDraftModel(model, drafter, tuple(layers))
+        return cls(model, nd, device)
+
+    @property
+    def gamma(self) -> int:
+        return int(self._nd.gamma)
+
+    def _ids(self, prompt: str):
+        import torch
+
+        seq = clean_prompt(prompt)
+        return seq, torch.as_tensor(tokenize(seq)[None], device=self.model.device)
+
+    def generate(self, prompt: str, n_tokens: int = 256, *, greedy: bool = False, gamma: int | None = None,
+                 seed: int = 0, temperature: float = 1.0, top_k: int = 4) -> GenerateResult:
+        import torch
+
+        from evspark_b200.specdec.block.loop import speculative_generate
+
+        seq, ids = self._ids(prompt)
+        g = int(gamma) if gamma else self.gamma
+        self._nd.capture_reset()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        spec = speculative_generate(self.model, self._nd, ids, int(n_tokens), g, greedy=greedy,
+                                    rng=np.random.default_rng(seed), temperature=temperature, top_k=top_k,
+                                    rollback="slice", timing=False)
+        torch.cuda.synchronize()
+        wall = time.perf_counter() - t0
+        spec.inference_params_dict.close()
+        ks = [int(r.k) for r in spec.rounds_log]
+        out = np.asarray(spec.emitted_ids)
+        return GenerateResult(text=ids_to_text(out), ids=out, mode="greedy" if greedy else "sampling",
+                              speculative=True, n_tokens=int(n_tokens), wall_s=wall,
+                              tok_s=float(n_tokens / wall) if wall > 0 else float("nan"),
+                              mean_tau=float(np.mean(ks) + 1.0) if ks else None, n_rounds=len(ks),
+                              extra={"gamma": g, "seed": seed, "prompt_bp": len(seq), "rounds": spec.rounds_log})
+
+    def generate_native(self, prompt: str, n_tokens: int = 256, *, greedy: bool = False, seed: int = 0,
+                        temperature: float = 1.0, top_k: int = 4) -> GenerateResult:
+        import torch
+
+        from evspark_b200.specdec.block.loop import native_greedy_reference, native_sample_reference
+
+        seq, ids = self._ids(prompt)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        if greedy:
+            out, ip, _ = native_greedy_reference(self.model, ids, int(n_tokens))
+            ip.close()
+        else:
+            out = native_sample_reference(self.model, ids, int(n_tokens), np.random.default_rng(seed),
+                                          temperature=temperature, top_k=top_k)
+        torch.cuda.synchronize()
+        wall = time.perf_counter() - t0
+        out = np.asarray(out)
+        return GenerateResult(text=ids_to_text(out), ids=out, mode="greedy" if greedy else "sampling",
+                              speculative=False, n_tokens=int(n_tokens), wall_s=wall,
+                              tok_s=float(n_tokens / wall) if wall > 0 else float("nan"),
+                              extra={"seed": seed, "prompt_bp": len(seq)})
+
+    def close(self) -> None:
+        if self._nd is not None:
+            self._nd.close()
+            self._nd = None
+        if self.model is not None:
+            self.model.close()
+
+    def __enter__(self) -> "EvSpark":
+        return self
+
+    def __exit__(self, *exc) -> None:
+        self.close()

@@ -181,6 +181,7 @@ int launch_attention_t(const evs_model* m, evs_state* s, int layer, int B, int T
   attn_combine_kernel<TD><<<dim3(M, H), Dh, 0, st>>>(s->attn_part, s->d_len, T, d, H, Dh, s->attn_blocks,
                                                      s->max_chunk, static_cast<TD*>(s->act), s->ld_act);
   EVS_CUDA_TRY(cudaGetLastError());
+  evs_count_launch(3);
   return EVS_OK;
 }
 

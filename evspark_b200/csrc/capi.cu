@@ -1,5 +1,6 @@
 // C ABI entry points: model / state handles and the layer-loop orchestration of one forward.
 #include <algorithm>
+#include <atomic>
 #include <cstring>
 #include <string>
 
@@ -74,6 +75,28 @@ int gemm(const evs_model* m, evs_state* s, const CUtensorMap* tA, const CUtensor
   return launch_gemm_simt(W, W2, s->act, s->ld_act, m->cfg.dtype, p, s->ws, st);
 }
 
+cudaEvent_t take_event(evs_state* s) {
+  if (s->ev_used == s->ev_pool.size()) {
+    cudaEvent_t e;
+    if (cudaEventCreate(&e) != cudaSuccess) return nullptr;
+    s->ev_pool.push_back(e);
+  }
+  return s->ev_pool[s->ev_used++];
+}
+
+// run fn(); when profiling, bracket it with events on the stream and record its algorithmic bytes
+template <typename F>
+int timed(evs_state* s, cudaStream_t st, int kind, double bytes, F&& fn) {
+  if (!s->prof) return fn();
+  cudaEvent_t a = take_event(s), b = take_event(s);
+  if (a == nullptr || b == nullptr) return fn();
+  cudaEventRecord(a, st);
+  const int r = fn();
+  cudaEventRecord(b, st);
+  s->prof_recs.push_back({kind, a, b, bytes});
+  return r;
+}
+
 int run_forward(const evs_model* m, evs_state* s, const int64_t* ids, int B, int T, int prefill, int retain,
                 float* logits, int out_T, int t0, int last_only, cudaStream_t st) {
   const evs_model_config& c = m->cfg;
@@ -85,29 +108,51 @@ int run_forward(const evs_model* m, evs_state* s, const int64_t* ids, int B, int
   EVS_CHECK_RANGE(maxlen + T <= s->max_seqlen, "sequence would exceed max_seqlen");
   const int M = B * T;
   const int kv_blocks = (maxlen + T + ATTN_BLOCK - 1) / ATTN_BLOCK;
-  EVS_TRY(launch_embed_norm(m, s, ids, M, static_cast<const float*>(m->L[0].pre_norm), st));
+  const double el = static_cast<double>(m->elem());
+  const int H = c.n_heads, Dh = c.head_dim, S = c.state_size;
   int sp = 1;
+  // one projection, timed with its algorithmic bytes (weights + activations in + fp32 partials out)
+  auto G = [&](const CUtensorMap* tA, const CUtensorMap* tA2, const void* W, const void* W2, int N, int K, int dual) {
+    const GemmPlan pl = gemm_plan(m, N, K, M, dual);
+    const double bytes = (static_cast<double>(N) * K + static_cast<double>(M) * K) * el + 4.0 * pl.splits * M * N;
+    return timed(s, st, EVS_PROF_GEMM, bytes, [&] { return gemm(m, s, tA, tA2, W, W2, N, K, M, dual, st, &sp); });
+  };
+  const double row_bytes = static_cast<double>(M) * d * (8.0 + el);
+  EVS_TRY(timed(s, st, EVS_PROF_ROW, row_bytes,
+                [&] { return launch_embed_norm(m, s, ids, M, static_cast<const float*>(m->L[0].pre_norm), st); }));
   for (int i = 0; i < c.n_layers; ++i) {
     const LayerDev& L = m->L[i];
     if (L.kind == EVS_LAYER_MHA) {
-      EVS_TRY(gemm(m, s, &L.tm_qkv, nullptr, L.w_qkv, nullptr, 3 * d, d, M, 0, st, &sp));
-      EVS_TRY(launch_attention(m, s, i, B, T, sp, kv_blocks, st));
-      EVS_TRY(gemm(m, s, &L.tm_o, nullptr, L.w_o, nullptr, d, d, M, 0, st, &sp));
+      EVS_TRY(G(&L.tm_qkv, nullptr, L.w_qkv, nullptr, 3 * d, d, 0));
+      const double kv_bytes = 2.0 * B * (maxlen + T) * H * Dh * el + 4.0 * sp * M * 3 * d + 2.0 * M * d * el;
+      EVS_TRY(timed(s, st, EVS_PROF_ATTN, kv_bytes, [&] { return launch_attention(m, s, i, B, T, sp, kv_blocks, st); }));
+      EVS_TRY(G(&L.tm_o, nullptr, L.w_o, nullptr, d, d, 0));
     } else {
-      EVS_TRY(gemm(m, s, &L.tm_in, nullptr, L.w_in, nullptr, 3 * d, d, M, 0, st, &sp));
-      EVS_TRY(launch_hyena(m, s, i, B, T, sp, prefill, retain, st));
-      EVS_TRY(gemm(m, s, &L.tm_out, nullptr, L.w_out, nullptr, d, d, M, 0, st, &sp));
+      EVS_TRY(G(&L.tm_in, nullptr, L.w_in, nullptr, 3 * d, d, 0));
+      const int K = L.kind == EVS_LAYER_HCM ? c.hcm_filter_length : c.hcs_filter_length;
+      const int K0 = c.short_filter_length;
+      // u in + y out + outer history read/write + taps; inner FIR history or IIR states
+      double hb = B * ((2.0 * T * 3 * d + (K0 - 1) * 3.0 * d + T * d) * el) + 3.0 * d * K0 * 4;
+      if (L.kind == EVS_LAYER_HCL)
+        hb += B * (static_cast<double>(d) * S * 4 * (1 + (retain ? T : 1))) + 3.0 * d * S * 4;
+      else
+        hb += B * ((K - 1.0 + T) * d * el) + static_cast<double>(d) * K * 4;
+      EVS_TRY(timed(s, st, EVS_PROF_HYENA, hb, [&] { return launch_hyena(m, s, i, B, T, sp, prefill, retain, st); }));
+      EVS_TRY(G(&L.tm_out, nullptr, L.w_out, nullptr, d, d, 0));
     }
-    EVS_TRY(launch_res_add_norm(m, s, M, sp, static_cast<const float*>(L.post_norm), -1, T, st));
-    EVS_TRY(gemm(m, s, &L.tm_w1, &L.tm_w2, L.w1, L.w2, 2 * F, d, M, 1, st, &sp));
-    EVS_TRY(launch_swiglu(m, s, M, sp, st));
-    EVS_TRY(gemm(m, s, &L.tm_w3, nullptr, L.w3, nullptr, d, F, M, 0, st, &sp));
+    EVS_TRY(timed(s, st, EVS_PROF_ROW, row_bytes + 4.0 * sp * M * d,
+                  [&] { return launch_res_add_norm(m, s, M, sp, static_cast<const float*>(L.post_norm), -1, T, st); }));
+    EVS_TRY(G(&L.tm_w1, &L.tm_w2, L.w1, L.w2, 2 * F, d, 1));
+    EVS_TRY(timed(s, st, EVS_PROF_ROW, 8.0 * sp * M * F + M * F * el, [&] { return launch_swiglu(m, s, M, sp, st); }));
+    EVS_TRY(G(&L.tm_w3, nullptr, L.w3, nullptr, d, F, 0));
     const float* next = static_cast<const float*>(i + 1 < c.n_layers ? m->L[i + 1].pre_norm : m->final_norm);
-    EVS_TRY(launch_res_add_norm(m, s, M, sp, next, m->capture_slot(i), T, st));
+    EVS_TRY(timed(s, st, EVS_PROF_ROW, row_bytes + 4.0 * sp * M * d,
+                  [&] { return launch_res_add_norm(m, s, M, sp, next, m->capture_slot(i), T, st); }));
   }
   if (logits != nullptr) {
-    EVS_TRY(gemm(m, s, &m->tm_embed, nullptr, m->embed, nullptr, V, d, M, 0, st, &sp));
-    EVS_TRY(launch_logits(m, s, M, T, sp, logits, out_T, t0, last_only, st));
+    EVS_TRY(G(&m->tm_embed, nullptr, m->embed, nullptr, V, d, 0));
+    EVS_TRY(timed(s, st, EVS_PROF_ROW, 4.0 * (sp + 1) * M * V,
+                  [&] { return launch_logits(m, s, M, T, sp, logits, out_T, t0, last_only, st); }));
   }
   EVS_TRY(launch_bookkeeping(s, B, T, retain, st));
   for (int b = 0; b < B; ++b) s->h_len[b] += T;
@@ -116,6 +161,12 @@ int run_forward(const evs_model* m, evs_state* s, const int64_t* ids, int B, int
 }
 
 }  // namespace
+
+namespace {
+std::atomic<long long> g_launches{0};
+}
+
+void evs_count_launch(int n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
 
 void evs_set_last_error(int code, const char* msg) {
   (void)code;
@@ -380,6 +431,7 @@ int evs_state_create(const evs_model* m, int max_batch, int max_seqlen, int max_
 
 void evs_state_destroy(evs_state* s) {
   if (s == nullptr) return;
+  for (cudaEvent_t e : s->ev_pool) cudaEventDestroy(e);
   for (void* p : s->owned) cudaFree(p);
   delete s;
 }
@@ -563,6 +615,37 @@ int evs_gemm_bf16(const void* W, const void* X, float* out, int N, int K, int M,
   EVS_CHECK_ARG(p.splits == 1, "evs_gemm_bf16 writes out directly: use splits == 1 or <= 0 with one split");
   return launch_gemm_tc(&ta, nullptr, &tb, p, out, nullptr, st);
 }
+
+int evs_profile_start(evs_state* s) {
+  EVS_CHECK_ARG(s != nullptr, "null state");
+  s->prof = true;
+  s->prof_recs.clear();
+  s->ev_used = 0;
+  return EVS_OK;
+}
+
+int evs_profile_stop(evs_state* s, int64_t* launches, double* ms, double* bytes) {
+  EVS_CHECK_ARG(s && launches && ms && bytes, "null argument");
+  for (int k = 0; k < EVS_PROF_KINDS; ++k) {
+    launches[k] = 0;
+    ms[k] = 0.0;
+    bytes[k] = 0.0;
+  }
+  if (!s->prof_recs.empty()) EVS_CUDA_TRY(cudaEventSynchronize(s->prof_recs.back().b));
+  for (const auto& r : s->prof_recs) {
+    float t = 0.f;
+    EVS_CUDA_TRY(cudaEventElapsedTime(&t, r.a, r.b));
+    launches[r.kind] += 1;
+    ms[r.kind] += t;
+    bytes[r.kind] += r.bytes;
+  }
+  s->prof = false;
+  s->prof_recs.clear();
+  s->ev_used = 0;
+  return EVS_OK;
+}
+
+int64_t evs_launch_count(void) { return g_launches.load(); }
 
 int evs_get_device_error(const evs_state* s, int32_t* code, int32_t* where, int32_t* info) {
   EVS_CHECK_ARG(s && code && where && info, "null argument");

@@ -204,6 +204,8 @@ __host__ __device__ constexpr uint32_t umma_idesc_bf16(int M, int N) {
 // host-side status plumbing
 // ---------------------------------------------------------------------------
 void evs_set_last_error(int code, const char* msg);
+// process-wide count of kernels launched by this library (evs_launch_count)
+void evs_count_launch(int n);
 
 #define EVS_CUDA_TRY(expr)                                   \
   do {                                                       \

@@ -484,6 +484,9 @@ int evs_draft_propose(evs_drafter* dr, const evs_state* s, const int64_t* anchor
   bias_pos_kernel<<<blocks_for(static_cast<size_t>(rows) * d, 256), 256, 0, st>>>(dr->pe, T[EVS_D_IN_B], nullptr, g,
                                                                                  d, rows);
   conf_kernel<<<blocks_for(rows, 4), 128, 0, st>>>(dr->xb, dr->pe, T[EVS_D_CONF_W], T[EVS_D_CONF_B], d, rows, conf);
+  // non-GEMM kernels of this call (the projections count themselves): context gather + norm,
+  // embed + bias/pos, 7 per layer, final norm + bias + scale, serial head, conf embed + bias + dot
+  evs_count_launch((c.n_inject > 0 ? 2 : 0) + 2 + 7 * c.n_layers + 3 + 4);
   if (U_out != nullptr)
     EVS_CUDA_TRY(cudaMemcpyAsync(U_out, dr->U, sizeof(float) * rows * V, cudaMemcpyDeviceToDevice, st));
   EVS_CUDA_TRY(cudaGetLastError());

@@ -194,6 +194,7 @@ int launch_tc(const CUtensorMap* tmA, const CUtensorMap* tmA2, const CUtensorMap
   gemm_tc_kernel<NT><<<grid, 192, C::SMEM, st>>>(*tmA, tmA2 ? *tmA2 : *tmA, *tmB, ws, p.N, p.K, p.M, p.splits,
                                                   p.dual, err);
   EVS_CUDA_TRY(cudaGetLastError());
+  evs_count_launch(1);
   return EVS_OK;
 }
 
@@ -257,5 +258,6 @@ int launch_gemm_simt(const void* W, const void* W2, const void* X, int ldx, int 
                                                          p.splits, p.dual);
   }
   EVS_CUDA_TRY(cudaGetLastError());
+  evs_count_launch(1);
   return EVS_OK;
 }

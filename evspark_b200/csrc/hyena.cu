@@ -281,6 +281,7 @@ int launch_hyena_t(const evs_model* m, evs_state* s, int layer, int B, int T, in
     }
   }
   EVS_CUDA_TRY(cudaGetLastError());
+  evs_count_launch(1);
   return EVS_OK;
 }
 
@@ -297,6 +298,7 @@ int launch_hyena(const evs_model* m, evs_state* s, int layer, int B, int T, int 
 int launch_rollback(evs_state* s, const int32_t* k, int B, cudaStream_t st) {
   rollback_kernel<<<(B + 127) / 128, 128, 0, st>>>(s->d_len, s->d_len0, s->d_iir_cur, s->d_chunk, k, B, s->d_err);
   EVS_CUDA_TRY(cudaGetLastError());
+  evs_count_launch(1);
   return EVS_OK;
 }
 
@@ -335,5 +337,6 @@ int launch_state_export(const evs_state* s, int layer, int which, int row, int w
     EVS_CHECK_ARG(false, "unknown export kind");
   }
   EVS_CUDA_TRY(cudaGetLastError());
+  evs_count_launch(1);
   return EVS_OK;
 }

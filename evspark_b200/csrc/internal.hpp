@@ -90,6 +90,16 @@ struct evs_state {
   int64_t* ids_scratch = nullptr;  // [m_cap] chunk ids of a strided prefill
   EvsDevErr* d_err = nullptr;
   CUtensorMap tm_act_d, tm_act_f;  // activation buffer viewed with K = d and K = F
+  // profiling (evs_profile_start / evs_profile_stop)
+  struct ProfRec {
+    int kind;
+    cudaEvent_t a, b;
+    double bytes;
+  };
+  bool prof = false;
+  std::vector<ProfRec> prof_recs;
+  std::vector<cudaEvent_t> ev_pool;
+  size_t ev_used = 0;
   std::vector<void*> owned;        // [0] persistent arenas, [1] scratch
   std::vector<size_t> owned_bytes;
 };

@@ -146,6 +146,7 @@ int launch_embed_norm(const evs_model* m, evs_state* s, const int64_t* ids, int 
                                                         static_cast<float*>(s->act), s->ld_act, d,
                                                         m->cfg.vocab_size, m->cfg.eps, s->d_err);
   EVS_CUDA_TRY(cudaGetLastError());
+  evs_count_launch(1);
   return EVS_OK;
 }
 
@@ -162,6 +163,7 @@ int launch_res_add_norm(const evs_model* m, evs_state* s, int M, int splits, con
                                                           static_cast<float*>(s->act), s->ld_act, d, m->cfg.eps,
                                                           ring, s->ring_len, s->d_len, T);
   EVS_CUDA_TRY(cudaGetLastError());
+  evs_count_launch(1);
   return EVS_OK;
 }
 
@@ -174,6 +176,7 @@ int launch_swiglu(const evs_model* m, evs_state* s, int M, int splits, cudaStrea
   else
     swiglu_kernel<float><<<grid, ROW_THREADS, 0, st>>>(s->ws, splits, M, F, static_cast<float*>(s->act), s->ld_act);
   EVS_CUDA_TRY(cudaGetLastError());
+  evs_count_launch(1);
   return EVS_OK;
 }
 
@@ -183,17 +186,20 @@ int launch_logits(const evs_model* m, evs_state* s, int M, int T, int splits, fl
   dim3 grid((V + 255) / 256, M);
   logits_kernel<<<grid, 256, 0, st>>>(s->ws, splits, M, V, T, out_T, t0, last_only, logits);
   EVS_CUDA_TRY(cudaGetLastError());
+  evs_count_launch(1);
   return EVS_OK;
 }
 
 int launch_bookkeeping(evs_state* s, int B, int T, int retain, cudaStream_t st) {
   bookkeeping_kernel<<<(B + 127) / 128, 128, 0, st>>>(s->d_len, s->d_len0, s->d_iir_cur, s->d_chunk, B, T, retain);
   EVS_CUDA_TRY(cudaGetLastError());
+  evs_count_launch(1);
   return EVS_OK;
 }
 
 int launch_poles(const float* log_poles, float* poles, int n, cudaStream_t st) {
   poles_kernel<<<(n + 255) / 256, 256, 0, st>>>(log_poles, poles, n);
   EVS_CUDA_TRY(cudaGetLastError());
+  evs_count_launch(1);
   return EVS_OK;
 }

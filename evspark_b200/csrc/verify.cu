@@ -146,6 +146,7 @@ int launch_transform(const void* logits, int logits_fp64, int rows, int V, doubl
   if (rows <= 0) return EVS_OK;
   transform_kernel<<<rows, 256, 0, st>>>(logits, logits_fp64, V, temperature, top_k, probs);
   EVS_CUDA_TRY(cudaGetLastError());
+  evs_count_launch(1);
   return EVS_OK;
 }
 
@@ -157,6 +158,7 @@ int launch_verify(const double* p, const double* q, const int64_t* x, const doub
   if (B <= 0) return EVS_OK;
   verify_kernel<<<B, 256, 0, st>>>(p, q, x, u, gamma, V, greedy, accepted, tokens, info);
   EVS_CUDA_TRY(cudaGetLastError());
+  evs_count_launch(1);
   return EVS_OK;
 }
 
@@ -165,5 +167,6 @@ int launch_sample(const double* rows, int n, int V, const double* u, int64_t* ou
   if (n <= 0) return EVS_OK;
   sample_kernel<<<n, 256, 0, st>>>(rows, V, u, out);
   EVS_CUDA_TRY(cudaGetLastError());
+  evs_count_launch(1);
   return EVS_OK;
 }

@@ -1,0 +1,358 @@
+"""End-to-end speculative loop on the device path (mirror of evspark/specdec/block/loop.py).
+
+Anchor protocol (loop.py:1-19): the prompt's first L-1 tokens are prefilled, the last one is the
+anchor y; each round drafts γ tokens, verifies the chunk ``[y, x_1..x_γ]`` in one retained block
+forward (row i of the logits is p_{i+1}), accepts ``k`` drafts, emits ``k+1`` tokens, and rolls
+the state back to block index ``j* = take-1`` (skipped when all drafts are accepted and the round
+is not truncated).  The new anchor is the last emitted token.
+
+Per round on the device: drafting (neural drafter: one ``evs_draft_propose``), the block forward
+(``evs_forward``), the transform of the γ+1 target rows and verification (``evs_transform`` +
+``evs_verify``, fp64), and rollback (``evs_rollback``, zero data movement).  The host sees only
+the accepted length and tokens (one small copy per round).  The numpy generator advances exactly
+as in the reference: γ uniforms for sampled drafting, then the verifier's own draws.
+"""
+
+from __future__ import annotations
+
+import time
+from dataclasses import dataclass, field
+
+import numpy as np
+import torch
+
+from evspark_b200.specdec.block.driver import block_forward, prefill, step_forward_reference
+from evspark_b200.specdec.block.slice import slice_states_to_accept
+from evspark_b200.specdec.transforms import apply_transform, transform_rows
+from evspark_b200.specdec.verifier import draw_uniforms, rewind_uniforms, sample_categorical, verify_device
+
+VOCAB_SIZE = 512
+
+
+@dataclass
+class RoundLog:
+    k: int
+    replay_len: int
+    t_draft: float
+    t_block: float
+    t_verify: float
+    t_restore_replay: float
+    from_residual: bool = False
+    fallback: bool = False
+    n_emitted: int = 0
+    t_snapshot: float = 0.0
+    t_slice: float = 0.0
+    conf: list[float] | None = None
+    n_candidates: int = 1
+    winner: int = 0
+
+
+@dataclass
+class SpecGenerateResult:
+    emitted_ids: np.ndarray
+    rounds_log: list[RoundLog]
+    inference_params_dict: object = field(repr=False)
+    anchor: int = -1
+    emitted_logits: np.ndarray | None = None
+    rollback: str = "slice"
+
+    def __iter__(self):
+        yield self.emitted_ids
+        yield self.rounds_log
+
+
+def _as_prompt_ids(prompt_ids, device) -> torch.Tensor:
+    t = torch.as_tensor(prompt_ids).long()
+    if t.ndim == 1:
+        t = t[None]
+    if t.ndim != 2 or t.shape[0] != 1:
+        raise ValueError(f"prompt_ids must be [1, L] (independent streams use the batched API), got {tuple(t.shape)}")
+    return t.to(device)
+
+
+def _q_prime_from_raw(q: np.ndarray, temperature: float, top_k: int | None) -> np.ndarray:
+    """Draft distribution -> the target's sampling transform applied to log(q) (loop.py:111-128)."""
+    q = np.asarray(q, dtype=np.float64).ravel()
+    lg = np.full(q.shape[0], -np.inf)
+    pos = q > 0.0
+    if np.any(pos):
+        lg[pos] = np.log(q[pos])
+    else:
+        lg[:] = 0.0
+    return apply_transform(lg, temperature=temperature, top_k=top_k)
+
+
+def _propose_draft(draft, prefix: np.ndarray, gamma: int, greedy: bool, rng, *, temperature=1.0, top_k=4):
+    """``probs(prefix)`` drafters (identity, lookup, Markov): token by token (loop.py:131-162)."""
+    toks = np.empty(gamma, dtype=np.int64)
+    rows = np.empty((gamma, VOCAB_SIZE), dtype=np.float64)
+    buf = list(np.asarray(prefix, dtype=np.int64))
+    for i in range(gamma):
+        q = np.asarray(draft.probs(np.asarray(buf, dtype=np.int64)), dtype=np.float64).ravel()
+        if q.shape[0] != VOCAB_SIZE:
+            raise ValueError(f"draft.probs must return [{VOCAB_SIZE}], got {q.shape}")
+        if not greedy:
+            q = _q_prime_from_raw(q, temperature, top_k)
+        rows[i] = q
+        t = int(np.argmax(q)) if greedy else sample_categorical(q, rng)
+        toks[i] = t
+        buf.append(t)
+    return toks, rows
+
+
+def _sync(device) -> None:
+    torch.cuda.synchronize(device)
+
+
+@dataclass
+class RoundOutcome:
+    taken: np.ndarray
+    log: RoundLog
+    ip: object
+    logits_rows: list = field(default_factory=list)
+
+
+def spec_round(model, draft, ip, y: int, gamma: int, greedy: bool, rng: np.random.Generator, remaining: int, *,
+               seen: np.ndarray | None = None, temperature: float = 1.0, top_k: int | None = 4,
+               rollback: str = "slice", timing: bool = True, record_logits: bool = False,
+               chunk: torch.Tensor | None = None) -> RoundOutcome:
+    """One round of the anchor loop from state ``ip`` with anchor ``y``: draft, retained block
+    forward, device verification, rollback to j* = take-1, capture commit (loop.py:381-570)."""
+    device = model.device
+    has_device_draft = hasattr(draft, "propose_device")
+    has_propose = hasattr(draft, "propose_block")
+    has_capture = hasattr(draft, "capture_begin")
+    if chunk is None:
+        chunk = torch.empty(1, gamma + 1, dtype=torch.int64, device=device)
+    snap = None
+    t_snapshot = 0.0
+    if rollback == "snapshot":
+        t0 = time.perf_counter()
+        snap = ip.clone()
+        if timing:
+            _sync(device)
+        t_snapshot = time.perf_counter() - t0
+    # ---- draft ----
+    t0 = time.perf_counter()
+    conf_rows = None
+    conf_d = None
+    chunk[0, 0] = y
+    if has_device_draft:
+        toks_d, q_rows, conf_d = draft.propose_device(chunk[:, 0], gamma, greedy, rng, temperature=temperature,
+                                                      top_k=top_k, inference_params_dict=ip)
+        chunk[0, 1:] = toks_d[0]
+    else:
+        if has_propose:
+            toks, q_np, conf_rows = draft.propose_block(y, gamma, greedy, rng, temperature=temperature,
+                                                        top_k=top_k, inference_params_dict=ip)
+        else:
+            toks, q_np = _propose_draft(draft, seen, gamma, greedy, rng, temperature=temperature, top_k=top_k)
+        chunk[0, 1:] = torch.as_tensor(np.asarray(toks, dtype=np.int64), device=device)
+        q_rows = torch.as_tensor(np.ascontiguousarray(q_np), device=device)[None]
+    if timing:
+        _sync(device)
+    t_draft = time.perf_counter() - t0
+    # ---- block verify forward ----
+    if has_capture:
+        draft.capture_begin()
+    t0 = time.perf_counter()
+    logits, stash = block_forward(model, chunk, ip, retain=True)
+    if timing:
+        _sync(device)
+    t_block = time.perf_counter() - t0
+    # ---- verification (device, fp64) ----
+    t0 = time.perf_counter()
+    x = chunk[:, 1:]
+    state = None
+    if greedy:
+        acc, toks_v, info = verify_device(logits.double(), None, x, None, greedy=True)
+    else:
+        p = transform_rows(logits[0], temperature, top_k)[None]
+        uv, state = draw_uniforms(rng, gamma + 1)
+        acc, toks_v, info = verify_device(p, q_rows, x, torch.as_tensor(uv, device=device)[None], greedy=False)
+    res = torch.cat([acc.to(torch.int64), info[0].to(torch.int64), toks_v[0]]).cpu().numpy()
+    k = int(res[0])
+    from_residual, fallback, consumed = bool(res[1]), bool(res[2]), int(res[3])
+    tokens = res[4:4 + k + 1]
+    if state is not None:
+        rewind_uniforms(rng, state, consumed)
+    t_verify = time.perf_counter() - t0
+    take = min(k + 1, remaining)
+    taken = tokens[:take].astype(np.int64)
+    j_star = take - 1
+    full_accept_kept = (k == gamma) and (take == k + 1)
+    replay_len = 0
+    t_restore = t_snapshot
+    t_slice = 0.0
+    if not full_accept_kept:
+        if rollback == "snapshot":
+            t0 = time.perf_counter()
+            ip.close()
+            ip = snap
+            snap = None
+            consume = np.concatenate([[y], taken[:-1]]) if take > 1 else np.array([y])
+            replay_len = len(consume)
+            block_forward(model, torch.as_tensor(consume, device=device)[None], ip)
+            if timing:
+                _sync(device)
+            t_restore = t_snapshot + (time.perf_counter() - t0)
+        else:
+            t0 = time.perf_counter()
+            slice_states_to_accept(ip, stash, j_star)
+            if timing:
+                _sync(device)
+            t_slice = time.perf_counter() - t0
+    if snap is not None:
+        snap.close()
+    if has_capture:
+        draft.capture_commit(j_star + 1)
+    rows = []
+    if record_logits:
+        lg = logits[0].double().cpu().numpy()
+        rows = [lg[i] for i in range(take)]
+    if conf_d is not None:
+        conf_rows = conf_d[0].double().cpu().numpy()
+    log = RoundLog(k=k, replay_len=replay_len, t_draft=t_draft, t_block=t_block, t_verify=t_verify,
+                   t_restore_replay=t_restore, from_residual=from_residual, fallback=fallback, n_emitted=take,
+                   t_snapshot=t_snapshot, t_slice=t_slice,
+                   conf=None if conf_rows is None else [float(c) for c in conf_rows])
+    return RoundOutcome(taken=taken, log=log, ip=ip, logits_rows=rows)
+
+
+def speculative_generate(model, draft, prompt_ids, n_tokens: int, gamma: int, greedy: bool,
+                         rng: np.random.Generator, *, temperature: float = 1.0, top_k: int | None = 4,
+                         inference_params_dict=None, record_logits: bool = False, rollback: str = "slice",
+                         n_candidates: int = 1, timing: bool = True) -> SpecGenerateResult:
+    device = model.device
+    prompt = _as_prompt_ids(prompt_ids, device)
+    if int(n_candidates) != 1:
+        raise ValueError("n_candidates > 1 (multi-candidate verification) is not available on this path")
+    if n_tokens < 0:
+        raise ValueError("n_tokens must be >= 0")
+    if gamma < 1:
+        raise ValueError("gamma must be >= 1")
+    if rollback not in ("slice", "snapshot"):
+        raise ValueError(f"rollback must be 'slice' or 'snapshot', got {rollback!r}")
+    has_device_draft = hasattr(draft, "propose_device")
+    has_propose = hasattr(draft, "propose_block")
+    has_capture = hasattr(draft, "capture_begin")
+    if has_capture and rollback != "slice":
+        raise ValueError("the neural drafter needs rollback='slice' (rejected positions are trimmed at j*)")
+    if has_device_draft and int(gamma) > draft.gamma:
+        raise ValueError(f"decode γ={gamma} > drafter training γ={draft.gamma}")
+    L = int(prompt.shape[1])
+    if L < 2:
+        raise ValueError(f"prompt length must be >= 2 (the first round needs an anchor), got {L}")
+    prompt_np = prompt[0].cpu().numpy().astype(np.int64)
+    y = int(prompt_np[-1])
+    if n_tokens == 0:
+        ip = inference_params_dict or model.initialize_inference_params(max_seqlen=L + gamma + 2)
+        return SpecGenerateResult(np.empty(0, dtype=np.int64), [], ip, anchor=y, rollback=rollback)
+    seen = prompt_np.copy()
+    if inference_params_dict is None:
+        ip = model.initialize_inference_params(max_seqlen=L + n_tokens + gamma + 2)
+        if has_capture:
+            draft.capture_begin()
+        prefill(model, prompt[:, :-1], ip)
+        if has_capture:
+            draft.capture_commit(L - 1)
+    else:
+        ip = inference_params_dict
+        if has_capture and int(draft.capture_buffer_len()) != L - 1:
+            raise ValueError(f"external state: the drafter's H_ctx buffer is not aligned (对齐): consumed "
+                             f"{draft.capture_buffer_len()} != L-1={L - 1}")
+    emitted: list[int] = []
+    rounds: list[RoundLog] = []
+    logit_rows: list[np.ndarray] = []
+    chunk = torch.empty(1, gamma + 1, dtype=torch.int64, device=device)
+    while len(emitted) < n_tokens:
+        out = spec_round(model, draft, ip, y, gamma, greedy, rng, n_tokens - len(emitted), seen=seen,
+                         temperature=temperature, top_k=top_k, rollback=rollback, timing=timing,
+                         record_logits=record_logits, chunk=chunk)
+        ip = out.ip
+        if record_logits:
+            logit_rows.extend(out.logits_rows)
+        emitted.extend(int(t) for t in out.taken)
+        seen = np.concatenate([seen, out.taken])
+        y = int(out.taken[-1])
+        rounds.append(out.log)
+    out_logits = np.stack(logit_rows[:n_tokens]) if record_logits else None
+    return SpecGenerateResult(np.asarray(emitted[:n_tokens], dtype=np.int64), rounds, ip, anchor=y,
+                              emitted_logits=out_logits, rollback=rollback)
+
+
+def native_greedy_reference(model, prompt_ids, n_tokens: int, *, record_logits: bool = False):
+    """Token-by-token argmax (lowest index on ties) on the same kernels (loop.py:584-624)."""
+    device = model.device
+    prompt = _as_prompt_ids(prompt_ids, device)
+    if n_tokens < 0:
+        raise ValueError("n_tokens must be >= 0")
+    L = int(prompt.shape[1])
+    ip = model.initialize_inference_params(max_seqlen=L + max(n_tokens, 0) + 2)
+    if n_tokens == 0:
+        return np.empty(0, dtype=np.int64), ip, None
+    last = prefill(model, prompt, ip)[0, -1]
+    emitted = np.empty(n_tokens, dtype=np.int64)
+    rows = []
+    x = torch.empty(1, 1, dtype=torch.int64, device=device)
+    for i in range(n_tokens):
+        lg = last.double().cpu().numpy()
+        if record_logits:
+            rows.append(lg)
+        tok = int(np.argmax(lg))
+        emitted[i] = tok
+        if i + 1 < n_tokens:
+            x[0, 0] = tok
+            last = step_forward_reference(model, x, ip)[0, -1]
+    return emitted, ip, (np.stack(rows) if record_logits else None)
+
+
+def native_sample_reference(model, prompt_ids, n_tokens: int, rng: np.random.Generator, *,
+                            temperature: float = 1.0, top_k: int | None = 4) -> np.ndarray:
+    """Token-by-token sampling with the shared transform (loop.py:627-658)."""
+    device = model.device
+    prompt = _as_prompt_ids(prompt_ids, device)
+    if n_tokens < 0:
+        raise ValueError("n_tokens must be >= 0")
+    if n_tokens == 0:
+        return np.empty(0, dtype=np.int64)
+    L = int(prompt.shape[1])
+    ip = model.initialize_inference_params(max_seqlen=L + n_tokens + 2)
+    last = prefill(model, prompt, ip)[0, -1]
+    emitted = np.empty(n_tokens, dtype=np.int64)
+    x = torch.empty(1, 1, dtype=torch.int64, device=device)
+    from evspark_b200 import _native as N
+
+    for i in range(n_tokens):
+        probs = transform_rows(last[None], temperature, top_k)
+        u = torch.tensor([float(rng.random())], dtype=torch.float64, device=device)
+        out = torch.empty(1, dtype=torch.int64, device=device)
+        N.check(N.lib().evs_sample(probs.data_ptr(), 1, probs.shape[1], u.data_ptr(), out.data_ptr(),
+                                   N.stream_ptr()), "evs_sample")
+        tok = int(out.item())
+        emitted[i] = tok
+        if i + 1 < n_tokens:
+            x[0, 0] = tok
+            last = step_forward_reference(model, x, ip)[0, -1]
+    ip.close()
+    return emitted
+
+
+def teacher_force_to_spec_state(model, prompt_ids, emitted_ids, *, max_seqlen: int | None = None):
+    """Prefill the prompt, then step ``emitted[:-1]`` (loop.py:661-685)."""
+    prompt = _as_prompt_ids(prompt_ids, model.device)
+    emitted = np.asarray(emitted_ids, dtype=np.int64).ravel()
+    L, n = int(prompt.shape[1]), int(emitted.size)
+    ip = model.initialize_inference_params(max_seqlen=max_seqlen or L + n + 2)
+    prefill(model, prompt, ip)
+    if n > 1:
+        step_forward_reference(model, torch.as_tensor(emitted[:-1], device=model.device)[None], ip)
+    return ip
+
+
+def spec_end_kv_len(prompt_len: int, n_emitted: int) -> int:
+    return int(prompt_len) + int(n_emitted) - 1
+
+
+__all__ = ["RoundLog", "RoundOutcome", "SpecGenerateResult", "spec_round", "native_greedy_reference", "native_sample_reference",
+           "spec_end_kv_len", "speculative_generate", "teacher_force_to_spec_state"]

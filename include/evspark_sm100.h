@@ -216,6 +216,20 @@ EVS_API int evs_draft_propose(evs_drafter* d, const evs_state* s, const int64_t*
                       int greedy, double temperature, int top_k, const double* u, const int64_t* forced,
                       int64_t* tokens, double* q, float* conf, float* U, cudaStream_t stream);
 
+/* ---- tracing ----
+ * evs_profile_start arms per-launch CUDA events inside evs_prefill / evs_forward on the call's
+ * stream; evs_profile_stop synchronises and returns, per kernel group (EVS_PROF_*), the number of
+ * launches, their summed device time (ms) and their algorithmic HBM bytes. */
+#define EVS_PROF_GEMM 0  /* tcgen05 / SIMT projections                */
+#define EVS_PROF_HYENA 1 /* fused outer FIR + inner FIR / modal IIR    */
+#define EVS_PROF_ATTN 2  /* RoPE + KV append + attention + combine     */
+#define EVS_PROF_ROW 3   /* embedding, residual + norm, SwiGLU, logits */
+#define EVS_PROF_KINDS 4
+EVS_API int evs_profile_start(evs_state* s);
+EVS_API int evs_profile_stop(evs_state* s, int64_t* launches, double* ms, double* bytes);
+/* number of kernels this library has launched in the process (all entry points) */
+EVS_API int64_t evs_launch_count(void);
+
 /* ---- device error word ---- */
 EVS_API int evs_get_device_error(const evs_state* s, int32_t* code, int32_t* where, int32_t* info);
 EVS_API int evs_clear_device_error(evs_state* s, cudaStream_t stream);

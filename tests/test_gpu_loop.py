@@ -1,0 +1,193 @@
+"""GPU: speculative loop, native references and the device drafter against the reference.
+
+* The loop with the identity drafter reproduces, token for token, the reference's own
+  ``speculative_generate`` outputs on the same model and seeds (golden fixtures), in greedy and
+  in seeded-sampling mode, with the same per-round accepted lengths.
+* Greedy speculative decoding equals native decoding exactly (fp32 tiny and bf16 7B-width).
+* The device drafter (trunk + serial Markov head + confidence) matches the reference ``Drafter``.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import glob
+import os
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def cuda():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    from evspark_b200 import _native as N
+
+    N.call("evs_device_check")
+    return torch.device("cuda:0")
+
+
+@pytest.fixture(scope="module")
+def tiny(cuda):
+    from evspark_b200.config import TINY
+    from evspark_b200.model import TargetModel
+    from evspark_b200.weights import init_target_weights
+
+    w = init_target_weights(TINY, seed=20260820)
+    return TargetModel(TINY, w, device=cuda, capture_layers=(2,)), w
+
+
+def _cudart():
+    import torch as _t
+
+    roots = [os.path.dirname(_t.__file__)] + [p for p in __import__("sys").path if "site-packages" in p]
+    for r in roots:
+        hits = glob.glob(os.path.join(r, "**", "libcudart.so*"), recursive=True)
+        if hits:
+            lib = ctypes.CDLL(sorted(hits)[0])
+            lib.cudaMemcpy.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int]
+            return lib
+    pytest.skip("libcudart not found for raw device copies")
+
+
+def test_tiny_loop_identity_matches_reference_golden(golden, tiny):
+    from evspark_b200.specdec.block.loop import native_greedy_reference, speculative_generate
+    from oracle.loop import IdentityDraft
+
+    model, _ = tiny
+    g = golden("tiny_model.npz")
+    prompt = torch.tensor(g["loop/prompt"])[None]
+    n = len(g["loop/native_greedy"])
+    nat, ip, _ = native_greedy_reference(model, prompt, n)
+    np.testing.assert_array_equal(nat, g["loop/native_greedy"])
+    for gamma in (4, 12):
+        spec = speculative_generate(model, IdentityDraft(), prompt, n, gamma, greedy=True, rng=np.random.default_rng(0))
+        np.testing.assert_array_equal(spec.emitted_ids, g[f"loop/spec_greedy_g{gamma}"])
+        assert [r.k for r in spec.rounds_log] == g[f"loop/spec_greedy_g{gamma}_ks"].tolist()
+        rng = np.random.default_rng(7)
+        spec = speculative_generate(model, IdentityDraft(), prompt, n, gamma, greedy=False, rng=rng,
+                                    temperature=1.0, top_k=4)
+        np.testing.assert_array_equal(spec.emitted_ids, g[f"loop/spec_sample_g{gamma}"])
+        assert [r.k for r in spec.rounds_log] == g[f"loop/spec_sample_g{gamma}_ks"].tolist()
+
+
+def test_tiny_loop_end_state_equals_teacher_forced(golden, tiny):
+    from evspark_b200.specdec.block import diff_states, snapshot_states
+    from evspark_b200.specdec.block.loop import spec_end_kv_len, speculative_generate, teacher_force_to_spec_state
+    from oracle.loop import IdentityDraft
+
+    model, _ = tiny
+    g = golden("tiny_model.npz")
+    prompt = torch.tensor(g["loop/prompt"])[None]
+    for rollback in ("slice", "snapshot"):
+        spec = speculative_generate(model, IdentityDraft(), prompt, 40, 8, greedy=True, rng=np.random.default_rng(0),
+                                    rollback=rollback)
+        assert any(r.k < 8 for r in spec.rounds_log)
+        kv = spec_end_kv_len(prompt.shape[1], 40)
+        assert spec.inference_params_dict.offset == kv
+        ref = teacher_force_to_spec_state(model, prompt, spec.emitted_ids)
+        d = diff_states(snapshot_states(spec.inference_params_dict, kv_len=kv), snapshot_states(ref, kv_len=kv))
+        assert max(v["max_abs"] for v in d.values()) == 0.0
+
+
+def test_truncation_round(golden, tiny):
+    from evspark_b200.specdec.block.loop import native_greedy_reference, speculative_generate
+
+    model, _ = tiny
+    g = golden("tiny_model.npz")
+    prompt = torch.tensor(g["loop/prompt"])[None]
+    nat, _, _ = native_greedy_reference(model, prompt, 10)
+
+    class Oracle:
+        def probs(self, prefix):
+            out = np.zeros(512)
+            i = len(prefix) - prompt.shape[1]
+            out[int(nat[i]) if 0 <= i < len(nat) else 65] = 1.0
+            return out
+
+    spec = speculative_generate(model, Oracle(), prompt, 10, 8, greedy=True, rng=np.random.default_rng(0))
+    np.testing.assert_array_equal(spec.emitted_ids, nat)
+    assert any(r.n_emitted < r.k + 1 for r in spec.rounds_log)
+    assert spec.inference_params_dict.offset == prompt.shape[1] + 10 - 1
+
+
+@pytest.mark.parametrize("T", [0, 9, 64])
+def test_device_drafter_matches_reference_drafter(golden, tiny, T):
+    from evspark_b200.config import DRAFTERS
+    from evspark_b200.drafter import DeviceDrafter
+    from evspark_b200.weights import init_drafter_weights
+
+    model, w = tiny
+    d = golden("drafter_tiny.npz")
+    dcfg = DRAFTERS["tiny"]
+    dw = init_drafter_weights(dcfg, seed=20260830, embed=w["embed"])
+    dr = DeviceDrafter(dcfg, dw, device=model.device)
+    ip = model.initialize_inference_params(256)
+    if T:
+        ip.prefill(torch.full((1, T), 65, dtype=torch.long))
+        ring, ring_len = ip.capture_ring(0)
+        h_raw = np.ascontiguousarray(d[f"ctx{T}/h_raw"].astype(np.float32))
+        rt = _cudart()
+        H = model.cfg.d_model
+        torch.cuda.synchronize()
+        for j in range(T):  # context rows live at positions len-T .. len-1
+            dst = ring + (j % ring_len) * H * 4
+            assert rt.cudaMemcpy(dst, h_raw[j].ctypes.data, H * 4, 1) == 0
+    anchor = torch.tensor([71], device=model.device)
+    toks, q, conf, U = dr.propose(ip, anchor, dcfg.gamma, True, want_U=True)
+    np.testing.assert_allclose(U[0].cpu().numpy(), d[f"ctx{T}/U"], atol=2e-5, rtol=1e-4)
+    np.testing.assert_array_equal(toks[0].cpu().numpy(), d[f"ctx{T}/greedy_tokens"])
+    np.testing.assert_allclose(q[0].cpu().numpy(), d[f"ctx{T}/greedy_q"], atol=1e-6)
+    np.testing.assert_allclose(conf[0].double().cpu().numpy(), d[f"ctx{T}/greedy_conf"], atol=1e-5)
+    u = torch.as_tensor(np.random.default_rng(11).random(dcfg.gamma), device=model.device)[None]
+    toks, q, conf, _ = dr.propose(ip, anchor, dcfg.gamma, False, temperature=1.0, top_k=4, uniforms=u)
+    np.testing.assert_array_equal(toks[0].cpu().numpy(), d[f"ctx{T}/sample_tokens"])
+    np.testing.assert_allclose(q[0].cpu().numpy(), d[f"ctx{T}/sample_q"], atol=1e-6)
+    # decode γ' < training γ is an exact prefix computation
+    toks5, _, _, U5 = dr.propose(ip, anchor, 5, True, want_U=True)
+    np.testing.assert_allclose(U5[0].cpu().numpy(), d[f"ctx{T}/U_g5"], atol=2e-5, rtol=1e-4)
+    with pytest.raises(ValueError, match="γ"):
+        dr.propose(ip, anchor, dcfg.gamma + 1, True)
+    ip.close()
+    dr.close()
+
+
+def test_neural_loop_greedy_equals_native(tiny):
+    from evspark_b200.config import DRAFTERS
+    from evspark_b200.drafter import DeviceDrafter
+    from evspark_b200.specdec.block.loop import native_greedy_reference, speculative_generate
+    from evspark_b200.specdec.block.neural_draft import NeuralDraftModel
+
+    model, w = tiny
+    dr = DeviceDrafter.random(DRAFTERS["tiny"], embed=w["embed"], device=model.device)
+    nd = NeuralDraftModel(model, dr, ("blocks.2",))
+    prompt = torch.tensor(np.random.default_rng(5).choice([65, 67, 71, 84], size=200))[None]
+    spec = speculative_generate(model, nd, prompt, 64, 12, greedy=True, rng=np.random.default_rng(0))
+    nat, _, _ = native_greedy_reference(model, prompt, 64)
+    np.testing.assert_array_equal(spec.emitted_ids, nat)
+    assert all(r.conf is not None and len(r.conf) == 12 for r in spec.rounds_log)
+    assert nd.capture_buffer_len() == spec.inference_params_dict.offset
+    nd.capture_reset()
+    spec = speculative_generate(model, nd, prompt, 64, 12, greedy=False, rng=np.random.default_rng(3))
+    assert spec.emitted_ids.shape == (64,)
+    with pytest.raises(ValueError, match="slice"):
+        speculative_generate(model, nd, prompt, 4, 12, greedy=True, rng=np.random.default_rng(0),
+                             rollback="snapshot")
+    nd.close()
+
+
+def test_7b_width_bf16_greedy_spec_equals_native(cuda):
+    from evspark_b200.config import EVO2_7B_SLICE
+    from evspark_b200.model import TargetModel
+    from evspark_b200.specdec.block.loop import native_greedy_reference, speculative_generate
+    from oracle.loop import IdentityDraft
+
+    model = TargetModel.random(EVO2_7B_SLICE, seed=11, device=cuda, init_on="cuda")
+    prompt = torch.tensor(np.random.default_rng(9).choice([65, 67, 71, 84], size=96))[None]
+    nat, _, _ = native_greedy_reference(model, prompt, 48)
+    spec = speculative_generate(model, IdentityDraft(), prompt, 48, 12, greedy=True, rng=np.random.default_rng(0))
+    np.testing.assert_array_equal(spec.emitted_ids, nat)
+    model.close()

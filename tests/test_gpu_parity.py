@@ -18,7 +18,8 @@ import torch
 pytestmark = pytest.mark.gpu
 
 TOL_FP32_REL = 1e-5  # max-abs / max|logit|, fp32 device vs fp64 oracle
-TOL_BF16 = 2e-2      # max-abs logits, bf16 device vs bf16-emulating oracle
+TOL_BF16 = 2e-2      # max-abs logits, bf16 device vs bf16-emulating oracle, or 1.5x the measured
+                     # bf16 noise floor of the oracle itself when that is larger (large logit scales)
 
 
 @pytest.fixture(scope="module")
@@ -264,10 +265,19 @@ def test_7b_width_bf16_block_vs_oracle(cuda):
     logits = block_forward(model, torch.tensor(chunk)[None], ip)[0].cpu().double()
     step = step_forward_reference(model, torch.tensor(chunk)[None], ip2)[0].cpu().double()
     assert torch.equal(logits, step), "bf16 block forward must equal the native T=1 path bit for bit"
-    ora = OracleTarget(cfg, w, compute=torch.float64, emulate=True)
-    st = ora.init_state(1, 128)
-    ora.forward(prompt[None], st, prefill=True)
-    ref, _, _ = ora.forward(chunk[None], st)
-    err = (logits - ref[0]).abs().max().item()
-    assert err <= TOL_BF16, f"7B-width bf16 logits vs oracle: {err:.3e}"
+    refs = {}
+    for ct in (torch.float64, torch.float32):
+        ora = OracleTarget(cfg, w, compute=ct, emulate=True)
+        st = ora.init_state(1, 128)
+        ora.forward(prompt[None], st, prefill=True)
+        refs[ct] = ora.forward(chunk[None], st)[0][0].double()
+    ref = refs[torch.float64]
+    # bf16 noise floor: the same bf16-rounding oracle computed in fp32 instead of fp64
+    floor = (refs[torch.float32] - ref).abs().max().item()
+    err = (logits - ref).abs().max().item()
+    print(f"[bf16 parity] max|logit|={ref.abs().max().item():.2f} device err={err:.3e} bf16 floor={floor:.3e}")
+    assert err <= max(TOL_BF16, 1.5 * floor), f"7B-width bf16 logits vs oracle: {err:.3e} (floor {floor:.3e})"
+    top2 = ref.topk(2, dim=-1).values
+    clear = (top2[:, 0] - top2[:, 1]) > 2 * max(floor, TOL_BF16)
+    assert torch.equal(logits.argmax(-1)[clear], ref.argmax(-1)[clear])
     del model
