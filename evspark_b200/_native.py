@@ -72,6 +72,7 @@ _PROTOS = {
     "evs_state_copy": (_I, [_P, _P, _P]),
     "evs_state_get_lengths": (_I, [_P, _P, _I, _P]),
     "evs_state_set_lengths": (_I, [_P, _P, _I, _P]),
+    "evs_state_note_lengths": (_I, [_P, _P, _I]),
     "evs_state_expand": (_I, [_P, _I, _P]),
     "evs_state_collapse": (_I, [_P, _I, _P]),
     "evs_state_export": (_I, [_P, _I, _I, _I, _I, _P, _P]),

@@ -477,6 +477,15 @@ int evs_state_set_lengths(evs_state* s, const int32_t* host_lengths, int batch, 
   return EVS_OK;
 }
 
+int evs_state_note_lengths(evs_state* s, const int32_t* host_lengths, int batch) {
+  EVS_CHECK_ARG(s && host_lengths && batch >= 1 && batch <= s->max_batch, "bad arguments");
+  for (int b = 0; b < batch; ++b) {
+    EVS_CHECK_RANGE(host_lengths[b] >= 0 && host_lengths[b] <= s->max_seqlen, "length outside [0, max_seqlen]");
+    s->h_len[b] = host_lengths[b];
+  }
+  return EVS_OK;
+}
+
 namespace {
 // copy every per-row arena of row src into row dst (KV: first kv_len positions)
 int copy_row(evs_state* s, int src, int dst, cudaStream_t st) {

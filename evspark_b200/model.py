@@ -283,6 +283,8 @@ class InferenceParams(dict):
         kd = torch.as_tensor(ks.astype(np.int32), device=self.model.device)
         N.check(N.lib().evs_rollback(self._h, kd.data_ptr(), ks.size, self._stream()), "evs_rollback")
         self.lengths[: ks.size] = self.retained_len0[: ks.size] + ks + 1
+        arr = (C.c_int32 * ks.size)(*[int(x) for x in self.lengths[: ks.size]])
+        N.check(N.lib().evs_state_note_lengths(self._h, arr, ks.size), "evs_state_note_lengths")
 
     # -- state management ----------------------------------------------------
     def clone(self) -> "InferenceParams":

@@ -117,6 +117,10 @@ EVS_API int evs_state_copy(evs_state* dst, const evs_state* src, cudaStream_t st
 /* per-row consumed lengths (device-resident truth) -> host, and host -> device */
 EVS_API int evs_state_get_lengths(const evs_state* s, int32_t* host_lengths, int batch, cudaStream_t stream);
 EVS_API int evs_state_set_lengths(evs_state* s, const int32_t* host_lengths, int batch, cudaStream_t stream);
+/* host-side note of the exact lengths after a device-side evs_rollback whose k the caller also
+ * knows: tightens the library's host bound (used for max_seqlen checks and attention grid sizes);
+ * no device traffic.  Lengths must not be below the device truth. */
+EVS_API int evs_state_note_lengths(evs_state* s, const int32_t* host_lengths, int batch);
 /* replicate row 0 into rows [1, batch) (expand_inference_params, driver.py:96-142) */
 EVS_API int evs_state_expand(evs_state* s, int batch, cudaStream_t stream);
 /* move row idx into row 0 (collapse_inference_params, driver.py:145-176) */
