@@ -84,6 +84,7 @@ _PROTOS = {
     "evs_verify": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _P, _P, _P, _P]),
     "evs_sample": (_I, [_P, _I, _I, _P, _P, _P]),
     "evs_gemm_bf16": (_I, [_P, _P, _P, _I, _I, _I, _I, _P]),
+    "evs_gemm_bf16_noalloc": (_I, [_P, _P, _P, _I, _I, _I, _P]),
     "evs_drafter_create": (_I, [C.POINTER(DrafterConfig), _I, C.POINTER(_P)]),
     "evs_drafter_set_tensor": (_I, [_P, _I, _P, C.c_int64]),
     "evs_drafter_finalize": (_I, [_P]),

@@ -176,6 +176,17 @@ EVS_API int evs_sample(const double* rows, int n, int V, const double* u, int64_
 EVS_API int evs_gemm_bf16(const void* W, const void* X, float* out, int N, int K, int M, int splits,
                   cudaStream_t stream);
 
+/* The split-K projection above for callers that cannot allocate device memory when they need it
+ * (a host that has handed all device memory to its own pool, code running during stream capture,
+ * plugins barred from allocating after start-up).  No counterpart in the reference.  Partial sums
+ * go to one fixed 4 MiB file-scope device array (1,048,576 fp32; each GPU that loads the library
+ * holds it until exit) instead of allocated scratch; calls needing more than that (splits*M*N,
+ * splits chosen as in evs_forward) fail with EVS_ERANGE.  No cudaMalloc/cudaFree.  The first call
+ * on a device looks up the array's address — make it before any stream capture.  All calls share
+ * the array (last call's contents remain): calls that may overlap on the GPU race. */
+EVS_API int evs_gemm_bf16_noalloc(const void* W, const void* X, float* out, int N, int K, int M,
+                                  cudaStream_t stream);
+
 /* ---- γ-parallel drafter (fp32; evspark/train/drafter.py Drafter parameters) ---- */
 typedef struct evs_drafter_config {
   int32_t d_model, n_layers, n_heads, gamma, n_inject, target_hidden, vocab_size, mask_id, ctx_window,

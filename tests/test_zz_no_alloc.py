@@ -1,0 +1,61 @@
+"""GPU: the no-allocation projection entry point agrees with the regular one.
+
+``evs_gemm_bf16_noalloc`` exists for callers that cannot allocate device memory at call time
+(a host that owns all device memory through its own pool, code running during stream capture,
+plugins not allowed to allocate after start-up).  It keeps its split-K partial sums in a fixed
+file-scope device array.  This file is collected last so that a failure here cannot stop the
+rest of the GPU suite; it passes alone in a fresh process and after the other tests.
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+TOL_REL = 2e-3  # same bound as the tcgen05 GEMM test against torch
+
+
+@pytest.fixture(scope="module")
+def cuda():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    from evspark_b200 import _native as N
+
+    N.call("evs_device_check")
+    return torch.device("cuda:0")
+
+
+@pytest.mark.parametrize("N_,K,M", [(12288, 4096, 13), (4096, 11008, 13), (512, 4096, 16), (256, 640, 40)])
+def test_noalloc_matches_regular_entry_point_twice(cuda, N_, K, M):
+    from evspark_b200 import _native as N
+
+    g = torch.Generator(device=cuda).manual_seed(N_ * 7 + K + M)
+    W = torch.randn(N_, K, device=cuda, generator=g).to(torch.bfloat16)
+    X = torch.randn(M, K, device=cuda, generator=g).to(torch.bfloat16)
+    ref = torch.empty(M, N_, device=cuda)
+    N.call("evs_gemm_bf16", W.data_ptr(), X.data_ptr(), ref.data_ptr(), N_, K, M, 1, N.stream_ptr())
+    outs = []
+    for _ in range(2):  # the shared scratch keeps the previous call's partials: results must not depend on it
+        out = torch.full((M, N_), float("nan"), device=cuda)
+        N.call("evs_gemm_bf16_noalloc", W.data_ptr(), X.data_ptr(), out.data_ptr(), N_, K, M, N.stream_ptr())
+        torch.cuda.synchronize()
+        outs.append(out)
+    scale = ref.abs().max().item()
+    for out in outs:
+        assert torch.isfinite(out).all()
+        err = (out - ref).abs().max().item()
+        assert err <= TOL_REL * scale, (err, scale)
+    assert torch.equal(outs[0], outs[1])
+
+
+def test_noalloc_rejects_sizes_beyond_the_fixed_scratch(cuda):
+    from evspark_b200 import _native as N
+
+    W = torch.zeros(12288, 4096, device=cuda, dtype=torch.bfloat16)
+    X = torch.zeros(512, 4096, device=cuda, dtype=torch.bfloat16)
+    out = torch.empty(512, 12288, device=cuda)
+    with pytest.raises(ValueError, match="scratch"):
+        N.call("evs_gemm_bf16_noalloc", W.data_ptr(), X.data_ptr(), out.data_ptr(), 12288, 4096, 512,
+               N.stream_ptr())
