@@ -180,8 +180,10 @@ def run_ours(args) -> int:
     from evspark_b200.specdec.block.neural_draft import NeuralDraftModel
     from evspark_b200.workload import markov_prompt, to_text
 
-    cfg = EVO2_7B
-    dcfg = DRAFTERS["evo2_7b"]
+    from evspark_b200.config import target_config
+
+    cfg = target_config(args.config)
+    dcfg = DRAFTERS[args.config]
     model = TargetModel.random(cfg, seed=20260820, device=device, init_on="cuda",
                                capture_layers=tuple(layer_index(n) for n in dcfg.inject_layers))
     drafter = DeviceDrafter.random(dcfg, seed=20260830, embed=model.weights["embed"], device=device, init_on="cuda")
@@ -248,6 +250,15 @@ def run_ours(args) -> int:
     verify_block_us = kernel_ms / args.steps * 1e3
 
     # ---- e2e through the public API: host prompt -> EvSpark.generate -> host tokens ----
+    if args.no_extras:
+        if rank == 0:
+            print(json.dumps({"metric": METRIC, "value": round(value, 3), "unit": "tok/s", "config": args.config,
+                              "ms_per_step": round(ms / args.steps, 4), "verify_block_us": round(verify_block_us, 1),
+                              "gemm_gbs": round(achieved, 1), "gpu_launches": int(launches)}), flush=True)
+        ip.close()
+        nd.close()
+        model.close()
+        return 0
     es = EvSpark(model, nd, str(device))
     text = to_text(prompt)
     e2e_res = es.generate(text, n_tokens=E2E_TOKENS, seed=11 + rank)
@@ -340,6 +351,8 @@ def main() -> int:
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
     ap.add_argument("--cpu-steps", type=int, default=3)
+    ap.add_argument("--config", default="evo2_7b", help="evo2_7b (headline) or evo2_7b_slice (4 blocks, profiling)")
+    ap.add_argument("--no-extras", action="store_true", help="time the rounds only (profiling runs)")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
