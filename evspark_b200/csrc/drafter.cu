@@ -10,6 +10,7 @@
 //   conf = σ(conf_w [h ; in_proj(embed(prev))]).
 // The context comes straight from the state's capture ring (written by the target forward), so
 // drafting needs no host copy of hidden states.
+#include <algorithm>
 #include <cstring>
 #include <string>
 
@@ -27,6 +28,8 @@ struct evs_drafter {
   float *kv_in = nullptr, *kb = nullptr, *vb = nullptr, *y = nullptr, *tmp = nullptr, *m1 = nullptr;
   float *z = nullptr, *U = nullptr, *pe = nullptr;
   int64_t* prev = nullptr;
+  float* ws = nullptr;  // split-K partials of the projections
+  size_t ws_floats = 0;
   void* block = nullptr;
 };
 
@@ -187,10 +190,11 @@ __global__ void __launch_bounds__(256) serial_head_kernel(const float* U, const 
                                                           const double* u, const int64_t* forced, int64_t* tokens,
                                                           double* qout, int64_t* prev_ids) {
   __shared__ float lg[VMAX];
-  __shared__ double e[VMAX], row[VMAX], masked[VMAX], sv[256], scal[1];
-  __shared__ int keep[VMAX], si[256];
+  __shared__ double e[VMAX], row[VMAX], masked[VMAX];
+  __shared__ int keep[VMAX];
+  __shared__ SampScratch sc;
   __shared__ float fred[9];
-  __shared__ int s_prev, s_tok;
+  __shared__ int s_prev;
   const int b = blockIdx.x;
   if (threadIdx.x == 0) s_prev = static_cast<int>(anchor[b]);
   __syncthreads();
@@ -198,6 +202,7 @@ __global__ void __launch_bounds__(256) serial_head_kernel(const float* U, const 
     const int prev = s_prev;
     const float* Ur = U + (static_cast<size_t>(b) * g + k) * V;
     const float* Br = markov + static_cast<size_t>(prev) * V;
+    // q_k = softmax(U_k + B[prev]) in fp32
     float mx = -CUDART_INF_F;
     for (int v = threadIdx.x; v < V; v += blockDim.x) {
       lg[v] = Ur[v] + Br[v];
@@ -232,23 +237,23 @@ __global__ void __launch_bounds__(256) serial_head_kernel(const float* U, const 
     for (int v = threadIdx.x; v < V; v += blockDim.x) e[v] = static_cast<double>(lg[v] / zs);
     __syncthreads();
     double* qo = qout + (static_cast<size_t>(b) * g + k) * V;
+    int tok;
     if (greedy) {
-      const int am = block_argmax(e, V, sv, si);
-      if (threadIdx.x == 0) s_tok = am;
+      tok = block_argmax(e, V, &sc);
       for (int v = threadIdx.x; v < V; v += blockDim.x) qo[v] = e[v];
-      __syncthreads();
     } else {
-      // log(q) on the support, -inf elsewhere (all zeros when q has no positive entry)
+      // q' = apply_transform(log q): log on the support, -inf elsewhere
       for (int v = threadIdx.x; v < V; v += blockDim.x) row[v] = e[v] > 0.0 ? log(e[v]) : -CUDART_INF;
       __syncthreads();
-      transform_row(row, V, temperature, top_k, qo, keep, masked, sv, si, scal);
-      for (int v = threadIdx.x; v < V; v += blockDim.x) masked[v] = fmax(qo[v], 0.0);
+      transform_row(row, V, temperature, top_k, masked, keep, e, &sc);
+      for (int v = threadIdx.x; v < V; v += blockDim.x) {
+        qo[v] = masked[v];
+        row[v] = fmax(masked[v], 0.0);
+      }
       __syncthreads();
-      if (threadIdx.x == 0) s_tok = sample_clipped(masked, V, u[static_cast<size_t>(b) * g + k]);
-      __syncthreads();
+      tok = block_sample_clipped(row, V, u[static_cast<size_t>(b) * g + k], &sc);
     }
     if (threadIdx.x == 0) {
-      int tok = s_tok;
       if (forced) tok = static_cast<int>(forced[static_cast<size_t>(b) * g + k]);
       tokens[static_cast<size_t>(b) * g + k] = tok;
       prev_ids[static_cast<size_t>(b) * g + k] = prev;
@@ -309,9 +314,14 @@ int64_t drafter_numel(const evs_drafter_config& c, int id) {
   }
 }
 
-int sgemm(const float* W, const float* X, int ldx, float* out, int N, int K, int M, cudaStream_t st) {
-  GemmPlan p{N, K, M, 1, 0};
-  return launch_gemm_simt(W, nullptr, X, ldx, EVS_DTYPE_FP32, p, out, st);
+// out[M][N] = X W^T (fp32, split-K partials reduced in split order)
+int sgemm(evs_drafter* dr, const float* W, const float* X, int ldx, float* out, int N, int K, int M,
+          cudaStream_t st) {
+  const GemmPlan p = gemm_plan_f32(N, K, M, 0);
+  EVS_CHECK_RANGE(static_cast<size_t>(p.splits) * M * N <= dr->ws_floats, "drafter workspace too small");
+  if (p.splits == 1) return launch_gemm_simt(W, nullptr, X, ldx, EVS_DTYPE_FP32, p, out, st);
+  EVS_TRY(launch_gemm_simt(W, nullptr, X, ldx, EVS_DTYPE_FP32, p, dr->ws, st));
+  return launch_reduce_splits(dr->ws, p.splits, M, N, nullptr, out, st);
 }
 
 inline unsigned blocks_for(size_t n, int t) { return static_cast<unsigned>((n + t - 1) / t); }
@@ -350,6 +360,21 @@ int evs_drafter_create(const evs_drafter_config* cfg, int max_batch, evs_drafter
   const size_t o_y = take(4 * B * g * d), o_tmp = take(4 * B * g * d), o_m1 = take(4 * B * g * hid);
   const size_t o_z = take(4 * B * g * H), o_U = take(4 * B * g * V), o_pe = take(4 * B * g * d);
   const size_t o_prev = take(8 * B * g);
+  // largest split-K partial buffer over the drafter's projections
+  size_t wsf = 0;
+  auto need = [&](size_t M_, size_t N_, size_t K_) {
+    const GemmPlan p = gemm_plan_f32(static_cast<int>(N_), static_cast<int>(K_), static_cast<int>(M_), 0);
+    wsf = std::max(wsf, static_cast<size_t>(p.splits) * M_ * N_);
+  };
+  need(B * CW, d, nI * H);
+  need(B * g, d, H);
+  need(B * g, d, d);
+  need(B * (CW + g), d, d);
+  need(B * g, hid, d);
+  need(B * g, d, hid);
+  need(B * g, H, d);
+  need(B * g, V, H);
+  const size_t o_ws = take(4 * wsf);
   if (cudaMalloc(&dr->block, off) != cudaSuccess) {
     cudaGetLastError();
     delete dr;
@@ -373,6 +398,8 @@ int evs_drafter_create(const evs_drafter_config* cfg, int max_batch, evs_drafter
   dr->U = reinterpret_cast<float*>(base + o_U);
   dr->pe = reinterpret_cast<float*>(base + o_pe);
   dr->prev = reinterpret_cast<int64_t*>(base + o_prev);
+  dr->ws = reinterpret_cast<float*>(base + o_ws);
+  dr->ws_floats = wsf;
   EVS_CUDA_TRY(cudaMemset(dr->block, 0, off));
   *out = dr;
   return EVS_OK;
@@ -434,7 +461,7 @@ int evs_draft_propose(evs_drafter* dr, const evs_state* s, const int64_t* anchor
     for (int k = 0; k < 4; ++k) rg.p[k] = s->cap_ring[k];
     gather_ctx_kernel<<<dim3(CW, B), 256, 0, st>>>(rg, c.n_inject, s->ring_len, H, s->d_len, CW, dr->ctx_in);
     EVS_CUDA_TRY(cudaGetLastError());
-    EVS_TRY(sgemm(T[EVS_D_CTX_W], dr->ctx_in, c.n_inject * H, dr->kb, d, c.n_inject * H, B * CW, st));
+    EVS_TRY(sgemm(dr, T[EVS_D_CTX_W], dr->ctx_in, c.n_inject * H, dr->kb, d, c.n_inject * H, B * CW, st));
     bias_rmsnorm_kernel<<<B * CW, 256, 0, st>>>(dr->kb, T[EVS_D_CTX_B], T[EVS_D_CTX_NORM], dr->ctx, d, eps);
   } else {
     EVS_CUDA_TRY(cudaMemsetAsync(dr->ctx, 0, sizeof(float) * B * CW * d, st));
@@ -444,35 +471,35 @@ int evs_draft_propose(evs_drafter* dr, const evs_state* s, const int64_t* anchor
   if (c.n_inject == 0) EVS_CUDA_TRY(cudaMemsetAsync(dr->prev, 0, sizeof(int32_t) * B, st));
   // ---- h = in_proj(embed([anchor, MASK...])) + pos ----
   embed_rows_kernel<<<rows, 256, 0, st>>>(T[EVS_D_EMBED], H, anchor, nullptr, g, c.mask_id, dr->emb);
-  EVS_TRY(sgemm(T[EVS_D_IN_W], dr->emb, H, dr->h, d, H, rows, st));
+  EVS_TRY(sgemm(dr, T[EVS_D_IN_W], dr->emb, H, dr->h, d, H, rows, st));
   bias_pos_kernel<<<blocks_for(static_cast<size_t>(rows) * d, 256), 256, 0, st>>>(dr->h, T[EVS_D_IN_B], T[EVS_D_POS],
                                                                                  g, d, rows);
   for (int l = 0; l < c.n_layers; ++l) {
     const float* const* L = T + EVS_D_LAYER0 + l * EVS_D_PER_LAYER;
     bias_rmsnorm_kernel<<<rows, 256, 0, st>>>(dr->h, nullptr, L[EVS_D_LN1], dr->xb, d, eps);
-    EVS_TRY(sgemm(L[EVS_D_Q], dr->xb, d, dr->q, d, d, rows, st));
+    EVS_TRY(sgemm(dr, L[EVS_D_Q], dr->xb, d, dr->q, d, d, rows, st));
     build_kv_kernel<<<dim3(nk, B), 256, 0, st>>>(dr->ctx, dr->xb, CW, g, d, dr->kv_in);
-    EVS_TRY(sgemm(L[EVS_D_K], dr->kv_in, d, dr->kb, d, d, B * nk, st));
-    EVS_TRY(sgemm(L[EVS_D_V], dr->kv_in, d, dr->vb, d, d, B * nk, st));
+    EVS_TRY(sgemm(dr, L[EVS_D_K], dr->kv_in, d, dr->kb, d, d, B * nk, st));
+    EVS_TRY(sgemm(dr, L[EVS_D_V], dr->kv_in, d, dr->vb, d, d, B * nk, st));
     draft_attn_kernel<<<dim3(g, c.n_heads, B), 128, 0, st>>>(dr->q, dr->kb, dr->vb, ctx_len, CW, g, d, c.n_heads,
                                                             dr->y);
-    EVS_TRY(sgemm(L[EVS_D_O], dr->y, d, dr->tmp, d, d, rows, st));
+    EVS_TRY(sgemm(dr, L[EVS_D_O], dr->y, d, dr->tmp, d, d, rows, st));
     residual_add_kernel<<<blocks_for(static_cast<size_t>(rows) * d, 256), 256, 0, st>>>(dr->h, dr->tmp, nullptr, d,
                                                                                         rows);
     bias_rmsnorm_kernel<<<rows, 256, 0, st>>>(dr->h, nullptr, L[EVS_D_LN2], dr->xb, d, eps);
-    EVS_TRY(sgemm(L[EVS_D_MLP0_W], dr->xb, d, dr->m1, hid, d, rows, st));
+    EVS_TRY(sgemm(dr, L[EVS_D_MLP0_W], dr->xb, d, dr->m1, hid, d, rows, st));
     bias_silu_kernel<<<blocks_for(static_cast<size_t>(rows) * hid, 256), 256, 0, st>>>(dr->m1, L[EVS_D_MLP0_B], hid,
                                                                                       rows);
-    EVS_TRY(sgemm(L[EVS_D_MLP2_W], dr->m1, hid, dr->tmp, d, hid, rows, st));
+    EVS_TRY(sgemm(dr, L[EVS_D_MLP2_W], dr->m1, hid, dr->tmp, d, hid, rows, st));
     residual_add_kernel<<<blocks_for(static_cast<size_t>(rows) * d, 256), 256, 0, st>>>(dr->h, dr->tmp,
                                                                                         L[EVS_D_MLP2_B], d, rows);
   }
   // ---- U = (final_ln(h) out_proj) embedᵀ H^-1/2 ----
   bias_rmsnorm_kernel<<<rows, 256, 0, st>>>(dr->h, nullptr, T[EVS_D_FINAL_LN], dr->xb, d, eps);
-  EVS_TRY(sgemm(T[EVS_D_OUT_W], dr->xb, d, dr->z, H, d, rows, st));
+  EVS_TRY(sgemm(dr, T[EVS_D_OUT_W], dr->xb, d, dr->z, H, d, rows, st));
   bias_pos_kernel<<<blocks_for(static_cast<size_t>(rows) * H, 256), 256, 0, st>>>(dr->z, T[EVS_D_OUT_B], nullptr, g,
                                                                                  H, rows);
-  EVS_TRY(sgemm(T[EVS_D_EMBED], dr->z, H, dr->U, V, H, rows, st));
+  EVS_TRY(sgemm(dr, T[EVS_D_EMBED], dr->z, H, dr->U, V, H, rows, st));
   scale_kernel<<<blocks_for(static_cast<size_t>(rows) * V, 256), 256, 0, st>>>(
       dr->U, 1.0f / sqrtf(static_cast<float>(H)), static_cast<size_t>(rows) * V);
   // ---- serial Markov head ----
@@ -480,7 +507,7 @@ int evs_draft_propose(evs_drafter* dr, const evs_state* s, const int64_t* anchor
                                         tokens, qrows, dr->prev);
   // ---- confidence: σ(conf_w [final_ln(h) ; in_proj(embed(prev))]) ----
   embed_rows_kernel<<<rows, 256, 0, st>>>(T[EVS_D_EMBED], H, nullptr, dr->prev, g, 0, dr->emb);
-  EVS_TRY(sgemm(T[EVS_D_IN_W], dr->emb, H, dr->pe, d, H, rows, st));
+  EVS_TRY(sgemm(dr, T[EVS_D_IN_W], dr->emb, H, dr->pe, d, H, rows, st));
   bias_pos_kernel<<<blocks_for(static_cast<size_t>(rows) * d, 256), 256, 0, st>>>(dr->pe, T[EVS_D_IN_B], nullptr, g,
                                                                                  d, rows);
   conf_kernel<<<blocks_for(rows, 4), 128, 0, st>>>(dr->xb, dr->pe, T[EVS_D_CONF_W], T[EVS_D_CONF_B], d, rows, conf);

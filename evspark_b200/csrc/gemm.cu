@@ -8,7 +8,7 @@
 // partial sums land in ws[split][token][row] and the consumer kernel adds them in split
 // order, so every token row is computed by the same arithmetic whatever the batch size.
 //
-// fp32 path (SIMT): one warp per output row, lanes stride K, fixed butterfly reduction.
+// fp32 path (CUDA cores): register-tiled 64x32 tiles through shared memory, fixed split of K.
 #include "internal.hpp"
 
 namespace {
@@ -126,43 +126,88 @@ __global__ void __launch_bounds__(192, 1)
   }
 }
 
+// fp32 / generic-dtype projection on CUDA cores, register tiled: CTA tile 64 output columns x
+// 32 token rows, K staged 32 at a time through shared memory; each thread owns 4 columns x 2 rows.
+// Partials go to ws[split][row][col]; the reduction order over k inside a split is fixed, and a
+// row's result never depends on the other rows of its tile.
+constexpr int SG_BN = 64, SG_BM = 32, SG_BK = 32;
+
 template <typename TW, typename TX>
-__global__ void __launch_bounds__(128) gemm_simt_kernel(const TW* __restrict__ W, const TW* __restrict__ W2,
-                                                        const TX* __restrict__ X, int ldx, float* __restrict__ ws,
-                                                        int N, int K, int M, int splits, int dual) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n = blockIdx.x * 4 + warp;
-  if (n >= N) return;
-  const TW* wrow;
-  if (dual) {
-    const int t = n / GEMM_BM, r = n % GEMM_BM;
-    wrow = r < GEMM_BM / 2 ? W + static_cast<size_t>(t * (GEMM_BM / 2) + r) * K
-                           : W2 + static_cast<size_t>(t * (GEMM_BM / 2) + r - GEMM_BM / 2) * K;
-  } else {
-    wrow = W + static_cast<size_t>(n) * K;
-  }
-  const int split = blockIdx.y;
+__global__ void __launch_bounds__(256) gemm_f32_kernel(const TW* __restrict__ W, const TW* __restrict__ W2,
+                                                       const TX* __restrict__ X, int ldx, float* __restrict__ ws,
+                                                       int N, int K, int M, int splits, int dual) {
+  __shared__ __align__(16) float Ws[SG_BK][SG_BN + 4];
+  __shared__ __align__(16) float Xs[SG_BK][SG_BM + 4];
+  const int tid = threadIdx.x;
+  const int tx = tid % 16, ty = tid / 16;  // 16 x 16 threads: 4 columns x 2 rows each
+  const int n0 = blockIdx.x * SG_BN, m0 = blockIdx.y * SG_BM, split = blockIdx.z;
   const int k0 = static_cast<int>(static_cast<long long>(K) * split / splits);
   const int k1 = static_cast<int>(static_cast<long long>(K) * (split + 1) / splits);
-  constexpr int TG = 8;
-  for (int t0 = 0; t0 < M; t0 += TG) {
-    float acc[TG];
-#pragma unroll
-    for (int j = 0; j < TG; ++j) acc[j] = 0.f;
-    for (int k = k0 + lane; k < k1; k += 32) {
-      const float w = to_f32(wrow[k]);
-#pragma unroll
-      for (int j = 0; j < TG; ++j)
-        if (t0 + j < M) acc[j] = fmaf(w, to_f32(X[static_cast<size_t>(t0 + j) * ldx + k]), acc[j]);
-    }
-#pragma unroll
-    for (int j = 0; j < TG; ++j) acc[j] = warp_sum(acc[j]);
-    if (lane == 0) {
-#pragma unroll
-      for (int j = 0; j < TG; ++j)
-        if (t0 + j < M) ws[(static_cast<size_t>(split) * M + t0 + j) * N + n] = acc[j];
+  float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+  // global -> smem assignments: W tile 64 x 32 (8 values / thread), X tile 32 x 32 (4 / thread)
+  const int wn = tid / 4, wk = (tid % 4) * 8;
+  const int xm = tid / 8, xk = (tid % 8) * 4;
+  const TW* wrow = nullptr;
+  {
+    const int n = n0 + wn;
+    if (n < N) {
+      if (dual) {
+        const int t = n / GEMM_BM, r = n % GEMM_BM;
+        wrow = r < GEMM_BM / 2 ? W + static_cast<size_t>(t * (GEMM_BM / 2) + r) * K
+                               : W2 + static_cast<size_t>(t * (GEMM_BM / 2) + r - GEMM_BM / 2) * K;
+      } else {
+        wrow = W + static_cast<size_t>(n) * K;
+      }
     }
   }
+  const TX* xrow = (m0 + xm < M) ? X + static_cast<size_t>(m0 + xm) * ldx : nullptr;
+  for (int kb = k0; kb < k1; kb += SG_BK) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int k = kb + wk + j;
+      Ws[wk + j][wn] = (wrow != nullptr && k < k1) ? to_f32(wrow[k]) : 0.f;
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int k = kb + xk + j;
+      Xs[xk + j][xm] = (xrow != nullptr && k < k1) ? to_f32(xrow[k]) : 0.f;
+    }
+    __syncthreads();
+#pragma unroll 8
+    for (int k = 0; k < SG_BK; ++k) {
+      const float4 w = *reinterpret_cast<const float4*>(&Ws[k][tx * 4]);
+      const float2 x = *reinterpret_cast<const float2*>(&Xs[k][ty * 2]);
+      acc[0][0] = fmaf(x.x, w.x, acc[0][0]);
+      acc[0][1] = fmaf(x.x, w.y, acc[0][1]);
+      acc[0][2] = fmaf(x.x, w.z, acc[0][2]);
+      acc[0][3] = fmaf(x.x, w.w, acc[0][3]);
+      acc[1][0] = fmaf(x.y, w.x, acc[1][0]);
+      acc[1][1] = fmaf(x.y, w.y, acc[1][1]);
+      acc[1][2] = fmaf(x.y, w.z, acc[1][2]);
+      acc[1][3] = fmaf(x.y, w.w, acc[1][3]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int m = m0 + ty * 2 + i;
+    if (m >= M) continue;
+    float* dst = ws + (static_cast<size_t>(split) * M + m) * N;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int n = n0 + tx * 4 + j;
+      if (n < N) dst[n] = acc[i][j];
+    }
+  }
+}
+
+__global__ void reduce_splits_kernel(const float* __restrict__ ws, int splits, int MN, const float* __restrict__ bias,
+                                     int N, float* __restrict__ out) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= MN) return;
+  float acc = 0.f;
+  for (int sp = 0; sp < splits; ++sp) acc += ws[static_cast<size_t>(sp) * MN + i];
+  out[i] = bias ? acc + bias[i % N] : acc;
 }
 
 typedef CUresult (*PFN_encodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -226,12 +271,20 @@ int make_tmap_2d_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64
 // Split count depends only on (N, K): at least 148 work units for one token tile.
 GemmPlan gemm_plan(const evs_model* m, int N, int K, int M, int dual) {
   GemmPlan p{N, K, M, 1, dual};
-  if (m->cfg.dtype != EVS_DTYPE_BF16) return p;
+  if (m->cfg.dtype != EVS_DTYPE_BF16) return gemm_plan_f32(N, K, M, dual);
   const int kblocks = K / GEMM_BK;
   const int tiles = N / GEMM_BM;
   int splits = 1;
   while (tiles * splits < 148 && splits < kblocks) ++splits;
   p.splits = splits;
+  return p;
+}
+
+// CUDA-core projection: split K (from N and K only) until >= 148 CTAs, each split >= 64 of K
+GemmPlan gemm_plan_f32(int N, int K, int M, int dual) {
+  GemmPlan p{N, K, M, 1, dual};
+  const int tiles = (N + SG_BN - 1) / SG_BN;
+  while (tiles * p.splits < 148 && K / (p.splits + 1) >= 64) ++p.splits;
   return p;
 }
 
@@ -246,17 +299,25 @@ int launch_gemm_tc(const CUtensorMap* tmA, const CUtensorMap* tmA2, const CUtens
 int launch_gemm_simt(const void* W, const void* W2, const void* X, int ldx, int dtype, const GemmPlan& p, float* ws,
                      cudaStream_t st) {
   if (p.M <= 0) return EVS_OK;
-  dim3 grid((p.N + 3) / 4, p.splits);
+  dim3 grid((p.N + SG_BN - 1) / SG_BN, (p.M + SG_BM - 1) / SG_BM, p.splits);
   if (dtype == EVS_DTYPE_BF16) {
-    gemm_simt_kernel<__nv_bfloat16, __nv_bfloat16><<<grid, 128, 0, st>>>(
+    gemm_f32_kernel<__nv_bfloat16, __nv_bfloat16><<<grid, 256, 0, st>>>(
         static_cast<const __nv_bfloat16*>(W), static_cast<const __nv_bfloat16*>(W2),
         static_cast<const __nv_bfloat16*>(X), ldx, ws, p.N, p.K, p.M, p.splits, p.dual);
   } else {
-    gemm_simt_kernel<float, float><<<grid, 128, 0, st>>>(static_cast<const float*>(W),
-                                                         static_cast<const float*>(W2),
-                                                         static_cast<const float*>(X), ldx, ws, p.N, p.K, p.M,
-                                                         p.splits, p.dual);
+    gemm_f32_kernel<float, float><<<grid, 256, 0, st>>>(static_cast<const float*>(W), static_cast<const float*>(W2),
+                                                        static_cast<const float*>(X), ldx, ws, p.N, p.K, p.M,
+                                                        p.splits, p.dual);
   }
+  EVS_CUDA_TRY(cudaGetLastError());
+  evs_count_launch(1);
+  return EVS_OK;
+}
+
+int launch_reduce_splits(const float* ws, int splits, int M, int N, const float* bias, float* out, cudaStream_t st) {
+  const int MN = M * N;
+  if (MN <= 0) return EVS_OK;
+  reduce_splits_kernel<<<(MN + 255) / 256, 256, 0, st>>>(ws, splits, MN, bias, N, out);
   EVS_CUDA_TRY(cudaGetLastError());
   evs_count_launch(1);
   return EVS_OK;

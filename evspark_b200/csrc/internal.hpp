@@ -110,6 +110,9 @@ struct GemmPlan {
   int N, K, M, splits, dual;
 };
 GemmPlan gemm_plan(const evs_model* m, int N, int K, int M, int dual);
+GemmPlan gemm_plan_f32(int N, int K, int M, int dual);
+// out[m][n] = sum of the split partials (in split order) + bias[n]
+int launch_reduce_splits(const float* ws, int splits, int M, int N, const float* bias, float* out, cudaStream_t st);
 int launch_gemm_tc(const CUtensorMap* tmA, const CUtensorMap* tmA2, const CUtensorMap* tmB, const GemmPlan& p,
                    float* ws, EvsDevErr* err, cudaStream_t st);
 int launch_gemm_simt(const void* W, const void* W2, const void* X, int ldx, int dtype, const GemmPlan& p, float* ws,

@@ -1,9 +1,11 @@
 // fp64 sampling helpers shared by the verifier and the drafter's serial head.
 //
-// Row sums use pairwise summation (blocks of 128 with eight running partials, halves split at a
-// multiple of 8) and cumulative sums run left to right, so that for the same inputs the
-// normalised rows equal the ones numpy produces (evspark/specdec/verifier.py:28-40 and
-// evspark/specdec/transforms.py:18-64 are written against numpy).
+// Row sums use pairwise summation — blocks of at most 128 values summed with eight running
+// partials combined as ((r0+r1)+(r2+r3))+((r4+r5)+(r6+r7)), larger ranges split in two at a
+// multiple of 8 — and cumulative sums run left to right, so that for the same inputs the
+// normalised rows and the inverse-CDF draws equal numpy's (evspark/specdec/verifier.py:28-40 and
+// evspark/specdec/transforms.py:18-64 are written against numpy).  The leaves of the summation
+// tree are evaluated by groups of eight threads in parallel; only the cumulative sum is serial.
 #pragma once
 
 #include <math_constants.h>
@@ -13,81 +15,99 @@
 namespace evs_sampling {
 
 constexpr int VMAX = 1024;
+constexpr int MAX_LEAVES = 16;  // VMAX / 64
 
-// pairwise sum of a[0..n) (8-way unrolled base case of 128 elements)
-__device__ inline double pairwise_sum(const double* a, int n) {
-  if (n < 8) {
-    double r = 0.0;
-    for (int i = 0; i < n; ++i) r += a[i];
-    return r;
-  }
-  if (n <= 128) {
-    double r[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) r[j] = a[j];
-    int i = 8;
-    for (; i < n - (n % 8); i += 8) {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) r[j] += a[i + j];
+// scratch the helpers share (one per block, in shared memory)
+struct SampScratch {
+  double leaf[MAX_LEAVES];
+  double dv[32];
+  int iv[32];
+  double scal[2];
+  int icount;
+};
+
+// leaf ranges of the pairwise-summation tree of n values, left to right
+__device__ inline int pw_leaves(int n, int* start, int* len) {
+  int cnt = 0;
+  // explicit stack of (offset, size), processed depth-first left to right
+  int so[32], ss[32], top = 0;
+  so[0] = 0;
+  ss[0] = n;
+  top = 1;
+  while (top > 0) {
+    --top;
+    const int o = so[top], m = ss[top];
+    if (m <= 128) {
+      start[cnt] = o;
+      len[cnt] = m;
+      ++cnt;
+    } else {
+      int n2 = m / 2;
+      n2 -= n2 % 8;
+      // push right then left so the left range is processed first
+      so[top] = o + n2;
+      ss[top] = m - n2;
+      ++top;
+      so[top] = o;
+      ss[top] = n2;
+      ++top;
     }
-    double res = ((r[0] + r[1]) + (r[2] + r[3])) + ((r[4] + r[5]) + (r[6] + r[7]));
-    for (; i < n; ++i) res += a[i];
-    return res;
   }
+  return cnt;
+}
+
+__device__ inline double pw_combine(const double* leaf, int n, int* idx) {
+  if (n <= 128) return leaf[(*idx)++];
   int n2 = n / 2;
   n2 -= n2 % 8;
-  return pairwise_sum(a, n2) + pairwise_sum(a + n2, n - n2);
+  const double a = pw_combine(leaf, n2, idx);
+  const double b = pw_combine(leaf, n - n2, idx);
+  return a + b;
 }
 
-// index of the max (lowest index on ties) of row[0..V), whole block participates
-__device__ inline int block_argmax(const double* row, int V, double* sv, int* si) {
-  double best = 0.0;
-  int bi = -1;
-  for (int i = threadIdx.x; i < V; i += blockDim.x) {
-    const double v = row[i];
-    if (bi < 0 || v > best) {  // i grows, so ties keep the lower index
-      best = v;
-      bi = i;
+// numpy-identical pairwise sum of a[0..n) (n <= VMAX); whole block participates, >= 128 threads
+__device__ inline double block_pairwise_sum(const double* a, int n, SampScratch* sc) {
+  int start[MAX_LEAVES], len[MAX_LEAVES];
+  const int nl = pw_leaves(n, start, len);
+  const int t = threadIdx.x;
+  const int leaf = t >> 3, j = t & 7;
+  // every thread of the first nl*8 takes part (others idle); groups of 8 are warp-aligned
+  double r = 0.0;
+  if (leaf < nl) {
+    const double* b = a + start[leaf];
+    const int m = len[leaf];
+    if (m >= 8) {
+      r = b[j];
+      for (int i = 8 + j; i < m - (m % 8); i += 8) r += b[i];
+    } else if (j == 0) {
+      for (int i = 0; i < m; ++i) r += b[i];
     }
   }
-  sv[threadIdx.x] = best;
-  si[threadIdx.x] = bi;
+  // ((r0+r1)+(r2+r3))+((r4+r5)+(r6+r7)) within each group of 8 lanes
+  const unsigned full = 0xffffffffu;
+  double o = __shfl_xor_sync(full, r, 1);
+  r = (j & 1) ? o + r : r + o;
+  o = __shfl_xor_sync(full, r, 2);
+  r = (j & 2) ? o + r : r + o;
+  o = __shfl_xor_sync(full, r, 4);
+  r = (j & 4) ? o + r : r + o;
+  if (leaf < nl && j == 0) {
+    const int m = len[leaf];
+    if (m >= 8) {
+      const double* b = a + start[leaf];
+      for (int i = m - (m % 8); i < m; ++i) r += b[i];
+    }
+    sc->leaf[leaf] = r;
+  }
   __syncthreads();
-  for (int s = blockDim.x / 2; s > 0; s >>= 1) {
-    if (threadIdx.x < s) {
-      const double ov = sv[threadIdx.x + s], mv = sv[threadIdx.x];
-      const int oi = si[threadIdx.x + s], mi = si[threadIdx.x];
-      if (oi >= 0 && (mi < 0 || ov > mv || (ov == mv && oi < mi))) {
-        sv[threadIdx.x] = ov;
-        si[threadIdx.x] = oi;
-      }
-    }
-    __syncthreads();
+  if (t == 0) {
+    int idx = 0;
+    sc->scal[0] = nl == 1 ? sc->leaf[0] : pw_combine(sc->leaf, n, &idx);
   }
-  const int out = si[0];
+  __syncthreads();
+  const double out = sc->scal[0];
   __syncthreads();
   return out;
-}
-
-// thread 0 only: sample_categorical(row, u) with row already clipped at 0 in `w` (length V)
-__device__ inline int sample_clipped(double* w, int V, double u) {
-  const double s = pairwise_sum(w, V);
-  if (!(s > 0.0) || !isfinite(s)) {
-    for (int i = 0; i < V; ++i) w[i] = 1.0 / V;
-  } else {
-    for (int i = 0; i < V; ++i) w[i] = w[i] / s;
-  }
-  double c = 0.0;
-  for (int i = 0; i < V; ++i) {
-    c += w[i];
-    w[i] = c;
-  }
-  const double last = w[V - 1];
-  int idx = 0;
-  for (int i = 0; i < V; ++i) {
-    if (w[i] / last <= u) idx = i + 1;
-  }
-  return idx < V ? idx : V - 1;
 }
 
 __device__ inline double accept_prob(double px, double qx) {
@@ -99,27 +119,95 @@ __device__ inline double accept_prob(double px, double qx) {
   return px > 0.0 ? 1.0 : 0.0;
 }
 
+// index of the max (lowest index on ties) of row[0..V); whole block participates
+__device__ inline int block_argmax(const double* row, int V, SampScratch* sc) {
+  double best = 0.0;
+  int bi = -1;
+  for (int i = threadIdx.x; i < V; i += blockDim.x) {
+    const double v = row[i];
+    if (bi < 0 || v > best) {  // i grows, so ties keep the lower index
+      best = v;
+      bi = i;
+    }
+  }
+  const unsigned full = 0xffffffffu;
+  for (int o = 16; o > 0; o >>= 1) {
+    const double ov = __shfl_xor_sync(full, best, o);
+    const int oi = __shfl_xor_sync(full, bi, o);
+    if (oi >= 0 && (bi < 0 || ov > best || (ov == best && oi < bi))) {
+      best = ov;
+      bi = oi;
+    }
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  if (lane == 0) {
+    sc->dv[warp] = best;
+    sc->iv[warp] = bi;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    best = lane < nw ? sc->dv[lane] : 0.0;
+    bi = lane < nw ? sc->iv[lane] : -1;
+    for (int o = 16; o > 0; o >>= 1) {
+      const double ov = __shfl_xor_sync(full, best, o);
+      const int oi = __shfl_xor_sync(full, bi, o);
+      if (oi >= 0 && (bi < 0 || ov > best || (ov == best && oi < bi))) {
+        best = ov;
+        bi = oi;
+      }
+    }
+    if (lane == 0) sc->iv[0] = bi;
+  }
+  __syncthreads();
+  const int out = sc->iv[0];
+  __syncthreads();
+  return out;
+}
 
-// apply_transform of the fp64 row e[0..V) (in shared memory; overwritten) into out (global or
-// shared).  Whole block participates.  keep / masked / sv / si are shared scratch of V / 256.
+// sample_categorical(w, u) with w already clipped at 0 (w is overwritten); whole block
+__device__ inline int block_sample_clipped(double* w, int V, double u, SampScratch* sc) {
+  const double s = block_pairwise_sum(w, V, sc);
+  const bool bad = !(s > 0.0) || !isfinite(s);
+  for (int i = threadIdx.x; i < V; i += blockDim.x) w[i] = bad ? 1.0 / V : w[i] / s;
+  __syncthreads();
+  if (threadIdx.x == 0) {  // left-to-right cumulative sum (numpy cumsum order)
+    double c = 0.0;
+    for (int i = 0; i < V; ++i) {
+      c += w[i];
+      w[i] = c;
+    }
+    sc->icount = 0;
+  }
+  __syncthreads();
+  const double last = w[V - 1];
+  int cnt = 0;
+  for (int i = threadIdx.x; i < V; i += blockDim.x) cnt += (w[i] / last <= u) ? 1 : 0;
+  for (int o = 16; o > 0; o >>= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, o);
+  if ((threadIdx.x & 31) == 0 && cnt) atomicAdd(&sc->icount, cnt);
+  __syncthreads();
+  const int idx = sc->icount;
+  __syncthreads();
+  return idx < V ? idx : V - 1;
+}
+
+// apply_transform of the fp64 row e[0..V) (shared memory; overwritten) into out (global or
+// shared).  Whole block participates.  keep / masked: shared scratch of V.
 __device__ inline void transform_row(double* e, int V, double temperature, int top_k, double* out, int* keep,
-                                     double* masked, double* sv, int* si, double* scal) {
+                                     double* masked, SampScratch* sc) {
   if (temperature <= 0.0) {
-    const int am = block_argmax(e, V, sv, si);
+    const int am = block_argmax(e, V, sc);
     for (int i = threadIdx.x; i < V; i += blockDim.x) out[i] = i == am ? 1.0 : 0.0;
     __syncthreads();
     return;
   }
   for (int i = threadIdx.x; i < V; i += blockDim.x) e[i] = e[i] / temperature;
   __syncthreads();
-  const int am = block_argmax(e, V, sv, si);
+  const int am = block_argmax(e, V, sc);
   const double mx = e[am];
   __syncthreads();
   for (int i = threadIdx.x; i < V; i += blockDim.x) e[i] = exp(e[i] - mx);
   __syncthreads();
-  if (threadIdx.x == 0) scal[0] = pairwise_sum(e, V);
-  __syncthreads();
-  const double z = scal[0];
+  const double z = block_pairwise_sum(e, V, sc);
   const bool bad = !(z > 0.0) || !isfinite(z);
   for (int i = threadIdx.x; i < V; i += blockDim.x) e[i] = bad ? 1.0 / V : e[i] / z;
   __syncthreads();
@@ -134,7 +222,7 @@ __device__ inline void transform_row(double* e, int V, double temperature, int t
   }
   __syncthreads();
   for (int k = 0; k < top_k; ++k) {
-    const int am2 = block_argmax(masked, V, sv, si);
+    const int am2 = block_argmax(masked, V, sc);
     if (threadIdx.x == 0) {
       keep[am2] = 1;
       masked[am2] = -CUDART_INF;
@@ -143,9 +231,7 @@ __device__ inline void transform_row(double* e, int V, double temperature, int t
   }
   for (int i = threadIdx.x; i < V; i += blockDim.x) masked[i] = keep[i] ? e[i] : 0.0;
   __syncthreads();
-  if (threadIdx.x == 0) scal[0] = pairwise_sum(masked, V);
-  __syncthreads();
-  const double ms = scal[0];
+  const double ms = block_pairwise_sum(masked, V, sc);
   const bool bad2 = !(ms > 0.0) || !isfinite(ms);
   for (int i = threadIdx.x; i < V; i += blockDim.x) out[i] = keep[i] ? (bad2 ? 1.0 / top_k : masked[i] / ms) : 0.0;
   __syncthreads();

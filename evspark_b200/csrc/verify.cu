@@ -22,8 +22,9 @@ using namespace evs_sampling;
 // one CTA per row
 __global__ void __launch_bounds__(256) transform_kernel(const void* __restrict__ logits, int f64, int V,
                                                         double temperature, int top_k, double* __restrict__ probs) {
-  __shared__ double e[VMAX], masked[VMAX], sv[256], scal[1];
-  __shared__ int keep[VMAX], si[256];
+  __shared__ double e[VMAX], masked[VMAX];
+  __shared__ int keep[VMAX];
+  __shared__ SampScratch sc;
   const int r = blockIdx.x;
   if (f64) {
     const double* lg = static_cast<const double*>(logits) + static_cast<size_t>(r) * V;
@@ -33,18 +34,17 @@ __global__ void __launch_bounds__(256) transform_kernel(const void* __restrict__
     for (int i = threadIdx.x; i < V; i += blockDim.x) e[i] = static_cast<double>(lg[i]);
   }
   __syncthreads();
-  transform_row(e, V, temperature, top_k, probs + static_cast<size_t>(r) * V, keep, masked, sv, si, scal);
+  transform_row(e, V, temperature, top_k, probs + static_cast<size_t>(r) * V, keep, masked, &sc);
 }
 
-// one CTA per row b
+// one CTA per row b; every block-wide helper is called by all threads (uniform control flow)
 __global__ void __launch_bounds__(256) verify_kernel(const double* __restrict__ p, const double* __restrict__ q,
                                                      const int64_t* __restrict__ x, const double* __restrict__ u,
                                                      int gamma, int V, int greedy, int32_t* __restrict__ accepted,
                                                      int64_t* __restrict__ tokens, int32_t* __restrict__ info) {
   __shared__ double w[VMAX];
-  __shared__ double sv[256];
-  __shared__ int si[256];
-  __shared__ int s_done, s_acc, s_tok, s_ui, s_res, s_fb;
+  __shared__ SampScratch sc;
+  __shared__ int s_done, s_acc, s_ui;
   const int b = blockIdx.x;
   const double* pb = p + static_cast<size_t>(b) * (gamma + 1) * V;
   const double* qb = q ? q + static_cast<size_t>(b) * gamma * V : nullptr;
@@ -55,87 +55,86 @@ __global__ void __launch_bounds__(256) verify_kernel(const double* __restrict__ 
     s_done = 0;
     s_acc = 0;
     s_ui = 0;
-    s_res = 0;
-    s_fb = 0;
-    s_tok = -1;
   }
   for (int i = threadIdx.x; i <= gamma; i += blockDim.x) tb[i] = -1;
   __syncthreads();
+  int tok = -1, from_res = 0, fb = 0;
   for (int i = 0; i < gamma; ++i) {
     const double* pi = pb + static_cast<size_t>(i) * V;
     const int64_t xi = xb[i];
     if (greedy) {
-      const int am = block_argmax(pi, V, sv, si);
-      if (threadIdx.x == 0) {
-        if (xi == am) {
-          tb[i] = am;
-          s_acc = i + 1;
-        } else {
-          s_tok = am;
-          s_res = 1;
-          s_done = 1;
-        }
+      const int am = block_argmax(pi, V, &sc);
+      if (xi != am) {
+        tok = am;
+        from_res = 1;
+        break;
       }
-      __syncthreads();
-    } else {
-      const double* qi = qb + static_cast<size_t>(i) * V;
-      if (threadIdx.x == 0) {
-        const double r = ub[s_ui++];
-        const bool ok = xi >= 0 && xi < V && r < accept_prob(pi[xi], qi[xi]);
-        if (ok) {
-          tb[i] = xi;
-          s_acc = i + 1;
-        } else {
-          s_done = 1;
-        }
-      }
-      __syncthreads();
-      if (s_done) {
-        for (int v = threadIdx.x; v < V; v += blockDim.x) w[v] = fmax(pi[v] - qi[v], 0.0);
-        __syncthreads();
-        if (threadIdx.x == 0) {
-          const double mass = pairwise_sum(w, V);
-          const bool fb = !(mass > 0.0) || !isfinite(mass);
-          if (fb)
-            for (int v = 0; v < V; ++v) w[v] = fmax(pi[v], 0.0);
-          s_fb = fb ? 1 : 0;
-          s_res = 1;
-          s_tok = sample_clipped(w, V, ub[s_ui++]);
-        }
-        __syncthreads();
-      }
+      if (threadIdx.x == 0) tb[i] = am;
+      continue;
     }
-    if (s_done) break;
-  }
-  if (!s_done) {
-    const double* pg = pb + static_cast<size_t>(gamma) * V;
-    if (greedy) {
-      const int am = block_argmax(pg, V, sv, si);
-      if (threadIdx.x == 0) s_tok = am;
-    } else {
-      for (int v = threadIdx.x; v < V; v += blockDim.x) w[v] = fmax(pg[v], 0.0);
-      __syncthreads();
-      if (threadIdx.x == 0) s_tok = sample_clipped(w, V, ub[s_ui++]);
+    const double* qi = qb + static_cast<size_t>(i) * V;
+    const double r = ub[i];  // draw i is the accept test of position i
+    const bool ok = xi >= 0 && xi < V && r < accept_prob(pi[xi], qi[xi]);
+    if (ok) {
+      if (threadIdx.x == 0) tb[i] = xi;
+      continue;
     }
+    // first rejection: sample norm(max(0, p - q)), or p when that mass underflows
+    for (int v = threadIdx.x; v < V; v += blockDim.x) w[v] = fmax(pi[v] - qi[v], 0.0);
     __syncthreads();
+    const double mass = block_pairwise_sum(w, V, &sc);
+    fb = (!(mass > 0.0) || !isfinite(mass)) ? 1 : 0;
+    if (fb) {
+      for (int v = threadIdx.x; v < V; v += blockDim.x) w[v] = fmax(pi[v], 0.0);
+      __syncthreads();
+    }
+    tok = block_sample_clipped(w, V, ub[i + 1], &sc);
+    from_res = 1;
+    if (threadIdx.x == 0) {
+      s_acc = i;
+      s_ui = i + 2;
+      s_done = 1;
+    }
+    break;
+  }
+  __syncthreads();
+  int acc_len, used;
+  if (greedy) {
+    // tokens accepted so far are the prefix written above
+    acc_len = 0;
+    while (acc_len < gamma && tb[acc_len] >= 0) ++acc_len;
+    if (tok < 0) tok = block_argmax(pb + static_cast<size_t>(gamma) * V, V, &sc);
+    used = 0;
+  } else if (!s_done) {
+    const double* pg = pb + static_cast<size_t>(gamma) * V;
+    for (int v = threadIdx.x; v < V; v += blockDim.x) w[v] = fmax(pg[v], 0.0);
+    __syncthreads();
+    tok = block_sample_clipped(w, V, ub[gamma], &sc);
+    acc_len = gamma;
+    used = gamma + 1;
+  } else {
+    acc_len = s_acc;
+    used = s_ui;
   }
   if (threadIdx.x == 0) {
-    tb[s_acc] = s_tok;
-    accepted[b] = s_acc;
-    info[3 * b + 0] = s_res;
-    info[3 * b + 1] = s_fb;
-    info[3 * b + 2] = s_ui;
+    tb[acc_len] = tok;
+    accepted[b] = acc_len;
+    info[3 * b + 0] = from_res;
+    info[3 * b + 1] = fb;
+    info[3 * b + 2] = used;
   }
 }
 
 __global__ void __launch_bounds__(256) sample_kernel(const double* __restrict__ rows, int V,
                                                      const double* __restrict__ u, int64_t* __restrict__ out) {
   __shared__ double w[VMAX];
+  __shared__ SampScratch sc;
   const int r = blockIdx.x;
   const double* row = rows + static_cast<size_t>(r) * V;
   for (int v = threadIdx.x; v < V; v += blockDim.x) w[v] = fmax(row[v], 0.0);
   __syncthreads();
-  if (threadIdx.x == 0) out[r] = sample_clipped(w, V, u[r]);
+  const int idx = block_sample_clipped(w, V, u[r], &sc);
+  if (threadIdx.x == 0) out[r] = idx;
 }
 
 }  // namespace
