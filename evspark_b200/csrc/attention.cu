@@ -4,7 +4,8 @@
 // flash_attn_with_kvcache through the model forward).
 //
 //   rope_append_kernel   qkv partials -> rotate-half RoPE (fp64 angle) -> q_rot, K/V cache append
-//   attn_block_kernel    one CTA per (256-key block, head, row): partial (max, sum, acc) per query
+//   attn_block_kernel    one CTA per (256-key block, head, row) staged in shared memory:
+//                        partial (max, sum, acc) per query
 //   attn_combine_kernel  folds the partials of blocks 0..P/256 in block order
 //
 // Blocks are aligned at absolute key positions and folded in a fixed order, so a query's result
@@ -54,87 +55,181 @@ __global__ void rope_append_kernel(const float* __restrict__ ws, int splits, int
   vdst[c2] = from_f32<TD>(v2);
 }
 
-constexpr int QG = 8;  // queries per score pass
+constexpr int QT = 16;           // queries per pass over the staged keys
+constexpr int ATTN_THREADS = 256;
 
-// grid (blocks, H, B); 256 threads; smem: q[T][Dh] + S[T][256] + stats[2T]
+// shared memory of attn_block_kernel: K rows padded by 16 bytes (conflict-free row-per-thread
+// reads), V rows dense, fp32 queries, scores and per-query stats
 template <typename TD>
-__global__ void __launch_bounds__(256) attn_block_kernel(const TD* __restrict__ qrot, const TD* __restrict__ kv,
-                                                        const int32_t* __restrict__ len, int T, int d, int H, int Dh,
-                                                        int Lmax, int nblk_cap, int tcap, float scale,
-                                                        float* __restrict__ part) {
-  extern __shared__ float sm[];
+__host__ __device__ constexpr size_t attn_smem_bytes(int Dh) {
+  return sizeof(TD) * (static_cast<size_t>(ATTN_BLOCK) * (Dh + 16 / sizeof(TD)) + static_cast<size_t>(ATTN_BLOCK) * Dh) +
+         sizeof(float) * (static_cast<size_t>(QT) * Dh + static_cast<size_t>(QT) * ATTN_BLOCK + 2 * QT);
+}
+
+// grid (blocks, H, B), 256 threads.  One CTA stages one 256-key block of one head in shared
+// memory with 16-byte asynchronous copies (K and V in two groups, so scores start while V is in
+// flight), then for each group of <= 16 queries computes scores (one key per thread), the block's
+// softmax stats (one warp per query) and P.V (two head columns x up to four queries per thread).
+// Keys past a query's position score -inf and contribute exact zeros, so a query's partial does
+// not depend on how many queries share the call.
+template <typename TD>
+__global__ void __launch_bounds__(ATTN_THREADS) attn_block_kernel(const TD* __restrict__ qrot,
+                                                                 const TD* __restrict__ kv,
+                                                                 const int32_t* __restrict__ len, int T, int d,
+                                                                 int H, int Dh, int Lmax, int nblk_cap, int tcap,
+                                                                 float scale, float* __restrict__ part) {
+  extern __shared__ __align__(16) unsigned char attn_sm[];
   const int j = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int L0 = len[b];
   const int Lend = L0 + T;
   const int k0 = j * ATTN_BLOCK;
   if (k0 >= Lend) return;
   const int nk = min(ATTN_BLOCK, Lend - k0);
-  float* qs = sm;                 // [T][Dh]
-  float* S = qs + T * Dh;         // [T][ATTN_BLOCK]
-  float* st = S + T * ATTN_BLOCK; // [T][2]
+  constexpr int EPC = 16 / sizeof(TD);  // elements per 16-byte chunk
+  const int kpad = Dh + EPC;
+  TD* Ks = reinterpret_cast<TD*>(attn_sm);
+  TD* Vs = Ks + ATTN_BLOCK * kpad;
+  float* qs = reinterpret_cast<float*>(Vs + ATTN_BLOCK * Dh);
+  float* S = qs + QT * Dh;
+  float* stt = S + QT * ATTN_BLOCK;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  for (int i = tid; i < T * Dh; i += blockDim.x) {
-    const int t = i / Dh, dd = i % Dh;
-    qs[i] = to_f32(qrot[static_cast<size_t>(b * T + t) * d + h * Dh + dd]);
-  }
-  __syncthreads();
   const size_t HD = static_cast<size_t>(H) * Dh;
-  if (tid < nk) {
-    const int kk = k0 + tid;
-    const TD* kp = kv + ((static_cast<size_t>(b) * Lmax + kk) * 2 + 0) * HD + h * Dh;
-    for (int tg = 0; tg < T; tg += QG) {
-      float acc[QG];
+  const TD* kb = kv + (static_cast<size_t>(b) * Lmax + k0) * 2 * HD + static_cast<size_t>(h) * Dh;
+  const int cpr = Dh / EPC;  // chunks per row
+  for (int i = tid; i < nk * cpr; i += ATTN_THREADS) {
+    const int r = i / cpr, c = i - r * cpr;
+    cp_async16(Ks + r * kpad + c * EPC, kb + static_cast<size_t>(r) * 2 * HD + c * EPC);
+  }
+  cp_async_commit();
+  for (int i = tid; i < nk * cpr; i += ATTN_THREADS) {
+    const int r = i / cpr, c = i - r * cpr;
+    cp_async16(Vs + r * Dh + c * EPC, kb + static_cast<size_t>(r) * 2 * HD + HD + c * EPC);
+  }
+  cp_async_commit();
+  bool k_ready = false, v_ready = false;
+  const int npair = Dh / 2, groups = ATTN_THREADS / npair;
+  const int pi = tid % npair, g = tid / npair;
+  for (int tq0 = 0; tq0 < T; tq0 += QT) {
+    const int nq = min(QT, T - tq0);
+    if (L0 + tq0 + nq - 1 < k0) continue;  // every query of the group precedes the block
+    for (int i = tid; i < nq * Dh; i += ATTN_THREADS) {
+      const int t = i / Dh, dd = i - t * Dh;
+      qs[i] = to_f32(qrot[static_cast<size_t>(b * T + tq0 + t) * d + h * Dh + dd]);
+    }
+    if (!k_ready) {
+      cp_async_wait<1>();
+      k_ready = true;
+    }
+    __syncthreads();
+    {  // scores: key tid against every query of the group
+      float acc[QT];
 #pragma unroll
-      for (int u = 0; u < QG; ++u) acc[u] = 0.f;
-      for (int dd = 0; dd < Dh; ++dd) {
-        const float kvv = to_f32(kp[dd]);
+      for (int u = 0; u < QT; ++u) acc[u] = 0.f;
+      if (tid < nk) {
+        const TD* kr = Ks + tid * kpad;
+        for (int c0 = 0; c0 < Dh; c0 += EPC) {
+          float kf[EPC];
+          if constexpr (sizeof(TD) == 2) {
+            const uint4 raw = *reinterpret_cast<const uint4*>(kr + c0);
+            const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
 #pragma unroll
-        for (int u = 0; u < QG; ++u)
-          if (tg + u < T) acc[u] = fmaf(qs[(tg + u) * Dh + dd], kvv, acc[u]);
+            for (int e = 0; e < 4; ++e) {
+              const float2 f2 = __bfloat1622float2(h2[e]);
+              kf[2 * e] = f2.x;
+              kf[2 * e + 1] = f2.y;
+            }
+          } else {
+            const float4 raw = *reinterpret_cast<const float4*>(kr + c0);
+            kf[0] = raw.x;
+            kf[1] = raw.y;
+            kf[2] = raw.z;
+            kf[3] = raw.w;
+          }
+#pragma unroll
+          for (int u = 0; u < QT; ++u) {
+            if (u < nq) {
+              const float* qr = qs + u * Dh + c0;
+#pragma unroll
+              for (int e = 0; e < EPC; ++e) acc[u] = fmaf(qr[e], kf[e], acc[u]);
+            }
+          }
+        }
       }
 #pragma unroll
-      for (int u = 0; u < QG; ++u) {
-        const int t = tg + u;
-        if (t < T) S[t * ATTN_BLOCK + tid] = kk <= L0 + t ? acc[u] * scale : -CUDART_INF_F;
+      for (int u = 0; u < QT; ++u) {
+        if (u < nq) {
+          const bool vis = tid < nk && k0 + tid <= L0 + tq0 + u;
+          S[u * ATTN_BLOCK + tid] = vis ? acc[u] * scale : -CUDART_INF_F;
+        }
       }
     }
-  }
-  __syncthreads();
-  for (int t = warp; t < T; t += blockDim.x / 32) {
-    float m = -CUDART_INF_F;
-    for (int i = lane; i < nk; i += 32) m = fmaxf(m, S[t * ATTN_BLOCK + i]);
-    m = warp_max(m);
-    float l = 0.f;
-    for (int i = lane; i < nk; i += 32) {
-      const float sv = S[t * ATTN_BLOCK + i];
-      const float pv = (m == -CUDART_INF_F || sv == -CUDART_INF_F) ? 0.f : expf(sv - m);
-      S[t * ATTN_BLOCK + i] = pv;
-      l += pv;
+    __syncthreads();
+    for (int t = warp; t < nq; t += ATTN_THREADS / 32) {
+      float* Sr = S + t * ATTN_BLOCK;
+      float mx = -CUDART_INF_F;
+      for (int i = lane; i < ATTN_BLOCK; i += 32) mx = fmaxf(mx, Sr[i]);
+      mx = warp_max(mx);
+      float l = 0.f;
+      for (int i = lane; i < ATTN_BLOCK; i += 32) {
+        const float sv = Sr[i];
+        const float pv = (mx == -CUDART_INF_F || sv == -CUDART_INF_F) ? 0.f : expf(sv - mx);
+        Sr[i] = pv;
+        l += pv;
+      }
+      l = warp_sum(l);
+      if (lane == 0) {
+        stt[2 * t] = mx;
+        stt[2 * t + 1] = l;
+      }
     }
-    l = warp_sum(l);
-    if (lane == 0) {
-      st[2 * t] = m;
-      st[2 * t + 1] = l;
+    if (!v_ready) {
+      cp_async_wait<0>();
+      v_ready = true;
     }
-  }
-  __syncthreads();
-  const int groups = blockDim.x / Dh;
-  const int dd = tid % Dh, g = tid / Dh;
-  if (g < groups) {
-    for (int t = g; t < T; t += groups) {
-      float acc = 0.f;
+    __syncthreads();
+    {  // P.V: head columns 2*pi, 2*pi+1 for queries g, g+groups, ...
+      constexpr int QPT = 4;
+      float a0[QPT], a1[QPT];
+#pragma unroll
+      for (int q = 0; q < QPT; ++q) a0[q] = a1[q] = 0.f;
       for (int i = 0; i < nk; ++i) {
-        const TD* vp = kv + ((static_cast<size_t>(b) * Lmax + k0 + i) * 2 + 1) * HD + h * Dh;
-        acc = fmaf(S[t * ATTN_BLOCK + i], to_f32(vp[dd]), acc);
+        float v0, v1;
+        if constexpr (sizeof(TD) == 2) {
+          const float2 f2 = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(Vs + i * Dh)[pi]);
+          v0 = f2.x;
+          v1 = f2.y;
+        } else {
+          const float2 f2 = reinterpret_cast<const float2*>(Vs + i * Dh)[pi];
+          v0 = f2.x;
+          v1 = f2.y;
+        }
+#pragma unroll
+        for (int q = 0; q < QPT; ++q) {
+          const int t = g + q * groups;
+          if (t < nq) {
+            const float pv = S[t * ATTN_BLOCK + i];
+            a0[q] = fmaf(pv, v0, a0[q]);
+            a1[q] = fmaf(pv, v1, a1[q]);
+          }
+        }
       }
-      float* pd = part + ((((static_cast<size_t>(b) * H + h) * nblk_cap + j) * tcap + t) * (Dh + 2));
-      pd[dd] = acc;
-      if (dd == 0) {
-        pd[Dh] = st[2 * t];
-        pd[Dh + 1] = st[2 * t + 1];
+#pragma unroll
+      for (int q = 0; q < QPT; ++q) {
+        const int t = g + q * groups;
+        if (t < nq && L0 + tq0 + t >= k0) {
+          float* pd = part + ((((static_cast<size_t>(b) * H + h) * nblk_cap + j) * tcap + tq0 + t) * (Dh + 2));
+          pd[2 * pi] = a0[q];
+          pd[2 * pi + 1] = a1[q];
+          if (pi == 0) {
+            pd[Dh] = stt[2 * t];
+            pd[Dh + 1] = stt[2 * t + 1];
+          }
+        }
       }
     }
+    __syncthreads();
   }
+  if (!v_ready) cp_async_wait<0>();  // no copy may outlive the CTA
 }
 
 template <typename TD>
@@ -170,11 +265,11 @@ int launch_attention_t(const evs_model* m, evs_state* s, int layer, int B, int T
   rope_append_kernel<TD><<<dim3(M, H), Dh / 2, 0, st>>>(s->ws, splits, M, T, d, H, Dh, log(m->cfg.rope_base),
                                                         s->d_len, s->max_seqlen, qrot, kv, s->d_err);
   EVS_CUDA_TRY(cudaGetLastError());
-  const size_t smem = sizeof(float) * (static_cast<size_t>(T) * Dh + static_cast<size_t>(T) * ATTN_BLOCK + 2 * T);
-  EVS_CHECK_RANGE(smem <= 200 * 1024, "too many queries per attention call");
+  const size_t smem = attn_smem_bytes<TD>(Dh);
+  EVS_CHECK_RANGE(smem <= 227 * 1024, "head_dim too large for the staged attention block");
   EVS_CUDA_TRY(cudaFuncSetAttribute(attn_block_kernel<TD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     static_cast<int>(smem)));
-  attn_block_kernel<TD><<<dim3(kv_blocks, H, B), 256, smem, st>>>(
+  attn_block_kernel<TD><<<dim3(kv_blocks, H, B), ATTN_THREADS, smem, st>>>(
       qrot, kv, s->d_len, T, d, H, Dh, s->max_seqlen, s->attn_blocks, s->max_chunk, 1.0f / sqrtf(static_cast<float>(Dh)),
       s->attn_part);
   EVS_CUDA_TRY(cudaGetLastError());
@@ -189,8 +284,9 @@ int launch_attention_t(const evs_model* m, evs_state* s, int layer, int B, int T
 
 int launch_attention(const evs_model* m, evs_state* s, int layer, int B, int T, int splits, int kv_blocks,
                      cudaStream_t st) {
-  EVS_CHECK_ARG(m->cfg.head_dim % 2 == 0 && m->cfg.head_dim <= 256 && 256 % m->cfg.head_dim == 0,
-                "head_dim must divide 256");
+  // P.V gives each thread two head columns and at most four of the 16 queries of a pass
+  EVS_CHECK_ARG(m->cfg.head_dim >= 8 && m->cfg.head_dim <= 128 && 256 % m->cfg.head_dim == 0,
+                "head_dim must be a power of two in [8, 128]");
   EVS_CHECK_RANGE(kv_blocks >= 1 && kv_blocks <= s->attn_blocks, "KV length beyond max_seqlen");
   if (m->cfg.dtype == EVS_DTYPE_BF16) return launch_attention_t<__nv_bfloat16>(m, s, layer, B, T, splits, kv_blocks, st);
   return launch_attention_t<float>(m, s, layer, B, T, splits, kv_blocks, st);

@@ -16,7 +16,11 @@
 
 namespace {
 
-constexpr int CH = 32;  // channels per CTA
+constexpr int CH = 32;          // output channels per CTA (96 interleaved in-projection channels)
+constexpr int C3 = 3 * CH;
+constexpr int TS = 32;          // chunk positions per pass
+constexpr int UW = 64;          // outer-FIR input window in shared memory (positions mod UW)
+constexpr int HY_THREADS = 128;
 
 template <typename TD>
 struct HyArgs {
@@ -42,146 +46,286 @@ struct HyArgs {
   int ld_y;
 };
 
-// data-dtype value of the in-projection output (channel c of a token row)
-template <typename TD>
-__device__ __forceinline__ float u_chunk(const HyArgs<TD>& a, int row, int c) {
-  float acc = 0.f;
-  for (int sp = 0; sp < a.splits; ++sp) acc += a.ws[(static_cast<size_t>(sp) * a.M + row) * (3 * a.d) + c];
-  return round_to<TD>(acc);
-}
-
-// outer-FIR input at absolute position P of row b (inside the chunk or in the ring)
-template <typename TD>
-__device__ __forceinline__ float u_at(const HyArgs<TD>& a, int b, int L0, int P, int c) {
-  if (P >= L0) return u_chunk(a, b * a.T + (P - L0), c);
-  return to_f32(a.outer_ring[(static_cast<size_t>(b) * a.cap_o + (P % a.cap_o)) * (3 * a.d) + c]);
-}
-
-// outer FIR (unflipped, K0 taps) for channel c at absolute position P
-template <typename TD>
-__device__ __forceinline__ float outer_fir(const HyArgs<TD>& a, int b, int L0, int P, int c, float u_now) {
-  const int K0 = a.K0;
-  const int cs = min(P, K0 - 1);
-  const int base = a.prefill ? K0 - 1 : cs;
-  const float* w = a.short_w + static_cast<size_t>(c) * K0;
-  float z = 0.f;
-  for (int age = cs; age >= 1; --age) z = fmaf(w[base - age], u_at(a, b, L0, P - age, c), z);
-  return fmaf(w[base], u_now, z);
-}
-
-// grid (d / 32, B); 128 threads; dynamic smem: hist[(K-1)+T][32] + x2[T][32] + taps[K][32]
-template <typename TD, bool FLIP>
-__global__ void __launch_bounds__(128) hyena_fir_kernel(HyArgs<TD> a) {
-  extern __shared__ float sm[];
-  const int K = a.K, T = a.T, H = K - 1;
-  float* hist = sm;                  // [(H + T)][CH]
-  float* x2s = hist + (H + T) * CH;  // [T][CH]
-  float* taps = x2s + T * CH;        // [K][CH]
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int h0 = blockIdx.x * CH, b = blockIdx.y;
-  const int h = h0 + lane;
-  const int L0 = a.len[b];
-
-  // history window of x1v (positions L0-H .. L0-1) and taps, transposed to [*][channel]
-  for (int i = threadIdx.x; i < H * CH; i += blockDim.x) {
-    const int r = i / CH, cc = i % CH;
-    const int P = L0 - H + r;
-    hist[r * CH + cc] =
-        P >= 0 ? to_f32(a.inner_ring[(static_cast<size_t>(b) * a.cap_i + (P % a.cap_i)) * a.d + h0 + cc]) : 0.f;
-  }
-  for (int i = threadIdx.x; i < K * CH; i += blockDim.x) {
-    const int cc = i / K, j = i % K;
-    taps[j * CH + cc] = a.inner_w[static_cast<size_t>(h0 + cc) * K + j];
-  }
-  // phase 1: outer FIR, de-interleave, x1v for every chunk position
-  for (int t = warp; t < T; t += 4) {
-    const int P = L0 + t, row = b * T + t;
-    float zq[3];
+// n element copies dst(i) <- src(i) with four loads in flight per thread before the stores
+template <typename LoadF, typename StoreF>
+__device__ __forceinline__ void batched_copy(int n, LoadF ld, StoreF stf) {
+  for (int i0 = threadIdx.x; i0 < n; i0 += 4 * blockDim.x) {
+    float v[4];
 #pragma unroll
-    for (int j = 0; j < 3; ++j) {
-      const int c = 3 * h + j;
-      const float un = u_chunk(a, row, c);
-      a.outer_ring[(static_cast<size_t>(b) * a.cap_o + (P % a.cap_o)) * (3 * a.d) + c] = from_f32<TD>(un);
-      zq[j] = round_to<TD>(outer_fir(a, b, L0, P, c, un));
+    for (int k = 0; k < 4; ++k) {
+      const int i = i0 + k * blockDim.x;
+      if (i < n) v[k] = ld(i);
     }
-    const float x1v = round_to<TD>(zq[1] * zq[2]);
-    hist[(H + t) * CH + lane] = x1v;
-    x2s[t * CH + lane] = zq[0];
-    a.inner_ring[(static_cast<size_t>(b) * a.cap_i + (P % a.cap_i)) * a.d + h] = from_f32<TD>(x1v);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int i = i0 + k * blockDim.x;
+      if (i < n) stf(i, v[k]);
+    }
+  }
+}
+
+// Stage the outer-FIR history (positions L0-K0+1 .. L0-1 of the outer ring) and the outer taps
+// of channels 3h0 .. 3h0+95 in shared memory.
+template <typename TD>
+__device__ void outer_stage(const HyArgs<TD>& a, int b, int L0, int h0, float* uw, float* wo) {
+  const size_t N3 = 3 * static_cast<size_t>(a.d);
+  const int c0 = 3 * h0, Hh = a.K0 - 1;
+  const TD* ring = a.outer_ring;
+  const int cap = a.cap_o;
+  batched_copy(
+      Hh * C3,
+      [&](int i) {
+        const int r = i / C3, cc = i - r * C3;
+        const int P = L0 - Hh + r;
+        return P >= 0 ? to_f32(ring[(static_cast<size_t>(b) * cap + (P % cap)) * N3 + c0 + cc]) : 0.f;
+      },
+      [&](int i, float v) {
+        const int r = i / C3, cc = i - r * C3;
+        const int P = L0 - Hh + r;
+        if (P >= 0) uw[(P & (UW - 1)) * C3 + cc] = v;
+      });
+  const float* sw = a.short_w + static_cast<size_t>(c0) * a.K0;
+  batched_copy(C3 * a.K0, [&](int i) { return __ldg(sw + i); }, [&](int i, float v) { wo[i] = v; });
+}
+
+// One pass over chunk positions t0 .. t0+ns-1 of row b: in-projection values u (sum of the
+// split partials in split order, rounded to the data dtype) into the outer ring and the window uw,
+// then the outer FIR outputs z (rounded) into zs[ns][96].  Starts and ends with a block barrier.
+template <typename TD>
+__device__ void outer_pass(const HyArgs<TD>& a, int b, int L0, int h0, int t0, int ns, float* uw, const float* wo,
+                           float* zs) {
+  const size_t N3 = 3 * static_cast<size_t>(a.d);
+  const size_t split_stride = static_cast<size_t>(a.M) * N3;
+  const int c0 = 3 * h0;
+  constexpr int Q = C3 / 4;  // float4s per position
+  const int n4 = ns * Q;
+  __syncthreads();  // the previous pass has finished reading uw / zs
+  for (int i0 = threadIdx.x; i0 < n4; i0 += 4 * blockDim.x) {
+    float4 acc[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int sp = 0; sp < a.splits; ++sp) {
+      float4 v[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int i = i0 + k * blockDim.x;
+        if (i < n4) {
+          const int t = i / Q, q4 = i - t * Q;
+          v[k] = __ldg(reinterpret_cast<const float4*>(a.ws + sp * split_stride +
+                                                       static_cast<size_t>(b * a.T + t0 + t) * N3 + c0) + q4);
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        acc[k].x += v[k].x;
+        acc[k].y += v[k].y;
+        acc[k].z += v[k].z;
+        acc[k].w += v[k].w;
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int i = i0 + k * blockDim.x;
+      if (i < n4) {
+        const int t = i / Q, q4 = i - t * Q;
+        const int P = L0 + t0 + t;
+        const float4 un = make_float4(round_to<TD>(acc[k].x), round_to<TD>(acc[k].y), round_to<TD>(acc[k].z),
+                                      round_to<TD>(acc[k].w));
+        *reinterpret_cast<float4*>(uw + (P & (UW - 1)) * C3 + 4 * q4) = un;
+        TD* dst = a.outer_ring + (static_cast<size_t>(b) * a.cap_o + (P % a.cap_o)) * N3 + c0 + 4 * q4;
+        dst[0] = from_f32<TD>(un.x);
+        dst[1] = from_f32<TD>(un.y);
+        dst[2] = from_f32<TD>(un.z);
+        dst[3] = from_f32<TD>(un.w);
+      }
+    }
   }
   __syncthreads();
-  // phase 2: inner FIR over [history | chunk]
-  const float Dh = FLIP ? a.D[h] : 0.f;
-  for (int t = warp; t < T; t += 4) {
-    const int P = L0 + t;
-    const int cs = min(P, H);
+  const int K0 = a.K0;
+  for (int i = threadIdx.x; i < ns * C3; i += blockDim.x) {
+    const int t = i / C3, cc = i - t * C3;
+    const int P = L0 + t0 + t;
+    const int cs = min(P, K0 - 1);
+    const int base = a.prefill ? K0 - 1 : cs;
+    const float* w = wo + cc * K0;
     float z = 0.f;
-    if (FLIP) {
-      for (int age = cs; age >= 0; --age) z = fmaf(taps[age * CH + lane], hist[(H + t - age) * CH + lane], z);
-      z = fmaf(Dh, hist[(H + t) * CH + lane], z);
-    } else {
-      const int base = a.prefill ? H : cs;
-      for (int age = cs; age >= 0; --age)
-        z = fmaf(taps[(base - age) * CH + lane], hist[(H + t - age) * CH + lane], z);
+    for (int age = cs; age >= 1; --age) z = fmaf(w[base - age], uw[((P - age) & (UW - 1)) * C3 + cc], z);
+    z = fmaf(w[base], uw[(P & (UW - 1)) * C3 + cc], z);
+    zs[t * C3 + cc] = round_to<TD>(z);
+  }
+  __syncthreads();
+}
+
+// tap row stride in shared memory: a multiple of 4 floats whose quarter is odd, so that eight
+// lanes reading 16 bytes from eight consecutive rows hit distinct banks
+__host__ __device__ constexpr int tap_stride(int K) {
+  const int k4 = (K + 3) / 4;
+  return 4 * ((k4 & 1) ? k4 : k4 + 1);
+}
+
+// grid (d / 32, B), 128 threads.  Shared memory: uw[UW][96] f32 | zs[TS][96] f32 | wo[96][K0] f32 |
+// taps[32][tap_stride(K)] f32 | hist[win][32] TD (x1v by position mod win) | x2s[TS][32] f32
+template <typename TD, bool FLIP>
+__global__ void __launch_bounds__(HY_THREADS) hyena_fir_kernel(HyArgs<TD> a, int win) {
+  extern __shared__ __align__(16) float sm[];
+  const int K = a.K, H = K - 1, KS = tap_stride(K), T = a.T;
+  float* uw = sm;
+  float* zs = uw + UW * C3;
+  float* wo = zs + TS * C3;
+  float* taps = wo + C3 * a.K0;
+  TD* hist = reinterpret_cast<TD*>(taps + CH * KS);
+  float* x2s = reinterpret_cast<float*>(hist + win * CH);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int h0 = blockIdx.x * CH, b = blockIdx.y;
+  const int L0 = a.len[b];
+  const int wm = win - 1;
+  // asynchronous copies first: inner-FIR history rows and (K % 4 == 0) the tap rows
+  constexpr int EPC = 16 / sizeof(TD);
+  constexpr int RC = CH / EPC;  // 16-byte chunks per history row
+  for (int i = threadIdx.x; i < H * RC; i += blockDim.x) {
+    const int r = i / RC, c = i - r * RC;
+    const int P = L0 - H + r;
+    if (P >= 0)
+      cp_async16(hist + (P & wm) * CH + c * EPC,
+                 a.inner_ring + (static_cast<size_t>(b) * a.cap_i + (P % a.cap_i)) * a.d + h0 + c * EPC);
+  }
+  const float* iw = a.inner_w + static_cast<size_t>(h0) * K;
+  if (K % 4 == 0) {
+    const int k4 = K / 4;
+    for (int i = threadIdx.x; i < CH * k4; i += blockDim.x) {
+      const int cc = i / k4, j = i - cc * k4;
+      cp_async16(taps + cc * KS + 4 * j, iw + cc * K + 4 * j);
     }
-    const float yv = round_to<TD>(x2s[t * CH + lane] * round_to<TD>(z));
-    a.y[static_cast<size_t>(b * T + t) * a.ld_y + h] = from_f32<TD>(yv);
+  }
+  cp_async_commit();
+  if (K % 4 != 0)
+    batched_copy(CH * K, [&](int i) { return __ldg(iw + i); },
+                 [&](int i, float v) { taps[(i / K) * KS + i % K] = v; });
+  outer_stage(a, b, L0, h0, uw, wo);
+  const float Dg = FLIP ? a.D[h0 + lane] : 0.f;
+  const float* tp = taps + lane * KS;
+  for (int t0 = 0; t0 < T; t0 += TS) {
+    const int ns = min(TS, T - t0);
+    outer_pass(a, b, L0, h0, t0, ns, uw, wo, zs);
+    if (t0 == 0) {
+      cp_async_wait<0>();
+      __syncthreads();
+    }
+    // de-interleave (channel 3h+j -> group j): x2 = z[3h], x1v = z[3h+1] * z[3h+2]
+    for (int i = threadIdx.x; i < ns * CH; i += blockDim.x) {
+      const int t = i / CH, cc = i - t * CH;
+      const int P = L0 + t0 + t;
+      const float* zr = zs + t * C3 + 3 * cc;
+      const float x1v = round_to<TD>(zr[1] * zr[2]);
+      hist[(P & wm) * CH + cc] = from_f32<TD>(x1v);
+      x2s[t * CH + cc] = zr[0];
+      a.inner_ring[(static_cast<size_t>(b) * a.cap_i + (P % a.cap_i)) * a.d + h0 + cc] = from_f32<TD>(x1v);
+    }
+    __syncthreads();
+    // inner FIR, lane = channel, one position per warp at a time, ages in descending order
+    for (int t = warp; t < ns; t += HY_THREADS / 32) {
+      const int P = L0 + t0 + t;
+      const int cs = min(P, H);
+      float z = 0.f;
+      if (FLIP) {
+        for (int a4 = cs >> 2; a4 >= 0; --a4) {
+          const float4 w4 = *reinterpret_cast<const float4*>(tp + 4 * a4);
+          const float wv[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+          for (int e = 3; e >= 0; --e) {
+            const int age = 4 * a4 + e;
+            if (age <= cs) z = fmaf(wv[e], to_f32(hist[((P - age) & wm) * CH + lane]), z);
+          }
+        }
+        z = fmaf(Dg, to_f32(hist[(P & wm) * CH + lane]), z);
+      } else {
+        const int base = a.prefill ? H : cs;
+        for (int age = cs; age >= 0; --age) z = fmaf(tp[base - age], to_f32(hist[((P - age) & wm) * CH + lane]), z);
+      }
+      const float yv = round_to<TD>(x2s[t * CH + lane] * round_to<TD>(z));
+      a.y[static_cast<size_t>(b * T + t0 + t) * a.ld_y + h0 + lane] = from_f32<TD>(yv);
+    }
+  }
+  if (T <= 0) cp_async_wait<0>();
+}
+
+template <int SPT>
+__device__ __forceinline__ void load_vec(const float* src, float* v) {
+  if constexpr (SPT % 4 == 0) {
+#pragma unroll
+    for (int j = 0; j < SPT; j += 4) {
+      const float4 f = *reinterpret_cast<const float4*>(src + j);
+      v[j] = f.x;
+      v[j + 1] = f.y;
+      v[j + 2] = f.z;
+      v[j + 3] = f.w;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < SPT; ++j) v[j] = src[j];
   }
 }
 
-// grid (d / 32, B); 128 threads = 32 channels x 4 pole groups (S / 4 poles each)
+template <int SPT>
+__device__ __forceinline__ void store_vec(float* dst, const float* v) {
+  if constexpr (SPT % 4 == 0) {
+#pragma unroll
+    for (int j = 0; j < SPT; j += 4) *reinterpret_cast<float4*>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+  } else {
+#pragma unroll
+    for (int j = 0; j < SPT; ++j) dst[j] = v[j];
+  }
+}
+
+// grid (d / 32, B), 128 threads = 32 channels x 4 pole groups (SPT = S / 4 poles each).
+// Shared memory (floats): uw[UW][96] | zs[TS][96] | wo[96][K0]
 template <typename TD, int SPT>
-__global__ void __launch_bounds__(128) hyena_iir_kernel(HyArgs<TD> a) {
-  const int q = threadIdx.x & 3;
-  const int h = blockIdx.x * CH + (threadIdx.x >> 2);
+__global__ void __launch_bounds__(HY_THREADS) hyena_iir_kernel(HyArgs<TD> a) {
+  extern __shared__ __align__(16) float sm[];
+  float* uw = sm;
+  float* zs = uw + UW * C3;
+  float* wo = zs + TS * C3;
+  const int q = threadIdx.x & 3, hl = threadIdx.x >> 2;
+  const int h0 = blockIdx.x * CH, h = h0 + hl;
   const int b = blockIdx.y;
   const int T = a.T, S = a.S, d = a.d;
   const int L0 = a.len[b];
+  outer_stage(a, b, L0, h0, uw, wo);
   float p[SPT], r[SPT], s[SPT];
-  const float* src = a.s_all + ((static_cast<size_t>(b) * a.slots + a.iir_cur[b]) * d + h) * S + q * SPT;
+  load_vec<SPT>(a.poles + static_cast<size_t>(h) * S + q * SPT, p);
+  load_vec<SPT>(a.residues + static_cast<size_t>(h) * S + q * SPT, r);
+  if (L0 > 0) {
+    load_vec<SPT>(a.s_all + ((static_cast<size_t>(b) * a.slots + a.iir_cur[b]) * d + h) * S + q * SPT, s);
+  } else {
 #pragma unroll
-  for (int j = 0; j < SPT; ++j) {
-    p[j] = a.poles[static_cast<size_t>(h) * S + q * SPT + j];
-    r[j] = a.residues[static_cast<size_t>(h) * S + q * SPT + j];
-    s[j] = L0 > 0 ? src[j] : 0.f;
+    for (int j = 0; j < SPT; ++j) s[j] = 0.f;
   }
-  const float Dh = a.D[h];
-  for (int t = 0; t < T; ++t) {
-    const int P = L0 + t, row = b * T + t;
-    float zq[3];
+  const float Dg = a.D[h];
+  __syncthreads();
+  for (int t0 = 0; t0 < T; t0 += TS) {
+    const int ns = min(TS, T - t0);
+    outer_pass(a, b, L0, h0, t0, ns, uw, wo, zs);
+    for (int t = 0; t < ns; ++t) {
+      const float* zr = zs + t * C3 + 3 * hl;
+      const float x1v = round_to<TD>(zr[1] * zr[2]);
+      float part = 0.f;
 #pragma unroll
-    for (int j = 0; j < 3; ++j) {
-      const int c = 3 * h + j;
-      const float un = u_chunk(a, row, c);
-      if (q == 0)
-        a.outer_ring[(static_cast<size_t>(b) * a.cap_o + (P % a.cap_o)) * (3 * d) + c] = from_f32<TD>(un);
-      zq[j] = round_to<TD>(outer_fir(a, b, L0, P, c, un));
+      for (int j = 0; j < SPT; ++j) {
+        s[j] = fmaf(p[j], s[j], x1v);
+        part = fmaf(r[j], s[j], part);
+      }
+      part += __shfl_xor_sync(0xffffffffu, part, 1);
+      part += __shfl_xor_sync(0xffffffffu, part, 2);
+      if (q == 0) {
+        const float yv = round_to<TD>(zr[0] * (part + Dg * x1v));
+        a.y[static_cast<size_t>(b * T + t0 + t) * a.ld_y + h] = from_f32<TD>(yv);
+      }
+      if (a.retain) store_vec<SPT>(a.s_all + ((static_cast<size_t>(b) * a.slots + t0 + t) * d + h) * S + q * SPT, s);
     }
-    const float x1v = round_to<TD>(zq[1] * zq[2]);
-    float part = 0.f;
-#pragma unroll
-    for (int j = 0; j < SPT; ++j) {
-      s[j] = fmaf(p[j], s[j], x1v);
-      part = fmaf(r[j], s[j], part);
-    }
-    part += __shfl_xor_sync(0xffffffffu, part, 1);
-    part += __shfl_xor_sync(0xffffffffu, part, 2);
-    if (q == 0) {
-      const float yv = round_to<TD>(zq[0] * (part + Dh * x1v));
-      a.y[static_cast<size_t>(row) * a.ld_y + h] = from_f32<TD>(yv);
-    }
-    if (a.retain) {
-      float* dst = a.s_all + ((static_cast<size_t>(b) * a.slots + t) * d + h) * S + q * SPT;
-#pragma unroll
-      for (int j = 0; j < SPT; ++j) dst[j] = s[j];
-    }
+    __syncthreads();
   }
-  if (!a.retain) {
-    // final state into slot 0 (this thread read its old slot before writing anything)
-    float* dst = a.s_all + ((static_cast<size_t>(b) * a.slots + 0) * d + h) * S + q * SPT;
-#pragma unroll
-    for (int j = 0; j < SPT; ++j) dst[j] = s[j];
-  }
+  // final state into slot 0 (this thread read its old slot before writing anything)
+  if (!a.retain) store_vec<SPT>(a.s_all + ((static_cast<size_t>(b) * a.slots + 0) * d + h) * S + q * SPT, s);
 }
 
 __global__ void rollback_kernel(int32_t* len, const int32_t* len0, int32_t* iir_cur, const int32_t* chunk,
@@ -258,27 +402,38 @@ int launch_hyena_t(const evs_model* m, evs_state* s, int layer, int B, int T, in
   a.retain = retain;
   a.y = static_cast<TD*>(s->act);
   a.ld_y = s->ld_act;
+  EVS_CHECK_ARG(a.K0 >= 1 && a.K0 - 1 + TS <= UW, "short filter too long for the outer-FIR window");
   dim3 grid(d / CH, B);
+  const size_t outer_floats = static_cast<size_t>(UW) * C3 + TS * C3 + C3 * a.K0;
   if (L.kind == EVS_LAYER_HCL) {
+    const size_t smem = sizeof(float) * outer_floats;
+    auto launch = [&](auto kern) -> int {
+      EVS_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+      kern<<<grid, HY_THREADS, smem, st>>>(a);
+      return EVS_OK;
+    };
     switch (a.S / 4) {
-      case 4: hyena_iir_kernel<TD, 4><<<grid, 128, 0, st>>>(a); break;
-      case 8: hyena_iir_kernel<TD, 8><<<grid, 128, 0, st>>>(a); break;
-      case 2: hyena_iir_kernel<TD, 2><<<grid, 128, 0, st>>>(a); break;
-      case 1: hyena_iir_kernel<TD, 1><<<grid, 128, 0, st>>>(a); break;
+      case 4: EVS_TRY(launch(hyena_iir_kernel<TD, 4>)); break;
+      case 8: EVS_TRY(launch(hyena_iir_kernel<TD, 8>)); break;
+      case 2: EVS_TRY(launch(hyena_iir_kernel<TD, 2>)); break;
+      case 1: EVS_TRY(launch(hyena_iir_kernel<TD, 1>)); break;
       default: EVS_CHECK_ARG(false, "state_size must be 4, 8, 16 or 32");
     }
   } else {
-    const size_t smem = sizeof(float) * (static_cast<size_t>(a.K - 1 + T) * CH + T * CH + a.K * CH);
-    EVS_CHECK_RANGE(smem <= 200 * 1024, "chunk too long for the FIR shared-memory window");
-    if (L.kind == EVS_LAYER_HCM) {
-      EVS_CUDA_TRY(cudaFuncSetAttribute(hyena_fir_kernel<TD, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        static_cast<int>(smem)));
-      hyena_fir_kernel<TD, true><<<grid, 128, smem, st>>>(a);
-    } else {
-      EVS_CUDA_TRY(cudaFuncSetAttribute(hyena_fir_kernel<TD, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        static_cast<int>(smem)));
-      hyena_fir_kernel<TD, false><<<grid, 128, smem, st>>>(a);
-    }
+    int win = 1;
+    while (win < a.K - 1 + TS) win <<= 1;
+    const size_t smem = sizeof(float) * (outer_floats + static_cast<size_t>(CH) * tap_stride(a.K) + TS * CH) +
+                        sizeof(TD) * static_cast<size_t>(win) * CH;
+    EVS_CHECK_RANGE(smem <= 220 * 1024, "FIR filter too long for the shared-memory window");
+    auto launch = [&](auto kern) -> int {
+      EVS_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+      kern<<<grid, HY_THREADS, smem, st>>>(a, win);
+      return EVS_OK;
+    };
+    if (L.kind == EVS_LAYER_HCM)
+      EVS_TRY(launch(hyena_fir_kernel<TD, true>));
+    else
+      EVS_TRY(launch(hyena_fir_kernel<TD, false>));
   }
   EVS_CUDA_TRY(cudaGetLastError());
   evs_count_launch(1);

@@ -1,7 +1,11 @@
 // Row-wise kernels between the GEMMs: embedding + pre-norm, split-K reduction + residual
 // add + RMSNorm (+ drafter-context capture), SwiGLU gating, logits, per-row bookkeeping.
 // Every reduction runs in a fixed order that does not depend on the number of token rows.
+#include <cooperative_groups.h>
+
 #include "internal.hpp"
+
+namespace cg = cooperative_groups;
 
 namespace {
 
@@ -52,53 +56,129 @@ __global__ void __launch_bounds__(ROW_THREADS) embed_norm_kernel(const int64_t* 
   }
 }
 
+// A cluster of NORM_CL CTAs per token row: CTA r owns columns [r*d/NORM_CL, (r+1)*d/NORM_CL) as
+// float4s held in registers.  Split partials are summed in split order, the residual updated (and
+// captured), and the row's sum of squares formed as: per-thread components in order -> warp
+// butterfly -> warps in order -> cluster ranks in order (read through distributed shared memory),
+// so every CTA of the cluster sees the same value and the result does not depend on M.
+constexpr int NORM_CL = 8;
+constexpr int NORM_THREADS = 128;
+constexpr int NORM_VPT = 4;  // float4s per thread: d <= NORM_CL * NORM_THREADS * 4 * NORM_VPT = 16384
+
 template <typename TD>
-__global__ void __launch_bounds__(ROW_THREADS) res_add_norm_kernel(
-    const float* __restrict__ ws, int splits, int M, float* __restrict__ resid, const float* __restrict__ scale,
-    TD* __restrict__ act, int ld_act, int d, float eps, float* __restrict__ ring, int ring_len,
-    const int32_t* __restrict__ len, int T) {
-  __shared__ float red[33];
-  const int row = blockIdx.x;
+__device__ inline void store4(TD* dst, float4 v) {
+  if constexpr (sizeof(TD) == 2) {
+    __nv_bfloat162 lo = __floats2bfloat162_rn(v.x, v.y), hi = __floats2bfloat162_rn(v.z, v.w);
+    uint2 u;
+    u.x = *reinterpret_cast<uint32_t*>(&lo);
+    u.y = *reinterpret_cast<uint32_t*>(&hi);
+    *reinterpret_cast<uint2*>(dst) = u;
+  } else {
+    *reinterpret_cast<float4*>(dst) = v;
+  }
+}
+
+template <typename TD>
+__global__ void __cluster_dims__(NORM_CL, 1, 1) __launch_bounds__(NORM_THREADS)
+    res_add_norm_kernel(const float* __restrict__ ws, int splits, int M, float* __restrict__ resid,
+                        const float* __restrict__ scale, TD* __restrict__ act, int ld_act, int d, float eps,
+                        float* __restrict__ ring, int ring_len, const int32_t* __restrict__ len, int T) {
+  __shared__ float red[NORM_THREADS / 32];
+  __shared__ float cta_ss;
+  cg::cluster_group cluster = cg::this_cluster();
+  const int rank = static_cast<int>(cluster.block_rank());
+  const int row = blockIdx.y;
   const int b = row / T, t = row % T;
   float* cap = nullptr;
   if (ring != nullptr && t >= T - ring_len) {
     const int P = len[b] + t;
     cap = ring + (static_cast<size_t>(b) * ring_len + P % ring_len) * d;
   }
+  const int cpc = d / NORM_CL, n4 = cpc / 4;
+  const int c_base = rank * cpc;
+  float4 r[NORM_VPT];
   float ss = 0.f;
-  for (int c = threadIdx.x; c < d; c += ROW_THREADS) {
-    float acc = 0.f;
-    for (int sp = 0; sp < splits; ++sp) acc += ws[(static_cast<size_t>(sp) * M + row) * d + c];
-    const float v = resid[static_cast<size_t>(row) * d + c] + acc;
-    resid[static_cast<size_t>(row) * d + c] = v;
-    if (cap != nullptr) cap[c] = v;
-    ss = fmaf(v, v, ss);
+#pragma unroll
+  for (int v = 0; v < NORM_VPT; ++v) {
+    const int c4 = threadIdx.x + v * NORM_THREADS;
+    if (c4 < n4) {
+      const int c = c_base + c4 * 4;
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int sp = 0; sp < splits; ++sp) {
+        const float4 w = *reinterpret_cast<const float4*>(ws + (static_cast<size_t>(sp) * M + row) * d + c);
+        acc.x += w.x;
+        acc.y += w.y;
+        acc.z += w.z;
+        acc.w += w.w;
+      }
+      float4* rp = reinterpret_cast<float4*>(resid + static_cast<size_t>(row) * d + c);
+      float4 x = *rp;
+      x.x += acc.x;
+      x.y += acc.y;
+      x.z += acc.z;
+      x.w += acc.w;
+      *rp = x;
+      if (cap != nullptr) *reinterpret_cast<float4*>(cap + c) = x;
+      ss = fmaf(x.x, x.x, ss);
+      ss = fmaf(x.y, x.y, ss);
+      ss = fmaf(x.z, x.z, ss);
+      ss = fmaf(x.w, x.w, ss);
+      r[v] = x;
+    }
   }
-  ss = block_sum_fixed(ss, red);
-  const float inv = 1.0f / sqrtf(ss / static_cast<float>(d) + eps);
-  for (int c = threadIdx.x; c < d; c += ROW_THREADS) {
-    const float v = resid[static_cast<size_t>(row) * d + c];
-    act[static_cast<size_t>(row) * ld_act + c] = from_f32<TD>(v * inv * scale[c]);
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float a = 0.f;
+    for (int w = 0; w < NORM_THREADS / 32; ++w) a += red[w];
+    cta_ss = a;
+  }
+  cluster.sync();
+  float tot = 0.f;
+  for (int q = 0; q < NORM_CL; ++q) tot += *cluster.map_shared_rank(&cta_ss, q);
+  cluster.sync();  // peers stay resident until every CTA has read their sums
+  const float inv = 1.0f / sqrtf(tot / static_cast<float>(d) + eps);
+#pragma unroll
+  for (int v = 0; v < NORM_VPT; ++v) {
+    const int c4 = threadIdx.x + v * NORM_THREADS;
+    if (c4 < n4) {
+      const int c = c_base + c4 * 4;
+      const float4 sc = *reinterpret_cast<const float4*>(scale + c);
+      const float4 x = r[v];
+      store4<TD>(act + static_cast<size_t>(row) * ld_act + c,
+                 make_float4(x.x * inv * sc.x, x.y * inv * sc.y, x.z * inv * sc.z, x.w * inv * sc.w));
+    }
   }
 }
 
-// ws holds the dual GEMM: virtual row (f / 64) * 128 + j * 64 + f % 64 is w_{j+1} feature f
+// ws holds the dual GEMM: virtual row (f / 64) * 128 + j * 64 + f % 64 is w_{j+1} feature f.
+// Each thread gates four consecutive features (one float4 of each half).
 template <typename TD>
 __global__ void __launch_bounds__(ROW_THREADS) swiglu_kernel(const float* __restrict__ ws, int splits, int M, int F,
                                                             TD* __restrict__ act, int ld_act) {
   const int row = blockIdx.y;
-  const int f = blockIdx.x * ROW_THREADS + threadIdx.x;
+  const int f = (blockIdx.x * ROW_THREADS + threadIdx.x) * 4;
   if (f >= F) return;
   const int N2 = 2 * F;
   const int v1 = (f / 64) * 128 + (f % 64), v2 = v1 + 64;
-  float g1 = 0.f, g2 = 0.f;
+  float4 g1 = make_float4(0.f, 0.f, 0.f, 0.f), g2 = g1;
   for (int sp = 0; sp < splits; ++sp) {
     const float* r = ws + (static_cast<size_t>(sp) * M + row) * N2;
-    g1 += r[v1];
-    g2 += r[v2];
+    const float4 a = *reinterpret_cast<const float4*>(r + v1);
+    const float4 c = *reinterpret_cast<const float4*>(r + v2);
+    g1.x += a.x;
+    g1.y += a.y;
+    g1.z += a.z;
+    g1.w += a.w;
+    g2.x += c.x;
+    g2.y += c.y;
+    g2.z += c.z;
+    g2.w += c.w;
   }
-  const float sig = 1.0f / (1.0f + expf(-g1));
-  act[static_cast<size_t>(row) * ld_act + f] = from_f32<TD>(g1 * sig * g2);
+  auto gate = [](float a, float c) { return a * (1.0f / (1.0f + expf(-a))) * c; };
+  store4<TD>(act + static_cast<size_t>(row) * ld_act + f,
+             make_float4(gate(g1.x, g2.x), gate(g1.y, g2.y), gate(g1.z, g2.z), gate(g1.w, g2.w)));
 }
 
 __global__ void logits_kernel(const float* __restrict__ ws, int splits, int M, int V, int T, int out_T, int t0,
@@ -154,12 +234,14 @@ int launch_res_add_norm(const evs_model* m, evs_state* s, int M, int splits, con
                         int T, cudaStream_t st) {
   const int d = m->cfg.d_model;
   float* ring = capture_slot >= 0 ? s->cap_ring[capture_slot] : nullptr;
+  EVS_CHECK_ARG(d % (NORM_CL * 4) == 0 && d <= NORM_CL * NORM_THREADS * 4 * NORM_VPT && s->ld_act % 4 == 0,
+                "d_model must be a multiple of 32 and at most 16384");
   if (m->cfg.dtype == EVS_DTYPE_BF16)
-    res_add_norm_kernel<__nv_bfloat16><<<M, ROW_THREADS, 0, st>>>(
+    res_add_norm_kernel<__nv_bfloat16><<<dim3(NORM_CL, M), NORM_THREADS, 0, st>>>(
         s->ws, splits, M, s->resid, scale, static_cast<__nv_bfloat16*>(s->act), s->ld_act, d, m->cfg.eps, ring,
         s->ring_len, s->d_len, T);
   else
-    res_add_norm_kernel<float><<<M, ROW_THREADS, 0, st>>>(s->ws, splits, M, s->resid, scale,
+    res_add_norm_kernel<float><<<dim3(NORM_CL, M), NORM_THREADS, 0, st>>>(s->ws, splits, M, s->resid, scale,
                                                           static_cast<float*>(s->act), s->ld_act, d, m->cfg.eps,
                                                           ring, s->ring_len, s->d_len, T);
   EVS_CUDA_TRY(cudaGetLastError());
@@ -169,7 +251,8 @@ int launch_res_add_norm(const evs_model* m, evs_state* s, int M, int splits, con
 
 int launch_swiglu(const evs_model* m, evs_state* s, int M, int splits, cudaStream_t st) {
   const int F = m->cfg.mlp_inner;
-  dim3 grid((F + ROW_THREADS - 1) / ROW_THREADS, M);
+  EVS_CHECK_ARG(F % 64 == 0, "mlp_inner must be a multiple of 64");
+  dim3 grid((F / 4 + ROW_THREADS - 1) / ROW_THREADS, M);
   if (m->cfg.dtype == EVS_DTYPE_BF16)
     swiglu_kernel<__nv_bfloat16><<<grid, ROW_THREADS, 0, st>>>(s->ws, splits, M, F,
                                                                 static_cast<__nv_bfloat16*>(s->act), s->ld_act);

@@ -18,8 +18,11 @@ import torch
 pytestmark = pytest.mark.gpu
 
 TOL_FP32_REL = 1e-5  # max-abs / max|logit|, fp32 device vs fp64 oracle
-TOL_BF16 = 2e-2      # max-abs logits, bf16 device vs bf16-emulating oracle, or 1.5x the measured
-                     # bf16 noise floor of the oracle itself when that is larger (large logit scales)
+TOL_BF16 = 2e-2      # max-abs logits, bf16 device vs bf16-emulating oracle, or FLOOR_X times the
+FLOOR_X = 2.0        # measured bf16 noise floor of the oracle itself when that is larger (large logit
+                     # scales): the floor is how far the same bf16-rounding oracle moves when its
+                     # fp64 arithmetic becomes fp32; any other fp32 summation order lands a similar
+                     # distance away, in max-abs and in RMS
 
 
 @pytest.fixture(scope="module")
@@ -274,9 +277,13 @@ def test_7b_width_bf16_block_vs_oracle(cuda):
     ref = refs[torch.float64]
     # bf16 noise floor: the same bf16-rounding oracle computed in fp32 instead of fp64
     floor = (refs[torch.float32] - ref).abs().max().item()
+    floor_rms = (refs[torch.float32] - ref).pow(2).mean().sqrt().item()
     err = (logits - ref).abs().max().item()
-    print(f"[bf16 parity] max|logit|={ref.abs().max().item():.2f} device err={err:.3e} bf16 floor={floor:.3e}")
-    assert err <= max(TOL_BF16, 1.5 * floor), f"7B-width bf16 logits vs oracle: {err:.3e} (floor {floor:.3e})"
+    err_rms = (logits - ref).pow(2).mean().sqrt().item()
+    print(f"[bf16 parity] max|logit|={ref.abs().max().item():.2f} device err={err:.3e} (rms {err_rms:.3e}) "
+          f"bf16 floor={floor:.3e} (rms {floor_rms:.3e})")
+    assert err <= max(TOL_BF16, FLOOR_X * floor), f"7B-width bf16 logits vs oracle: {err:.3e} (floor {floor:.3e})"
+    assert err_rms <= max(TOL_BF16 / 4, FLOOR_X * floor_rms), f"RMS {err_rms:.3e} (floor {floor_rms:.3e})"
     top2 = ref.topk(2, dim=-1).values
     clear = (top2[:, 0] - top2[:, 1]) > 2 * max(floor, TOL_BF16)
     assert torch.equal(logits.argmax(-1)[clear], ref.argmax(-1)[clear])
