@@ -4,9 +4,9 @@
 // flash_attn_with_kvcache through the model forward).
 //
 //   rope_append_kernel   qkv partials -> rotate-half RoPE (fp64 angle) -> q_rot, K/V cache append
-//   attn_block_kernel    one CTA per (256-key block, head, row) staged in shared memory:
+//   attn_block_kernel    one CTA per (64-key block, head, row) staged in shared memory:
 //                        partial (max, sum, acc) per query
-//   attn_combine_kernel  folds the partials of blocks 0..P/256 in block order
+//   attn_combine_kernel  folds the partials of blocks 0..P/64 in block order
 //
 // Blocks are aligned at absolute key positions and folded in a fixed order, so a query's result
 // does not depend on how many other queries share the call (native T=1 == verify T=γ+1).
@@ -56,7 +56,9 @@ __global__ void rope_append_kernel(const float* __restrict__ ws, int splits, int
 }
 
 constexpr int QT = 16;           // queries per pass over the staged keys
-constexpr int ATTN_THREADS = 256;
+constexpr int ATTN_THREADS = 128;
+constexpr int QK_Q = QT / (ATTN_THREADS / ATTN_BLOCK);  // queries per thread in the score pass
+constexpr int PV_QMAX = 8;       // queries per thread in P.V (head_dim <= 128)
 
 // shared memory of attn_block_kernel: K rows padded by 16 bytes (conflict-free row-per-thread
 // reads), V rows dense, fp32 queries, scores and per-query stats
@@ -66,12 +68,12 @@ __host__ __device__ constexpr size_t attn_smem_bytes(int Dh) {
          sizeof(float) * (static_cast<size_t>(QT) * Dh + static_cast<size_t>(QT) * ATTN_BLOCK + 2 * QT);
 }
 
-// grid (blocks, H, B), 256 threads.  One CTA stages one 256-key block of one head in shared
-// memory with 16-byte asynchronous copies (K and V in two groups, so scores start while V is in
-// flight), then for each group of <= 16 queries computes scores (one key per thread), the block's
-// softmax stats (one warp per query) and P.V (two head columns x up to four queries per thread).
-// Keys past a query's position score -inf and contribute exact zeros, so a query's partial does
-// not depend on how many queries share the call.
+// grid (blocks, H, B), ATTN_THREADS threads.  One CTA stages one ATTN_BLOCK-key block of one head
+// in shared memory with 16-byte asynchronous copies (K and V in two groups, so scores start while
+// V is in flight), then for each group of <= 16 queries computes scores (one key and QK_Q queries
+// per thread), the block's softmax stats (one warp per query) and P.V (two head columns and up to
+// PV_QMAX queries per thread).  Keys past a query's position score -inf and contribute exact
+// zeros, so a query's partial does not depend on how many queries share the call.
 template <typename TD>
 __global__ void __launch_bounds__(ATTN_THREADS) attn_block_kernel(const TD* __restrict__ qrot,
                                                                  const TD* __restrict__ kv,
@@ -107,6 +109,7 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_block_kernel(const TD* __re
   }
   cp_async_commit();
   bool k_ready = false, v_ready = false;
+  const int key = tid % ATTN_BLOCK, qh = tid / ATTN_BLOCK;
   const int npair = Dh / 2, groups = ATTN_THREADS / npair;
   const int pi = tid % npair, g = tid / npair;
   for (int tq0 = 0; tq0 < T; tq0 += QT) {
@@ -121,12 +124,13 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_block_kernel(const TD* __re
       k_ready = true;
     }
     __syncthreads();
-    {  // scores: key tid against every query of the group
-      float acc[QT];
+    {  // scores: one key against QK_Q queries of the group
+      float acc[QK_Q];
 #pragma unroll
-      for (int u = 0; u < QT; ++u) acc[u] = 0.f;
-      if (tid < nk) {
-        const TD* kr = Ks + tid * kpad;
+      for (int u = 0; u < QK_Q; ++u) acc[u] = 0.f;
+      const int u0 = qh * QK_Q;
+      if (key < nk && u0 < nq) {
+        const TD* kr = Ks + key * kpad;
         for (int c0 = 0; c0 < Dh; c0 += EPC) {
           float kf[EPC];
           if constexpr (sizeof(TD) == 2) {
@@ -146,20 +150,27 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_block_kernel(const TD* __re
             kf[3] = raw.w;
           }
 #pragma unroll
-          for (int u = 0; u < QT; ++u) {
-            if (u < nq) {
-              const float* qr = qs + u * Dh + c0;
+          for (int u = 0; u < QK_Q; ++u) {
+            if (u0 + u < nq) {
+              const float* qr = qs + (u0 + u) * Dh + c0;
 #pragma unroll
-              for (int e = 0; e < EPC; ++e) acc[u] = fmaf(qr[e], kf[e], acc[u]);
+              for (int e = 0; e < EPC; e += 4) {
+                const float4 q4 = *reinterpret_cast<const float4*>(qr + e);
+                acc[u] = fmaf(q4.x, kf[e], acc[u]);
+                acc[u] = fmaf(q4.y, kf[e + 1], acc[u]);
+                acc[u] = fmaf(q4.z, kf[e + 2], acc[u]);
+                acc[u] = fmaf(q4.w, kf[e + 3], acc[u]);
+              }
             }
           }
         }
       }
 #pragma unroll
-      for (int u = 0; u < QT; ++u) {
-        if (u < nq) {
-          const bool vis = tid < nk && k0 + tid <= L0 + tq0 + u;
-          S[u * ATTN_BLOCK + tid] = vis ? acc[u] * scale : -CUDART_INF_F;
+      for (int u = 0; u < QK_Q; ++u) {
+        const int t = u0 + u;
+        if (t < nq) {
+          const bool vis = key < nk && k0 + key <= L0 + tq0 + t;
+          S[t * ATTN_BLOCK + key] = vis ? acc[u] * scale : -CUDART_INF_F;
         }
       }
     }
@@ -188,10 +199,9 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_block_kernel(const TD* __re
     }
     __syncthreads();
     {  // P.V: head columns 2*pi, 2*pi+1 for queries g, g+groups, ...
-      constexpr int QPT = 4;
-      float a0[QPT], a1[QPT];
+      float a0[PV_QMAX], a1[PV_QMAX];
 #pragma unroll
-      for (int q = 0; q < QPT; ++q) a0[q] = a1[q] = 0.f;
+      for (int q = 0; q < PV_QMAX; ++q) a0[q] = a1[q] = 0.f;
       for (int i = 0; i < nk; ++i) {
         float v0, v1;
         if constexpr (sizeof(TD) == 2) {
@@ -204,7 +214,7 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_block_kernel(const TD* __re
           v1 = f2.y;
         }
 #pragma unroll
-        for (int q = 0; q < QPT; ++q) {
+        for (int q = 0; q < PV_QMAX; ++q) {
           const int t = g + q * groups;
           if (t < nq) {
             const float pv = S[t * ATTN_BLOCK + i];
@@ -214,7 +224,7 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_block_kernel(const TD* __re
         }
       }
 #pragma unroll
-      for (int q = 0; q < QPT; ++q) {
+      for (int q = 0; q < PV_QMAX; ++q) {
         const int t = g + q * groups;
         if (t < nq && L0 + tq0 + t >= k0) {
           float* pd = part + ((((static_cast<size_t>(b) * H + h) * nblk_cap + j) * tcap + tq0 + t) * (Dh + 2));
@@ -241,16 +251,29 @@ __global__ void attn_combine_kernel(const float* __restrict__ part, const int32_
   const int P = len[b] + t;
   const int jmax = P / ATTN_BLOCK;
   float m = -CUDART_INF_F, l = 0.f, acc = 0.f;
-  for (int j = 0; j <= jmax; ++j) {
-    const float* pj = part + ((((static_cast<size_t>(b) * H + h) * nblk_cap + j) * tcap + t) * (Dh + 2));
-    const float mj = pj[Dh];
-    if (mj == -CUDART_INF_F) continue;
-    const float mn = fmaxf(m, mj);
-    const float a = m == -CUDART_INF_F ? 0.f : expf(m - mn);
-    const float bj = expf(mj - mn);
-    l = l * a + pj[Dh + 1] * bj;
-    acc = acc * a + pj[dd] * bj;
-    m = mn;
+  const float* pb = part + ((static_cast<size_t>(b) * H + h) * nblk_cap * tcap + t) * (Dh + 2);
+  const size_t jstride = static_cast<size_t>(tcap) * (Dh + 2);
+  for (int j0 = 0; j0 <= jmax; j0 += 4) {  // four blocks' loads in flight, folded in block order
+    float mj[4], lj[4], aj[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      if (j0 + k <= jmax) {
+        const float* pj = pb + (j0 + k) * jstride;
+        mj[k] = pj[Dh];
+        lj[k] = pj[Dh + 1];
+        aj[k] = pj[dd];
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      if (j0 + k > jmax || mj[k] == -CUDART_INF_F) continue;
+      const float mn = fmaxf(m, mj[k]);
+      const float a = m == -CUDART_INF_F ? 0.f : expf(m - mn);
+      const float bj = expf(mj[k] - mn);
+      l = l * a + lj[k] * bj;
+      acc = acc * a + aj[k] * bj;
+      m = mn;
+    }
   }
   out[static_cast<size_t>(row) * ld_out + h * Dh + dd] = from_f32<TD>(acc / l);
 }
@@ -284,9 +307,9 @@ int launch_attention_t(const evs_model* m, evs_state* s, int layer, int B, int T
 
 int launch_attention(const evs_model* m, evs_state* s, int layer, int B, int T, int splits, int kv_blocks,
                      cudaStream_t st) {
-  // P.V gives each thread two head columns and at most four of the 16 queries of a pass
-  EVS_CHECK_ARG(m->cfg.head_dim >= 8 && m->cfg.head_dim <= 128 && 256 % m->cfg.head_dim == 0,
-                "head_dim must be a power of two in [8, 128]");
+  // P.V gives each thread two head columns and at most PV_QMAX of the QT queries of a pass
+  EVS_CHECK_ARG(m->cfg.head_dim >= 32 && m->cfg.head_dim <= 128 && 256 % m->cfg.head_dim == 0,
+                "head_dim must be 32, 64 or 128");
   EVS_CHECK_RANGE(kv_blocks >= 1 && kv_blocks <= s->attn_blocks, "KV length beyond max_seqlen");
   if (m->cfg.dtype == EVS_DTYPE_BF16) return launch_attention_t<__nv_bfloat16>(m, s, layer, B, T, splits, kv_blocks, st);
   return launch_attention_t<float>(m, s, layer, B, T, splits, kv_blocks, st);

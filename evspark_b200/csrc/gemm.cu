@@ -9,6 +9,8 @@
 // order, so every token row is computed by the same arithmetic whatever the batch size.
 //
 // fp32 path (CUDA cores): register-tiled 64x32 tiles through shared memory, fixed split of K.
+#include <algorithm>
+
 #include "internal.hpp"
 
 namespace {
@@ -126,78 +128,90 @@ __global__ void __launch_bounds__(192, 1)
   }
 }
 
-// fp32 / generic-dtype projection on CUDA cores, register tiled: CTA tile 64 output columns x
-// 32 token rows, K staged 32 at a time through shared memory; each thread owns 4 columns x 2 rows.
-// Partials go to ws[split][row][col]; the reduction order over k inside a split is fixed, and a
-// row's result never depends on the other rows of its tile.
-constexpr int SG_BN = 64, SG_BM = 32, SG_BK = 32;
+// fp32 projection for few token rows (the drafter, fp32 targets): CTA = 8 warps x 4 weight rows,
+// one split of K (SK_KC <= 1024 columns) and up to 16 token rows.  The token rows of the split are
+// staged in shared memory with 16-byte asynchronous copies; each warp streams its 4 weight rows
+// with coalesced float4 loads (lane l takes columns 4l..4l+3 of every 128) and keeps 4 x 16
+// accumulators.  Lane partials are summed in lane order through shared memory, so an output's
+// arithmetic does not depend on its token slot or on M (row invariance).  Partials go to
+// ws[split][row][col]; dual: virtual row v is w_{(v % 128) / 64} feature (v / 128) * 64 + v % 64.
+constexpr int SK_WARPS = 8, SK_R = 4, SK_ROWS = SK_WARPS * SK_R, SK_TOK = 16, SK_KC_MAX = 1024;
+constexpr size_t SK_SMEM = sizeof(float) * SK_TOK * SK_KC_MAX;  // also holds 8 x 64 x 32 lane partials
 
-template <typename TW, typename TX>
-__global__ void __launch_bounds__(256) gemm_f32_kernel(const TW* __restrict__ W, const TW* __restrict__ W2,
-                                                       const TX* __restrict__ X, int ldx, float* __restrict__ ws,
-                                                       int N, int K, int M, int splits, int dual) {
-  __shared__ __align__(16) float Ws[SG_BK][SG_BN + 4];
-  __shared__ __align__(16) float Xs[SG_BK][SG_BM + 4];
-  const int tid = threadIdx.x;
-  const int tx = tid % 16, ty = tid / 16;  // 16 x 16 threads: 4 columns x 2 rows each
-  const int n0 = blockIdx.x * SG_BN, m0 = blockIdx.y * SG_BM, split = blockIdx.z;
-  const int k0 = static_cast<int>(static_cast<long long>(K) * split / splits);
-  const int k1 = static_cast<int>(static_cast<long long>(K) * (split + 1) / splits);
-  float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-  // global -> smem assignments: W tile 64 x 32 (8 values / thread), X tile 32 x 32 (4 / thread)
-  const int wn = tid / 4, wk = (tid % 4) * 8;
-  const int xm = tid / 8, xk = (tid % 8) * 4;
-  const TW* wrow = nullptr;
-  {
-    const int n = n0 + wn;
-    if (n < N) {
-      if (dual) {
-        const int t = n / GEMM_BM, r = n % GEMM_BM;
-        wrow = r < GEMM_BM / 2 ? W + static_cast<size_t>(t * (GEMM_BM / 2) + r) * K
-                               : W2 + static_cast<size_t>(t * (GEMM_BM / 2) + r - GEMM_BM / 2) * K;
-      } else {
-        wrow = W + static_cast<size_t>(n) * K;
+__global__ void __launch_bounds__(SK_WARPS * 32) gemm_skinny_f32_kernel(const float* __restrict__ W,
+                                                                        const float* __restrict__ W2,
+                                                                        const float* __restrict__ X, int ldx,
+                                                                        float* __restrict__ ws, int N, int K, int M,
+                                                                        int kc, int dual) {
+  extern __shared__ __align__(16) float sk_sm[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * SK_ROWS, sp = blockIdx.y, m0 = blockIdx.z * SK_TOK;
+  const int mt = min(SK_TOK, M - m0);
+  const int kb = sp * kc, ke = min(K, kb + kc);
+  const int kw = ke - kb;  // multiple of 4
+  // stage X[m0 .. m0+mt)[kb .. ke) as xs[m][k - kb] (row stride kc)
+  const int c4 = kw / 4;
+  for (int i = threadIdx.x; i < mt * c4; i += blockDim.x) {
+    const int m = i / c4, c = i - m * c4;
+    cp_async16(sk_sm + m * kc + 4 * c, X + static_cast<size_t>(m0 + m) * ldx + kb + 4 * c);
+  }
+  cp_async_commit();
+  const float* wr[SK_R];
+#pragma unroll
+  for (int i = 0; i < SK_R; ++i) {
+    const int v = n0 + warp * SK_R + i;
+    const int vr = v < N ? v : N - 1;
+    if (dual) {
+      const int f = (vr / 128) * 64 + (vr % 64);
+      wr[i] = ((vr % 128) < 64 ? W : W2) + static_cast<size_t>(f) * K;
+    } else {
+      wr[i] = W + static_cast<size_t>(vr) * K;
+    }
+  }
+  float acc[SK_R][SK_TOK];
+#pragma unroll
+  for (int i = 0; i < SK_R; ++i)
+#pragma unroll
+    for (int m = 0; m < SK_TOK; ++m) acc[i][m] = 0.f;
+  cp_async_wait<0>();
+  __syncthreads();
+#pragma unroll 2
+  for (int k = 4 * lane; k < kw; k += 128) {
+    float4 w4[SK_R];
+#pragma unroll
+    for (int i = 0; i < SK_R; ++i) w4[i] = __ldg(reinterpret_cast<const float4*>(wr[i] + kb + k));
+#pragma unroll
+    for (int m = 0; m < SK_TOK; ++m) {
+      if (m < mt) {
+        const float4 x4 = *reinterpret_cast<const float4*>(sk_sm + m * kc + k);
+#pragma unroll
+        for (int i = 0; i < SK_R; ++i) {
+          acc[i][m] = fmaf(w4[i].x, x4.x, acc[i][m]);
+          acc[i][m] = fmaf(w4[i].y, x4.y, acc[i][m]);
+          acc[i][m] = fmaf(w4[i].z, x4.z, acc[i][m]);
+          acc[i][m] = fmaf(w4[i].w, x4.w, acc[i][m]);
+        }
       }
     }
   }
-  const TX* xrow = (m0 + xm < M) ? X + static_cast<size_t>(m0 + xm) * ldx : nullptr;
-  for (int kb = k0; kb < k1; kb += SG_BK) {
+  __syncthreads();  // xs no longer needed: reuse it for the lane partials
+  float* red = sk_sm + warp * (SK_R * SK_TOK * 32);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const int k = kb + wk + j;
-      Ws[wk + j][wn] = (wrow != nullptr && k < k1) ? to_f32(wrow[k]) : 0.f;
-    }
+  for (int i = 0; i < SK_R; ++i)
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int k = kb + xk + j;
-      Xs[xk + j][xm] = (xrow != nullptr && k < k1) ? to_f32(xrow[k]) : 0.f;
+    for (int m = 0; m < SK_TOK; ++m) {
+      const int v = i * SK_TOK + m;
+      red[v * 32 + (lane ^ (v & 31))] = acc[i][m];
     }
-    __syncthreads();
-#pragma unroll 8
-    for (int k = 0; k < SG_BK; ++k) {
-      const float4 w = *reinterpret_cast<const float4*>(&Ws[k][tx * 4]);
-      const float2 x = *reinterpret_cast<const float2*>(&Xs[k][ty * 2]);
-      acc[0][0] = fmaf(x.x, w.x, acc[0][0]);
-      acc[0][1] = fmaf(x.x, w.y, acc[0][1]);
-      acc[0][2] = fmaf(x.x, w.z, acc[0][2]);
-      acc[0][3] = fmaf(x.x, w.w, acc[0][3]);
-      acc[1][0] = fmaf(x.y, w.x, acc[1][0]);
-      acc[1][1] = fmaf(x.y, w.y, acc[1][1]);
-      acc[1][2] = fmaf(x.y, w.z, acc[1][2]);
-      acc[1][3] = fmaf(x.y, w.w, acc[1][3]);
-    }
-    __syncthreads();
-  }
+  __syncwarp();
 #pragma unroll
-  for (int i = 0; i < 2; ++i) {
-    const int m = m0 + ty * 2 + i;
-    if (m >= M) continue;
-    float* dst = ws + (static_cast<size_t>(split) * M + m) * N;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int n = n0 + tx * 4 + j;
-      if (n < N) dst[n] = acc[i][j];
-    }
+  for (int h = 0; h < 2; ++h) {
+    const int v = lane + 32 * h;
+    const int i = v / SK_TOK, m = v % SK_TOK;
+    float sum = 0.f;
+    for (int j = 0; j < 32; ++j) sum += red[v * 32 + (j ^ (v & 31))];
+    const int n = n0 + warp * SK_R + i;
+    if (m < mt && n < N) ws[(static_cast<size_t>(sp) * M + m0 + m) * N + n] = sum;
   }
 }
 
@@ -280,11 +294,15 @@ GemmPlan gemm_plan(const evs_model* m, int N, int K, int M, int dual) {
   return p;
 }
 
-// CUDA-core projection: split K (from N and K only) until >= 148 CTAs, each split >= 64 of K
+// fp32 projection plan, from N and K only: K chunks of at most 1024 columns (multiples of 128),
+// shrunk until one token group gives >= 2 CTAs per SM
 GemmPlan gemm_plan_f32(int N, int K, int M, int dual) {
   GemmPlan p{N, K, M, 1, dual};
-  const int tiles = (N + SG_BN - 1) / SG_BN;
-  while (tiles * p.splits < 148 && K / (p.splits + 1) >= 64) ++p.splits;
+  const int tiles = (N + SK_ROWS - 1) / SK_ROWS;
+  int kc = std::min(SK_KC_MAX, (K + 127) / 128 * 128);
+  while (kc > 128 && tiles * ((K + kc - 1) / kc) < 296) kc -= 128;
+  p.kchunk = kc;
+  p.splits = (K + kc - 1) / kc;
   return p;
 }
 
@@ -299,16 +317,24 @@ int launch_gemm_tc(const CUtensorMap* tmA, const CUtensorMap* tmA2, const CUtens
 int launch_gemm_simt(const void* W, const void* W2, const void* X, int ldx, int dtype, const GemmPlan& p, float* ws,
                      cudaStream_t st) {
   if (p.M <= 0) return EVS_OK;
-  dim3 grid((p.N + SG_BN - 1) / SG_BN, (p.M + SG_BM - 1) / SG_BM, p.splits);
-  if (dtype == EVS_DTYPE_BF16) {
-    gemm_f32_kernel<__nv_bfloat16, __nv_bfloat16><<<grid, 256, 0, st>>>(
-        static_cast<const __nv_bfloat16*>(W), static_cast<const __nv_bfloat16*>(W2),
-        static_cast<const __nv_bfloat16*>(X), ldx, ws, p.N, p.K, p.M, p.splits, p.dual);
-  } else {
-    gemm_f32_kernel<float, float><<<grid, 256, 0, st>>>(static_cast<const float*>(W), static_cast<const float*>(W2),
-                                                        static_cast<const float*>(X), ldx, ws, p.N, p.K, p.M,
-                                                        p.splits, p.dual);
+  EVS_CHECK_ARG(dtype == EVS_DTYPE_FP32, "CUDA-core projection is fp32 only");
+  EVS_CHECK_ARG(p.K % 4 == 0 && ldx % 4 == 0 && reinterpret_cast<uintptr_t>(X) % 16 == 0 &&
+                    reinterpret_cast<uintptr_t>(W) % 16 == 0,
+                "fp32 projection needs K and the row stride multiples of 4 and 16-byte aligned operands");
+  EVS_CHECK_ARG(p.kchunk > 0 && p.kchunk % 128 == 0 && p.kchunk <= SK_KC_MAX && p.splits * p.kchunk >= p.K,
+                "bad fp32 projection plan");
+  static bool attr_set = false;
+  if (!attr_set) {
+    EVS_CUDA_TRY(cudaFuncSetAttribute(gemm_skinny_f32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      static_cast<int>(SK_SMEM)));
+    attr_set = true;
   }
+  const size_t smem = std::max(sizeof(float) * SK_TOK * p.kchunk, sizeof(float) * SK_WARPS * SK_R * SK_TOK * 32);
+  dim3 grid((p.N + SK_ROWS - 1) / SK_ROWS, p.splits, (p.M + SK_TOK - 1) / SK_TOK);
+  gemm_skinny_f32_kernel<<<grid, SK_WARPS * 32, smem, st>>>(static_cast<const float*>(W),
+                                                            static_cast<const float*>(W2 ? W2 : W),
+                                                            static_cast<const float*>(X), ldx, ws, p.N, p.K, p.M,
+                                                            p.kchunk, p.dual);
   EVS_CUDA_TRY(cudaGetLastError());
   evs_count_launch(1);
   return EVS_OK;

@@ -9,7 +9,7 @@
 constexpr int GEMM_BM = 128;
 constexpr int GEMM_BK = 64;
 constexpr int TOK_TILE = 16;  // token rows per decode tile (MMA N)
-constexpr int ATTN_BLOCK = 256;  // keys per attention partial (aligned at absolute positions)
+constexpr int ATTN_BLOCK = 64;  // keys per attention partial (aligned at absolute positions)
 
 // HBM layout of the per-sequence state ------------------------------------
 //   outer FIR history ring   [B][cap_outer][3d]   data dtype  (positions mod cap_outer)
@@ -108,6 +108,7 @@ struct evs_state {
 // GEMM partial sums ws[split][tok][n] over the weight rows; dual: w1/w2 interleaved per 64 rows
 struct GemmPlan {
   int N, K, M, splits, dual;
+  int kchunk = 0;  // fp32 path: K columns per split (multiple of 128)
 };
 GemmPlan gemm_plan(const evs_model* m, int N, int K, int M, int dual);
 GemmPlan gemm_plan_f32(int N, int K, int M, int dual);
