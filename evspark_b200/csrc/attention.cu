@@ -20,6 +20,8 @@ template <typename TD>
 __global__ void rope_append_kernel(const float* __restrict__ ws, int splits, int M, int T, int d, int H, int Dh,
                                    double log_base, const int32_t* __restrict__ len, int Lmax, TD* __restrict__ qrot,
                                    TD* __restrict__ kv, EvsDevErr* err) {
+  pdl_trigger();
+  pdl_wait();
   const int row = blockIdx.x, h = blockIdx.y, j = threadIdx.x;
   const int half = Dh / 2;
   if (j >= half) return;
@@ -80,6 +82,8 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_block_kernel(const TD* __re
                                                                  const int32_t* __restrict__ len, int T, int d,
                                                                  int H, int Dh, int Lmax, int nblk_cap, int tcap,
                                                                  float scale, float* __restrict__ part) {
+  pdl_trigger();
+  pdl_wait();
   extern __shared__ __align__(16) unsigned char attn_sm[];
   const int j = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int L0 = len[b];
@@ -245,6 +249,8 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_block_kernel(const TD* __re
 template <typename TD>
 __global__ void attn_combine_kernel(const float* __restrict__ part, const int32_t* __restrict__ len, int T, int d,
                                     int H, int Dh, int nblk_cap, int tcap, TD* __restrict__ out, int ld_out) {
+  pdl_trigger();
+  pdl_wait();
   const int row = blockIdx.x, h = blockIdx.y, dd = threadIdx.x;
   if (dd >= Dh) return;
   const int b = row / T, t = row % T;
@@ -285,20 +291,21 @@ int launch_attention_t(const evs_model* m, evs_state* s, int layer, int B, int T
   const int M = B * T;
   TD* kv = static_cast<TD*>(s->kv[layer]);
   TD* qrot = static_cast<TD*>(s->qrot);
-  rope_append_kernel<TD><<<dim3(M, H), Dh / 2, 0, st>>>(s->ws, splits, M, T, d, H, Dh, log(m->cfg.rope_base),
-                                                        s->d_len, s->max_seqlen, qrot, kv, s->d_err);
-  EVS_CUDA_TRY(cudaGetLastError());
+  const bool pdl = s->use_pdl();
+  EVS_CUDA_TRY(evs_launch(rope_append_kernel<TD>, dim3(M, H), dim3(Dh / 2), 0, st, pdl,
+                          static_cast<const float*>(s->ws), splits, M, T, d, H, Dh, log(m->cfg.rope_base),
+                          static_cast<const int32_t*>(s->d_len), s->max_seqlen, qrot, kv, s->d_err));
   const size_t smem = attn_smem_bytes<TD>(Dh);
   EVS_CHECK_RANGE(smem <= 227 * 1024, "head_dim too large for the staged attention block");
   EVS_CUDA_TRY(cudaFuncSetAttribute(attn_block_kernel<TD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     static_cast<int>(smem)));
-  attn_block_kernel<TD><<<dim3(kv_blocks, H, B), ATTN_THREADS, smem, st>>>(
-      qrot, kv, s->d_len, T, d, H, Dh, s->max_seqlen, s->attn_blocks, s->max_chunk, 1.0f / sqrtf(static_cast<float>(Dh)),
-      s->attn_part);
-  EVS_CUDA_TRY(cudaGetLastError());
-  attn_combine_kernel<TD><<<dim3(M, H), Dh, 0, st>>>(s->attn_part, s->d_len, T, d, H, Dh, s->attn_blocks,
-                                                     s->max_chunk, static_cast<TD*>(s->act), s->ld_act);
-  EVS_CUDA_TRY(cudaGetLastError());
+  EVS_CUDA_TRY(evs_launch(attn_block_kernel<TD>, dim3(kv_blocks, H, B), dim3(ATTN_THREADS), smem, st, pdl,
+                          static_cast<const TD*>(qrot), static_cast<const TD*>(kv),
+                          static_cast<const int32_t*>(s->d_len), T, d, H, Dh, s->max_seqlen, s->attn_blocks,
+                          s->max_chunk, 1.0f / sqrtf(static_cast<float>(Dh)), s->attn_part));
+  EVS_CUDA_TRY(evs_launch(attn_combine_kernel<TD>, dim3(M, H), dim3(Dh), 0, st, pdl,
+                          static_cast<const float*>(s->attn_part), static_cast<const int32_t*>(s->d_len), T, d, H,
+                          Dh, s->attn_blocks, s->max_chunk, static_cast<TD*>(s->act), s->ld_act));
   evs_count_launch(3);
   return EVS_OK;
 }

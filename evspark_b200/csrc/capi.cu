@@ -1,6 +1,7 @@
 // C ABI entry points: model / state handles and the layer-loop orchestration of one forward.
 #include <algorithm>
 #include <atomic>
+#include <cstdlib>
 #include <cstring>
 #include <string>
 
@@ -70,9 +71,9 @@ int gemm(const evs_model* m, evs_state* s, const CUtensorMap* tA, const CUtensor
   *splits = p.splits;
   if (m->cfg.dtype == EVS_DTYPE_BF16) {
     const CUtensorMap* tB = K == m->cfg.d_model ? &s->tm_act_d : &s->tm_act_f;
-    return launch_gemm_tc(tA, tA2, tB, p, s->ws, s->d_err, st);
+    return launch_gemm_tc(tA, tA2, tB, p, s->ws, s->d_err, st, s->use_pdl());
   }
-  return launch_gemm_simt(W, W2, s->act, s->ld_act, m->cfg.dtype, p, s->ws, st);
+  return launch_gemm_simt(W, W2, s->act, s->ld_act, m->cfg.dtype, p, s->ws, st, s->use_pdl());
 }
 
 cudaEvent_t take_event(evs_state* s) {
@@ -320,6 +321,8 @@ int evs_state_create(const evs_model* m, int max_batch, int max_seqlen, int max_
   s->max_batch = max_batch;
   s->max_seqlen = max_seqlen;
   s->max_chunk = max_chunk;
+  // EVS_NO_PDL=1 serialises the kernels of a forward (programmatic dependent launch off)
+  s->pdl = std::getenv("EVS_NO_PDL") == nullptr;
   s->cap_outer = next_pow2(c.short_filter_length - 1 + max_chunk);
   s->cap_hcs = next_pow2(c.hcs_filter_length - 1 + max_chunk);
   s->cap_hcm = next_pow2(c.hcm_filter_length - 1 + max_chunk);

@@ -1,6 +1,8 @@
 // Shared device/host helpers for the sm_100a kernels of libevspark_sm100.
 #pragma once
 
+#include <utility>
+
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -130,6 +132,13 @@ __device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint64_t* ba
       : "memory");
 }
 
+// Programmatic dependent launch.  A kernel launched with programmatic stream serialization may
+// start before its predecessor in the stream has finished: it must call pdl_wait() before it
+// reads anything an earlier kernel wrote or writes anything an earlier kernel reads.
+// pdl_trigger() lets the next such kernel start launching.  Both are no-ops for ordinary launches.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // 16-byte global -> shared copy that bypasses registers (both addresses 16-byte aligned)
 __device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gmem_src) : "memory");
@@ -241,6 +250,23 @@ void evs_count_launch(int n);
       return EVS_ERANGE;                     \
     }                                        \
   } while (0)
+
+// launch a kernel, optionally with programmatic stream serialization (the kernel calls pdl_wait)
+template <typename... KArgs, typename... Args>
+cudaError_t evs_launch(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, bool pdl,
+                       Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
 
 #define EVS_TRY(expr)         \
   do {                        \

@@ -20,7 +20,7 @@ constexpr int A_STAGE_BYTES = GEMM_BM * GEMM_BK * 2;  // 16 KiB
 template <int NT>
 struct TcCfg {
   static constexpr int B_STAGE_BYTES = NT * GEMM_BK * 2;
-  static constexpr int STAGES = NT <= 16 ? 5 : (NT <= 64 ? 4 : 3);
+  static constexpr int STAGES = NT <= 16 ? 6 : (NT <= 64 ? 4 : 3);  // NT=16: 2 CTAs per SM
   static constexpr int STAGE_BYTES = A_STAGE_BYTES + B_STAGE_BYTES;
   static constexpr int TMEM_COLS = NT < 32 ? 32 : NT;
   static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
@@ -47,6 +47,7 @@ __global__ void __launch_bounds__(192, 1)
   const int kb_begin = static_cast<int>(static_cast<long long>(kblocks) * split / splits);
   const int kb_end = static_cast<int>(static_cast<long long>(kblocks) * (split + 1) / splits);
   const int nkb = kb_end - kb_begin;
+  pdl_trigger();
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
@@ -69,11 +70,7 @@ __global__ void __launch_bounds__(192, 1)
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
     if (dual) prefetch_tmap(&tmA2);
-    for (int i = 0; i < nkb; ++i) {
-      const int s = i % C::STAGES;
-      const uint32_t ph = (i / C::STAGES) & 1;
-      if (i >= C::STAGES && !mbar_wait_bounded(&empty[s], ph ^ 1, err, EVS_K_GEMM_TC, 1)) break;
-      mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
+    auto load_a = [&](int i, int s) {
       const int kx = (kb_begin + i) * GEMM_BK;
       uint8_t* a_dst = sA + s * A_STAGE_BYTES;
       if (dual) {
@@ -82,7 +79,26 @@ __global__ void __launch_bounds__(192, 1)
       } else {
         tma_load_2d(&tmA, &full[s], a_dst, kx, tile * GEMM_BM);
       }
-      tma_load_2d(&tmB, &full[s], sB + s * C::B_STAGE_BYTES, kx, ttile * NT);
+    };
+    auto load_b = [&](int i, int s) {
+      tma_load_2d(&tmB, &full[s], sB + s * C::B_STAGE_BYTES, (kb_begin + i) * GEMM_BK, ttile * NT);
+    };
+    // the weights do not depend on earlier kernels: fill every stage with them before waiting
+    // for the kernel that produces the activations (programmatic dependent launch)
+    const int pre = nkb < C::STAGES ? nkb : C::STAGES;
+    for (int i = 0; i < pre; ++i) {
+      mbar_arrive_expect_tx(&full[i], C::STAGE_BYTES);
+      load_a(i, i);
+    }
+    pdl_wait();
+    for (int i = 0; i < pre; ++i) load_b(i, i);
+    for (int i = pre; i < nkb; ++i) {
+      const int s = i % C::STAGES;
+      const uint32_t ph = (i / C::STAGES) & 1;
+      if (!mbar_wait_bounded(&empty[s], ph ^ 1, err, EVS_K_GEMM_TC, 1)) break;
+      mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
+      load_a(i, s);
+      load_b(i, s);
     }
   } else if (warp == 1 && lane == 0) {
     constexpr uint32_t idesc = umma_idesc_bf16(GEMM_BM, NT);
@@ -105,6 +121,7 @@ __global__ void __launch_bounds__(192, 1)
     const int q = warp & 3;  // TMEM lane quadrant this warp may access
     const bool ok = mbar_wait_bounded(accum, 0, err, EVS_K_GEMM_TC, 3);
     tc_fence_after();
+    pdl_wait();  // (already satisfied: the MMAs consumed activations loaded after the wait)
     if (ok) {
       const int row = tile * GEMM_BM + q * 32 + lane;
 #pragma unroll
@@ -144,6 +161,8 @@ __global__ void __launch_bounds__(SK_WARPS * 32) gemm_skinny_f32_kernel(const fl
                                                                         float* __restrict__ ws, int N, int K, int M,
                                                                         int kc, int dual) {
   extern __shared__ __align__(16) float sk_sm[];
+  pdl_trigger();
+  pdl_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n0 = blockIdx.x * SK_ROWS, sp = blockIdx.y, m0 = blockIdx.z * SK_TOK;
   const int mt = min(SK_TOK, M - m0);
@@ -242,7 +261,7 @@ PFN_encodeTiled get_encode() {
 
 template <int NT>
 int launch_tc(const CUtensorMap* tmA, const CUtensorMap* tmA2, const CUtensorMap* tmB, const GemmPlan& p, float* ws,
-              EvsDevErr* err, cudaStream_t st) {
+              EvsDevErr* err, cudaStream_t st, bool pdl) {
   using C = TcCfg<NT>;
   static bool attr_set = false;
   if (!attr_set) {
@@ -250,9 +269,8 @@ int launch_tc(const CUtensorMap* tmA, const CUtensorMap* tmA2, const CUtensorMap
     attr_set = true;
   }
   dim3 grid(p.N / GEMM_BM, p.splits, (p.M + NT - 1) / NT);
-  gemm_tc_kernel<NT><<<grid, 192, C::SMEM, st>>>(*tmA, tmA2 ? *tmA2 : *tmA, *tmB, ws, p.N, p.K, p.M, p.splits,
-                                                  p.dual, err);
-  EVS_CUDA_TRY(cudaGetLastError());
+  EVS_CUDA_TRY(evs_launch(gemm_tc_kernel<NT>, grid, dim3(192), C::SMEM, st, pdl, *tmA, tmA2 ? *tmA2 : *tmA, *tmB,
+                          ws, p.N, p.K, p.M, p.splits, p.dual, err));
   evs_count_launch(1);
   return EVS_OK;
 }
@@ -307,15 +325,15 @@ GemmPlan gemm_plan_f32(int N, int K, int M, int dual) {
 }
 
 int launch_gemm_tc(const CUtensorMap* tmA, const CUtensorMap* tmA2, const CUtensorMap* tmB, const GemmPlan& p,
-                   float* ws, EvsDevErr* err, cudaStream_t st) {
+                   float* ws, EvsDevErr* err, cudaStream_t st, bool pdl) {
   EVS_CHECK_ARG(p.N % GEMM_BM == 0 && p.K % GEMM_BK == 0, "tcgen05 GEMM needs N % 128 == 0 and K % 64 == 0");
   EVS_CHECK_ARG(p.splits >= 1 && p.splits <= p.K / GEMM_BK, "bad split count");
   if (p.M <= 0) return EVS_OK;
-  return launch_tc<TOK_TILE>(tmA, tmA2, tmB, p, ws, err, st);
+  return launch_tc<TOK_TILE>(tmA, tmA2, tmB, p, ws, err, st, pdl);
 }
 
 int launch_gemm_simt(const void* W, const void* W2, const void* X, int ldx, int dtype, const GemmPlan& p, float* ws,
-                     cudaStream_t st) {
+                     cudaStream_t st, bool pdl) {
   if (p.M <= 0) return EVS_OK;
   EVS_CHECK_ARG(dtype == EVS_DTYPE_FP32, "CUDA-core projection is fp32 only");
   EVS_CHECK_ARG(p.K % 4 == 0 && ldx % 4 == 0 && reinterpret_cast<uintptr_t>(X) % 16 == 0 &&
@@ -331,11 +349,9 @@ int launch_gemm_simt(const void* W, const void* W2, const void* X, int ldx, int 
   }
   const size_t smem = std::max(sizeof(float) * SK_TOK * p.kchunk, sizeof(float) * SK_WARPS * SK_R * SK_TOK * 32);
   dim3 grid((p.N + SK_ROWS - 1) / SK_ROWS, p.splits, (p.M + SK_TOK - 1) / SK_TOK);
-  gemm_skinny_f32_kernel<<<grid, SK_WARPS * 32, smem, st>>>(static_cast<const float*>(W),
-                                                            static_cast<const float*>(W2 ? W2 : W),
-                                                            static_cast<const float*>(X), ldx, ws, p.N, p.K, p.M,
-                                                            p.kchunk, p.dual);
-  EVS_CUDA_TRY(cudaGetLastError());
+  EVS_CUDA_TRY(evs_launch(gemm_skinny_f32_kernel, grid, dim3(SK_WARPS * 32), smem, st, pdl,
+                          static_cast<const float*>(W), static_cast<const float*>(W2 ? W2 : W),
+                          static_cast<const float*>(X), ldx, ws, p.N, p.K, p.M, p.kchunk, p.dual));
   evs_count_launch(1);
   return EVS_OK;
 }

@@ -167,6 +167,8 @@ __host__ __device__ constexpr int tap_stride(int K) {
 // taps[32][tap_stride(K)] f32 | hist[win][32] TD (x1v by position mod win) | x2s[TS][32] f32
 template <typename TD, bool FLIP>
 __global__ void __launch_bounds__(HY_THREADS) hyena_fir_kernel(HyArgs<TD> a, int win) {
+  pdl_trigger();
+  pdl_wait();
   extern __shared__ __align__(16) float sm[];
   const int K = a.K, H = K - 1, KS = tap_stride(K), T = a.T;
   float* uw = sm;
@@ -281,6 +283,8 @@ __device__ __forceinline__ void store_vec(float* dst, const float* v) {
 // Shared memory (floats): uw[UW][96] | zs[TS][96] | wo[96][K0]
 template <typename TD, int SPT>
 __global__ void __launch_bounds__(HY_THREADS) hyena_iir_kernel(HyArgs<TD> a) {
+  pdl_trigger();
+  pdl_wait();
   extern __shared__ __align__(16) float sm[];
   float* uw = sm;
   float* zs = uw + UW * C3;
@@ -409,7 +413,7 @@ int launch_hyena_t(const evs_model* m, evs_state* s, int layer, int B, int T, in
     const size_t smem = sizeof(float) * outer_floats;
     auto launch = [&](auto kern) -> int {
       EVS_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
-      kern<<<grid, HY_THREADS, smem, st>>>(a);
+      EVS_CUDA_TRY(evs_launch(kern, grid, dim3(HY_THREADS), smem, st, s->use_pdl(), a));
       return EVS_OK;
     };
     switch (a.S / 4) {
@@ -427,7 +431,7 @@ int launch_hyena_t(const evs_model* m, evs_state* s, int layer, int B, int T, in
     EVS_CHECK_RANGE(smem <= 220 * 1024, "FIR filter too long for the shared-memory window");
     auto launch = [&](auto kern) -> int {
       EVS_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
-      kern<<<grid, HY_THREADS, smem, st>>>(a, win);
+      EVS_CUDA_TRY(evs_launch(kern, grid, dim3(HY_THREADS), smem, st, s->use_pdl(), a, win));
       return EVS_OK;
     };
     if (L.kind == EVS_LAYER_HCM)

@@ -97,6 +97,8 @@ struct evs_state {
     double bytes;
   };
   bool prof = false;
+  bool pdl = true;  // programmatic dependent launch inside a forward (off while profiling)
+  bool use_pdl() const { return pdl && !prof; }
   std::vector<ProfRec> prof_recs;
   std::vector<cudaEvent_t> ev_pool;
   size_t ev_used = 0;
@@ -114,10 +116,11 @@ GemmPlan gemm_plan(const evs_model* m, int N, int K, int M, int dual);
 GemmPlan gemm_plan_f32(int N, int K, int M, int dual);
 // out[m][n] = sum of the split partials (in split order) + bias[n]
 int launch_reduce_splits(const float* ws, int splits, int M, int N, const float* bias, float* out, cudaStream_t st);
+// pdl: launch with programmatic stream serialization (see pdl_wait)
 int launch_gemm_tc(const CUtensorMap* tmA, const CUtensorMap* tmA2, const CUtensorMap* tmB, const GemmPlan& p,
-                   float* ws, EvsDevErr* err, cudaStream_t st);
+                   float* ws, EvsDevErr* err, cudaStream_t st, bool pdl = false);
 int launch_gemm_simt(const void* W, const void* W2, const void* X, int ldx, int dtype, const GemmPlan& p, float* ws,
-                     cudaStream_t st);
+                     cudaStream_t st, bool pdl = false);
 int make_tmap_2d_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t row_stride_bytes,
                       uint32_t box_inner, uint32_t box_outer);
 

@@ -35,6 +35,8 @@ __global__ void __launch_bounds__(ROW_THREADS) embed_norm_kernel(const int64_t* 
                                                                  float* __restrict__ resid, TD* __restrict__ act,
                                                                  int ld_act, int d, int V, float eps,
                                                                  EvsDevErr* err) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ float red[33];
   const int row = blockIdx.x;
   int64_t id = ids[row];
@@ -83,6 +85,8 @@ __global__ void __cluster_dims__(NORM_CL, 1, 1) __launch_bounds__(NORM_THREADS)
     res_add_norm_kernel(const float* __restrict__ ws, int splits, int M, float* __restrict__ resid,
                         const float* __restrict__ scale, TD* __restrict__ act, int ld_act, int d, float eps,
                         float* __restrict__ ring, int ring_len, const int32_t* __restrict__ len, int T) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ float red[NORM_THREADS / 32];
   __shared__ float cta_ss;
   cg::cluster_group cluster = cg::this_cluster();
@@ -157,6 +161,8 @@ __global__ void __cluster_dims__(NORM_CL, 1, 1) __launch_bounds__(NORM_THREADS)
 template <typename TD>
 __global__ void __launch_bounds__(ROW_THREADS) swiglu_kernel(const float* __restrict__ ws, int splits, int M, int F,
                                                             TD* __restrict__ act, int ld_act) {
+  pdl_trigger();
+  pdl_wait();
   const int row = blockIdx.y;
   const int f = (blockIdx.x * ROW_THREADS + threadIdx.x) * 4;
   if (f >= F) return;
@@ -183,6 +189,8 @@ __global__ void __launch_bounds__(ROW_THREADS) swiglu_kernel(const float* __rest
 
 __global__ void logits_kernel(const float* __restrict__ ws, int splits, int M, int V, int T, int out_T, int t0,
                               int last_only, float* __restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
   const int row = blockIdx.y;
   const int v = blockIdx.x * blockDim.x + threadIdx.x;
   if (v >= V) return;
@@ -197,6 +205,8 @@ __global__ void logits_kernel(const float* __restrict__ ws, int splits, int M, i
 
 __global__ void bookkeeping_kernel(int32_t* len, int32_t* len0, int32_t* iir_cur, int32_t* chunk, int B, int T,
                                    int retain) {
+  pdl_trigger();
+  pdl_wait();
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b < B) {
     const int old = len[b];
@@ -218,14 +228,14 @@ int launch_embed_norm(const evs_model* m, evs_state* s, const int64_t* ids, int 
                       cudaStream_t st) {
   const int d = m->cfg.d_model;
   if (m->cfg.dtype == EVS_DTYPE_BF16)
-    embed_norm_kernel<__nv_bfloat16><<<M, ROW_THREADS, 0, st>>>(
-        ids, static_cast<const __nv_bfloat16*>(m->embed), scale, s->resid, static_cast<__nv_bfloat16*>(s->act),
-        s->ld_act, d, m->cfg.vocab_size, m->cfg.eps, s->d_err);
+    EVS_CUDA_TRY(evs_launch(embed_norm_kernel<__nv_bfloat16>, dim3(M), dim3(ROW_THREADS), 0, st, s->use_pdl(), ids,
+                            static_cast<const __nv_bfloat16*>(m->embed), scale, s->resid,
+                            static_cast<__nv_bfloat16*>(s->act), s->ld_act, d, m->cfg.vocab_size, m->cfg.eps,
+                            s->d_err));
   else
-    embed_norm_kernel<float><<<M, ROW_THREADS, 0, st>>>(ids, static_cast<const float*>(m->embed), scale, s->resid,
-                                                        static_cast<float*>(s->act), s->ld_act, d,
-                                                        m->cfg.vocab_size, m->cfg.eps, s->d_err);
-  EVS_CUDA_TRY(cudaGetLastError());
+    EVS_CUDA_TRY(evs_launch(embed_norm_kernel<float>, dim3(M), dim3(ROW_THREADS), 0, st, s->use_pdl(), ids,
+                            static_cast<const float*>(m->embed), scale, s->resid, static_cast<float*>(s->act),
+                            s->ld_act, d, m->cfg.vocab_size, m->cfg.eps, s->d_err));
   evs_count_launch(1);
   return EVS_OK;
 }
@@ -237,14 +247,15 @@ int launch_res_add_norm(const evs_model* m, evs_state* s, int M, int splits, con
   EVS_CHECK_ARG(d % (NORM_CL * 4) == 0 && d <= NORM_CL * NORM_THREADS * 4 * NORM_VPT && s->ld_act % 4 == 0,
                 "d_model must be a multiple of 32 and at most 16384");
   if (m->cfg.dtype == EVS_DTYPE_BF16)
-    res_add_norm_kernel<__nv_bfloat16><<<dim3(NORM_CL, M), NORM_THREADS, 0, st>>>(
-        s->ws, splits, M, s->resid, scale, static_cast<__nv_bfloat16*>(s->act), s->ld_act, d, m->cfg.eps, ring,
-        s->ring_len, s->d_len, T);
+    EVS_CUDA_TRY(evs_launch(res_add_norm_kernel<__nv_bfloat16>, dim3(NORM_CL, M), dim3(NORM_THREADS), 0, st,
+                            s->use_pdl(), static_cast<const float*>(s->ws), splits, M, s->resid, scale,
+                            static_cast<__nv_bfloat16*>(s->act), s->ld_act, d, m->cfg.eps, ring, s->ring_len,
+                            static_cast<const int32_t*>(s->d_len), T));
   else
-    res_add_norm_kernel<float><<<dim3(NORM_CL, M), NORM_THREADS, 0, st>>>(s->ws, splits, M, s->resid, scale,
-                                                          static_cast<float*>(s->act), s->ld_act, d, m->cfg.eps,
-                                                          ring, s->ring_len, s->d_len, T);
-  EVS_CUDA_TRY(cudaGetLastError());
+    EVS_CUDA_TRY(evs_launch(res_add_norm_kernel<float>, dim3(NORM_CL, M), dim3(NORM_THREADS), 0, st, s->use_pdl(),
+                            static_cast<const float*>(s->ws), splits, M, s->resid, scale,
+                            static_cast<float*>(s->act), s->ld_act, d, m->cfg.eps, ring, s->ring_len,
+                            static_cast<const int32_t*>(s->d_len), T));
   evs_count_launch(1);
   return EVS_OK;
 }
@@ -254,11 +265,12 @@ int launch_swiglu(const evs_model* m, evs_state* s, int M, int splits, cudaStrea
   EVS_CHECK_ARG(F % 64 == 0, "mlp_inner must be a multiple of 64");
   dim3 grid((F / 4 + ROW_THREADS - 1) / ROW_THREADS, M);
   if (m->cfg.dtype == EVS_DTYPE_BF16)
-    swiglu_kernel<__nv_bfloat16><<<grid, ROW_THREADS, 0, st>>>(s->ws, splits, M, F,
-                                                                static_cast<__nv_bfloat16*>(s->act), s->ld_act);
+    EVS_CUDA_TRY(evs_launch(swiglu_kernel<__nv_bfloat16>, grid, dim3(ROW_THREADS), 0, st, s->use_pdl(),
+                            static_cast<const float*>(s->ws), splits, M, F, static_cast<__nv_bfloat16*>(s->act),
+                            s->ld_act));
   else
-    swiglu_kernel<float><<<grid, ROW_THREADS, 0, st>>>(s->ws, splits, M, F, static_cast<float*>(s->act), s->ld_act);
-  EVS_CUDA_TRY(cudaGetLastError());
+    EVS_CUDA_TRY(evs_launch(swiglu_kernel<float>, grid, dim3(ROW_THREADS), 0, st, s->use_pdl(),
+                            static_cast<const float*>(s->ws), splits, M, F, static_cast<float*>(s->act), s->ld_act));
   evs_count_launch(1);
   return EVS_OK;
 }
@@ -267,15 +279,15 @@ int launch_logits(const evs_model* m, evs_state* s, int M, int T, int splits, fl
                   int last_only, cudaStream_t st) {
   const int V = m->cfg.vocab_size;
   dim3 grid((V + 255) / 256, M);
-  logits_kernel<<<grid, 256, 0, st>>>(s->ws, splits, M, V, T, out_T, t0, last_only, logits);
-  EVS_CUDA_TRY(cudaGetLastError());
+  EVS_CUDA_TRY(evs_launch(logits_kernel, grid, dim3(256), 0, st, s->use_pdl(), static_cast<const float*>(s->ws),
+                          splits, M, V, T, out_T, t0, last_only, logits));
   evs_count_launch(1);
   return EVS_OK;
 }
 
 int launch_bookkeeping(evs_state* s, int B, int T, int retain, cudaStream_t st) {
-  bookkeeping_kernel<<<(B + 127) / 128, 128, 0, st>>>(s->d_len, s->d_len0, s->d_iir_cur, s->d_chunk, B, T, retain);
-  EVS_CUDA_TRY(cudaGetLastError());
+  EVS_CUDA_TRY(evs_launch(bookkeeping_kernel, dim3((B + 127) / 128), dim3(128), 0, st, s->use_pdl(), s->d_len,
+                          s->d_len0, s->d_iir_cur, s->d_chunk, B, T, retain));
   evs_count_launch(1);
   return EVS_OK;
 }
