@@ -70,7 +70,7 @@ int gemm(const evs_model* m, evs_state* s, const CUtensorMap* tA, const CUtensor
   EVS_CHECK_RANGE(static_cast<size_t>(p.splits) * M * N <= s->ws_floats, "split-K workspace too small");
   *splits = p.splits;
   if (m->cfg.dtype == EVS_DTYPE_BF16) {
-    const CUtensorMap* tB = K == m->cfg.d_model ? &s->tm_act_d : &s->tm_act_f;
+    const CUtensorMap* tB = K == m->cfg.d_model ? s->tm_act_d : s->tm_act_f;
     return launch_gemm_tc(tA, tA2, tB, p, s->ws, s->d_err, st, s->use_pdl());
   }
   return launch_gemm_simt(W, W2, s->act, s->ld_act, m->cfg.dtype, p, s->ws, st, s->use_pdl());
@@ -422,10 +422,12 @@ int evs_state_create(const evs_model* m, int max_batch, int max_seqlen, int max_
   EVS_CUDA_TRY(cudaMemset(pers, 0, s->owned_bytes[0]));
   EVS_CUDA_TRY(cudaMemset(scr, 0, s->owned_bytes[1]));
   if (c.dtype == EVS_DTYPE_BF16) {
-    EVS_TRY(make_tmap_2d_bf16(&s->tm_act_d, s->act, d, s->m_cap, static_cast<uint64_t>(s->ld_act) * 2, GEMM_BK,
-                              TOK_TILE));
-    EVS_TRY(make_tmap_2d_bf16(&s->tm_act_f, s->act, F, s->m_cap, static_cast<uint64_t>(s->ld_act) * 2, GEMM_BK,
-                              TOK_TILE));
+    for (int t = 0; t < 3; ++t) {
+      EVS_TRY(make_tmap_2d_bf16(&s->tm_act_d[t], s->act, d, s->m_cap, static_cast<uint64_t>(s->ld_act) * 2, GEMM_BK,
+                                GEMM_NT[t]));
+      EVS_TRY(make_tmap_2d_bf16(&s->tm_act_f[t], s->act, F, s->m_cap, static_cast<uint64_t>(s->ld_act) * 2, GEMM_BK,
+                                GEMM_NT[t]));
+    }
   }
   EVS_CUDA_TRY(cudaDeviceSynchronize());
   *out = s;
@@ -614,9 +616,10 @@ int evs_sample(const double* rows, int n, int V, const double* u, int64_t* out, 
 int evs_gemm_bf16(const void* W, const void* X, float* out, int N, int K, int M, int splits, cudaStream_t st) {
   EVS_CHECK_ARG(W && X && out, "null argument");
   EVS_CHECK_ARG(N % GEMM_BM == 0 && K % GEMM_BK == 0 && M >= 1 && M <= 4096, "bad GEMM shape");
-  CUtensorMap ta, tb;
+  CUtensorMap ta, tb[3];
   EVS_TRY(make_tmap_2d_bf16(&ta, W, K, N, static_cast<uint64_t>(K) * 2, GEMM_BK, GEMM_BM));
-  EVS_TRY(make_tmap_2d_bf16(&tb, X, K, M, static_cast<uint64_t>(K) * 2, GEMM_BK, TOK_TILE));
+  for (int t = 0; t < 3; ++t)
+    EVS_TRY(make_tmap_2d_bf16(&tb[t], X, K, M, static_cast<uint64_t>(K) * 2, GEMM_BK, GEMM_NT[t]));
   GemmPlan p{N, K, M, 1, 0};
   if (splits <= 0) {
     const int kblocks = K / GEMM_BK, tiles = N / GEMM_BM;
@@ -625,7 +628,7 @@ int evs_gemm_bf16(const void* W, const void* X, float* out, int N, int K, int M,
     p.splits = splits;
   }
   EVS_CHECK_ARG(p.splits == 1, "evs_gemm_bf16 writes out directly: use splits == 1 or <= 0 with one split");
-  return launch_gemm_tc(&ta, nullptr, &tb, p, out, nullptr, st);
+  return launch_gemm_tc(&ta, nullptr, tb, p, out, nullptr, st);
 }
 
 int evs_profile_start(evs_state* s) {

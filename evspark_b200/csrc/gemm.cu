@@ -42,7 +42,8 @@ __global__ void __launch_bounds__(192, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tile = blockIdx.x, split = blockIdx.y, ttile = blockIdx.z;
+  // token tile fastest: the CTAs that share a weight tile run side by side and share its L2 lines
+  const int ttile = blockIdx.x, tile = blockIdx.y, split = blockIdx.z;
   const int kblocks = K / GEMM_BK;
   const int kb_begin = static_cast<int>(static_cast<long long>(kblocks) * split / splits);
   const int kb_end = static_cast<int>(static_cast<long long>(kblocks) * (split + 1) / splits);
@@ -262,13 +263,14 @@ PFN_encodeTiled get_encode() {
 template <int NT>
 int launch_tc(const CUtensorMap* tmA, const CUtensorMap* tmA2, const CUtensorMap* tmB, const GemmPlan& p, float* ws,
               EvsDevErr* err, cudaStream_t st, bool pdl) {
+  static_assert(NT % 16 == 0 && NT <= 256, "UMMA N");
   using C = TcCfg<NT>;
   static bool attr_set = false;
   if (!attr_set) {
     EVS_CUDA_TRY(cudaFuncSetAttribute(gemm_tc_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
     attr_set = true;
   }
-  dim3 grid(p.N / GEMM_BM, p.splits, (p.M + NT - 1) / NT);
+  dim3 grid((p.M + NT - 1) / NT, p.N / GEMM_BM, p.splits);
   EVS_CUDA_TRY(evs_launch(gemm_tc_kernel<NT>, grid, dim3(192), C::SMEM, st, pdl, *tmA, tmA2 ? *tmA2 : *tmA, *tmB,
                           ws, p.N, p.K, p.M, p.splits, p.dual, err));
   evs_count_launch(1);
@@ -324,12 +326,18 @@ GemmPlan gemm_plan_f32(int N, int K, int M, int dual) {
   return p;
 }
 
+int gemm_tile_index(int M) { return M <= GEMM_NT[0] ? 0 : (M <= GEMM_NT[1] ? 1 : 2); }
+
 int launch_gemm_tc(const CUtensorMap* tmA, const CUtensorMap* tmA2, const CUtensorMap* tmB, const GemmPlan& p,
                    float* ws, EvsDevErr* err, cudaStream_t st, bool pdl) {
   EVS_CHECK_ARG(p.N % GEMM_BM == 0 && p.K % GEMM_BK == 0, "tcgen05 GEMM needs N % 128 == 0 and K % 64 == 0");
   EVS_CHECK_ARG(p.splits >= 1 && p.splits <= p.K / GEMM_BK, "bad split count");
   if (p.M <= 0) return EVS_OK;
-  return launch_tc<TOK_TILE>(tmA, tmA2, tmB, p, ws, err, st, pdl);
+  switch (gemm_tile_index(p.M)) {
+    case 0: return launch_tc<GEMM_NT[0]>(tmA, tmA2, &tmB[0], p, ws, err, st, pdl);
+    case 1: return launch_tc<GEMM_NT[1]>(tmA, tmA2, &tmB[1], p, ws, err, st, pdl);
+    default: return launch_tc<GEMM_NT[2]>(tmA, tmA2, &tmB[2], p, ws, err, st, pdl);
+  }
 }
 
 int launch_gemm_simt(const void* W, const void* W2, const void* X, int ldx, int dtype, const GemmPlan& p, float* ws,

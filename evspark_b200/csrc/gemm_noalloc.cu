@@ -80,10 +80,11 @@ extern "C" EVS_API int evs_gemm_bf16_noalloc(const void* W, const void* X, float
   }
   float* ws = nullptr;
   EVS_TRY(noalloc_scratch(&ws));
-  CUtensorMap ta, tb;
+  CUtensorMap ta, tb[3];
   EVS_TRY(make_tmap_2d_bf16(&ta, W, K, N, static_cast<uint64_t>(K) * 2, GEMM_BK, GEMM_BM));
-  EVS_TRY(make_tmap_2d_bf16(&tb, X, K, M, static_cast<uint64_t>(K) * 2, GEMM_BK, TOK_TILE));
-  EVS_TRY(launch_gemm_tc(&ta, nullptr, &tb, p, ws, nullptr, st));
+  for (int t = 0; t < 3; ++t)
+    EVS_TRY(make_tmap_2d_bf16(&tb[t], X, K, M, static_cast<uint64_t>(K) * 2, GEMM_BK, GEMM_NT[t]));
+  EVS_TRY(launch_gemm_tc(&ta, nullptr, tb, p, ws, nullptr, st));
   const int MN = M * N;
   noalloc_reduce_kernel<<<(MN + 255) / 256, 256, 0, st>>>(ws, p.splits, MN, out);
   EVS_CUDA_TRY(cudaGetLastError());

@@ -9,6 +9,8 @@
 constexpr int GEMM_BM = 128;
 constexpr int GEMM_BK = 64;
 constexpr int TOK_TILE = 16;  // token rows per decode tile (MMA N)
+// token tiles (MMA N) of the projection kernel, chosen from the token count M
+constexpr int GEMM_NT[3] = {16, 64, 128};
 constexpr int ATTN_BLOCK = 64;  // keys per attention partial (aligned at absolute positions)
 
 // HBM layout of the per-sequence state ------------------------------------
@@ -89,7 +91,7 @@ struct evs_state {
   float* attn_part = nullptr;  // [B][H][attn_blocks][max_chunk][Dh+2] fp32
   int64_t* ids_scratch = nullptr;  // [m_cap] chunk ids of a strided prefill
   EvsDevErr* d_err = nullptr;
-  CUtensorMap tm_act_d, tm_act_f;  // activation buffer viewed with K = d and K = F
+  CUtensorMap tm_act_d[3], tm_act_f[3];  // activation buffer, K = d and K = F, box rows GEMM_NT[i]
   // profiling (evs_profile_start / evs_profile_stop)
   struct ProfRec {
     int kind;
@@ -117,6 +119,8 @@ GemmPlan gemm_plan_f32(int N, int K, int M, int dual);
 // out[m][n] = sum of the split partials (in split order) + bias[n]
 int launch_reduce_splits(const float* ws, int splits, int M, int N, const float* bias, float* out, cudaStream_t st);
 // pdl: launch with programmatic stream serialization (see pdl_wait)
+// tmB: three maps of the activations with box rows GEMM_NT[0..2]; the tile is chosen from p.M
+int gemm_tile_index(int M);
 int launch_gemm_tc(const CUtensorMap* tmA, const CUtensorMap* tmA2, const CUtensorMap* tmB, const GemmPlan& p,
                    float* ws, EvsDevErr* err, cudaStream_t st, bool pdl = false);
 int launch_gemm_simt(const void* W, const void* W2, const void* X, int ldx, int dtype, const GemmPlan& p, float* ws,

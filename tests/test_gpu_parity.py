@@ -57,7 +57,8 @@ def oracle_tiny(tiny):
 # tcgen05 GEMM
 # ---------------------------------------------------------------------------
 
-@pytest.mark.parametrize("N_,K,M", [(256, 1024, 1), (512, 512, 13), (384, 4096, 16), (256, 640, 40)])
+@pytest.mark.parametrize("N_,K,M", [(256, 1024, 1), (512, 512, 13), (384, 4096, 16), (256, 640, 40),
+                                    (512, 1024, 200)])
 def test_gemm_bf16_tcgen05_vs_torch(cuda, N_, K, M):
     from evspark_b200 import _native as N
 
@@ -75,6 +76,27 @@ def test_gemm_bf16_tcgen05_vs_torch(cuda, N_, K, M):
     N.call("evs_gemm_bf16", W.data_ptr(), X[M - 1:].contiguous().data_ptr(), out1.data_ptr(), N_, K, 1, 1,
            N.stream_ptr())
     assert torch.equal(out1[0], out[M - 1])
+
+
+def test_gemm_token_tile_widths_agree_bitwise(cuda):
+    """Batched streams use 64- and 128-token MMA tiles; a token row must come out bit-identical
+    to the 16-token tile a single stream uses, so batching never changes a stream's logits."""
+    from evspark_b200 import _native as N
+
+    N_, K = 768, 2048
+    g = torch.Generator(device=cuda).manual_seed(11)
+    W = torch.randn(N_, K, device=cuda, generator=g).to(torch.bfloat16)
+    X = torch.randn(300, K, device=cuda, generator=g).to(torch.bfloat16)
+    outs = {}
+    for M in (13, 60, 300):  # 16-, 64- and 128-token tiles
+        out = torch.empty(M, N_, device=cuda)
+        N.call("evs_gemm_bf16", W.data_ptr(), X[:M].contiguous().data_ptr(), out.data_ptr(), N_, K, M, 1,
+               N.stream_ptr())
+        outs[M] = out
+    torch.cuda.synchronize()
+    assert torch.equal(outs[13], outs[60][:13])
+    assert torch.equal(outs[13], outs[300][:13])
+    assert torch.equal(outs[60], outs[300][:60])
 
 
 # ---------------------------------------------------------------------------
