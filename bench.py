@@ -181,6 +181,7 @@ def run_streams(args) -> int:
     from evspark_b200.drafter import DeviceDrafter, layer_index
     from evspark_b200.model import TargetModel
     from evspark_b200.specdec.block.neural_draft import NeuralDraftModel
+    from evspark_b200.ranks import combine_timing
     from evspark_b200.specdec.block.streams import StreamBatch
     from evspark_b200.workload import markov_prompt
 
@@ -216,13 +217,7 @@ def run_streams(args) -> int:
     clk = clocks.stop()
     ms = ev0.elapsed_time(ev1)
     tokens = float(sum(len(e) for e in sb.emitted) - emitted0)
-    if world > 1:
-        t = torch.tensor([ms], device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-        a = torch.tensor([tokens], device=device)
-        dist.all_reduce(a, op=dist.ReduceOp.SUM)
-        tokens = float(a.item())
+    ms, tokens = combine_timing(ms, tokens, device)
     if rank == 0:
         line = {
             "metric": "accepted tok/s multi-stream Evo2-7B-shape γ=12", "value": round(tokens / (ms / 1e3), 3),

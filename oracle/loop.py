@@ -91,3 +91,21 @@ def native_greedy(model: OracleTarget, prompt, n_tokens: int):
         if i + 1 < n_tokens:
             last = model.forward(np.array([[t]]), st)[0][0, -1].double().numpy()
     return np.asarray(out, dtype=np.int64), st
+
+
+def oracle_streams(prompts, n_tokens: int, seeds, gamma: int = 4):
+    """Independent streams on the tiny oracle model (seeded weights), each with its own
+    generator: the per-stream result a multi-stream decoder must reproduce, however the streams
+    are grouped into batches or spread over ranks (scripts/regulatory_design/generation.py:
+    196-277 runs streams independently)."""
+    import torch
+
+    from evspark_b200.config import TINY
+    from evspark_b200.weights import init_target_weights
+
+    model = OracleTarget(TINY, init_target_weights(TINY, seed=20260820), compute=torch.float64)
+    out = []
+    for p, s in zip(np.asarray(prompts, dtype=np.int64), seeds):
+        em, _, _ = speculative_generate(model, IdentityDraft(), p, n_tokens, gamma, False, np.random.default_rng(s))
+        out.append(em)
+    return out
