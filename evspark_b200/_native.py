@@ -48,6 +48,7 @@ class ModelConfig(C.Structure):
         ("short_filter_length", C.c_int32), ("hcs_filter_length", C.c_int32), ("hcm_filter_length", C.c_int32),
         ("dtype", C.c_int32), ("eps", C.c_float), ("rope_base", C.c_float),
         ("layer_kind", C.c_int32 * EVS_MAX_LAYERS), ("capture_layers", C.c_int32 * 4),
+        ("tp_world", C.c_int32), ("tp_rank", C.c_int32),
     ]
 
 
@@ -67,6 +68,9 @@ _PROTOS = {
     "evs_model_finalize": (_I, [_P]),
     "evs_model_destroy": (None, [_P]),
     "evs_state_create": (_I, [_P, _I, _I, _I, C.POINTER(_P)]),
+    "evs_state_tp_handle": (_I, [_P, _P]),
+    "evs_state_tp_connect": (_I, [_P, _P, _I]),
+    "evs_state_tp_disconnect": (_I, [_P]),
     "evs_state_destroy": (None, [_P]),
     "evs_state_reset": (_I, [_P, _P]),
     "evs_state_copy": (_I, [_P, _P, _P]),

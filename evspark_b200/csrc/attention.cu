@@ -287,7 +287,7 @@ __global__ void attn_combine_kernel(const float* __restrict__ part, const int32_
 template <typename TD>
 int launch_attention_t(const evs_model* m, evs_state* s, int layer, int B, int T, int splits, int kv_blocks,
                        cudaStream_t st) {
-  const int d = m->cfg.d_model, H = m->cfg.n_heads, Dh = m->cfg.head_dim;
+  const int d = m->dl, H = m->Hl, Dh = m->cfg.head_dim;  // this rank's channels and heads
   const int M = B * T;
   TD* kv = static_cast<TD*>(s->kv[layer]);
   TD* qrot = static_cast<TD*>(s->qrot);

@@ -19,26 +19,27 @@ int next_pow2(int x) {
 
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
-// expected element count of a slot for a layer kind (0 = slot unused)
-int64_t expected_numel(const evs_model_config& c, int kind, int slot) {
-  const int64_t d = c.d_model, F = c.mlp_inner, S = c.state_size;
+// element count of a slot on this rank (0 = slot unused); sharded slots use the local widths
+int64_t expected_numel(const evs_model* m, int kind, int slot) {
+  const evs_model_config& c = m->cfg;
+  const int64_t D = c.d_model, d = m->dl, F = m->Fl, S = c.state_size;
   const bool hy = kind != EVS_LAYER_MHA;
   switch (slot) {
     case EVS_W_PRE_NORM:
-    case EVS_W_POST_NORM: return d;
-    case EVS_W_IN: return hy ? 3 * d * d : 0;
+    case EVS_W_POST_NORM: return D;
+    case EVS_W_IN: return hy ? 3 * d * D : 0;
     case EVS_W_SHORT: return hy ? 3 * d * c.short_filter_length : 0;
     case EVS_W_INNER:
       return kind == EVS_LAYER_HCS ? d * c.hcs_filter_length : (kind == EVS_LAYER_HCM ? d * c.hcm_filter_length : 0);
     case EVS_W_D: return (kind == EVS_LAYER_HCM || kind == EVS_LAYER_HCL) ? d : 0;
     case EVS_W_LOG_POLES:
     case EVS_W_RESIDUES: return kind == EVS_LAYER_HCL ? d * S : 0;
-    case EVS_W_OUT: return hy ? d * d : 0;
-    case EVS_W_QKV: return hy ? 0 : 3 * d * d;
-    case EVS_W_O: return hy ? 0 : d * d;
+    case EVS_W_OUT: return hy ? D * d : 0;
+    case EVS_W_QKV: return hy ? 0 : 3 * d * D;
+    case EVS_W_O: return hy ? 0 : D * d;
     case EVS_W_W1:
-    case EVS_W_W2: return F * d;
-    case EVS_W_W3: return d * F;
+    case EVS_W_W2: return F * D;
+    case EVS_W_W3: return D * F;
     default: return 0;
   }
 }
@@ -64,16 +65,17 @@ const void** slot_ptr(LayerDev& L, int slot) {
 }
 
 // one GEMM: bf16 -> tcgen05 (TMA maps), fp32 -> SIMT
+// out: partial sums [splits][M][N] (s->ws, or a shared buffer of a row-parallel projection)
 int gemm(const evs_model* m, evs_state* s, const CUtensorMap* tA, const CUtensorMap* tA2, const void* W,
-         const void* W2, int N, int K, int M, int dual, cudaStream_t st, int* splits) {
+         const void* W2, int N, int K, int M, int dual, float* out, size_t out_floats, cudaStream_t st, int* splits) {
   GemmPlan p = gemm_plan(m, N, K, M, dual);
-  EVS_CHECK_RANGE(static_cast<size_t>(p.splits) * M * N <= s->ws_floats, "split-K workspace too small");
+  EVS_CHECK_RANGE(static_cast<size_t>(p.splits) * M * N <= out_floats, "split-K workspace too small");
   *splits = p.splits;
   if (m->cfg.dtype == EVS_DTYPE_BF16) {
-    const CUtensorMap* tB = K == m->cfg.d_model ? s->tm_act_d : s->tm_act_f;
-    return launch_gemm_tc(tA, tA2, tB, p, s->ws, s->d_err, st, s->use_pdl());
+    const CUtensorMap* tB = K == m->cfg.d_model ? s->tm_act_d : (K == m->Fl ? s->tm_act_f : s->tm_act_l);
+    return launch_gemm_tc(tA, tA2, tB, p, out, s->d_err, st, s->use_pdl());
   }
-  return launch_gemm_simt(W, W2, s->act, s->ld_act, m->cfg.dtype, p, s->ws, st, s->use_pdl());
+  return launch_gemm_simt(W, W2, s->act, s->ld_act, m->cfg.dtype, p, out, st, s->use_pdl());
 }
 
 cudaEvent_t take_event(evs_state* s) {
@@ -101,7 +103,10 @@ int timed(evs_state* s, cudaStream_t st, int kind, double bytes, F&& fn) {
 int run_forward(const evs_model* m, evs_state* s, const int64_t* ids, int B, int T, int prefill, int retain,
                 float* logits, int out_T, int t0, int last_only, cudaStream_t st) {
   const evs_model_config& c = m->cfg;
-  const int d = c.d_model, F = c.mlp_inner, V = c.vocab_size;
+  // d: residual width; dl, F, H: this rank's Hyena channels, MLP features and heads
+  const int d = c.d_model, dl = m->dl, F = m->Fl, V = c.vocab_size;
+  const bool tp = m->tp_world > 1;
+  EVS_CHECK_ARG(!tp || s->tp_connected, "channel-sharded state not connected to its peers (evs_state_tp_connect)");
   EVS_CHECK_ARG(B >= 1 && B <= s->max_batch, "batch outside [1, max_batch]");
   EVS_CHECK_ARG(T >= 1 && T <= s->max_chunk, "chunk length outside [1, max_chunk]");
   int maxlen = 0;
@@ -110,13 +115,41 @@ int run_forward(const evs_model* m, evs_state* s, const int64_t* ids, int B, int
   const int M = B * T;
   const int kv_blocks = (maxlen + T + ATTN_BLOCK - 1) / ATTN_BLOCK;
   const double el = static_cast<double>(m->elem());
-  const int H = c.n_heads, Dh = c.head_dim, S = c.state_size;
+  const int H = m->Hl, Dh = c.head_dim, S = c.state_size;
   int sp = 1;
   // one projection, timed with its algorithmic bytes (weights + activations in + fp32 partials out)
-  auto G = [&](const CUtensorMap* tA, const CUtensorMap* tA2, const void* W, const void* W2, int N, int K, int dual) {
+  auto G = [&](const CUtensorMap* tA, const CUtensorMap* tA2, const void* W, const void* W2, int N, int K, int dual,
+               float* out = nullptr, size_t out_floats = 0) {
     const GemmPlan pl = gemm_plan(m, N, K, M, dual);
     const double bytes = (static_cast<double>(N) * K + static_cast<double>(M) * K) * el + 4.0 * pl.splits * M * N;
-    return timed(s, st, EVS_PROF_GEMM, bytes, [&] { return gemm(m, s, tA, tA2, W, W2, N, K, M, dual, st, &sp); });
+    float* o = out != nullptr ? out : s->ws;
+    const size_t of = out != nullptr ? out_floats : s->ws_floats;
+    return timed(s, st, EVS_PROF_GEMM, bytes,
+                 [&] { return gemm(m, s, tA, tA2, W, W2, N, K, M, dual, o, of, st, &sp); });
+  };
+  // row-parallel projection [d x K] whose partial sums the next residual + RMSNorm adds up: with
+  // channel sharding it writes to the shared buffer of reduction `epoch` and signals the peers
+  TpPartials parts{};
+  auto RP = [&](const CUtensorMap* tA, const void* W, int K) -> int {
+    parts = TpPartials{};
+    if (!tp) {
+      EVS_TRY(G(tA, nullptr, W, nullptr, d, K, 0));
+      parts.R = 1;
+      parts.buf[0] = s->ws;
+      return EVS_OK;
+    }
+    const long long epoch = ++s->tp_epoch;
+    const size_t boff = static_cast<size_t>(epoch & 1) * s->tp_buf_bytes;
+    EVS_TRY(G(tA, nullptr, W, nullptr, d, K, 0, reinterpret_cast<float*>(s->tp_base[m->tp_rank] + boff),
+              s->tp_buf_bytes / sizeof(float)));
+    EVS_TRY(launch_tp_signal(s, epoch, st));
+    parts.R = m->tp_world;
+    parts.epoch = epoch;
+    for (int r = 0; r < m->tp_world; ++r) {
+      parts.buf[r] = reinterpret_cast<const float*>(s->tp_base[r] + boff);
+      parts.flag[r] = reinterpret_cast<const long long*>(s->tp_base[r] + 2 * s->tp_buf_bytes);
+    }
+    return EVS_OK;
   };
   const double row_bytes = static_cast<double>(M) * d * (8.0 + el);
   EVS_TRY(timed(s, st, EVS_PROF_ROW, row_bytes,
@@ -124,31 +157,32 @@ int run_forward(const evs_model* m, evs_state* s, const int64_t* ids, int B, int
   for (int i = 0; i < c.n_layers; ++i) {
     const LayerDev& L = m->L[i];
     if (L.kind == EVS_LAYER_MHA) {
-      EVS_TRY(G(&L.tm_qkv, nullptr, L.w_qkv, nullptr, 3 * d, d, 0));
-      const double kv_bytes = 2.0 * B * (maxlen + T) * H * Dh * el + 4.0 * sp * M * 3 * d + 2.0 * M * d * el;
+      EVS_TRY(G(&L.tm_qkv, nullptr, L.w_qkv, nullptr, 3 * dl, d, 0));
+      const double kv_bytes = 2.0 * B * (maxlen + T) * H * Dh * el + 4.0 * sp * M * 3 * dl + 2.0 * M * dl * el;
       EVS_TRY(timed(s, st, EVS_PROF_ATTN, kv_bytes, [&] { return launch_attention(m, s, i, B, T, sp, kv_blocks, st); }));
-      EVS_TRY(G(&L.tm_o, nullptr, L.w_o, nullptr, d, d, 0));
+      EVS_TRY(RP(&L.tm_o, L.w_o, dl));
     } else {
-      EVS_TRY(G(&L.tm_in, nullptr, L.w_in, nullptr, 3 * d, d, 0));
+      EVS_TRY(G(&L.tm_in, nullptr, L.w_in, nullptr, 3 * dl, d, 0));
       const int K = L.kind == EVS_LAYER_HCM ? c.hcm_filter_length : c.hcs_filter_length;
       const int K0 = c.short_filter_length;
       // u in + y out + outer history read/write + taps; inner FIR history or IIR states
-      double hb = B * ((2.0 * T * 3 * d + (K0 - 1) * 3.0 * d + T * d) * el) + 3.0 * d * K0 * 4;
+      double hb = B * ((2.0 * T * 3 * dl + (K0 - 1) * 3.0 * dl + T * dl) * el) + 3.0 * dl * K0 * 4;
       if (L.kind == EVS_LAYER_HCL)
-        hb += B * (static_cast<double>(d) * S * 4 * (1 + (retain ? T : 1))) + 3.0 * d * S * 4;
+        hb += B * (static_cast<double>(dl) * S * 4 * (1 + (retain ? T : 1))) + 3.0 * dl * S * 4;
       else
-        hb += B * ((K - 1.0 + T) * d * el) + static_cast<double>(d) * K * 4;
+        hb += B * ((K - 1.0 + T) * dl * el) + static_cast<double>(dl) * K * 4;
       EVS_TRY(timed(s, st, EVS_PROF_HYENA, hb, [&] { return launch_hyena(m, s, i, B, T, sp, prefill, retain, st); }));
-      EVS_TRY(G(&L.tm_out, nullptr, L.w_out, nullptr, d, d, 0));
+      EVS_TRY(RP(&L.tm_out, L.w_out, dl));
     }
-    EVS_TRY(timed(s, st, EVS_PROF_ROW, row_bytes + 4.0 * sp * M * d,
-                  [&] { return launch_res_add_norm(m, s, M, sp, static_cast<const float*>(L.post_norm), -1, T, st); }));
+    EVS_TRY(timed(s, st, EVS_PROF_ROW, row_bytes + 4.0 * sp * M * d * parts.R, [&] {
+      return launch_res_add_norm(m, s, M, sp, parts, static_cast<const float*>(L.post_norm), -1, T, st);
+    }));
     EVS_TRY(G(&L.tm_w1, &L.tm_w2, L.w1, L.w2, 2 * F, d, 1));
     EVS_TRY(timed(s, st, EVS_PROF_ROW, 8.0 * sp * M * F + M * F * el, [&] { return launch_swiglu(m, s, M, sp, st); }));
-    EVS_TRY(G(&L.tm_w3, nullptr, L.w3, nullptr, d, F, 0));
+    EVS_TRY(RP(&L.tm_w3, L.w3, F));
     const float* next = static_cast<const float*>(i + 1 < c.n_layers ? m->L[i + 1].pre_norm : m->final_norm);
-    EVS_TRY(timed(s, st, EVS_PROF_ROW, row_bytes + 4.0 * sp * M * d,
-                  [&] { return launch_res_add_norm(m, s, M, sp, next, m->capture_slot(i), T, st); }));
+    EVS_TRY(timed(s, st, EVS_PROF_ROW, row_bytes + 4.0 * sp * M * d * parts.R,
+                  [&] { return launch_res_add_norm(m, s, M, sp, parts, next, m->capture_slot(i), T, st); }));
   }
   if (logits != nullptr) {
     EVS_TRY(G(&m->tm_embed, nullptr, m->embed, nullptr, V, d, 0));
@@ -214,8 +248,20 @@ int evs_model_create(const evs_model_config* cfg, evs_model** out) {
                   "bf16 models need d_model and vocab_size multiples of 128");
   for (int i = 0; i < c.n_layers; ++i)
     EVS_CHECK_ARG(c.layer_kind[i] >= 0 && c.layer_kind[i] <= 3, "unknown layer kind");
+  const int tw = c.tp_world > 1 ? c.tp_world : 1;
+  EVS_CHECK_ARG(tw <= EVS_TP_MAX && c.tp_rank >= 0 && c.tp_rank < tw, "tp_rank / tp_world out of range");
+  EVS_CHECK_ARG(c.n_heads % tw == 0 && c.mlp_inner % (64 * tw) == 0 && (c.d_model / tw) % 32 == 0,
+                "heads, mlp_inner / 64 and d_model / 32 must divide by tp_world");
+  if (tw > 1)
+    EVS_CHECK_ARG(c.dtype == EVS_DTYPE_BF16 && (c.d_model / tw) % 128 == 0,
+                  "channel sharding needs a bf16 model with d_model / tp_world a multiple of 128");
   evs_model* m = new evs_model();
   m->cfg = c;
+  m->tp_world = tw;
+  m->tp_rank = tw > 1 ? c.tp_rank : 0;
+  m->dl = c.d_model / tw;
+  m->Hl = c.n_heads / tw;
+  m->Fl = c.mlp_inner / tw;
   EVS_CUDA_TRY(cudaGetDevice(&m->device));
   for (int i = 0; i < c.n_layers; ++i) m->L[i].kind = c.layer_kind[i];
   for (int k = 0; k < 4; ++k) {
@@ -255,7 +301,7 @@ int evs_model_set_tensor(evs_model* m, int layer, int slot, const void* dev_ptr,
   EVS_CHECK_ARG(layer < c.n_layers, "layer index out of range");
   EVS_CHECK_ARG(slot >= EVS_W_PRE_NORM && slot < EVS_W_NUM_SLOTS, "bad slot");
   LayerDev& L = m->L[layer];
-  const int64_t want = expected_numel(c, L.kind, slot);
+  const int64_t want = expected_numel(m, L.kind, slot);
   EVS_CHECK_ARG(want > 0, "slot not used by this layer kind");
   EVS_CHECK_ARG(numel == want, "tensor numel does not match the slot shape");
   *slot_ptr(L, slot) = dev_ptr;
@@ -267,28 +313,29 @@ int evs_model_finalize(evs_model* m) {
   EVS_CHECK_ARG(m != nullptr, "null model");
   if (m->finalized) return EVS_OK;
   const evs_model_config& c = m->cfg;
-  const int d = c.d_model, F = c.mlp_inner, V = c.vocab_size;
+  const int d = c.d_model, dl = m->dl, F = m->Fl, V = c.vocab_size;
   EVS_CHECK_ARG(m->embed && m->final_norm, "embed / final_norm not set");
   for (int i = 0; i < c.n_layers; ++i) {
     LayerDev& L = m->L[i];
     for (int slot = EVS_W_PRE_NORM; slot < EVS_W_NUM_SLOTS; ++slot) {
-      if (expected_numel(c, L.kind, slot) > 0 && *slot_ptr(L, slot) == nullptr) {
+      if (expected_numel(m, L.kind, slot) > 0 && *slot_ptr(L, slot) == nullptr) {
         evs_set_last_error(EVS_EINVAL, ("layer " + std::to_string(i) + " slot " + std::to_string(slot) +
                                         " not set").c_str());
         return EVS_EINVAL;
       }
     }
     if (L.kind == EVS_LAYER_HCL) {
-      EVS_CUDA_TRY(cudaMalloc(&L.poles, sizeof(float) * d * c.state_size));
-      EVS_TRY(launch_poles(static_cast<const float*>(L.log_poles), L.poles, d * c.state_size, 0));
+      EVS_CUDA_TRY(cudaMalloc(&L.poles, sizeof(float) * dl * c.state_size));
+      EVS_TRY(launch_poles(static_cast<const float*>(L.log_poles), L.poles, dl * c.state_size, 0));
     }
     if (c.dtype == EVS_DTYPE_BF16) {
+      // local shapes: column-parallel [3 dl, d] / [Fl, d], row-parallel [d, dl] / [d, Fl]
       if (L.kind == EVS_LAYER_MHA) {
-        EVS_TRY(make_tmap_2d_bf16(&L.tm_qkv, L.w_qkv, d, 3 * d, d * 2, GEMM_BK, GEMM_BM));
-        EVS_TRY(make_tmap_2d_bf16(&L.tm_o, L.w_o, d, d, d * 2, GEMM_BK, GEMM_BM));
+        EVS_TRY(make_tmap_2d_bf16(&L.tm_qkv, L.w_qkv, d, 3 * dl, d * 2, GEMM_BK, GEMM_BM));
+        EVS_TRY(make_tmap_2d_bf16(&L.tm_o, L.w_o, dl, d, dl * 2, GEMM_BK, GEMM_BM));
       } else {
-        EVS_TRY(make_tmap_2d_bf16(&L.tm_in, L.w_in, d, 3 * d, d * 2, GEMM_BK, GEMM_BM));
-        EVS_TRY(make_tmap_2d_bf16(&L.tm_out, L.w_out, d, d, d * 2, GEMM_BK, GEMM_BM));
+        EVS_TRY(make_tmap_2d_bf16(&L.tm_in, L.w_in, d, 3 * dl, d * 2, GEMM_BK, GEMM_BM));
+        EVS_TRY(make_tmap_2d_bf16(&L.tm_out, L.w_out, dl, d, dl * 2, GEMM_BK, GEMM_BM));
       }
       EVS_TRY(make_tmap_2d_bf16(&L.tm_w1, L.w1, d, F, d * 2, GEMM_BK, GEMM_BM / 2));
       EVS_TRY(make_tmap_2d_bf16(&L.tm_w2, L.w2, d, F, d * 2, GEMM_BK, GEMM_BM / 2));
@@ -314,7 +361,8 @@ int evs_state_create(const evs_model* m, int max_batch, int max_seqlen, int max_
   EVS_CHECK_ARG(m->finalized, "model not finalized");
   EVS_CHECK_ARG(max_batch >= 1 && max_seqlen >= 2 && max_chunk >= 1, "bad state sizes");
   const evs_model_config& c = m->cfg;
-  const int d = c.d_model, F = c.mlp_inner, H = c.n_heads, Dh = c.head_dim, S = c.state_size;
+  // d: residual width; dl, H, F: this rank's Hyena channels, heads and MLP features
+  const int d = c.d_model, dl = m->dl, F = m->Fl, H = m->Hl, Dh = c.head_dim, S = c.state_size;
   const size_t el = m->elem();
   evs_state* s = new evs_state();
   s->m = m;
@@ -349,10 +397,10 @@ int evs_state_create(const evs_model* m, int max_batch, int max_seqlen, int max_
     if (k == EVS_LAYER_MHA) {
       o_kv[i] = take(B * max_seqlen * 2 * H * Dh * el);
     } else {
-      o_outer[i] = take(B * s->cap_outer * 3 * d * el);
-      if (k == EVS_LAYER_HCS) o_inner[i] = take(B * s->cap_hcs * d * el);
-      if (k == EVS_LAYER_HCM) o_inner[i] = take(B * s->cap_hcm * d * el);
-      if (k == EVS_LAYER_HCL) o_iir[i] = take(B * s->iir_slots * d * S * sizeof(float));
+      o_outer[i] = take(B * s->cap_outer * 3 * dl * el);
+      if (k == EVS_LAYER_HCS) o_inner[i] = take(B * s->cap_hcs * dl * el);
+      if (k == EVS_LAYER_HCM) o_inner[i] = take(B * s->cap_hcm * dl * el);
+      if (k == EVS_LAYER_HCL) o_iir[i] = take(B * s->iir_slots * dl * S * sizeof(float));
     }
   }
   size_t o_ring[4];
@@ -385,19 +433,26 @@ int evs_state_create(const evs_model* m, int max_batch, int max_seqlen, int max_
     GemmPlan p = gemm_plan(m, N, K, s->m_cap, dual);
     ws_cols = std::max(ws_cols, static_cast<size_t>(p.splits) * N);
   };
-  plan_cols(3 * d, d, 0);
-  plan_cols(d, d, 0);
+  plan_cols(3 * dl, d, 0);
+  plan_cols(d, dl, 0);
   plan_cols(2 * F, d, 1);
   plan_cols(d, F, 0);
   plan_cols(c.vocab_size, d, 0);
   s->ws_floats = ws_cols * s->m_cap;
+  // row-parallel partial sums exchanged with the peers: two buffers of splits x m_cap x d fp32
+  if (m->tp_world > 1) {
+    size_t rp = 0;
+    rp = std::max(rp, static_cast<size_t>(gemm_plan(m, d, dl, s->m_cap, 0).splits));
+    rp = std::max(rp, static_cast<size_t>(gemm_plan(m, d, F, s->m_cap, 0).splits));
+    s->tp_buf_bytes = align256(rp * s->m_cap * d * sizeof(float));
+  }
   bool any_mha = false;
   for (int i = 0; i < c.n_layers; ++i) any_mha |= c.layer_kind[i] == EVS_LAYER_MHA;
   off = 0;
   const size_t o_resid = take(static_cast<size_t>(s->m_cap) * d * 4);
   const size_t o_act = take(static_cast<size_t>(s->m_cap) * s->ld_act * el);
   const size_t o_ws = take(s->ws_floats * 4);
-  const size_t o_qrot = take(static_cast<size_t>(s->m_cap) * d * el);
+  const size_t o_qrot = take(static_cast<size_t>(s->m_cap) * dl * el);
   const size_t o_part = any_mha ? take(B * H * s->attn_blocks * max_chunk * (Dh + 2) * 4) : SIZE_MAX;
   const size_t o_ids = take(static_cast<size_t>(s->m_cap) * 8);
   const size_t o_err = take(sizeof(EvsDevErr));
@@ -421,12 +476,25 @@ int evs_state_create(const evs_model* m, int max_batch, int max_seqlen, int max_
   s->d_err = reinterpret_cast<EvsDevErr*>(base + o_err);
   EVS_CUDA_TRY(cudaMemset(pers, 0, s->owned_bytes[0]));
   EVS_CUDA_TRY(cudaMemset(scr, 0, s->owned_bytes[1]));
+  if (m->tp_world > 1) {
+    // [buffer 0 | buffer 1 | epoch flag]; its own allocation so that it can be shared over IPC
+    const size_t bytes = 2 * s->tp_buf_bytes + 256;
+    if (cudaMalloc(&s->tp_region, bytes) != cudaSuccess) {
+      cudaGetLastError();
+      for (void* p : s->owned) cudaFree(p);
+      delete s;
+      evs_set_last_error(EVS_ECUDA, "cudaMalloc of the shared partial-sum region failed");
+      return EVS_ECUDA;
+    }
+    EVS_CUDA_TRY(cudaMemset(s->tp_region, 0, bytes));
+    s->tp_base[m->tp_rank] = static_cast<char*>(s->tp_region);
+  }
   if (c.dtype == EVS_DTYPE_BF16) {
     for (int t = 0; t < 3; ++t) {
-      EVS_TRY(make_tmap_2d_bf16(&s->tm_act_d[t], s->act, d, s->m_cap, static_cast<uint64_t>(s->ld_act) * 2, GEMM_BK,
-                                GEMM_NT[t]));
-      EVS_TRY(make_tmap_2d_bf16(&s->tm_act_f[t], s->act, F, s->m_cap, static_cast<uint64_t>(s->ld_act) * 2, GEMM_BK,
-                                GEMM_NT[t]));
+      const uint64_t ld = static_cast<uint64_t>(s->ld_act) * 2;
+      EVS_TRY(make_tmap_2d_bf16(&s->tm_act_d[t], s->act, d, s->m_cap, ld, GEMM_BK, GEMM_NT[t]));
+      EVS_TRY(make_tmap_2d_bf16(&s->tm_act_f[t], s->act, F, s->m_cap, ld, GEMM_BK, GEMM_NT[t]));
+      EVS_TRY(make_tmap_2d_bf16(&s->tm_act_l[t], s->act, dl, s->m_cap, ld, GEMM_BK, GEMM_NT[t]));
     }
   }
   EVS_CUDA_TRY(cudaDeviceSynchronize());
@@ -436,9 +504,59 @@ int evs_state_create(const evs_model* m, int max_batch, int max_seqlen, int max_
 
 void evs_state_destroy(evs_state* s) {
   if (s == nullptr) return;
+  if (s->tp_connected) evs_state_tp_disconnect(s);
   for (cudaEvent_t e : s->ev_pool) cudaEventDestroy(e);
   for (void* p : s->owned) cudaFree(p);
+  if (s->tp_region) cudaFree(s->tp_region);
   delete s;
+}
+
+int evs_state_tp_handle(const evs_state* s, void* handle64) {
+  EVS_CHECK_ARG(s && handle64, "null argument");
+  EVS_CHECK_ARG(s->tp_region != nullptr, "state of a model without channel sharding");
+  static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+  cudaIpcMemHandle_t h;
+  EVS_CUDA_TRY(cudaIpcGetMemHandle(&h, s->tp_region));
+  std::memcpy(handle64, &h, sizeof(h));
+  return EVS_OK;
+}
+
+int evs_state_tp_connect(evs_state* s, const void* handles, int world) {
+  EVS_CHECK_ARG(s && handles, "null argument");
+  EVS_CHECK_ARG(s->tp_region != nullptr, "state of a model without channel sharding");
+  EVS_CHECK_ARG(world == s->m->tp_world, "handle count != tp_world");
+  EVS_CHECK_ARG(!s->tp_connected, "state already connected");
+  for (int r = 0; r < world; ++r) {
+    if (r == s->m->tp_rank) continue;
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, static_cast<const char*>(handles) + 64 * r, sizeof(h));
+    void* p = nullptr;
+    const cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) {
+      for (int q = 0; q < r; ++q)
+        if (q != s->m->tp_rank && s->tp_base[q]) {
+          cudaIpcCloseMemHandle(s->tp_base[q]);
+          s->tp_base[q] = nullptr;
+        }
+      evs_set_last_error(EVS_ECUDA, (std::string("cudaIpcOpenMemHandle: ") + cudaGetErrorString(e)).c_str());
+      return EVS_ECUDA;
+    }
+    s->tp_base[r] = static_cast<char*>(p);
+  }
+  s->tp_connected = true;
+  return EVS_OK;
+}
+
+int evs_state_tp_disconnect(evs_state* s) {
+  EVS_CHECK_ARG(s != nullptr, "null state");
+  if (!s->tp_connected) return EVS_OK;
+  for (int r = 0; r < s->m->tp_world; ++r)
+    if (r != s->m->tp_rank && s->tp_base[r]) {
+      cudaIpcCloseMemHandle(s->tp_base[r]);
+      s->tp_base[r] = nullptr;
+    }
+  s->tp_connected = false;
+  return EVS_OK;
 }
 
 int evs_state_reset(evs_state* s, cudaStream_t st) {

@@ -379,7 +379,7 @@ int launch_hyena_t(const evs_model* m, evs_state* s, int layer, int B, int T, in
                    cudaStream_t st) {
   const LayerDev& L = m->L[layer];
   const HyenaDev& hy = s->hy[layer];
-  const int d = m->cfg.d_model;
+  const int d = m->dl;  // this rank's channels
   HyArgs<TD> a;
   a.ws = s->ws;
   a.splits = splits;
@@ -448,7 +448,7 @@ int launch_hyena_t(const evs_model* m, evs_state* s, int layer, int B, int T, in
 
 int launch_hyena(const evs_model* m, evs_state* s, int layer, int B, int T, int splits, int prefill, int retain,
                  cudaStream_t st) {
-  EVS_CHECK_ARG(m->cfg.d_model % CH == 0, "d_model must be a multiple of 32");
+  EVS_CHECK_ARG(m->dl % CH == 0, "d_model / tp_world must be a multiple of 32");
   if (m->cfg.dtype == EVS_DTYPE_BF16)
     return launch_hyena_t<__nv_bfloat16>(m, s, layer, B, T, splits, prefill, retain, st);
   return launch_hyena_t<float>(m, s, layer, B, T, splits, prefill, retain, st);
@@ -463,7 +463,7 @@ int launch_rollback(evs_state* s, const int32_t* k, int B, cudaStream_t st) {
 
 int launch_state_export(const evs_state* s, int layer, int which, int row, int width, void* dst, cudaStream_t st) {
   const evs_model* m = s->m;
-  const int d = m->cfg.d_model;
+  const int d = m->dl;  // this rank's channels
   const HyenaDev& hy = s->hy[layer];
   const bool bf = m->cfg.dtype == EVS_DTYPE_BF16;
   if (which == 0 || which == 1) {
@@ -484,7 +484,7 @@ int launch_state_export(const evs_state* s, int layer, int which, int row, int w
                                           s->d_len, static_cast<float*>(dst));
   } else if (which == 3) {
     EVS_CHECK_ARG(s->kv[layer] != nullptr, "layer has no KV cache");
-    const int HD2 = 2 * m->cfg.n_heads * m->cfg.head_dim;
+    const int HD2 = 2 * m->Hl * m->cfg.head_dim;
     if (bf)
       export_kv_kernel<__nv_bfloat16><<<64, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(s->kv[layer]),
                                                           s->max_seqlen, HD2, row, s->d_len, width,

@@ -12,6 +12,7 @@ constexpr int TOK_TILE = 16;  // token rows per decode tile (MMA N)
 // token tiles (MMA N) of the projection kernel, chosen from the token count M
 constexpr int GEMM_NT[3] = {16, 64, 128};
 constexpr int ATTN_BLOCK = 64;  // keys per attention partial (aligned at absolute positions)
+constexpr int EVS_TP_MAX = 8;   // channel-sharding ranks
 
 // HBM layout of the per-sequence state ------------------------------------
 //   outer FIR history ring   [B][cap_outer][3d]   data dtype  (positions mod cap_outer)
@@ -43,6 +44,9 @@ struct LayerDev {
 struct evs_model {
   evs_model_config cfg;
   int device = 0;
+  // channel sharding: this rank's Hyena channels, attention heads and MLP features
+  int tp_world = 1, tp_rank = 0;
+  int dl = 0, Hl = 0, Fl = 0;
   bool finalized = false;
   const void* embed = nullptr;
   const void* final_norm = nullptr;
@@ -91,7 +95,15 @@ struct evs_state {
   float* attn_part = nullptr;  // [B][H][attn_blocks][max_chunk][Dh+2] fp32
   int64_t* ids_scratch = nullptr;  // [m_cap] chunk ids of a strided prefill
   EvsDevErr* d_err = nullptr;
-  CUtensorMap tm_act_d[3], tm_act_f[3];  // activation buffer, K = d and K = F, box rows GEMM_NT[i]
+  // channel sharding: partial sums of the row-parallel projections, double-buffered, and an
+  // epoch flag, in one region shared with the peers over CUDA IPC (tp_base[rank] = own region)
+  void* tp_region = nullptr;
+  size_t tp_buf_bytes = 0;  // one of the two partial-sum buffers (splits x m_cap x d fp32)
+  char* tp_base[EVS_TP_MAX] = {nullptr};
+  bool tp_connected = false;
+  long long tp_epoch = 0;  // row-parallel reductions issued so far (same count on every rank)
+  // activation buffer as GEMM B operand, K = d, K = local F and K = local d, box rows GEMM_NT[i]
+  CUtensorMap tm_act_d[3], tm_act_f[3], tm_act_l[3];
   // profiling (evs_profile_start / evs_profile_stop)
   struct ProfRec {
     int kind;
@@ -131,8 +143,18 @@ int make_tmap_2d_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64
 // row kernels
 int launch_embed_norm(const evs_model* m, evs_state* s, const int64_t* ids, int M, const float* scale,
                       cudaStream_t st);
-int launch_res_add_norm(const evs_model* m, evs_state* s, int M, int splits, const float* scale, int capture_slot,
-                        int T, cudaStream_t st);
+// partial sums a residual + RMSNorm adds, rank by rank in rank order: buf[r] + split x M x d fp32;
+// for R > 1 the kernel first waits (bounded) until every rank's flag has reached epoch
+struct TpPartials {
+  const float* buf[EVS_TP_MAX];
+  const long long* flag[EVS_TP_MAX];
+  int R;
+  long long epoch;
+};
+int launch_res_add_norm(const evs_model* m, evs_state* s, int M, int splits, const TpPartials& parts,
+                        const float* scale, int capture_slot, int T, cudaStream_t st);
+// publish this rank's partial sums of reduction `epoch` to the peers (after the producing kernel)
+int launch_tp_signal(evs_state* s, long long epoch, cudaStream_t st);
 int launch_swiglu(const evs_model* m, evs_state* s, int M, int splits, cudaStream_t st);
 // logits rows go to out[(b * out_T + t0 + t) * V] (or out[b * V] for the last row when last_only)
 int launch_logits(const evs_model* m, evs_state* s, int M, int T, int splits, float* logits, int out_T, int t0,

@@ -82,11 +82,32 @@ __device__ inline void store4(TD* dst, float4 v) {
 
 template <typename TD>
 __global__ void __cluster_dims__(NORM_CL, 1, 1) __launch_bounds__(NORM_THREADS)
-    res_add_norm_kernel(const float* __restrict__ ws, int splits, int M, float* __restrict__ resid,
+    res_add_norm_kernel(TpPartials parts, int splits, int M, float* __restrict__ resid,
                         const float* __restrict__ scale, TD* __restrict__ act, int ld_act, int d, float eps,
-                        float* __restrict__ ring, int ring_len, const int32_t* __restrict__ len, int T) {
+                        float* __restrict__ ring, int ring_len, const int32_t* __restrict__ len, int T,
+                        EvsDevErr* err) {
   pdl_trigger();
   pdl_wait();
+  if (parts.R > 1) {
+    // every rank's partial sums of this reduction are published once its flag reaches the epoch
+    __shared__ int ok;
+    if (threadIdx.x == 0) {
+      ok = 1;
+      for (int r = 0; r < parts.R; ++r) {
+        if (ld_acquire_sys(parts.flag[r]) >= parts.epoch) continue;
+        const uint64_t t0 = globaltimer_ns();
+        while (ld_acquire_sys(parts.flag[r]) < parts.epoch) {
+          if (globaltimer_ns() - t0 > EVS_WAIT_LIMIT_NS) {
+            evs_record_error(err, EVS_ETIMEOUT, EVS_K_ROW, 1000 + r);
+            ok = 0;
+            break;
+          }
+        }
+      }
+    }
+    __syncthreads();
+    (void)ok;  // on a timeout the sums below use whatever the buffers hold; the error word reports it
+  }
   __shared__ float red[NORM_THREADS / 32];
   __shared__ float cta_ss;
   cg::cluster_group cluster = cg::this_cluster();
@@ -108,12 +129,16 @@ __global__ void __cluster_dims__(NORM_CL, 1, 1) __launch_bounds__(NORM_THREADS)
     if (c4 < n4) {
       const int c = c_base + c4 * 4;
       float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int sp = 0; sp < splits; ++sp) {
-        const float4 w = *reinterpret_cast<const float4*>(ws + (static_cast<size_t>(sp) * M + row) * d + c);
-        acc.x += w.x;
-        acc.y += w.y;
-        acc.z += w.z;
-        acc.w += w.w;
+      for (int r = 0; r < parts.R; ++r) {  // ranks in rank order, each rank's splits in split order
+        const float* ws = parts.buf[r];
+        for (int sp = 0; sp < splits; ++sp) {
+          const float4* src = reinterpret_cast<const float4*>(ws + (static_cast<size_t>(sp) * M + row) * d + c);
+          const float4 w = parts.R > 1 ? __ldcv(src) : *src;
+          acc.x += w.x;
+          acc.y += w.y;
+          acc.z += w.z;
+          acc.w += w.w;
+        }
       }
       float4* rp = reinterpret_cast<float4*>(resid + static_cast<size_t>(row) * d + c);
       float4 x = *rp;
@@ -217,6 +242,14 @@ __global__ void bookkeeping_kernel(int32_t* len, int32_t* len0, int32_t* iir_cur
   if (b == 0) chunk[0] = retain ? T : 0;
 }
 
+// publish this rank's partial sums (written by the preceding projection) to the peers
+__global__ void tp_signal_kernel(long long* flag, long long epoch) {
+  pdl_trigger();
+  pdl_wait();
+  __threadfence_system();
+  st_release_sys(flag, epoch);
+}
+
 __global__ void poles_kernel(const float* lp, float* p, int n) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) p[i] = expf(lp[i]);
@@ -240,28 +273,28 @@ int launch_embed_norm(const evs_model* m, evs_state* s, const int64_t* ids, int 
   return EVS_OK;
 }
 
-int launch_res_add_norm(const evs_model* m, evs_state* s, int M, int splits, const float* scale, int capture_slot,
-                        int T, cudaStream_t st) {
+int launch_res_add_norm(const evs_model* m, evs_state* s, int M, int splits, const TpPartials& parts,
+                        const float* scale, int capture_slot, int T, cudaStream_t st) {
   const int d = m->cfg.d_model;
   float* ring = capture_slot >= 0 ? s->cap_ring[capture_slot] : nullptr;
   EVS_CHECK_ARG(d % (NORM_CL * 4) == 0 && d <= NORM_CL * NORM_THREADS * 4 * NORM_VPT && s->ld_act % 4 == 0,
                 "d_model must be a multiple of 32 and at most 16384");
+  EVS_CHECK_ARG(parts.R >= 1 && parts.R <= EVS_TP_MAX, "bad partial-sum ranks");
   if (m->cfg.dtype == EVS_DTYPE_BF16)
     EVS_CUDA_TRY(evs_launch(res_add_norm_kernel<__nv_bfloat16>, dim3(NORM_CL, M), dim3(NORM_THREADS), 0, st,
-                            s->use_pdl(), static_cast<const float*>(s->ws), splits, M, s->resid, scale,
-                            static_cast<__nv_bfloat16*>(s->act), s->ld_act, d, m->cfg.eps, ring, s->ring_len,
-                            static_cast<const int32_t*>(s->d_len), T));
+                            s->use_pdl(), parts, splits, M, s->resid, scale, static_cast<__nv_bfloat16*>(s->act),
+                            s->ld_act, d, m->cfg.eps, ring, s->ring_len, static_cast<const int32_t*>(s->d_len), T,
+                            s->d_err));
   else
     EVS_CUDA_TRY(evs_launch(res_add_norm_kernel<float>, dim3(NORM_CL, M), dim3(NORM_THREADS), 0, st, s->use_pdl(),
-                            static_cast<const float*>(s->ws), splits, M, s->resid, scale,
-                            static_cast<float*>(s->act), s->ld_act, d, m->cfg.eps, ring, s->ring_len,
-                            static_cast<const int32_t*>(s->d_len), T));
+                            parts, splits, M, s->resid, scale, static_cast<float*>(s->act), s->ld_act, d, m->cfg.eps,
+                            ring, s->ring_len, static_cast<const int32_t*>(s->d_len), T, s->d_err));
   evs_count_launch(1);
   return EVS_OK;
 }
 
 int launch_swiglu(const evs_model* m, evs_state* s, int M, int splits, cudaStream_t st) {
-  const int F = m->cfg.mlp_inner;
+  const int F = m->Fl;  // this rank's MLP features
   EVS_CHECK_ARG(F % 64 == 0, "mlp_inner must be a multiple of 64");
   dim3 grid((F / 4 + ROW_THREADS - 1) / ROW_THREADS, M);
   if (m->cfg.dtype == EVS_DTYPE_BF16)
@@ -288,6 +321,13 @@ int launch_logits(const evs_model* m, evs_state* s, int M, int T, int splits, fl
 int launch_bookkeeping(evs_state* s, int B, int T, int retain, cudaStream_t st) {
   EVS_CUDA_TRY(evs_launch(bookkeeping_kernel, dim3((B + 127) / 128), dim3(128), 0, st, s->use_pdl(), s->d_len,
                           s->d_len0, s->d_iir_cur, s->d_chunk, B, T, retain));
+  evs_count_launch(1);
+  return EVS_OK;
+}
+
+int launch_tp_signal(evs_state* s, long long epoch, cudaStream_t st) {
+  long long* flag = reinterpret_cast<long long*>(s->tp_base[s->m->tp_rank] + 2 * s->tp_buf_bytes);
+  EVS_CUDA_TRY(evs_launch(tp_signal_kernel, dim3(1), dim3(1), 0, st, s->use_pdl(), flag, epoch));
   evs_count_launch(1);
   return EVS_OK;
 }

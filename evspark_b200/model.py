@@ -60,12 +60,15 @@ class _Config:
 
 class TargetModel:
     def __init__(self, cfg: TargetConfig, weights: dict[str, torch.Tensor], *, capture_layers=(),
-                 device="cuda:0", max_chunk: int = 32):
+                 device="cuda:0", max_chunk: int = 32, tp: tuple[int, int] | None = None):
+        """``tp=(rank, world)`` builds rank ``rank`` of a channel-sharded model: ``weights`` are then this
+        rank's shards (``evspark_b200.tp.shard_target_weights``) and every rank runs the same calls."""
         self.device = require_device(device)
         self.cfg = cfg
         self.config = _Config(cfg)
         self.max_chunk = int(max_chunk)
         self.capture_layers = tuple(int(x) for x in capture_layers)
+        self.tp_rank, self.tp_world = (int(tp[0]), int(tp[1])) if tp else (0, 1)
         if len(self.capture_layers) > 4:
             raise ValueError("at most 4 capture (injection) layers")
         dd = data_dtype(cfg)
@@ -84,6 +87,7 @@ class TargetModel:
             mc.layer_kind[i] = LAYER_CODE[k]
         for j in range(4):
             mc.capture_layers[j] = self.capture_layers[j] if j < len(self.capture_layers) else -1
+        mc.tp_world, mc.tp_rank = self.tp_world, self.tp_rank
         h = C.c_void_p()
         with torch.cuda.device(self.device):
             N.check(N.lib().evs_model_create(C.byref(mc), C.byref(h)), "evs_model_create")
@@ -102,7 +106,14 @@ class TargetModel:
         """Seeded random-init weights (drawn on ``init_on``: 'cpu' to share weights with a CPU
         reference run, 'cuda' for speed at 7B scale)."""
         gen_dev = device if init_on == "cuda" else "cpu"
-        return cls(cfg, init_target_weights(cfg, seed=seed, device=gen_dev), device=device, **kw)
+        tp = kw.get("tp")
+        if tp and int(tp[1]) > 1:
+            from .tp import init_target_weights_sharded
+
+            w = init_target_weights_sharded(cfg, int(tp[0]), int(tp[1]), seed=seed, device=gen_dev)
+        else:
+            w = init_target_weights(cfg, seed=seed, device=gen_dev)
+        return cls(cfg, w, device=device, **kw)
 
     @property
     def handle(self):
@@ -209,6 +220,10 @@ class InferenceParams(dict):
             N.check(N.lib().evs_state_create(model.handle, max_batch, max_seqlen, max_chunk, C.byref(h)),
                     "evs_state_create")
         self._h = h
+        if model.tp_world > 1:  # collective: every rank creates its state in the same order
+            from .tp import connect_state
+
+            connect_state(h, N.lib(), model.tp_world, model.device)
         for k in PARAM_KEYS:
             dict.__setitem__(self, k, _KeyParams(self, k))
 
@@ -360,15 +375,21 @@ class InferenceParams(dict):
         N.check(N.lib().evs_get_device_error(self._h, C.byref(code), C.byref(where), C.byref(info)))
         return code.value, where.value, info.value
 
-    def close(self):
+    def close(self, collective: bool = True):
+        """Free the state.  A channel-sharded state closes collectively (every rank calls close):
+        no rank frees its shared region while a peer may still read it."""
         if getattr(self, "_h", None):
             torch.cuda.synchronize(self.model.device)
+            if self.model.tp_world > 1 and collective:
+                from .tp import disconnect_state
+
+                disconnect_state(self._h, N.lib(), self.model.device)
             N.lib().evs_state_destroy(self._h)
             self._h = None
 
     def __del__(self):
         try:
-            self.close()
+            self.close(collective=False)
         except Exception:
             pass
 

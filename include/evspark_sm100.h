@@ -85,6 +85,13 @@ typedef struct evs_model_config {
   int32_t layer_kind[EVS_MAX_LAYERS];
   /* blocks whose output (residual stream, fp32) feeds the drafter context ring; -1 = unused */
   int32_t capture_layers[4];
+  /* channel sharding over tp_world GPUs (0 or 1 = one GPU).  Rank tp_rank holds d_model/tp_world
+   * Hyena channels (in-projection rows 3h..3h+2, filters, poles), n_heads/tp_world heads and
+   * mlp_inner/tp_world MLP features; out-/o-projection and w3 are row-parallel and their partial
+   * sums are added across ranks by the following residual + RMSNorm.  Norms, embedding and
+   * unembedding are replicated (evspark has no sharded target; this follows the depthwise-filter
+   * channel split of Evo2-40B inference). */
+  int32_t tp_world, tp_rank;
 } evs_model_config;
 
 typedef struct evs_model evs_model;
@@ -134,6 +141,16 @@ EVS_API int evs_state_export(const evs_state* s, int layer, int which, int row, 
 /* device address of the drafter-context ring of capture slot c: [max_batch, ring_len, d] fp32,
  * row P mod ring_len holds the injection-layer output at absolute position P */
 EVS_API int evs_state_capture_ring(const evs_state* s, int c, float** dev_ptr, int* ring_len);
+
+/* ---- channel sharding (tp_world > 1): every rank's state shares one device region (partial
+ * sums of the row-parallel projections, double-buffered, and an epoch flag) with its peers over
+ * CUDA IPC.  Call evs_state_tp_handle on every rank, exchange the 64-byte handles (rank order),
+ * then evs_state_tp_connect on every rank before the first forward.  Before destroying a state,
+ * synchronise, call evs_state_tp_disconnect on every rank, and wait for all ranks to get there.
+ * No reference counterpart: the reference runs one GPU per model (evspark/api.py:94-98). */
+EVS_API int evs_state_tp_handle(const evs_state* s, void* handle64);
+EVS_API int evs_state_tp_connect(evs_state* s, const void* handles, int world);
+EVS_API int evs_state_tp_disconnect(evs_state* s);
 
 /* ---- forward passes ----
  * ids: device int64 [batch, T] (row-major).  logits: device fp32 [batch, T, V] or NULL.
