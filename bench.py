@@ -18,6 +18,11 @@ HBM-bound weight streaming) timed with CUDA events inside the library over the t
 Multi-GPU (torchrun, one process per GPU): every rank decodes its own independent stream
 (different prompt seed) with no collectives; the timing is the max over ranks (weak scaling).
 
+``--config evo2_40b`` on N > 1 GPUs (or ``--tp``) shards the target by channels over the N GPUs:
+every rank runs the same single stream on its share of the Hyena channels, heads and MLP
+features, and the row-parallel partial sums are added across ranks over NVLink inside the
+residual RMSNorm; ``value`` = that one stream's accepted tok/s (strong scaling).
+
 ``--streams S`` switches to multi-stream decoding: every rank decodes S independent streams
 (per-stream prompt and generator seeds) in lockstep batched rounds, one verify forward of
 M = 13·S token rows per round; ``value`` = tokens emitted by all streams of all ranks / the
@@ -27,6 +32,7 @@ slowest rank's device time.
 from __future__ import annotations
 
 import argparse
+import ctypes as C
 import json
 import os
 import subprocess
@@ -243,6 +249,98 @@ def run_streams(args) -> int:
     return 0
 
 
+def run_tp(args) -> int:
+    """One stream on a target channel-sharded over all ranks (config 5: Evo2-40B shape)."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    world, rank, local = dist_setup()
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=device)
+    from evspark_b200 import _native as N
+    from evspark_b200.config import DRAFTERS, target_config
+    from evspark_b200.drafter import DeviceDrafter, layer_index
+    from evspark_b200.model import TargetModel
+    from evspark_b200.ranks import combine_timing
+    from evspark_b200.specdec.block.driver import prefill
+    from evspark_b200.specdec.block.loop import spec_round
+    from evspark_b200.specdec.block.neural_draft import NeuralDraftModel
+    from evspark_b200.workload import markov_prompt
+
+    cfg = target_config(args.config)
+    dcfg = DRAFTERS[args.config]
+    L = args.prompt_len or (8192 if args.config == "evo2_40b" else PROMPT_LEN)
+    model = TargetModel.random(cfg, seed=20260820, device=device, init_on="cuda", tp=(rank, world),
+                               capture_layers=tuple(layer_index(n) for n in dcfg.inject_layers))
+    drafter = DeviceDrafter.random(dcfg, seed=20260830, embed=model.weights["embed"], device=device, init_on="cuda")
+    nd = NeuralDraftModel(model, drafter, dcfg.inject_layers)
+    prompt = markov_prompt(L, seed=20260821)  # the same stream on every rank
+    rounds = args.warmup + args.steps
+    ip = model.initialize_inference_params(L + (rounds + 4) * (GAMMA + 1) + 64)
+    nd.capture_begin()
+    t0 = time.perf_counter()
+    prefill(model, torch.as_tensor(prompt[:-1], device=device)[None], ip)
+    torch.cuda.synchronize()
+    prefill_s = time.perf_counter() - t0
+    nd.capture_commit(L - 1)
+    rng = np.random.default_rng(7)
+    state = {"ip": ip, "y": int(prompt[-1])}
+    chunk = torch.empty(1, GAMMA + 1, dtype=torch.int64, device=device)
+
+    def one_round():
+        out = spec_round(model, nd, state["ip"], state["y"], GAMMA, False, rng, 1 << 30, temperature=1.0, top_k=4,
+                         timing=False, chunk=chunk)
+        state["ip"], state["y"] = out.ip, int(out.taken[-1])
+        return len(out.taken)
+
+    for _ in range(args.warmup):
+        one_round()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = ClockSampler(local)
+    n0 = N.lib().evs_launch_count()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    ev0.record()
+    tokens = 0
+    for _ in range(args.steps):
+        tokens += one_round()
+    ev1.record()
+    torch.cuda.synchronize()
+    launches = N.lib().evs_launch_count() - n0
+    clk = clocks.stop()
+    ms, _ = combine_timing(ev0.elapsed_time(ev1), 0.0, device)
+    err = [C.c_int32(), C.c_int32(), C.c_int32()]
+    N.check(N.lib().evs_get_device_error(state["ip"].handle, *[C.byref(e) for e in err]), "evs_get_device_error")
+    if rank == 0:
+        line = {
+            "metric": f"accepted tok/s single-stream {args.config} γ=12, channel-sharded", "value":
+                round(tokens / (ms / 1e3), 3), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": f"{args.config}-shaped single-stream speculative round, target sharded by "
+                                   f"channels over {world} GPU(s) (row-parallel sums added across ranks over "
+                                   "NVLink in the residual RMSNorm), drafter replicated, T=1.0 top_k=4",
+                       "prompt": f"{L}-token order-3 Markov ACGT, GC~0.5", "gamma": GAMMA,
+                       "d_model": cfg.d_model, "n_layers": cfg.n_layers, "parallelism": f"tp{world}",
+                       "l2": "inputs larger than L2: the bf16 weight shards are streamed every round"},
+            "tau": round(tokens / args.steps, 4), "prefill_s": round(prefill_s, 3),
+            "device_error": int(err[0].value), "clocks": clk, "gpu_launches": int(launches),
+        }
+        print(json.dumps(line), flush=True)
+    state["ip"].close()
+    nd.close()
+    model.close()
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
 def run_ours(args) -> int:
     import torch
     import torch.distributed as dist
@@ -446,6 +544,8 @@ def main() -> int:
     ap.add_argument("--config", default="evo2_7b", help="evo2_7b (headline) or evo2_7b_slice (4 blocks, profiling)")
     ap.add_argument("--no-extras", action="store_true", help="time the rounds only (profiling runs)")
     ap.add_argument("--streams", type=int, default=1, help="independent streams per GPU, decoded in batched rounds")
+    ap.add_argument("--tp", action="store_true", help="shard the target by channels over the GPUs (one stream)")
+    ap.add_argument("--prompt-len", type=int, default=0, help="prompt length of --tp runs (default 8192 for 40B)")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
@@ -453,6 +553,8 @@ def main() -> int:
         return run_reference(args)
     if args.streams > 1:
         return run_streams(args)
+    if args.tp or (args.config == "evo2_40b" and int(os.environ.get("WORLD_SIZE", "1")) > 1):
+        return run_tp(args)
     return run_ours(args)
 
 
