@@ -86,6 +86,7 @@ _PROTOS = {
     "evs_rollback": (_I, [_P, _P, _I, _P]),
     "evs_transform": (_I, [_P, _I, _I, _I, C.c_double, _I, _P, _P]),
     "evs_verify": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _P, _P, _P, _P]),
+    "evs_verify_multicand": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _P, _P, _P]),
     "evs_sample": (_I, [_P, _I, _I, _P, _P, _P]),
     "evs_gemm_bf16": (_I, [_P, _P, _P, _I, _I, _I, _I, _P]),
     "evs_gemm_bf16_noalloc": (_I, [_P, _P, _P, _I, _I, _I, _P]),

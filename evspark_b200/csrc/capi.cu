@@ -614,7 +614,7 @@ namespace {
 int copy_row(evs_state* s, int src, int dst, cudaStream_t st) {
   const evs_model* m = s->m;
   const evs_model_config& c = m->cfg;
-  const int d = c.d_model;
+  const int d = m->dl;  // this rank's channels (the capture ring below is full width)
   const size_t el = m->elem();
   auto cp = [&](void* base, size_t row_bytes, size_t bytes) -> int {
     char* b = static_cast<char*>(base);
@@ -633,12 +633,12 @@ int copy_row(evs_state* s, int src, int dst, cudaStream_t st) {
       EVS_TRY(cp(hy.s_all, rb, rb));
     }
     if (s->kv[i]) {
-      const size_t pos = 2ull * c.n_heads * c.head_dim * el;
+      const size_t pos = 2ull * m->Hl * c.head_dim * el;
       EVS_TRY(cp(s->kv[i], pos * s->max_seqlen, pos * std::min(s->h_len[src], s->max_seqlen)));
     }
   }
   for (int k = 0; k < m->n_capture; ++k) {
-    const size_t rb = static_cast<size_t>(s->ring_len) * d * 4;
+    const size_t rb = static_cast<size_t>(s->ring_len) * c.d_model * 4;
     EVS_TRY(cp(s->cap_ring[k], rb, rb));
   }
   EVS_TRY(cp(s->d_len, 4, 4));
@@ -724,6 +724,12 @@ int evs_verify(const double* p, const double* q, const int64_t* x, const double*
                int greedy, int32_t* accepted, int64_t* tokens, int32_t* info, cudaStream_t st) {
   EVS_CHECK_ARG(p && x && accepted && tokens && info, "null argument");
   return launch_verify(p, q, x, u, batch, gamma, V, greedy, accepted, tokens, info, st);
+}
+
+int evs_verify_multicand(const double* p, const double* q, const int64_t* x, const double* u, int n_candidates,
+                         int gamma, int V, int greedy, int64_t* tokens, int32_t* info, cudaStream_t st) {
+  EVS_CHECK_ARG(p && x && tokens && info, "null argument");
+  return launch_verify_multicand(p, q, x, u, n_candidates, gamma, V, greedy, tokens, info, st);
 }
 
 int evs_sample(const double* rows, int n, int V, const double* u, int64_t* out, cudaStream_t st) {

@@ -254,7 +254,8 @@ __global__ void __launch_bounds__(256) serial_head_kernel(const float* U, const 
       tok = block_sample_clipped(row, V, u[static_cast<size_t>(b) * g + k], &sc);
     }
     if (threadIdx.x == 0) {
-      if (forced) tok = static_cast<int>(forced[static_cast<size_t>(b) * g + k]);
+      if (forced != nullptr && forced[static_cast<size_t>(b) * g + k] >= 0)  // negative: not forced
+        tok = static_cast<int>(forced[static_cast<size_t>(b) * g + k]);
       tokens[static_cast<size_t>(b) * g + k] = tok;
       prev_ids[static_cast<size_t>(b) * g + k] = prev;
       s_prev = tok;

@@ -178,3 +178,5 @@ int launch_transform(const void* logits, int logits_fp64, int rows, int V, doubl
 int launch_sample(const double* rows, int n, int V, const double* u, int64_t* out, cudaStream_t st);
 int launch_verify(const double* p, const double* q, const int64_t* x, const double* u, int B, int gamma, int V,
                   int greedy, int32_t* accepted, int64_t* tokens, int32_t* info, cudaStream_t st);
+int launch_verify_multicand(const double* p, const double* q, const int64_t* x, const double* u, int B, int gamma,
+                            int V, int greedy, int64_t* tokens, int32_t* info, cudaStream_t st);

@@ -137,6 +137,118 @@ __global__ void __launch_bounds__(256) sample_kernel(const double* __restrict__ 
   if (threadIdx.x == 0) out[r] = idx;
 }
 
+// dst = as_prob_row(src): clip at 0 and normalise (numpy pairwise sum), uniform when the mass is
+// zero or not finite.  src may be global or shared; dst shared.  Whole block.
+__device__ inline void as_prob_row(const double* src, double* dst, int V, SampScratch* sc) {
+  for (int v = threadIdx.x; v < V; v += blockDim.x) dst[v] = fmax(src[v], 0.0);
+  __syncthreads();
+  const double s = block_pairwise_sum(dst, V, sc);
+  const bool bad = !(s > 0.0) || !isfinite(s);
+  for (int v = threadIdx.x; v < V; v += blockDim.x) dst[v] = bad ? 1.0 / V : dst[v] / s;
+  __syncthreads();
+}
+
+// SpecInfer multi-candidate verification of B drafts of one stream (evspark/specdec/verifier.py:
+// 212-319).  Candidates that agree with the accepted prefix stay live; position i is tested
+// against the first live candidate's target and draft rows; each live candidate in order gets one
+// uniform, and a rejection replaces the working distribution by norm(max(0, work - q_lead)) (p_lead
+// when that mass underflows).  No candidate accepted: sample the working distribution.  All γ
+// accepted: sample the bonus from p_lead[γ].  Greedy: argmax of p_lead[i] (raw logits) against the
+// candidates.  One CTA; u holds up to γB + 1 uniforms, used in order.
+// out tokens [γ+1]; info = {accepted, from_residual, fallback, uniforms consumed, winner}
+__global__ void __launch_bounds__(256) multicand_kernel(const double* __restrict__ p, const double* __restrict__ q,
+                                                        const int64_t* __restrict__ x, const double* __restrict__ u,
+                                                        int B, int gamma, int V, int greedy,
+                                                        int64_t* __restrict__ tokens, int32_t* __restrict__ info) {
+  __shared__ double pi[VMAX], qi[VMAX], work[VMAX], tmp[VMAX];
+  __shared__ SampScratch sc;
+  __shared__ unsigned live_s;
+  __shared__ int chosen_s;
+  const int g1 = gamma + 1;
+  unsigned live = B >= 32 ? 0xffffffffu : ((1u << B) - 1u);
+  int used = 0, acc = gamma, from_res = 0, fb = 0, tok = -1;
+  auto lead_of = [](unsigned m) { return __ffs(static_cast<int>(m)) - 1; };
+  for (int i = 0; i < gamma; ++i) {
+    const int lead = lead_of(live);
+    const double* prow = p + (static_cast<size_t>(lead) * g1 + i) * V;
+    if (greedy) {
+      const int t = block_argmax(prow, V, &sc);
+      unsigned m = 0;
+      for (int b = 0; b < B; ++b)
+        if ((live >> b & 1u) && x[static_cast<size_t>(b) * gamma + i] == t) m |= 1u << b;
+      if (threadIdx.x == 0) tokens[i] = t;
+      if (m == 0) {
+        tok = t;
+        acc = i;
+        from_res = 1;
+        break;
+      }
+      live = m;
+      continue;
+    }
+    as_prob_row(prow, pi, V, &sc);
+    as_prob_row(q + (static_cast<size_t>(lead) * gamma + i) * V, qi, V, &sc);
+    for (int v = threadIdx.x; v < V; v += blockDim.x) work[v] = pi[v];
+    __syncthreads();
+    int chosen = -1;
+    for (int b = 0; b < B; ++b) {
+      if (!(live >> b & 1u)) continue;
+      const int64_t xx = x[static_cast<size_t>(b) * gamma + i];
+      const double r = u[used++];
+      if (xx >= 0 && xx < V && r < accept_prob(work[xx], qi[xx])) {
+        chosen = static_cast<int>(xx);
+        break;
+      }
+      for (int v = threadIdx.x; v < V; v += blockDim.x) tmp[v] = fmax(work[v] - qi[v], 0.0);
+      __syncthreads();
+      const double mass = block_pairwise_sum(tmp, V, &sc);
+      if (!(mass > 0.0) || !isfinite(mass)) {
+        fb = 1;
+        as_prob_row(pi, work, V, &sc);
+        break;
+      }
+      for (int v = threadIdx.x; v < V; v += blockDim.x) work[v] = tmp[v] / mass;
+      __syncthreads();
+    }
+    if (chosen < 0) {
+      // sample_categorical(work): clip, normalise, inverse CDF
+      for (int v = threadIdx.x; v < V; v += blockDim.x) tmp[v] = fmax(work[v], 0.0);
+      __syncthreads();
+      tok = block_sample_clipped(tmp, V, u[used++], &sc);
+      acc = i;
+      from_res = 1;
+      break;
+    }
+    if (threadIdx.x == 0) tokens[i] = chosen;
+    unsigned m = 0;
+    for (int b = 0; b < B; ++b)
+      if ((live >> b & 1u) && x[static_cast<size_t>(b) * gamma + i] == chosen) m |= 1u << b;
+    live = m;
+  }
+  const int lead = lead_of(live);
+  if (tok < 0) {  // every position accepted: the bonus from the lead candidate's last row
+    const double* prow = p + (static_cast<size_t>(lead) * g1 + gamma) * V;
+    if (greedy) {
+      tok = block_argmax(prow, V, &sc);
+    } else {
+      as_prob_row(prow, work, V, &sc);
+      for (int v = threadIdx.x; v < V; v += blockDim.x) tmp[v] = fmax(work[v], 0.0);
+      __syncthreads();
+      tok = block_sample_clipped(tmp, V, u[used++], &sc);
+    }
+  }
+  (void)live_s;
+  (void)chosen_s;
+  if (threadIdx.x == 0) {
+    tokens[acc] = tok;
+    info[0] = acc;
+    info[1] = from_res;
+    info[2] = fb;
+    info[3] = used;
+    info[4] = lead;
+  }
+}
+
 }  // namespace
 
 int launch_transform(const void* logits, int logits_fp64, int rows, int V, double temperature, int top_k,
@@ -156,6 +268,18 @@ int launch_verify(const double* p, const double* q, const int64_t* x, const doub
   EVS_CHECK_ARG(greedy || (q != nullptr && u != nullptr), "sampling verification needs q and uniforms");
   if (B <= 0) return EVS_OK;
   verify_kernel<<<B, 256, 0, st>>>(p, q, x, u, gamma, V, greedy, accepted, tokens, info);
+  EVS_CUDA_TRY(cudaGetLastError());
+  evs_count_launch(1);
+  return EVS_OK;
+}
+
+int launch_verify_multicand(const double* p, const double* q, const int64_t* x, const double* u, int B, int gamma,
+                            int V, int greedy, int64_t* tokens, int32_t* info, cudaStream_t st) {
+  EVS_CHECK_ARG(V > 0 && V <= VMAX, "vocabulary must be in [1, 1024]");
+  EVS_CHECK_ARG(gamma >= 1, "gamma must be >= 1");
+  EVS_CHECK_ARG(B >= 1 && B <= 32, "n_candidates must be in [1, 32]");
+  EVS_CHECK_ARG(greedy || (q != nullptr && u != nullptr), "sampling verification needs q and uniforms");
+  multicand_kernel<<<1, 256, 0, st>>>(p, q, x, u, B, gamma, V, greedy, tokens, info);
   EVS_CUDA_TRY(cudaGetLastError());
   evs_count_launch(1);
   return EVS_OK;

@@ -24,7 +24,8 @@ import torch
 from evspark_b200.specdec.block.driver import block_forward, prefill, step_forward_reference
 from evspark_b200.specdec.block.slice import slice_states_to_accept
 from evspark_b200.specdec.transforms import apply_transform, transform_rows
-from evspark_b200.specdec.verifier import draw_uniforms, rewind_uniforms, sample_categorical, verify_device
+from evspark_b200.specdec.verifier import (draw_uniforms, rewind_uniforms, sample_categorical, verify_device,
+                                           verify_device_multicand)
 
 VOCAB_SIZE = 512
 
@@ -219,14 +220,79 @@ def spec_round(model, draft, ip, y: int, gamma: int, greedy: bool, rng: np.rando
     return RoundOutcome(taken=taken, log=log, ip=ip, logits_rows=rows)
 
 
+def spec_round_multi(model, draft, ip, y: int, gamma: int, greedy: bool, rng: np.random.Generator, remaining: int,
+                     n_candidates: int, *, seen: np.ndarray | None = None, temperature: float = 1.0,
+                     top_k: int | None = 4, record_logits: bool = False) -> RoundOutcome:
+    """One SpecInfer round with ``n_candidates`` drafts (loop.py:396-525): B drafts from anchor y, the
+    state expanded to B rows, one retained block forward of [B, γ+1], multi-candidate verification
+    on the device, rollback of every row to j* and collapse onto the winning row."""
+    device = model.device
+    B = int(n_candidates)
+    V = model.cfg.vocab_size
+    t0 = time.perf_counter()
+    ip.expand(B)
+    if hasattr(draft, "propose_blocks_device"):
+        toks_d, q_d, conf_d = draft.propose_blocks_device(y, gamma, greedy, rng, B, temperature=temperature,
+                                                          top_k=top_k, inference_params_dict=ip)
+    else:
+        rows = [_propose_draft(draft, seen, gamma, greedy, rng, temperature=temperature, top_k=top_k)
+                for _ in range(B)]
+        toks_d = torch.as_tensor(np.stack([t for t, _ in rows]), device=device)
+        q_d = torch.as_tensor(np.stack([q for _, q in rows]), device=device)
+        conf_d = None
+    t_draft = time.perf_counter() - t0
+    chunk = torch.cat([torch.full((B, 1), int(y), dtype=torch.int64, device=device), toks_d], dim=1)
+    if hasattr(draft, "capture_begin"):
+        draft.capture_begin()
+    t0 = time.perf_counter()
+    logits, stash = block_forward(model, chunk, ip, retain=True)
+    t_block = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    state = None
+    if greedy:
+        tv, info = verify_device_multicand(logits.double(), None, toks_d, None, greedy=True)
+    else:
+        p = transform_rows(logits.reshape(B * (gamma + 1), V), temperature, top_k).reshape(B, gamma + 1, V)
+        uv, state = draw_uniforms(rng, gamma * B + 1)
+        tv, info = verify_device_multicand(p, q_d, toks_d, torch.as_tensor(uv, device=device), greedy=False)
+    res = torch.cat([info.to(torch.int64), tv]).cpu().numpy()
+    k, from_residual, fallback, consumed, winner = (int(v) for v in res[:5])
+    tokens = res[5:5 + k + 1]
+    if state is not None:
+        rewind_uniforms(rng, state, consumed)
+    t_verify = time.perf_counter() - t0
+    take = min(k + 1, remaining)
+    taken = tokens[:take].astype(np.int64)
+    j_star = take - 1
+    t0 = time.perf_counter()
+    if not (k == gamma and take == k + 1):
+        slice_states_to_accept(ip, stash, j_star)
+    ip.collapse(winner)
+    t_slice = time.perf_counter() - t0
+    if hasattr(draft, "capture_commit"):
+        draft.capture_commit(j_star + 1, batch_idx=winner)
+    rows_out = []
+    if record_logits:
+        lg = logits[winner].double().cpu().numpy()
+        rows_out = [lg[i] for i in range(take)]
+    conf = None if conf_d is None else [float(c) for c in conf_d[winner].double().cpu().numpy()]
+    log = RoundLog(k=k, replay_len=0, t_draft=t_draft, t_block=t_block, t_verify=t_verify, t_restore_replay=0.0,
+                   from_residual=bool(from_residual), fallback=bool(fallback), n_emitted=take, t_slice=t_slice,
+                   conf=conf, n_candidates=B, winner=winner)
+    return RoundOutcome(taken=taken, log=log, ip=ip, logits_rows=rows_out)
+
+
 def speculative_generate(model, draft, prompt_ids, n_tokens: int, gamma: int, greedy: bool,
                          rng: np.random.Generator, *, temperature: float = 1.0, top_k: int | None = 4,
                          inference_params_dict=None, record_logits: bool = False, rollback: str = "slice",
                          n_candidates: int = 1, timing: bool = True) -> SpecGenerateResult:
     device = model.device
     prompt = _as_prompt_ids(prompt_ids, device)
-    if int(n_candidates) != 1:
-        raise ValueError("n_candidates > 1 (multi-candidate verification) is not available on this path")
+    n_candidates = int(n_candidates)
+    if n_candidates < 1:
+        raise ValueError(f"n_candidates must be >= 1, got {n_candidates}")
+    if n_candidates > 1 and rollback != "slice":
+        raise ValueError("n_candidates > 1 needs rollback='slice' (the winner row is sliced at j*)")
     if n_tokens < 0:
         raise ValueError("n_tokens must be >= 0")
     if gamma < 1:
@@ -250,7 +316,7 @@ def speculative_generate(model, draft, prompt_ids, n_tokens: int, gamma: int, gr
         return SpecGenerateResult(np.empty(0, dtype=np.int64), [], ip, anchor=y, rollback=rollback)
     seen = prompt_np.copy()
     if inference_params_dict is None:
-        ip = model.initialize_inference_params(max_seqlen=L + n_tokens + gamma + 2)
+        ip = model.initialize_inference_params(max_seqlen=L + n_tokens + gamma + 2, max_batch=n_candidates)
         if has_capture:
             draft.capture_begin()
         prefill(model, prompt[:, :-1], ip)
@@ -258,6 +324,9 @@ def speculative_generate(model, draft, prompt_ids, n_tokens: int, gamma: int, gr
             draft.capture_commit(L - 1)
     else:
         ip = inference_params_dict
+        if ip.max_batch < n_candidates:
+            raise ValueError(f"inference state max_batch={ip.max_batch} < n_candidates={n_candidates}: create the "
+                             "state with a larger max_batch")
         if has_capture and int(draft.capture_buffer_len()) != L - 1:
             raise ValueError(f"external state: the drafter's H_ctx buffer is not aligned (对齐): consumed "
                              f"{draft.capture_buffer_len()} != L-1={L - 1}")
@@ -266,9 +335,13 @@ def speculative_generate(model, draft, prompt_ids, n_tokens: int, gamma: int, gr
     logit_rows: list[np.ndarray] = []
     chunk = torch.empty(1, gamma + 1, dtype=torch.int64, device=device)
     while len(emitted) < n_tokens:
-        out = spec_round(model, draft, ip, y, gamma, greedy, rng, n_tokens - len(emitted), seen=seen,
-                         temperature=temperature, top_k=top_k, rollback=rollback, timing=timing,
-                         record_logits=record_logits, chunk=chunk)
+        if n_candidates > 1:
+            out = spec_round_multi(model, draft, ip, y, gamma, greedy, rng, n_tokens - len(emitted), n_candidates,
+                                   seen=seen, temperature=temperature, top_k=top_k, record_logits=record_logits)
+        else:
+            out = spec_round(model, draft, ip, y, gamma, greedy, rng, n_tokens - len(emitted), seen=seen,
+                             temperature=temperature, top_k=top_k, rollback=rollback, timing=timing,
+                             record_logits=record_logits, chunk=chunk)
         ip = out.ip
         if record_logits:
             logit_rows.extend(out.logits_rows)
@@ -354,5 +427,5 @@ def spec_end_kv_len(prompt_len: int, n_emitted: int) -> int:
     return int(prompt_len) + int(n_emitted) - 1
 
 
-__all__ = ["RoundLog", "RoundOutcome", "SpecGenerateResult", "spec_round", "native_greedy_reference", "native_sample_reference",
+__all__ = ["RoundLog", "RoundOutcome", "SpecGenerateResult", "spec_round", "spec_round_multi", "native_greedy_reference", "native_sample_reference",
            "spec_end_kv_len", "speculative_generate", "teacher_force_to_spec_state"]

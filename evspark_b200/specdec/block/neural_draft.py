@@ -79,6 +79,43 @@ class NeuralDraftModel:
                                                 top_k=top_k, uniforms=u)
         return toks, q, conf
 
+    def propose_blocks_device(self, anchor_id: int, gamma: int, greedy: bool, rng, n_candidates: int, *,
+                              temperature=1.0, top_k=4, inference_params_dict=None):
+        """``n_candidates`` drafts from one anchor (neural_draft.py:366-446), on rows 0..B-1 of a state
+        expanded to B identical rows.  Sampling: i.i.d. candidates, γ uniforms each, in candidate order.
+        Greedy: the B most probable first tokens of q_0 (ties: lower id), each followed by argmax steps.
+        Returns device (tokens [B, γ], q fp64 [B, γ, V], conf [B, γ])."""
+        self._check_gamma(gamma)
+        ip = inference_params_dict
+        if ip is None:
+            raise ValueError("the device drafter reads its context from inference_params_dict")
+        B = int(n_candidates)
+        if B < 1:
+            raise ValueError(f"n_candidates must be >= 1, got {B}")
+        dev = self.drafter.device
+        anchors = torch.full((B,), int(anchor_id), dtype=torch.int64, device=dev)
+        if greedy:
+            _, _, _, U = self.drafter.propose(ip, anchors[:1], int(gamma), True, want_U=True)
+            q0 = torch.softmax((U[0, 0] + self.drafter.weights["markov"][int(anchor_id)]).float(), dim=-1)
+            top = torch.sort(-q0, stable=True).indices[:B]
+            forced = torch.full((B, int(gamma)), -1, dtype=torch.int64, device=dev)
+            forced[:, 0] = top
+            toks, q, conf, _ = self.drafter.propose(ip, anchors, int(gamma), True, forced=forced)
+        else:
+            u = torch.as_tensor(np.stack([rng.random(int(gamma)) for _ in range(B)]), device=dev)
+            toks, q, conf, _ = self.drafter.propose(ip, anchors, int(gamma), False, temperature=temperature,
+                                                    top_k=top_k, uniforms=u)
+        return toks, q, conf
+
+    @torch.no_grad()
+    def propose_blocks(self, anchor_id: int, gamma: int, greedy: bool, rng: np.random.Generator, n_candidates: int,
+                       *, temperature: float = 1.0, top_k: int | None = 4, inference_params_dict=None, **_kw):
+        """Host view of ``propose_blocks_device``: (tokens [B, γ], q_rows [B, γ, V], confs [B, γ])."""
+        toks, q, conf = self.propose_blocks_device(anchor_id, gamma, greedy, rng, n_candidates,
+                                                   temperature=temperature, top_k=top_k,
+                                                   inference_params_dict=inference_params_dict)
+        return toks.cpu().numpy(), q.cpu().numpy(), conf.double().cpu().numpy()
+
     @torch.no_grad()
     def propose_block(self, anchor_id: int, gamma: int, greedy: bool, rng: np.random.Generator, *,
                       temperature: float = 1.0, top_k: int | None = 4, inference_params_dict=None, **_kw):

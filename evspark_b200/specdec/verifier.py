@@ -72,6 +72,21 @@ def verify_device(p: torch.Tensor, q: torch.Tensor | None, x: torch.Tensor, u: t
     return acc, toks, info
 
 
+def verify_device_multicand(p: torch.Tensor, q: torch.Tensor | None, x: torch.Tensor, u: torch.Tensor | None,
+                            greedy: bool):
+    """SpecInfer verification of B candidate drafts of one stream on the device:
+    p [B, γ+1, V] fp64 (greedy: raw logits), q [B, γ, V] fp64, x [B, γ] int64, u [γB+1] fp64.
+    Returns device (tokens [γ+1], info [5] = accepted, from_residual, fallback, consumed, winner)."""
+    B, g1, V = p.shape
+    g = g1 - 1
+    toks = torch.empty(g + 1, dtype=torch.int64, device=p.device)
+    info = torch.empty(5, dtype=torch.int32, device=p.device)
+    N.check(N.lib().evs_verify_multicand(p.contiguous().data_ptr(), N.ptr(q), x.contiguous().data_ptr(), N.ptr(u), B, g,
+                                         V, int(greedy), toks.data_ptr(), info.data_ptr(), N.stream_ptr()),
+            "evs_verify_multicand")
+    return toks, info
+
+
 def _result(acc: int, toks: np.ndarray, info: np.ndarray, gamma: int) -> VerifyResult:
     mask = np.zeros(gamma, dtype=bool)
     mask[:acc] = True

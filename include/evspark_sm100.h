@@ -184,6 +184,13 @@ EVS_API int evs_verify(const double* p, const double* q, const int64_t* x, const
 
 /* sample_categorical (verifier.py:37-40) for n rows: clip at 0, normalise, inverse CDF with u[r];
  * rows fp64 [n, V], u fp64 [n], out int64 [n] */
+/* SpecInfer multi-candidate verification of n_candidates drafts of one stream; replaces
+ * verify_round_multicand / verify_round_greedy_multicand (evspark/specdec/verifier.py:212-319).
+ * p [n, γ+1, V] target rows (transformed probabilities; greedy: raw logits), q [n, γ, V], x [n, γ],
+ * u: at least γ·n + 1 uniforms, used in order.  tokens [γ+1] receives the accepted prefix and the
+ * correction / bonus; info = {accepted, from_residual, fallback, uniforms consumed, winner row}. */
+EVS_API int evs_verify_multicand(const double* p, const double* q, const int64_t* x, const double* u, int n_candidates,
+                                 int gamma, int V, int greedy, int64_t* tokens, int32_t* info, cudaStream_t stream);
 EVS_API int evs_sample(const double* rows, int n, int V, const double* u, int64_t* out, cudaStream_t stream);
 
 /* Dense projection used inside evs_forward, exposed for tests and benchmarks:
