@@ -7,6 +7,8 @@
 //   attn_block_kernel    one CTA per (64-key block, head, row) staged in shared memory:
 //                        partial (max, sum, acc) per query
 //   attn_combine_kernel  folds the partials of blocks 0..P/64 in block order
+//   attn_fused_kernel    chunks longer than the split-KV query cap (prefill): the same per-block
+//                        partials and the same fold inside one CTA per (16 queries, head, row)
 //
 // Blocks are aligned at absolute key positions and folded in a fixed order, so a query's result
 // does not depend on how many other queries share the call (native T=1 == verify T=γ+1).
@@ -62,20 +64,182 @@ constexpr int ATTN_THREADS = 128;
 constexpr int QK_Q = QT / (ATTN_THREADS / ATTN_BLOCK);  // queries per thread in the score pass
 constexpr int PV_QMAX = 8;       // queries per thread in P.V (head_dim <= 128)
 
-// shared memory of attn_block_kernel: K rows padded by 16 bytes (conflict-free row-per-thread
-// reads), V rows dense, fp32 queries, scores and per-query stats
+// shared memory of both attention kernels: K rows padded by 16 bytes (conflict-free row-per-thread
+// reads), V rows dense, fp32 queries, scores and per-query stats (+ the running fold of the fused
+// kernel)
 template <typename TD>
 __host__ __device__ constexpr size_t attn_smem_bytes(int Dh) {
   return sizeof(TD) * (static_cast<size_t>(ATTN_BLOCK) * (Dh + 16 / sizeof(TD)) + static_cast<size_t>(ATTN_BLOCK) * Dh) +
-         sizeof(float) * (static_cast<size_t>(QT) * Dh + static_cast<size_t>(QT) * ATTN_BLOCK + 2 * QT);
+         sizeof(float) * (static_cast<size_t>(QT) * Dh + static_cast<size_t>(QT) * ATTN_BLOCK + 6 * QT);
 }
 
-// grid (blocks, H, B), ATTN_THREADS threads.  One CTA stages one ATTN_BLOCK-key block of one head
-// in shared memory with 16-byte asynchronous copies (K and V in two groups, so scores start while
-// V is in flight), then for each group of <= 16 queries computes scores (one key and QK_Q queries
-// per thread), the block's softmax stats (one warp per query) and P.V (two head columns and up to
-// PV_QMAX queries per thread).  Keys past a query's position score -inf and contribute exact
-// zeros, so a query's partial does not depend on how many queries share the call.
+template <typename TD>
+struct AttnSmem {
+  TD* Ks;
+  TD* Vs;
+  float* qs;
+  float* S;
+  float* stt;   // [2 QT]: block max, block sum
+  float* fold;  // [4 QT]: running max, running sum, scale of the old accumulator, scale of the block
+  int kpad;
+  __device__ AttnSmem(unsigned char* raw, int Dh) {
+    constexpr int EPC = 16 / sizeof(TD);
+    kpad = Dh + EPC;
+    Ks = reinterpret_cast<TD*>(raw);
+    Vs = Ks + ATTN_BLOCK * kpad;
+    qs = reinterpret_cast<float*>(Vs + ATTN_BLOCK * Dh);
+    S = qs + QT * Dh;
+    stt = S + QT * ATTN_BLOCK;
+    fold = stt + 2 * QT;
+  }
+};
+
+// 16-byte asynchronous copies of K and V rows [0, nk) of one key block (two commit groups: K, V)
+template <typename TD>
+__device__ __forceinline__ void stage_kv(const AttnSmem<TD>& sm, const TD* kb, size_t HD, int Dh, int nk) {
+  constexpr int EPC = 16 / sizeof(TD);
+  const int cpr = Dh / EPC;
+  for (int i = threadIdx.x; i < nk * cpr; i += ATTN_THREADS) {
+    const int r = i / cpr, c = i - r * cpr;
+    cp_async16(sm.Ks + r * sm.kpad + c * EPC, kb + static_cast<size_t>(r) * 2 * HD + c * EPC);
+  }
+  cp_async_commit();
+  for (int i = threadIdx.x; i < nk * cpr; i += ATTN_THREADS) {
+    const int r = i / cpr, c = i - r * cpr;
+    cp_async16(sm.Vs + r * Dh + c * EPC, kb + static_cast<size_t>(r) * 2 * HD + HD + c * EPC);
+  }
+  cp_async_commit();
+}
+
+// scores of one key block: thread = one key x QK_Q queries; keys past a query's position -> -inf
+template <typename TD>
+__device__ __forceinline__ void block_scores(const AttnSmem<TD>& sm, int Dh, int nk, int nq, int k0, int P0,
+                                             float scale) {
+  constexpr int EPC = 16 / sizeof(TD);
+  const int key = threadIdx.x % ATTN_BLOCK, qh = threadIdx.x / ATTN_BLOCK;
+  float acc[QK_Q];
+#pragma unroll
+  for (int u = 0; u < QK_Q; ++u) acc[u] = 0.f;
+  const int u0 = qh * QK_Q;
+  if (key < nk && u0 < nq) {
+    const TD* kr = sm.Ks + key * sm.kpad;
+    for (int c0 = 0; c0 < Dh; c0 += EPC) {
+      float kf[EPC];
+      if constexpr (sizeof(TD) == 2) {
+        const uint4 raw = *reinterpret_cast<const uint4*>(kr + c0);
+        const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f2 = __bfloat1622float2(h2[e]);
+          kf[2 * e] = f2.x;
+          kf[2 * e + 1] = f2.y;
+        }
+      } else {
+        const float4 raw = *reinterpret_cast<const float4*>(kr + c0);
+        kf[0] = raw.x;
+        kf[1] = raw.y;
+        kf[2] = raw.z;
+        kf[3] = raw.w;
+      }
+#pragma unroll
+      for (int u = 0; u < QK_Q; ++u) {
+        if (u0 + u < nq) {
+          const float* qr = sm.qs + (u0 + u) * Dh + c0;
+#pragma unroll
+          for (int e = 0; e < EPC; e += 4) {
+            const float4 q4 = *reinterpret_cast<const float4*>(qr + e);
+            acc[u] = fmaf(q4.x, kf[e], acc[u]);
+            acc[u] = fmaf(q4.y, kf[e + 1], acc[u]);
+            acc[u] = fmaf(q4.z, kf[e + 2], acc[u]);
+            acc[u] = fmaf(q4.w, kf[e + 3], acc[u]);
+          }
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int u = 0; u < QK_Q; ++u) {
+    const int t = u0 + u;
+    if (t < nq) {
+      const bool vis = key < nk && k0 + key <= P0 + t;  // P0: position of query 0 of the pass
+      sm.S[t * ATTN_BLOCK + key] = vis ? acc[u] * scale : -CUDART_INF_F;
+    }
+  }
+}
+
+// per query (one warp each): block max, p = exp(s - max) in place, block sum -> stt
+template <typename TD>
+__device__ __forceinline__ void block_softmax(const AttnSmem<TD>& sm, int nq) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int t = warp; t < nq; t += ATTN_THREADS / 32) {
+    float* Sr = sm.S + t * ATTN_BLOCK;
+    float mx = -CUDART_INF_F;
+    for (int i = lane; i < ATTN_BLOCK; i += 32) mx = fmaxf(mx, Sr[i]);
+    mx = warp_max(mx);
+    float l = 0.f;
+    for (int i = lane; i < ATTN_BLOCK; i += 32) {
+      const float sv = Sr[i];
+      const float pv = (mx == -CUDART_INF_F || sv == -CUDART_INF_F) ? 0.f : expf(sv - mx);
+      Sr[i] = pv;
+      l += pv;
+    }
+    l = warp_sum(l);
+    if (lane == 0) {
+      sm.stt[2 * t] = mx;
+      sm.stt[2 * t + 1] = l;
+    }
+  }
+}
+
+// P.V of one key block: head columns 2*pi, 2*pi+1 for queries g, g+groups, ...
+template <typename TD>
+__device__ __forceinline__ void block_pv(const AttnSmem<TD>& sm, int Dh, int nk, int nq, float (&a0)[PV_QMAX],
+                                         float (&a1)[PV_QMAX]) {
+  const int npair = Dh / 2, groups = ATTN_THREADS / npair;
+  const int pi = threadIdx.x % npair, g = threadIdx.x / npair;
+#pragma unroll
+  for (int q = 0; q < PV_QMAX; ++q) a0[q] = a1[q] = 0.f;
+  for (int i = 0; i < nk; ++i) {
+    float v0, v1;
+    if constexpr (sizeof(TD) == 2) {
+      const float2 f2 = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(sm.Vs + i * Dh)[pi]);
+      v0 = f2.x;
+      v1 = f2.y;
+    } else {
+      const float2 f2 = reinterpret_cast<const float2*>(sm.Vs + i * Dh)[pi];
+      v0 = f2.x;
+      v1 = f2.y;
+    }
+#pragma unroll
+    for (int q = 0; q < PV_QMAX; ++q) {
+      const int t = g + q * groups;
+      if (t < nq) {
+        const float pv = sm.S[t * ATTN_BLOCK + i];
+        a0[q] = fmaf(pv, v0, a0[q]);
+        a1[q] = fmaf(pv, v1, a1[q]);
+      }
+    }
+  }
+}
+
+// fold of block j's (max mj, sum lj) into the running (m, l): the scales of the old accumulator
+// (a) and of the block (bj); acc' = acc * a + acc_j * bj.  Blocks with mj = -inf are skipped.
+__device__ __forceinline__ void fold_stats(float& m, float& l, float mj, float lj, float& a, float& bj) {
+  const float mn = fmaxf(m, mj);
+  a = m == -CUDART_INF_F ? 0.f : expf(m - mn);
+  bj = expf(mj - mn);
+  l = fmaf(l, a, __fmul_rn(lj, bj));
+  m = mn;
+}
+__device__ __forceinline__ float fold_acc(float acc, float a, float accj, float bj) {
+  return fmaf(acc, a, __fmul_rn(accj, bj));
+}
+
+// Split-KV: grid (blocks, H, B), ATTN_THREADS threads.  One CTA stages one ATTN_BLOCK-key block
+// of one head (K and V in two asynchronous groups, so scores start while V is in flight) and
+// writes, for each query whose position reaches the block, the block's partial (acc, max, sum).
+// Keys past a query's position score -inf and contribute exact zeros, so a query's partial does
+// not depend on how many queries share the call.
 template <typename TD>
 __global__ void __launch_bounds__(ATTN_THREADS) attn_block_kernel(const TD* __restrict__ qrot,
                                                                  const TD* __restrict__ kv,
@@ -91,153 +255,44 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_block_kernel(const TD* __re
   const int k0 = j * ATTN_BLOCK;
   if (k0 >= Lend) return;
   const int nk = min(ATTN_BLOCK, Lend - k0);
-  constexpr int EPC = 16 / sizeof(TD);  // elements per 16-byte chunk
-  const int kpad = Dh + EPC;
-  TD* Ks = reinterpret_cast<TD*>(attn_sm);
-  TD* Vs = Ks + ATTN_BLOCK * kpad;
-  float* qs = reinterpret_cast<float*>(Vs + ATTN_BLOCK * Dh);
-  float* S = qs + QT * Dh;
-  float* stt = S + QT * ATTN_BLOCK;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  AttnSmem<TD> sm(attn_sm, Dh);
   const size_t HD = static_cast<size_t>(H) * Dh;
-  const TD* kb = kv + (static_cast<size_t>(b) * Lmax + k0) * 2 * HD + static_cast<size_t>(h) * Dh;
-  const int cpr = Dh / EPC;  // chunks per row
-  for (int i = tid; i < nk * cpr; i += ATTN_THREADS) {
-    const int r = i / cpr, c = i - r * cpr;
-    cp_async16(Ks + r * kpad + c * EPC, kb + static_cast<size_t>(r) * 2 * HD + c * EPC);
-  }
-  cp_async_commit();
-  for (int i = tid; i < nk * cpr; i += ATTN_THREADS) {
-    const int r = i / cpr, c = i - r * cpr;
-    cp_async16(Vs + r * Dh + c * EPC, kb + static_cast<size_t>(r) * 2 * HD + HD + c * EPC);
-  }
-  cp_async_commit();
+  stage_kv(sm, kv + (static_cast<size_t>(b) * Lmax + k0) * 2 * HD + static_cast<size_t>(h) * Dh, HD, Dh, nk);
   bool k_ready = false, v_ready = false;
-  const int key = tid % ATTN_BLOCK, qh = tid / ATTN_BLOCK;
   const int npair = Dh / 2, groups = ATTN_THREADS / npair;
-  const int pi = tid % npair, g = tid / npair;
+  const int pi = threadIdx.x % npair, g = threadIdx.x / npair;
   for (int tq0 = 0; tq0 < T; tq0 += QT) {
     const int nq = min(QT, T - tq0);
     if (L0 + tq0 + nq - 1 < k0) continue;  // every query of the group precedes the block
-    for (int i = tid; i < nq * Dh; i += ATTN_THREADS) {
+    for (int i = threadIdx.x; i < nq * Dh; i += ATTN_THREADS) {
       const int t = i / Dh, dd = i - t * Dh;
-      qs[i] = to_f32(qrot[static_cast<size_t>(b * T + tq0 + t) * d + h * Dh + dd]);
+      sm.qs[i] = to_f32(qrot[static_cast<size_t>(b * T + tq0 + t) * d + h * Dh + dd]);
     }
     if (!k_ready) {
       cp_async_wait<1>();
       k_ready = true;
     }
     __syncthreads();
-    {  // scores: one key against QK_Q queries of the group
-      float acc[QK_Q];
-#pragma unroll
-      for (int u = 0; u < QK_Q; ++u) acc[u] = 0.f;
-      const int u0 = qh * QK_Q;
-      if (key < nk && u0 < nq) {
-        const TD* kr = Ks + key * kpad;
-        for (int c0 = 0; c0 < Dh; c0 += EPC) {
-          float kf[EPC];
-          if constexpr (sizeof(TD) == 2) {
-            const uint4 raw = *reinterpret_cast<const uint4*>(kr + c0);
-            const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const float2 f2 = __bfloat1622float2(h2[e]);
-              kf[2 * e] = f2.x;
-              kf[2 * e + 1] = f2.y;
-            }
-          } else {
-            const float4 raw = *reinterpret_cast<const float4*>(kr + c0);
-            kf[0] = raw.x;
-            kf[1] = raw.y;
-            kf[2] = raw.z;
-            kf[3] = raw.w;
-          }
-#pragma unroll
-          for (int u = 0; u < QK_Q; ++u) {
-            if (u0 + u < nq) {
-              const float* qr = qs + (u0 + u) * Dh + c0;
-#pragma unroll
-              for (int e = 0; e < EPC; e += 4) {
-                const float4 q4 = *reinterpret_cast<const float4*>(qr + e);
-                acc[u] = fmaf(q4.x, kf[e], acc[u]);
-                acc[u] = fmaf(q4.y, kf[e + 1], acc[u]);
-                acc[u] = fmaf(q4.z, kf[e + 2], acc[u]);
-                acc[u] = fmaf(q4.w, kf[e + 3], acc[u]);
-              }
-            }
-          }
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < QK_Q; ++u) {
-        const int t = u0 + u;
-        if (t < nq) {
-          const bool vis = key < nk && k0 + key <= L0 + tq0 + t;
-          S[t * ATTN_BLOCK + key] = vis ? acc[u] * scale : -CUDART_INF_F;
-        }
-      }
-    }
+    block_scores(sm, Dh, nk, nq, k0, L0 + tq0, scale);
     __syncthreads();
-    for (int t = warp; t < nq; t += ATTN_THREADS / 32) {
-      float* Sr = S + t * ATTN_BLOCK;
-      float mx = -CUDART_INF_F;
-      for (int i = lane; i < ATTN_BLOCK; i += 32) mx = fmaxf(mx, Sr[i]);
-      mx = warp_max(mx);
-      float l = 0.f;
-      for (int i = lane; i < ATTN_BLOCK; i += 32) {
-        const float sv = Sr[i];
-        const float pv = (mx == -CUDART_INF_F || sv == -CUDART_INF_F) ? 0.f : expf(sv - mx);
-        Sr[i] = pv;
-        l += pv;
-      }
-      l = warp_sum(l);
-      if (lane == 0) {
-        stt[2 * t] = mx;
-        stt[2 * t + 1] = l;
-      }
-    }
+    block_softmax(sm, nq);
     if (!v_ready) {
       cp_async_wait<0>();
       v_ready = true;
     }
     __syncthreads();
-    {  // P.V: head columns 2*pi, 2*pi+1 for queries g, g+groups, ...
-      float a0[PV_QMAX], a1[PV_QMAX];
+    float a0[PV_QMAX], a1[PV_QMAX];
+    block_pv(sm, Dh, nk, nq, a0, a1);
 #pragma unroll
-      for (int q = 0; q < PV_QMAX; ++q) a0[q] = a1[q] = 0.f;
-      for (int i = 0; i < nk; ++i) {
-        float v0, v1;
-        if constexpr (sizeof(TD) == 2) {
-          const float2 f2 = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(Vs + i * Dh)[pi]);
-          v0 = f2.x;
-          v1 = f2.y;
-        } else {
-          const float2 f2 = reinterpret_cast<const float2*>(Vs + i * Dh)[pi];
-          v0 = f2.x;
-          v1 = f2.y;
-        }
-#pragma unroll
-        for (int q = 0; q < PV_QMAX; ++q) {
-          const int t = g + q * groups;
-          if (t < nq) {
-            const float pv = S[t * ATTN_BLOCK + i];
-            a0[q] = fmaf(pv, v0, a0[q]);
-            a1[q] = fmaf(pv, v1, a1[q]);
-          }
-        }
-      }
-#pragma unroll
-      for (int q = 0; q < PV_QMAX; ++q) {
-        const int t = g + q * groups;
-        if (t < nq && L0 + tq0 + t >= k0) {
-          float* pd = part + ((((static_cast<size_t>(b) * H + h) * nblk_cap + j) * tcap + tq0 + t) * (Dh + 2));
-          pd[2 * pi] = a0[q];
-          pd[2 * pi + 1] = a1[q];
-          if (pi == 0) {
-            pd[Dh] = stt[2 * t];
-            pd[Dh + 1] = stt[2 * t + 1];
-          }
+    for (int q = 0; q < PV_QMAX; ++q) {
+      const int t = g + q * groups;
+      if (t < nq && L0 + tq0 + t >= k0) {
+        float* pd = part + ((((static_cast<size_t>(b) * H + h) * nblk_cap + j) * tcap + tq0 + t) * (Dh + 2));
+        pd[2 * pi] = a0[q];
+        pd[2 * pi + 1] = a1[q];
+        if (pi == 0) {
+          pd[Dh] = sm.stt[2 * t];
+          pd[Dh + 1] = sm.stt[2 * t + 1];
         }
       }
     }
@@ -273,15 +328,97 @@ __global__ void attn_combine_kernel(const float* __restrict__ part, const int32_
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
       if (j0 + k > jmax || mj[k] == -CUDART_INF_F) continue;
-      const float mn = fmaxf(m, mj[k]);
-      const float a = m == -CUDART_INF_F ? 0.f : expf(m - mn);
-      const float bj = expf(mj[k] - mn);
-      l = l * a + lj[k] * bj;
-      acc = acc * a + aj[k] * bj;
-      m = mn;
+      float a, bj;
+      fold_stats(m, l, mj[k], lj[k], a, bj);
+      acc = fold_acc(acc, a, aj[k], bj);
     }
   }
   out[static_cast<size_t>(row) * ld_out + h * Dh + dd] = from_f32<TD>(acc / l);
+}
+
+// Fused (chunks of more than tcap queries, i.e. prefill): grid (query tiles of QT, H, B).  A CTA
+// walks the key blocks 0 .. (last query's position) / ATTN_BLOCK in order and computes each
+// block's partial with the split-KV kernel's arithmetic (block_scores / block_softmax / block_pv),
+// then folds it as the combine kernel does (fold_stats / fold_acc), so every query's output equals
+// the split-KV + combine result bit for bit, with no partial buffer and any chunk length.
+template <typename TD>
+__global__ void __launch_bounds__(ATTN_THREADS) attn_fused_kernel(const TD* __restrict__ qrot,
+                                                                 const TD* __restrict__ kv,
+                                                                 const int32_t* __restrict__ len, int T, int d,
+                                                                 int H, int Dh, int Lmax, float scale,
+                                                                 TD* __restrict__ out, int ld_out) {
+  pdl_trigger();
+  pdl_wait();
+  extern __shared__ __align__(16) unsigned char attn_sm[];
+  const int tq0 = blockIdx.x * QT, h = blockIdx.y, b = blockIdx.z;
+  const int nq = min(QT, T - tq0);
+  const int L0 = len[b];
+  const int Lend = L0 + T;
+  AttnSmem<TD> sm(attn_sm, Dh);
+  const size_t HD = static_cast<size_t>(H) * Dh;
+  const int npair = Dh / 2, groups = ATTN_THREADS / npair;
+  const int pi = threadIdx.x % npair, g = threadIdx.x / npair;
+  for (int i = threadIdx.x; i < nq * Dh; i += ATTN_THREADS) {
+    const int t = i / Dh, dd = i - t * Dh;
+    sm.qs[i] = to_f32(qrot[static_cast<size_t>(b * T + tq0 + t) * d + h * Dh + dd]);
+  }
+  for (int t = threadIdx.x; t < QT; t += ATTN_THREADS) {
+    sm.fold[4 * t] = -CUDART_INF_F;
+    sm.fold[4 * t + 1] = 0.f;
+  }
+  float c0[PV_QMAX], c1[PV_QMAX];  // running accumulators (the combine kernel's acc)
+#pragma unroll
+  for (int q = 0; q < PV_QMAX; ++q) c0[q] = c1[q] = 0.f;
+  const int jlast = (L0 + tq0 + nq - 1) / ATTN_BLOCK;
+  for (int j = 0; j <= jlast; ++j) {
+    const int k0 = j * ATTN_BLOCK;
+    const int nk = min(ATTN_BLOCK, Lend - k0);
+    __syncthreads();  // the previous block's K/V/S are no longer read
+    stage_kv(sm, kv + (static_cast<size_t>(b) * Lmax + k0) * 2 * HD + static_cast<size_t>(h) * Dh, HD, Dh, nk);
+    cp_async_wait<0>();
+    __syncthreads();
+    block_scores(sm, Dh, nk, nq, k0, L0 + tq0, scale);
+    __syncthreads();
+    block_softmax(sm, nq);
+    __syncthreads();
+    for (int t = threadIdx.x; t < nq; t += ATTN_THREADS) {
+      const float mj = sm.stt[2 * t];
+      float* f = sm.fold + 4 * t;
+      if (mj == -CUDART_INF_F) {  // the block lies past this query: the combine skips it
+        f[2] = 1.f;
+        f[3] = 0.f;
+        continue;
+      }
+      float m = f[0], l = f[1], a, bj;
+      fold_stats(m, l, mj, sm.stt[2 * t + 1], a, bj);
+      f[0] = m;
+      f[1] = l;
+      f[2] = a;
+      f[3] = bj;
+    }
+    __syncthreads();
+    float a0[PV_QMAX], a1[PV_QMAX];
+    block_pv(sm, Dh, nk, nq, a0, a1);
+#pragma unroll
+    for (int q = 0; q < PV_QMAX; ++q) {
+      const int t = g + q * groups;
+      if (t < nq && sm.stt[2 * t] != -CUDART_INF_F) {
+        const float a = sm.fold[4 * t + 2], bj = sm.fold[4 * t + 3];
+        c0[q] = fold_acc(c0[q], a, a0[q], bj);
+        c1[q] = fold_acc(c1[q], a, a1[q], bj);
+      }
+    }
+  }
+#pragma unroll
+  for (int q = 0; q < PV_QMAX; ++q) {
+    const int t = g + q * groups;
+    if (t < nq) {
+      const float l = sm.fold[4 * t + 1];
+      TD* o = out + static_cast<size_t>(b * T + tq0 + t) * ld_out + h * Dh + 2 * pi;
+      o[0] = from_f32<TD>(c0[q] / l);
+      o[1] = from_f32<TD>(c1[q] / l);
+    }
+  }
 }
 
 template <typename TD>
@@ -297,15 +434,26 @@ int launch_attention_t(const evs_model* m, evs_state* s, int layer, int B, int T
                           static_cast<const int32_t*>(s->d_len), s->max_seqlen, qrot, kv, s->d_err));
   const size_t smem = attn_smem_bytes<TD>(Dh);
   EVS_CHECK_RANGE(smem <= 227 * 1024, "head_dim too large for the staged attention block");
+  const float scale = 1.0f / sqrtf(static_cast<float>(Dh));
+  if (T > s->attn_tcap) {
+    EVS_CUDA_TRY(cudaFuncSetAttribute(attn_fused_kernel<TD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      static_cast<int>(smem)));
+    EVS_CUDA_TRY(evs_launch(attn_fused_kernel<TD>, dim3((T + QT - 1) / QT, H, B), dim3(ATTN_THREADS), smem, st, pdl,
+                            static_cast<const TD*>(qrot), static_cast<const TD*>(kv),
+                            static_cast<const int32_t*>(s->d_len), T, d, H, Dh, s->max_seqlen, scale,
+                            static_cast<TD*>(s->act), s->ld_act));
+    evs_count_launch(2);
+    return EVS_OK;
+  }
   EVS_CUDA_TRY(cudaFuncSetAttribute(attn_block_kernel<TD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     static_cast<int>(smem)));
   EVS_CUDA_TRY(evs_launch(attn_block_kernel<TD>, dim3(kv_blocks, H, B), dim3(ATTN_THREADS), smem, st, pdl,
                           static_cast<const TD*>(qrot), static_cast<const TD*>(kv),
                           static_cast<const int32_t*>(s->d_len), T, d, H, Dh, s->max_seqlen, s->attn_blocks,
-                          s->max_chunk, 1.0f / sqrtf(static_cast<float>(Dh)), s->attn_part));
+                          s->attn_tcap, scale, s->attn_part));
   EVS_CUDA_TRY(evs_launch(attn_combine_kernel<TD>, dim3(M, H), dim3(Dh), 0, st, pdl,
                           static_cast<const float*>(s->attn_part), static_cast<const int32_t*>(s->d_len), T, d, H,
-                          Dh, s->attn_blocks, s->max_chunk, static_cast<TD*>(s->act), s->ld_act));
+                          Dh, s->attn_blocks, s->attn_tcap, static_cast<TD*>(s->act), s->ld_act));
   evs_count_launch(3);
   return EVS_OK;
 }

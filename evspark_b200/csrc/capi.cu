@@ -109,6 +109,7 @@ int run_forward(const evs_model* m, evs_state* s, const int64_t* ids, int B, int
   EVS_CHECK_ARG(!tp || s->tp_connected, "channel-sharded state not connected to its peers (evs_state_tp_connect)");
   EVS_CHECK_ARG(B >= 1 && B <= s->max_batch, "batch outside [1, max_batch]");
   EVS_CHECK_ARG(T >= 1 && T <= s->max_chunk, "chunk length outside [1, max_chunk]");
+  EVS_CHECK_ARG(!retain || T <= s->iir_slots, "a retained forward holds at most 64 tokens per row");
   int maxlen = 0;
   for (int b = 0; b < B; ++b) maxlen = std::max(maxlen, s->h_len[b]);
   EVS_CHECK_RANGE(maxlen + T <= s->max_seqlen, "sequence would exceed max_seqlen");
@@ -374,11 +375,13 @@ int evs_state_create(const evs_model* m, int max_batch, int max_seqlen, int max_
   s->cap_outer = next_pow2(c.short_filter_length - 1 + max_chunk);
   s->cap_hcs = next_pow2(c.hcs_filter_length - 1 + max_chunk);
   s->cap_hcm = next_pow2(c.hcm_filter_length - 1 + max_chunk);
-  s->iir_slots = max_chunk;
+  // per-position IIR states are kept only for retained (verify) forwards of at most EVS_RETAIN_MAX
+  s->iir_slots = std::min(max_chunk, EVS_RETAIN_MAX);
   s->ring_len = next_pow2(64 + max_chunk);
   s->m_cap = (max_batch * max_chunk + TOK_TILE - 1) / TOK_TILE * TOK_TILE;
   s->ld_act = std::max(d, F);
   s->attn_blocks = (max_seqlen + ATTN_BLOCK - 1) / ATTN_BLOCK;
+  s->attn_tcap = std::min(max_chunk, ATTN_TCAP);
   s->h_len.assign(max_batch, 0);
   const size_t B = max_batch;
 
@@ -453,7 +456,7 @@ int evs_state_create(const evs_model* m, int max_batch, int max_seqlen, int max_
   const size_t o_act = take(static_cast<size_t>(s->m_cap) * s->ld_act * el);
   const size_t o_ws = take(s->ws_floats * 4);
   const size_t o_qrot = take(static_cast<size_t>(s->m_cap) * dl * el);
-  const size_t o_part = any_mha ? take(B * H * s->attn_blocks * max_chunk * (Dh + 2) * 4) : SIZE_MAX;
+  const size_t o_part = any_mha ? take(B * H * s->attn_blocks * s->attn_tcap * (Dh + 2) * 4) : SIZE_MAX;
   const size_t o_ids = take(static_cast<size_t>(s->m_cap) * 8);
   const size_t o_err = take(sizeof(EvsDevErr));
   void* scr = nullptr;

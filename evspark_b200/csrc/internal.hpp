@@ -13,6 +13,8 @@ constexpr int TOK_TILE = 16;  // token rows per decode tile (MMA N)
 constexpr int GEMM_NT[3] = {16, 64, 128};
 constexpr int ATTN_BLOCK = 64;  // keys per attention partial (aligned at absolute positions)
 constexpr int EVS_TP_MAX = 8;   // channel-sharding ranks
+constexpr int ATTN_TCAP = 16;   // split-KV attention handles chunks of at most this many queries
+constexpr int EVS_RETAIN_MAX = 64;  // tokens per row of a retained forward (per-position IIR slots)
 
 // HBM layout of the per-sequence state ------------------------------------
 //   outer FIR history ring   [B][cap_outer][3d]   data dtype  (positions mod cap_outer)
@@ -77,6 +79,7 @@ struct evs_state {
   int ld_act = 0;     // row stride (elements) of the activation buffer = max(d, F)
   size_t ws_floats = 0;  // capacity of the split-K workspace
   int attn_blocks = 0;   // ceil(max_seqlen / ATTN_BLOCK)
+  int attn_tcap = 0;     // queries per call of the split-KV attention (longer chunks use the fused kernel)
   // per-row bookkeeping (device truth) and a host upper bound of the lengths
   int32_t* d_len = nullptr;      // [B] tokens consumed
   int32_t* d_len0 = nullptr;     // [B] lengths before the last retained forward
@@ -92,7 +95,7 @@ struct evs_state {
   void* act = nullptr;         // [m_cap][ld_act] data dtype: GEMM B operand
   float* ws = nullptr;         // split-K partials [splits][m][n] fp32
   void* qrot = nullptr;        // [m_cap][d] data dtype rotated queries
-  float* attn_part = nullptr;  // [B][H][attn_blocks][max_chunk][Dh+2] fp32
+  float* attn_part = nullptr;  // [B][H][attn_blocks][attn_tcap][Dh+2] fp32
   int64_t* ids_scratch = nullptr;  // [m_cap] chunk ids of a strided prefill
   EvsDevErr* d_err = nullptr;
   // channel sharding: partial sums of the row-parallel projections, double-buffered, and an

@@ -177,6 +177,62 @@ def test_tiny_block_equals_step_bitwise(tiny, golden):
             assert torch.equal(ip.export(i, which), ip2.export(i, which))
 
 
+def _prefill_then_block(model, prompt, chunk, max_chunk):
+    from evspark_b200.specdec.block import block_forward, prefill
+
+    ip = model.initialize_inference_params(len(prompt) + 64, max_chunk=max_chunk)
+    pre = prefill(model, torch.tensor(prompt)[None], ip)
+    blk = block_forward(model, torch.tensor(chunk)[None], ip)
+    ip.close()
+    return pre, blk
+
+
+@pytest.mark.parametrize("which", ["tiny", "7b_slice"])
+def test_prefill_chunking_invariant_bitwise(cuda, tiny, which):
+    """Prefilling in 16-token chunks (split-KV attention) and in 64-token chunks (fused attention)
+    gives the same bits at every position, and the same verify block afterwards: the fused kernel
+    reproduces the split-KV partials and their fold exactly, and nothing else depends on chunking."""
+    if which == "tiny":
+        model, _ = tiny
+    else:
+        from evspark_b200.config import EVO2_7B_SLICE
+        from evspark_b200.model import TargetModel
+
+        model = TargetModel.random(EVO2_7B_SLICE, seed=5, device=cuda, init_on="cuda")
+    rng = np.random.default_rng(17)
+    prompt = rng.choice([65, 67, 71, 84], size=150)
+    chunk = rng.choice([65, 67, 71, 84], size=13)
+    pre16, blk16 = _prefill_then_block(model, prompt, chunk, 16)
+    pre64, blk64 = _prefill_then_block(model, prompt, chunk, 64)
+    assert torch.equal(pre16, pre64), (pre16 - pre64).abs().max().item()
+    assert torch.equal(blk16, blk64)
+    if which != "tiny":
+        model.close()
+
+
+def test_tiny_long_prefill_vs_oracle(tiny, oracle_tiny):
+    """2048-token prompt prefilled in 256-token chunks (IIR over long chunks, MR tail carry across
+    chunks, fused attention over 2 k keys), then a verify block: fp64 oracle agreement."""
+    from evspark_b200.specdec.block import block_forward, prefill
+
+    model, _ = tiny
+    rng = np.random.default_rng(23)
+    prompt = rng.choice([65, 67, 71, 84], size=2048)
+    chunk = rng.choice([65, 67, 71, 84], size=13)
+    ip = model.initialize_inference_params(2048 + 64, max_chunk=256)
+    pre = prefill(model, torch.tensor(prompt)[None], ip)
+    got = block_forward(model, torch.tensor(chunk)[None], ip)[0].cpu().double()
+    st = oracle_tiny.init_state(1, 2048 + 64)
+    ref_pre, _, _ = oracle_tiny.forward(prompt[None], st, prefill=True)
+    ref, _, _ = oracle_tiny.forward(chunk[None], st)
+    scale = ref.abs().max().item()
+    err_pre = (pre[0, -1].cpu().double() - ref_pre[0, -1].double()).abs().max().item()
+    err = (got - ref[0].double()).abs().max().item()
+    assert err_pre <= TOL_FP32_REL * scale * 4, err_pre
+    assert err <= TOL_FP32_REL * scale * 4, err
+    ip.close()
+
+
 def test_tiny_slice_equals_replay_bitwise(tiny, golden):
     """Rollback to k gives exactly the state of replaying the first k+1 chunk tokens."""
     from evspark_b200.specdec.block import (block_forward, clone_inference_params, prefill, slice_states_to_accept,
