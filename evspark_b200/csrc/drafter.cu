@@ -43,6 +43,8 @@ struct RingPtrs {
 
 __global__ void gather_ctx_kernel(RingPtrs rings, int n_inject, int ring_len, int H, const int32_t* len, int CW,
                                   float* out) {
+  pdl_trigger();
+  pdl_wait();
   const int j = blockIdx.x, b = blockIdx.y;
   const int L = len[b];
   const int n = min(CW, L);
@@ -62,6 +64,8 @@ __global__ void gather_ctx_kernel(RingPtrs rings, int n_inject, int ring_len, in
 // out = scale * (v / sqrt(mean(v²) + eps)), v = x (+ bias); one CTA per row
 __global__ void bias_rmsnorm_kernel(const float* x, const float* bias, const float* scale, float* out, int d,
                                     float eps) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ float red[33];
   const int row = blockIdx.x;
   const float* xr = x + static_cast<size_t>(row) * d;
@@ -90,6 +94,8 @@ __global__ void bias_rmsnorm_kernel(const float* x, const float* bias, const flo
 // rows b*g + t: embed[t == 0 ? anchor[b] : mask]  or embed[ids[b*g + t]] when ids is given
 __global__ void embed_rows_kernel(const float* embed, int H, const int64_t* anchor, const int64_t* ids, int g,
                                   int mask_id, float* out) {
+  pdl_trigger();
+  pdl_wait();
   const int row = blockIdx.x;
   const int b = row / g, t = row % g;
   const int64_t id = ids ? ids[row] : (t == 0 ? anchor[b] : mask_id);
@@ -100,6 +106,8 @@ __global__ void embed_rows_kernel(const float* embed, int H, const int64_t* anch
 
 // x[row] = (x[row] + bias) + pos[t]   (pos may be null)
 __global__ void bias_pos_kernel(float* x, const float* bias, const float* pos, int g, int d, int rows) {
+  pdl_trigger();
+  pdl_wait();
   const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= static_cast<size_t>(rows) * d) return;
   const int row = static_cast<int>(i / d), c = static_cast<int>(i % d);
@@ -110,6 +118,8 @@ __global__ void bias_pos_kernel(float* x, const float* bias, const float* pos, i
 
 // h += (x (+ bias))
 __global__ void residual_add_kernel(float* h, const float* x, const float* bias, int d, int rows) {
+  pdl_trigger();
+  pdl_wait();
   const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= static_cast<size_t>(rows) * d) return;
   const float v = bias ? x[i] + bias[i % d] : x[i];
@@ -117,6 +127,8 @@ __global__ void residual_add_kernel(float* h, const float* x, const float* bias,
 }
 
 __global__ void bias_silu_kernel(float* x, const float* bias, int n, int rows) {
+  pdl_trigger();
+  pdl_wait();
   const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= static_cast<size_t>(rows) * n) return;
   const float v = x[i] + bias[i % n];
@@ -124,12 +136,16 @@ __global__ void bias_silu_kernel(float* x, const float* bias, int n, int rows) {
 }
 
 __global__ void scale_kernel(float* x, float s, size_t n) {
+  pdl_trigger();
+  pdl_wait();
   const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i < n) x[i] = x[i] * s;
 }
 
 // kv_in[b] = [ctx[b] (CW rows) ; xb[b] (g rows)]
 __global__ void build_kv_kernel(const float* ctx, const float* xb, int CW, int g, int d, float* out) {
+  pdl_trigger();
+  pdl_wait();
   const int j = blockIdx.x, b = blockIdx.y;
   const float* src = j < CW ? ctx + (static_cast<size_t>(b) * CW + j) * d : xb + (static_cast<size_t>(b) * g + j - CW) * d;
   float* dst = out + (static_cast<size_t>(b) * (CW + g) + j) * d;
@@ -140,6 +156,8 @@ __global__ void build_kv_kernel(const float* ctx, const float* xb, int CW, int g
 __global__ void __launch_bounds__(128) draft_attn_kernel(const float* q, const float* kb, const float* vb,
                                                          const int32_t* len, int CW, int g, int d, int heads,
                                                          float* y) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ float sc[256];
   __shared__ float red[8];
   const int t = blockIdx.x, hh = blockIdx.y, b = blockIdx.z;
@@ -184,11 +202,229 @@ __global__ void __launch_bounds__(128) draft_attn_kernel(const float* q, const f
   }
 }
 
+// serial Markov head, one warp per row, for V = 128 * NL (NL = 1, 2, 4).  Lane L holds the 16
+// elements leaf * 128 + j + 8t (leaf = L / 8, j = L % 8, t = 0..15) in registers: exactly the
+// slots of numpy's pairwise sum (8 running partials per 128-element leaf), so sums are formed as
+// lane-local partials in t order -> ((r0+r1)+(r2+r3))+((r4+r5)+(r6+r7)) over the 8 lanes of a leaf
+// -> the leaf tree, and equal numpy's.  Argmax and top-k are warp shuffles (lowest index on ties);
+// only the left-to-right cumulative sum of sampling runs sequentially, in shared memory.
+template <int NL>
+__device__ __forceinline__ double warp_pw_sum(const double (&v)[16], int lane) {
+  double r = 0.0;
+#pragma unroll
+  for (int t = 0; t < 16; ++t) r += v[t];
+  const unsigned full = 0xffffffffu;
+  r = r + __shfl_xor_sync(full, r, 1);
+  r = r + __shfl_xor_sync(full, r, 2);
+  r = r + __shfl_xor_sync(full, r, 4);  // every lane of a leaf: that leaf's sum
+  if (NL >= 2) r = r + __shfl_xor_sync(full, r, 8);
+  if (NL >= 4) r = r + __shfl_xor_sync(full, r, 16);
+  (void)lane;
+  return r;
+}
+
+// index of the max of the row (lowest index on ties); every lane gets it
+__device__ __forceinline__ int warp_argmax16(const double (&v)[16], int base, double* best_out) {
+  double best = v[0];
+  int bi = base;
+#pragma unroll
+  for (int t = 1; t < 16; ++t)
+    if (v[t] > best) {  // indices grow with t: ties keep the lower index
+      best = v[t];
+      bi = base + 8 * t;
+    }
+  const unsigned full = 0xffffffffu;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const double ov = __shfl_xor_sync(full, best, o);
+    const int oi = __shfl_xor_sync(full, bi, o);
+    if (ov > best || (ov == best && oi < bi)) {
+      best = ov;
+      bi = oi;
+    }
+  }
+  if (best_out) *best_out = best;
+  return bi;
+}
+
+// 4 warps: the elementwise fp32/fp64 math of a step is spread over 128 threads (element i on
+// thread i % 128), through shared memory; warp 0 gathers the row into the pairwise-sum layout
+// above (lane L: elements leaf*128 + j + 8t) for the sums, argmax and top-k.
+template <int NL>
+__global__ void __launch_bounds__(128) serial_head_warp_kernel(const float* U, const float* markov,
+                                                              const int64_t* anchor, int g, int greedy,
+                                                              double temperature, int top_k, const double* u,
+                                                              const int64_t* forced, int64_t* tokens, double* qout,
+                                                              int64_t* prev_ids) {
+  pdl_trigger();
+  pdl_wait();
+  constexpr int V = 128 * NL;
+  constexpr int PT = V / 128;  // elements per thread in the elementwise phases
+  __shared__ double row[V];
+  __shared__ float fred[4];
+  __shared__ double dsh[2];
+  __shared__ int ish[1];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, leaf = lane >> 3, j = lane & 7;
+  const bool act = leaf < NL;
+  const int base = act ? leaf * 128 + j : 0;
+  const int b = blockIdx.x;
+  const unsigned full = 0xffffffffu;
+  int prev = static_cast<int>(anchor[b]);
+  for (int k = 0; k < g; ++k) {
+    const float* Ur = U + (static_cast<size_t>(b) * g + k) * V;
+    const float* Br = markov + static_cast<size_t>(prev) * V;
+    // q_k = softmax(U_k + B[prev]) in fp32
+    float lg[PT];
+    float mx = -CUDART_INF_F;
+#pragma unroll
+    for (int s2 = 0; s2 < PT; ++s2) {
+      lg[s2] = Ur[tid + 128 * s2] + Br[tid + 128 * s2];
+      mx = fmaxf(mx, lg[s2]);
+    }
+    mx = warp_max(mx);
+    if (lane == 0) fred[warp] = mx;
+    __syncthreads();
+    mx = fmaxf(fmaxf(fred[0], fred[1]), fmaxf(fred[2], fred[3]));
+    __syncthreads();
+    float ss = 0.f;
+#pragma unroll
+    for (int s2 = 0; s2 < PT; ++s2) {
+      lg[s2] = expf(lg[s2] - mx);
+      ss += lg[s2];
+    }
+    ss = warp_sum(ss);
+    if (lane == 0) fred[warp] = ss;
+    __syncthreads();
+    ss = (fred[0] + fred[1]) + (fred[2] + fred[3]);
+    double* qo = qout + (static_cast<size_t>(b) * g + k) * V;
+    int tok = 0;
+    if (greedy) {
+#pragma unroll
+      for (int s2 = 0; s2 < PT; ++s2) {
+        const double e = static_cast<double>(lg[s2] / ss);
+        row[tid + 128 * s2] = e;
+        qo[tid + 128 * s2] = e;
+      }
+      __syncthreads();
+      if (warp == 0) {
+        double e[16];
+#pragma unroll
+        for (int t = 0; t < 16; ++t) e[t] = act ? row[base + 8 * t] : -CUDART_INF;
+        tok = warp_argmax16(e, base, nullptr);
+        if (lane == 0) ish[0] = tok;
+      }
+      __syncthreads();
+      tok = ish[0];
+    } else {
+      // q' = apply_transform(log q): log on the support, -inf elsewhere, / temperature
+      const bool onehot = temperature <= 0.0;
+#pragma unroll
+      for (int s2 = 0; s2 < PT; ++s2) {
+        const double e = static_cast<double>(lg[s2] / ss);
+        const double x = e > 0.0 ? log(e) : -CUDART_INF;
+        row[tid + 128 * s2] = onehot ? x : x / temperature;
+      }
+      __syncthreads();
+      double p[16];
+      if (warp == 0) {
+        double x[16];
+#pragma unroll
+        for (int t = 0; t < 16; ++t) x[t] = act ? row[base + 8 * t] : -CUDART_INF;
+        double xm;
+        const int am = warp_argmax16(x, base, &xm);
+        if (lane == 0) {
+          dsh[0] = xm;
+          ish[0] = am;
+        }
+      }
+      __syncthreads();
+      if (onehot) {
+        const int am = ish[0];
+#pragma unroll
+        for (int s2 = 0; s2 < PT; ++s2) row[tid + 128 * s2] = (tid + 128 * s2 == am) ? 1.0 : 0.0;
+      } else {
+        const double xm = dsh[0];
+#pragma unroll
+        for (int s2 = 0; s2 < PT; ++s2) row[tid + 128 * s2] = exp(row[tid + 128 * s2] - xm);
+      }
+      __syncthreads();
+      if (warp == 0) {
+#pragma unroll
+        for (int t = 0; t < 16; ++t) p[t] = act ? row[base + 8 * t] : 0.0;
+        if (!onehot) {
+          const double z = warp_pw_sum<NL>(p, lane);
+          const bool bad = !(z > 0.0) || !isfinite(z);
+#pragma unroll
+          for (int t = 0; t < 16; ++t) p[t] = act ? (bad ? 1.0 / V : p[t] / z) : 0.0;
+          if (top_k > 0 && top_k < V) {
+            unsigned keep = 0;
+            double m[16];
+#pragma unroll
+            for (int t = 0; t < 16; ++t) m[t] = act ? p[t] : -CUDART_INF;
+            for (int r = 0; r < top_k; ++r) {
+              const int am = warp_argmax16(m, base, nullptr);
+#pragma unroll
+              for (int t = 0; t < 16; ++t)
+                if (act && base + 8 * t == am) {
+                  keep |= 1u << t;
+                  m[t] = -CUDART_INF;
+                }
+            }
+#pragma unroll
+            for (int t = 0; t < 16; ++t) m[t] = (keep >> t & 1u) ? p[t] : 0.0;
+            const double ms = warp_pw_sum<NL>(m, lane);
+            const bool bad2 = !(ms > 0.0) || !isfinite(ms);
+#pragma unroll
+            for (int t = 0; t < 16; ++t) p[t] = (keep >> t & 1u) ? (bad2 ? 1.0 / top_k : m[t] / ms) : 0.0;
+          }
+        }
+        // the q' row out, then sample_categorical(q'): clip, normalise (pairwise), cumsum, inverse CDF
+        double w[16];
+#pragma unroll
+        for (int t = 0; t < 16; ++t) {
+          if (act) qo[base + 8 * t] = p[t];
+          w[t] = fmax(p[t], 0.0);
+        }
+        const double s = warp_pw_sum<NL>(w, lane);
+        const bool bad = !(s > 0.0) || !isfinite(s);
+        __syncwarp();
+#pragma unroll
+        for (int t = 0; t < 16; ++t)
+          if (act) row[base + 8 * t] = bad ? 1.0 / V : w[t] / s;
+        __syncwarp();
+        if (lane == 0) seq_cumsum(row, V);
+        __syncwarp();
+        const double last = row[V - 1];
+        const double uu = u[static_cast<size_t>(b) * g + k];
+        int cnt = 0;
+#pragma unroll
+        for (int t = 0; t < 16; ++t)
+          if (act && row[base + 8 * t] / last <= uu) ++cnt;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) cnt += __shfl_xor_sync(full, cnt, o);
+        if (lane == 0) ish[0] = cnt < V ? cnt : V - 1;
+      }
+      __syncthreads();
+      tok = ish[0];
+    }
+    if (forced != nullptr && forced[static_cast<size_t>(b) * g + k] >= 0)  // negative: not forced
+      tok = static_cast<int>(forced[static_cast<size_t>(b) * g + k]);
+    if (tid == 0) {
+      tokens[static_cast<size_t>(b) * g + k] = tok;
+      prev_ids[static_cast<size_t>(b) * g + k] = prev;
+    }
+    prev = tok;
+    __syncthreads();  // row / fred / ish are reused by the next step
+  }
+}
+
 // serial Markov head, one CTA per row
 __global__ void __launch_bounds__(256) serial_head_kernel(const float* U, const float* markov, const int64_t* anchor,
                                                           int g, int V, int greedy, double temperature, int top_k,
                                                           const double* u, const int64_t* forced, int64_t* tokens,
                                                           double* qout, int64_t* prev_ids) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ float lg[VMAX];
   __shared__ double e[VMAX], row[VMAX], masked[VMAX];
   __shared__ int keep[VMAX];
@@ -267,6 +503,8 @@ __global__ void __launch_bounds__(256) serial_head_kernel(const float* U, const 
 // conf[row] = sigmoid([h ; pe] · w + bias); one warp per row
 __global__ void conf_kernel(const float* h, const float* pe, const float* w, const float* bias, int d, int rows,
                             float* conf) {
+  pdl_trigger();
+  pdl_wait();
   const int row = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -318,11 +556,11 @@ int64_t drafter_numel(const evs_drafter_config& c, int id) {
 // out[M][N] = X W^T (fp32, split-K partials reduced in split order)
 int sgemm(evs_drafter* dr, const float* W, const float* X, int ldx, float* out, int N, int K, int M,
           cudaStream_t st) {
-  const GemmPlan p = gemm_plan_f32(N, K, M, 0);
+  const GemmPlan p = gemm_plan_f32_drafter(N, K, M);
   EVS_CHECK_RANGE(static_cast<size_t>(p.splits) * M * N <= dr->ws_floats, "drafter workspace too small");
-  if (p.splits == 1) return launch_gemm_simt(W, nullptr, X, ldx, EVS_DTYPE_FP32, p, out, st);
-  EVS_TRY(launch_gemm_simt(W, nullptr, X, ldx, EVS_DTYPE_FP32, p, dr->ws, st));
-  return launch_reduce_splits(dr->ws, p.splits, M, N, nullptr, out, st);
+  if (p.splits == 1) return launch_gemm_simt(W, nullptr, X, ldx, EVS_DTYPE_FP32, p, out, st, true);
+  EVS_TRY(launch_gemm_simt(W, nullptr, X, ldx, EVS_DTYPE_FP32, p, dr->ws, st, true));
+  return launch_reduce_splits(dr->ws, p.splits, M, N, nullptr, out, st, true);
 }
 
 inline unsigned blocks_for(size_t n, int t) { return static_cast<unsigned>((n + t - 1) / t); }
@@ -364,7 +602,7 @@ int evs_drafter_create(const evs_drafter_config* cfg, int max_batch, evs_drafter
   // largest split-K partial buffer over the drafter's projections
   size_t wsf = 0;
   auto need = [&](size_t M_, size_t N_, size_t K_) {
-    const GemmPlan p = gemm_plan_f32(static_cast<int>(N_), static_cast<int>(K_), static_cast<int>(M_), 0);
+    const GemmPlan p = gemm_plan_f32_drafter(static_cast<int>(N_), static_cast<int>(K_), static_cast<int>(M_));
     wsf = std::max(wsf, static_cast<size_t>(p.splits) * M_ * N_);
   };
   need(B * CW, d, nI * H);
@@ -460,10 +698,10 @@ int evs_draft_propose(evs_drafter* dr, const evs_state* s, const int64_t* anchor
   if (c.n_inject > 0) {
     RingPtrs rg;
     for (int k = 0; k < 4; ++k) rg.p[k] = s->cap_ring[k];
-    gather_ctx_kernel<<<dim3(CW, B), 256, 0, st>>>(rg, c.n_inject, s->ring_len, H, s->d_len, CW, dr->ctx_in);
+    EVS_CUDA_TRY(evs_launch(gather_ctx_kernel, dim3(dim3(CW, B)), dim3(256), 0, st, true, rg, c.n_inject, s->ring_len, H, s->d_len, CW, dr->ctx_in));
     EVS_CUDA_TRY(cudaGetLastError());
     EVS_TRY(sgemm(dr, T[EVS_D_CTX_W], dr->ctx_in, c.n_inject * H, dr->kb, d, c.n_inject * H, B * CW, st));
-    bias_rmsnorm_kernel<<<B * CW, 256, 0, st>>>(dr->kb, T[EVS_D_CTX_B], T[EVS_D_CTX_NORM], dr->ctx, d, eps);
+    EVS_CUDA_TRY(evs_launch(bias_rmsnorm_kernel, dim3(B * CW), dim3(256), 0, st, true, dr->kb, T[EVS_D_CTX_B], T[EVS_D_CTX_NORM], dr->ctx, d, eps));
   } else {
     EVS_CUDA_TRY(cudaMemsetAsync(dr->ctx, 0, sizeof(float) * B * CW * d, st));
   }
@@ -471,47 +709,53 @@ int evs_draft_propose(evs_drafter* dr, const evs_state* s, const int64_t* anchor
   const int32_t* ctx_len = c.n_inject > 0 ? s->d_len : reinterpret_cast<const int32_t*>(dr->prev);
   if (c.n_inject == 0) EVS_CUDA_TRY(cudaMemsetAsync(dr->prev, 0, sizeof(int32_t) * B, st));
   // ---- h = in_proj(embed([anchor, MASK...])) + pos ----
-  embed_rows_kernel<<<rows, 256, 0, st>>>(T[EVS_D_EMBED], H, anchor, nullptr, g, c.mask_id, dr->emb);
+  EVS_CUDA_TRY(evs_launch(embed_rows_kernel, dim3(rows), dim3(256), 0, st, true, T[EVS_D_EMBED], H, anchor, nullptr, g, c.mask_id, dr->emb));
   EVS_TRY(sgemm(dr, T[EVS_D_IN_W], dr->emb, H, dr->h, d, H, rows, st));
-  bias_pos_kernel<<<blocks_for(static_cast<size_t>(rows) * d, 256), 256, 0, st>>>(dr->h, T[EVS_D_IN_B], T[EVS_D_POS],
-                                                                                 g, d, rows);
+  EVS_CUDA_TRY(evs_launch(bias_pos_kernel, dim3(blocks_for(static_cast<size_t>(rows) * d, 256)), dim3(256), 0, st, true, dr->h, T[EVS_D_IN_B], T[EVS_D_POS],
+                                                                                 g, d, rows));
   for (int l = 0; l < c.n_layers; ++l) {
     const float* const* L = T + EVS_D_LAYER0 + l * EVS_D_PER_LAYER;
-    bias_rmsnorm_kernel<<<rows, 256, 0, st>>>(dr->h, nullptr, L[EVS_D_LN1], dr->xb, d, eps);
+    EVS_CUDA_TRY(evs_launch(bias_rmsnorm_kernel, dim3(rows), dim3(256), 0, st, true, dr->h, nullptr, L[EVS_D_LN1], dr->xb, d, eps));
     EVS_TRY(sgemm(dr, L[EVS_D_Q], dr->xb, d, dr->q, d, d, rows, st));
-    build_kv_kernel<<<dim3(nk, B), 256, 0, st>>>(dr->ctx, dr->xb, CW, g, d, dr->kv_in);
+    EVS_CUDA_TRY(evs_launch(build_kv_kernel, dim3(dim3(nk, B)), dim3(256), 0, st, true, dr->ctx, dr->xb, CW, g, d, dr->kv_in));
     EVS_TRY(sgemm(dr, L[EVS_D_K], dr->kv_in, d, dr->kb, d, d, B * nk, st));
     EVS_TRY(sgemm(dr, L[EVS_D_V], dr->kv_in, d, dr->vb, d, d, B * nk, st));
-    draft_attn_kernel<<<dim3(g, c.n_heads, B), 128, 0, st>>>(dr->q, dr->kb, dr->vb, ctx_len, CW, g, d, c.n_heads,
-                                                            dr->y);
+    EVS_CUDA_TRY(evs_launch(draft_attn_kernel, dim3(dim3(g, c.n_heads, B)), dim3(128), 0, st, true, dr->q, dr->kb, dr->vb, ctx_len, CW, g, d, c.n_heads,
+                                                            dr->y));
     EVS_TRY(sgemm(dr, L[EVS_D_O], dr->y, d, dr->tmp, d, d, rows, st));
-    residual_add_kernel<<<blocks_for(static_cast<size_t>(rows) * d, 256), 256, 0, st>>>(dr->h, dr->tmp, nullptr, d,
-                                                                                        rows);
-    bias_rmsnorm_kernel<<<rows, 256, 0, st>>>(dr->h, nullptr, L[EVS_D_LN2], dr->xb, d, eps);
+    EVS_CUDA_TRY(evs_launch(residual_add_kernel, dim3(blocks_for(static_cast<size_t>(rows) * d, 256)), dim3(256), 0, st, true, dr->h, dr->tmp, nullptr, d,
+                                                                                        rows));
+    EVS_CUDA_TRY(evs_launch(bias_rmsnorm_kernel, dim3(rows), dim3(256), 0, st, true, dr->h, nullptr, L[EVS_D_LN2], dr->xb, d, eps));
     EVS_TRY(sgemm(dr, L[EVS_D_MLP0_W], dr->xb, d, dr->m1, hid, d, rows, st));
-    bias_silu_kernel<<<blocks_for(static_cast<size_t>(rows) * hid, 256), 256, 0, st>>>(dr->m1, L[EVS_D_MLP0_B], hid,
-                                                                                      rows);
+    EVS_CUDA_TRY(evs_launch(bias_silu_kernel, dim3(blocks_for(static_cast<size_t>(rows) * hid, 256)), dim3(256), 0, st, true, dr->m1, L[EVS_D_MLP0_B], hid,
+                                                                                      rows));
     EVS_TRY(sgemm(dr, L[EVS_D_MLP2_W], dr->m1, hid, dr->tmp, d, hid, rows, st));
-    residual_add_kernel<<<blocks_for(static_cast<size_t>(rows) * d, 256), 256, 0, st>>>(dr->h, dr->tmp,
-                                                                                        L[EVS_D_MLP2_B], d, rows);
+    EVS_CUDA_TRY(evs_launch(residual_add_kernel, dim3(blocks_for(static_cast<size_t>(rows) * d, 256)), dim3(256), 0, st, true, dr->h, dr->tmp,
+                                                                                        L[EVS_D_MLP2_B], d, rows));
   }
   // ---- U = (final_ln(h) out_proj) embedᵀ H^-1/2 ----
-  bias_rmsnorm_kernel<<<rows, 256, 0, st>>>(dr->h, nullptr, T[EVS_D_FINAL_LN], dr->xb, d, eps);
+  EVS_CUDA_TRY(evs_launch(bias_rmsnorm_kernel, dim3(rows), dim3(256), 0, st, true, dr->h, nullptr, T[EVS_D_FINAL_LN], dr->xb, d, eps));
   EVS_TRY(sgemm(dr, T[EVS_D_OUT_W], dr->xb, d, dr->z, H, d, rows, st));
-  bias_pos_kernel<<<blocks_for(static_cast<size_t>(rows) * H, 256), 256, 0, st>>>(dr->z, T[EVS_D_OUT_B], nullptr, g,
-                                                                                 H, rows);
+  EVS_CUDA_TRY(evs_launch(bias_pos_kernel, dim3(blocks_for(static_cast<size_t>(rows) * H, 256)), dim3(256), 0, st, true, dr->z, T[EVS_D_OUT_B], nullptr, g,
+                                                                                 H, rows));
   EVS_TRY(sgemm(dr, T[EVS_D_EMBED], dr->z, H, dr->U, V, H, rows, st));
-  scale_kernel<<<blocks_for(static_cast<size_t>(rows) * V, 256), 256, 0, st>>>(
-      dr->U, 1.0f / sqrtf(static_cast<float>(H)), static_cast<size_t>(rows) * V);
+  EVS_CUDA_TRY(evs_launch(scale_kernel, dim3(blocks_for(static_cast<size_t>(rows) * V, 256)), dim3(256), 0, st, true, 
+      dr->U, 1.0f / sqrtf(static_cast<float>(H)), static_cast<size_t>(rows) * V));
   // ---- serial Markov head ----
-  serial_head_kernel<<<B, 256, 0, st>>>(dr->U, T[EVS_D_MARKOV], anchor, g, V, greedy, temperature, top_k, u, forced,
-                                        tokens, qrows, dr->prev);
+  if (V == 512 || V == 256 || V == 128) {
+    auto head = V == 512 ? serial_head_warp_kernel<4> : (V == 256 ? serial_head_warp_kernel<2> : serial_head_warp_kernel<1>);
+    EVS_CUDA_TRY(evs_launch(head, dim3(B), dim3(128), 0, st, true, dr->U, T[EVS_D_MARKOV], anchor, g, greedy,
+                            temperature, top_k, u, forced, tokens, qrows, dr->prev));
+  } else {
+    EVS_CUDA_TRY(evs_launch(serial_head_kernel, dim3(B), dim3(256), 0, st, true, dr->U, T[EVS_D_MARKOV], anchor, g, V,
+                            greedy, temperature, top_k, u, forced, tokens, qrows, dr->prev));
+  }
   // ---- confidence: σ(conf_w [final_ln(h) ; in_proj(embed(prev))]) ----
-  embed_rows_kernel<<<rows, 256, 0, st>>>(T[EVS_D_EMBED], H, nullptr, dr->prev, g, 0, dr->emb);
+  EVS_CUDA_TRY(evs_launch(embed_rows_kernel, dim3(rows), dim3(256), 0, st, true, T[EVS_D_EMBED], H, nullptr, dr->prev, g, 0, dr->emb));
   EVS_TRY(sgemm(dr, T[EVS_D_IN_W], dr->emb, H, dr->pe, d, H, rows, st));
-  bias_pos_kernel<<<blocks_for(static_cast<size_t>(rows) * d, 256), 256, 0, st>>>(dr->pe, T[EVS_D_IN_B], nullptr, g,
-                                                                                 d, rows);
-  conf_kernel<<<blocks_for(rows, 4), 128, 0, st>>>(dr->xb, dr->pe, T[EVS_D_CONF_W], T[EVS_D_CONF_B], d, rows, conf);
+  EVS_CUDA_TRY(evs_launch(bias_pos_kernel, dim3(blocks_for(static_cast<size_t>(rows) * d, 256)), dim3(256), 0, st, true, dr->pe, T[EVS_D_IN_B], nullptr, g,
+                                                                                 d, rows));
+  EVS_CUDA_TRY(evs_launch(conf_kernel, dim3(blocks_for(rows, 4)), dim3(128), 0, st, true, dr->xb, dr->pe, T[EVS_D_CONF_W], T[EVS_D_CONF_B], d, rows, conf));
   // non-GEMM kernels of this call (the projections count themselves): context gather + norm,
   // embed + bias/pos, 7 per layer, final norm + bias + scale, serial head, conf embed + bias + dot
   evs_count_launch((c.n_inject > 0 ? 2 : 0) + 2 + 7 * c.n_layers + 3 + 4);

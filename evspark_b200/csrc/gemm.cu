@@ -167,15 +167,7 @@ __global__ void __launch_bounds__(SK_WARPS * 32) gemm_skinny_f32_kernel(const fl
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n0 = blockIdx.x * SK_ROWS, sp = blockIdx.y, m0 = blockIdx.z * SK_TOK;
   const int mt = min(SK_TOK, M - m0);
-  const int kb = sp * kc, ke = min(K, kb + kc);
-  const int kw = ke - kb;  // multiple of 4
-  // stage X[m0 .. m0+mt)[kb .. ke) as xs[m][k - kb] (row stride kc)
-  const int c4 = kw / 4;
-  for (int i = threadIdx.x; i < mt * c4; i += blockDim.x) {
-    const int m = i / c4, c = i - m * c4;
-    cp_async16(sk_sm + m * kc + 4 * c, X + static_cast<size_t>(m0 + m) * ldx + kb + 4 * c);
-  }
-  cp_async_commit();
+  const int kb = sp * kc, ke = min(K, kb + kc);  // this CTA's K range, staged SK_KC_MAX columns at a time
   const float* wr[SK_R];
 #pragma unroll
   for (int i = 0; i < SK_R; ++i) {
@@ -193,23 +185,34 @@ __global__ void __launch_bounds__(SK_WARPS * 32) gemm_skinny_f32_kernel(const fl
   for (int i = 0; i < SK_R; ++i)
 #pragma unroll
     for (int m = 0; m < SK_TOK; ++m) acc[i][m] = 0.f;
-  cp_async_wait<0>();
-  __syncthreads();
+  for (int cb = kb; cb < ke; cb += SK_KC_MAX) {
+    const int kw = min(SK_KC_MAX, ke - cb);  // multiple of 4
+    // stage X[m0 .. m0+mt)[cb .. cb+kw) as xs[m][k - cb] (row stride SK_KC_MAX)
+    const int c4 = kw / 4;
+    if (cb != kb) __syncthreads();  // every warp is done with the previous stage
+    for (int i = threadIdx.x; i < mt * c4; i += blockDim.x) {
+      const int m = i / c4, c = i - m * c4;
+      cp_async16(sk_sm + m * SK_KC_MAX + 4 * c, X + static_cast<size_t>(m0 + m) * ldx + cb + 4 * c);
+    }
+    cp_async_commit();
+    cp_async_wait<0>();
+    __syncthreads();
 #pragma unroll 2
-  for (int k = 4 * lane; k < kw; k += 128) {
-    float4 w4[SK_R];
+    for (int k = 4 * lane; k < kw; k += 128) {
+      float4 w4[SK_R];
 #pragma unroll
-    for (int i = 0; i < SK_R; ++i) w4[i] = __ldg(reinterpret_cast<const float4*>(wr[i] + kb + k));
+      for (int i = 0; i < SK_R; ++i) w4[i] = __ldg(reinterpret_cast<const float4*>(wr[i] + cb + k));
 #pragma unroll
-    for (int m = 0; m < SK_TOK; ++m) {
-      if (m < mt) {
-        const float4 x4 = *reinterpret_cast<const float4*>(sk_sm + m * kc + k);
+      for (int m = 0; m < SK_TOK; ++m) {
+        if (m < mt) {
+          const float4 x4 = *reinterpret_cast<const float4*>(sk_sm + m * SK_KC_MAX + k);
 #pragma unroll
-        for (int i = 0; i < SK_R; ++i) {
-          acc[i][m] = fmaf(w4[i].x, x4.x, acc[i][m]);
-          acc[i][m] = fmaf(w4[i].y, x4.y, acc[i][m]);
-          acc[i][m] = fmaf(w4[i].z, x4.z, acc[i][m]);
-          acc[i][m] = fmaf(w4[i].w, x4.w, acc[i][m]);
+          for (int i = 0; i < SK_R; ++i) {
+            acc[i][m] = fmaf(w4[i].x, x4.x, acc[i][m]);
+            acc[i][m] = fmaf(w4[i].y, x4.y, acc[i][m]);
+            acc[i][m] = fmaf(w4[i].z, x4.z, acc[i][m]);
+            acc[i][m] = fmaf(w4[i].w, x4.w, acc[i][m]);
+          }
         }
       }
     }
@@ -237,6 +240,8 @@ __global__ void __launch_bounds__(SK_WARPS * 32) gemm_skinny_f32_kernel(const fl
 
 __global__ void reduce_splits_kernel(const float* __restrict__ ws, int splits, int MN, const float* __restrict__ bias,
                                      int N, float* __restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= MN) return;
   float acc = 0.f;
@@ -326,6 +331,18 @@ GemmPlan gemm_plan_f32(int N, int K, int M, int dual) {
   return p;
 }
 
+// drafter projections: one split (no reduction launch) unless the GEMM has fewer than 64 row tiles
+GemmPlan gemm_plan_f32_drafter(int N, int K, int M) {
+  GemmPlan p{N, K, M, 1, 0};
+  const int tiles = (N + SK_ROWS - 1) / SK_ROWS;
+  int splits = 1;
+  while (tiles * splits < 64 && (K + 128 * (splits + 1) - 1) / (128 * (splits + 1)) >= 1 && splits < K / 128) ++splits;
+  p.kchunk = (K + splits - 1) / splits;
+  p.kchunk = (p.kchunk + 127) / 128 * 128;
+  p.splits = (K + p.kchunk - 1) / p.kchunk;
+  return p;
+}
+
 int gemm_tile_index(int M) { return M <= GEMM_NT[0] ? 0 : (M <= GEMM_NT[1] ? 1 : 2); }
 
 int launch_gemm_tc(const CUtensorMap* tmA, const CUtensorMap* tmA2, const CUtensorMap* tmB, const GemmPlan& p,
@@ -347,15 +364,14 @@ int launch_gemm_simt(const void* W, const void* W2, const void* X, int ldx, int 
   EVS_CHECK_ARG(p.K % 4 == 0 && ldx % 4 == 0 && reinterpret_cast<uintptr_t>(X) % 16 == 0 &&
                     reinterpret_cast<uintptr_t>(W) % 16 == 0,
                 "fp32 projection needs K and the row stride multiples of 4 and 16-byte aligned operands");
-  EVS_CHECK_ARG(p.kchunk > 0 && p.kchunk % 128 == 0 && p.kchunk <= SK_KC_MAX && p.splits * p.kchunk >= p.K,
-                "bad fp32 projection plan");
+  EVS_CHECK_ARG(p.kchunk > 0 && p.kchunk % 128 == 0 && p.splits * p.kchunk >= p.K, "bad fp32 projection plan");
   static bool attr_set = false;
   if (!attr_set) {
     EVS_CUDA_TRY(cudaFuncSetAttribute(gemm_skinny_f32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       static_cast<int>(SK_SMEM)));
     attr_set = true;
   }
-  const size_t smem = std::max(sizeof(float) * SK_TOK * p.kchunk, sizeof(float) * SK_WARPS * SK_R * SK_TOK * 32);
+  const size_t smem = SK_SMEM;
   dim3 grid((p.N + SK_ROWS - 1) / SK_ROWS, p.splits, (p.M + SK_TOK - 1) / SK_TOK);
   EVS_CUDA_TRY(evs_launch(gemm_skinny_f32_kernel, grid, dim3(SK_WARPS * 32), smem, st, pdl,
                           static_cast<const float*>(W), static_cast<const float*>(W2 ? W2 : W),
@@ -364,11 +380,12 @@ int launch_gemm_simt(const void* W, const void* W2, const void* X, int ldx, int 
   return EVS_OK;
 }
 
-int launch_reduce_splits(const float* ws, int splits, int M, int N, const float* bias, float* out, cudaStream_t st) {
+int launch_reduce_splits(const float* ws, int splits, int M, int N, const float* bias, float* out, cudaStream_t st,
+                         bool pdl) {
   const int MN = M * N;
   if (MN <= 0) return EVS_OK;
-  reduce_splits_kernel<<<(MN + 255) / 256, 256, 0, st>>>(ws, splits, MN, bias, N, out);
-  EVS_CUDA_TRY(cudaGetLastError());
+  EVS_CUDA_TRY(evs_launch(reduce_splits_kernel, dim3((MN + 255) / 256), dim3(256), 0, st, pdl, ws, splits, MN, bias,
+                          N, out));
   evs_count_launch(1);
   return EVS_OK;
 }

@@ -131,8 +131,10 @@ struct GemmPlan {
 };
 GemmPlan gemm_plan(const evs_model* m, int N, int K, int M, int dual);
 GemmPlan gemm_plan_f32(int N, int K, int M, int dual);
+GemmPlan gemm_plan_f32_drafter(int N, int K, int M);
 // out[m][n] = sum of the split partials (in split order) + bias[n]
-int launch_reduce_splits(const float* ws, int splits, int M, int N, const float* bias, float* out, cudaStream_t st);
+int launch_reduce_splits(const float* ws, int splits, int M, int N, const float* bias, float* out, cudaStream_t st,
+                         bool pdl = false);
 // pdl: launch with programmatic stream serialization (see pdl_wait)
 // tmB: three maps of the activations with box rows GEMM_NT[0..2]; the tile is chosen from p.M
 int gemm_tile_index(int M);

@@ -164,6 +164,23 @@ __device__ inline int block_argmax(const double* row, int V, SampScratch* sc) {
   return out;
 }
 
+// w[i] <- w[0] + ... + w[i], added left to right (numpy cumsum order), one thread.  Loads are
+// batched 32 at a time so that only the add chain is serial, and zero entries are skipped: adding
+// +0 to a non-negative running sum never changes it, so the result is the same bits.
+__device__ inline void seq_cumsum(double* w, int V) {
+  double c = 0.0;
+  for (int i0 = 0; i0 < V; i0 += 32) {
+    double v[32];
+#pragma unroll
+    for (int k = 0; k < 32; ++k) v[k] = i0 + k < V ? w[i0 + k] : 0.0;
+#pragma unroll
+    for (int k = 0; k < 32; ++k) {
+      if (v[k] != 0.0) c += v[k];
+      if (i0 + k < V) w[i0 + k] = c;
+    }
+  }
+}
+
 // sample_categorical(w, u) with w already clipped at 0 (w is overwritten); whole block
 __device__ inline int block_sample_clipped(double* w, int V, double u, SampScratch* sc) {
   const double s = block_pairwise_sum(w, V, sc);
@@ -171,11 +188,7 @@ __device__ inline int block_sample_clipped(double* w, int V, double u, SampScrat
   for (int i = threadIdx.x; i < V; i += blockDim.x) w[i] = bad ? 1.0 / V : w[i] / s;
   __syncthreads();
   if (threadIdx.x == 0) {  // left-to-right cumulative sum (numpy cumsum order)
-    double c = 0.0;
-    for (int i = 0; i < V; ++i) {
-      c += w[i];
-      w[i] = c;
-    }
+    seq_cumsum(w, V);
     sc->icount = 0;
   }
   __syncthreads();
