@@ -293,6 +293,18 @@ class InferenceParams(dict):
         self.lengths[:B] += T
         return logits
 
+    def rollback_launch(self, k_dev: torch.Tensor) -> None:
+        """Device-side rollback of the last retained forward to the per-row block indices in the int32
+        device tensor ``k_dev`` (no host copy).  The host mirror follows with ``note_rollback``."""
+        N.check(N.lib().evs_rollback(self._h, k_dev.data_ptr(), int(k_dev.numel()), self._stream()), "evs_rollback")
+
+    def note_rollback(self, ks) -> None:
+        """Host mirror of a ``rollback_launch`` whose block indices are now known on the host."""
+        ks = np.asarray(ks, dtype=np.int64).ravel()
+        self.lengths[: ks.size] = self.retained_len0[: ks.size] + ks + 1
+        arr = (C.c_int32 * ks.size)(*[int(x) for x in self.lengths[: ks.size]])
+        N.check(N.lib().evs_state_note_lengths(self._h, arr, ks.size), "evs_state_note_lengths")
+
     def rollback(self, ks: np.ndarray) -> None:
         ks = np.asarray(ks, dtype=np.int64).ravel()
         kd = torch.as_tensor(ks.astype(np.int32), device=self.model.device)

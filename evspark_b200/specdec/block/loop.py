@@ -113,6 +113,72 @@ class RoundOutcome:
     logits_rows: list = field(default_factory=list)
 
 
+class _RoundBuffers:
+    """Pinned host staging and device buffers of the device round, kept with the state."""
+
+    def __init__(self, device, gamma: int):
+        self.gamma = gamma
+        self.chunk = torch.empty(1, gamma + 1, dtype=torch.int64, device=device)
+        self.u_draft_h = torch.empty(gamma, dtype=torch.float64, pin_memory=True)
+        self.u_ver_h = torch.empty(gamma + 1, dtype=torch.float64, pin_memory=True)
+        self.u_draft = torch.empty(gamma, dtype=torch.float64, device=device)
+        self.u_ver = torch.empty(gamma + 1, dtype=torch.float64, device=device)
+        self.res_h = torch.empty(4 + gamma + 1, dtype=torch.int64, pin_memory=True)
+        self.conf_h = torch.empty(gamma, dtype=torch.float32, pin_memory=True)
+
+
+def _spec_round_device(model, draft, ip, y: int, gamma: int, greedy: bool, rng, remaining: int, temperature,
+                       top_k) -> RoundOutcome:
+    """The round of ``spec_round`` with the device drafter and slice rollback, with one host
+    synchronisation: the uniforms go through pinned buffers without waiting, and the rollback takes
+    its block index j* = min(k, remaining - 1) straight from the device verification, so the host
+    waits only for the small result copy (same RNG order, tokens and state as the general path)."""
+    bufs = getattr(ip, "_round_bufs", None)
+    if bufs is None or bufs.gamma != gamma:
+        bufs = ip._round_bufs = _RoundBuffers(model.device, gamma)
+    draft._check_gamma(gamma)
+    chunk = bufs.chunk
+    chunk[0, 0] = int(y)
+    u = None
+    if not greedy:
+        bufs.u_draft_h.numpy()[:] = rng.random(int(gamma))
+        bufs.u_draft.copy_(bufs.u_draft_h, non_blocking=True)
+        u = bufs.u_draft[None]
+    toks_d, q_rows, conf_d, _ = draft.drafter.propose(ip, chunk[:, 0], int(gamma), greedy, temperature=temperature,
+                                                      top_k=top_k, uniforms=u)
+    chunk[0, 1:] = toks_d[0]
+    draft.capture_begin()
+    logits = ip.forward(chunk, retain=True)
+    x = chunk[:, 1:]
+    state = None
+    if greedy:
+        acc, toks_v, info = verify_device(logits.double(), None, x, None, greedy=True)
+    else:
+        p = transform_rows(logits[0], temperature, top_k)[None]
+        uv, state = draw_uniforms(rng, gamma + 1)
+        bufs.u_ver_h.numpy()[:] = uv
+        bufs.u_ver.copy_(bufs.u_ver_h, non_blocking=True)
+        acc, toks_v, info = verify_device(p, q_rows, x, bufs.u_ver[None], greedy=False)
+    ip.rollback_launch(torch.clamp(acc, max=int(remaining) - 1))
+    bufs.res_h.copy_(torch.cat([acc.to(torch.int64), info[0].to(torch.int64), toks_v[0]]), non_blocking=True)
+    bufs.conf_h.copy_(conf_d[0], non_blocking=True)
+    torch.cuda.current_stream(model.device).synchronize()
+    res = bufs.res_h.numpy()
+    k = int(res[0])
+    from_residual, fallback, consumed = bool(res[1]), bool(res[2]), int(res[3])
+    tokens = res[4:4 + k + 1].copy()
+    if state is not None:
+        rewind_uniforms(rng, state, consumed)
+    take = min(k + 1, remaining)
+    j_star = take - 1
+    ip.note_rollback([j_star])
+    draft.capture_commit(j_star + 1)
+    log = RoundLog(k=k, replay_len=0, t_draft=0.0, t_block=0.0, t_verify=0.0, t_restore_replay=0.0,
+                   from_residual=from_residual, fallback=fallback, n_emitted=take,
+                   conf=[float(c) for c in bufs.conf_h.numpy()])
+    return RoundOutcome(taken=tokens[:take].astype(np.int64), log=log, ip=ip)
+
+
 def spec_round(model, draft, ip, y: int, gamma: int, greedy: bool, rng: np.random.Generator, remaining: int, *,
                seen: np.ndarray | None = None, temperature: float = 1.0, top_k: int | None = 4,
                rollback: str = "slice", timing: bool = True, record_logits: bool = False,
@@ -123,6 +189,8 @@ def spec_round(model, draft, ip, y: int, gamma: int, greedy: bool, rng: np.rando
     has_device_draft = hasattr(draft, "propose_device")
     has_propose = hasattr(draft, "propose_block")
     has_capture = hasattr(draft, "capture_begin")
+    if has_device_draft and rollback == "slice" and not timing and not record_logits and hasattr(draft, "drafter"):
+        return _spec_round_device(model, draft, ip, y, gamma, greedy, rng, remaining, temperature, top_k)
     if chunk is None:
         chunk = torch.empty(1, gamma + 1, dtype=torch.int64, device=device)
     snap = None

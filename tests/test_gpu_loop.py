@@ -191,3 +191,31 @@ def test_7b_width_bf16_greedy_spec_equals_native(cuda):
     spec = speculative_generate(model, IdentityDraft(), prompt, 48, 12, greedy=True, rng=np.random.default_rng(0))
     np.testing.assert_array_equal(spec.emitted_ids, nat)
     model.close()
+
+
+def test_single_sync_round_equals_general_round(tiny):
+    """The device round (pinned uniform buffers, rollback index taken from the device verification,
+    one host synchronisation) emits the same tokens and leaves the same state as the general round."""
+    from evspark_b200.config import DRAFTERS
+    from evspark_b200.drafter import DeviceDrafter
+    from evspark_b200.specdec.block.loop import speculative_generate
+    from evspark_b200.specdec.block.neural_draft import NeuralDraftModel
+
+    model, w = tiny
+    dr = DeviceDrafter.random(DRAFTERS["tiny"], embed=w["embed"], device=model.device)
+    nd = NeuralDraftModel(model, dr, ("blocks.2",))
+    prompt = torch.tensor(np.random.default_rng(31).choice([65, 67, 71, 84], size=120))[None]
+    for greedy, seed in ((True, 0), (False, 5), (False, 6)):
+        outs = []
+        for timing in (True, False):
+            nd.capture_reset()
+            spec = speculative_generate(model, nd, prompt, 37, 12, greedy=greedy, rng=np.random.default_rng(seed),
+                                        timing=timing)
+            ip = spec.inference_params_dict
+            outs.append((spec.emitted_ids, [r.k for r in spec.rounds_log], ip.offset, ip.export(0, 0), ip.export(2, 2)))
+            ip.close()
+        (e1, k1, o1, f1, s1), (e2, k2, o2, f2, s2) = outs
+        np.testing.assert_array_equal(e1, e2)
+        assert k1 == k2 and o1 == o2
+        assert torch.equal(f1, f2) and torch.equal(s1, s2)
+    nd.close()
