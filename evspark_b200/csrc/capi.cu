@@ -67,12 +67,14 @@ const void** slot_ptr(LayerDev& L, int slot) {
 // one GEMM: bf16 -> tcgen05 (TMA maps), fp32 -> SIMT
 // out: partial sums [splits][M][N] (s->ws, or a shared buffer of a row-parallel projection)
 int gemm(const evs_model* m, evs_state* s, const CUtensorMap* tA, const CUtensorMap* tA2, const void* W,
-         const void* W2, int N, int K, int M, int dual, float* out, size_t out_floats, cudaStream_t st, int* splits) {
+         const void* W2, int N, int K, int M, int dual, float* out, size_t out_floats, cudaStream_t st, int* splits,
+         const CUtensorMap* tB_override = nullptr) {
   GemmPlan p = gemm_plan(m, N, K, M, dual);
   EVS_CHECK_RANGE(static_cast<size_t>(p.splits) * M * N <= out_floats, "split-K workspace too small");
   *splits = p.splits;
   if (m->cfg.dtype == EVS_DTYPE_BF16) {
-    const CUtensorMap* tB = K == m->cfg.d_model ? s->tm_act_d : (K == m->Fl ? s->tm_act_f : s->tm_act_l);
+    const CUtensorMap* tB =
+        tB_override ? tB_override : (K == m->cfg.d_model ? s->tm_act_d : (K == m->Fl ? s->tm_act_f : s->tm_act_l));
     return launch_gemm_tc(tA, tA2, tB, p, out, s->d_err, st, s->use_pdl());
   }
   return launch_gemm_simt(W, W2, s->act, s->ld_act, m->cfg.dtype, p, out, st, s->use_pdl());
@@ -119,22 +121,23 @@ int run_forward(const evs_model* m, evs_state* s, const int64_t* ids, int B, int
   const int H = m->Hl, Dh = c.head_dim, S = c.state_size;
   int sp = 1;
   // one projection, timed with its algorithmic bytes (weights + activations in + fp32 partials out)
+  const CUtensorMap* w3_act = nullptr;  // set when the w1/w2 projection wrote the fused SwiGLU output
   auto G = [&](const CUtensorMap* tA, const CUtensorMap* tA2, const void* W, const void* W2, int N, int K, int dual,
-               float* out = nullptr, size_t out_floats = 0) {
+               float* out = nullptr, size_t out_floats = 0, const CUtensorMap* tB = nullptr) {
     const GemmPlan pl = gemm_plan(m, N, K, M, dual);
     const double bytes = (static_cast<double>(N) * K + static_cast<double>(M) * K) * el + 4.0 * pl.splits * M * N;
     float* o = out != nullptr ? out : s->ws;
     const size_t of = out != nullptr ? out_floats : s->ws_floats;
     return timed(s, st, EVS_PROF_GEMM, bytes,
-                 [&] { return gemm(m, s, tA, tA2, W, W2, N, K, M, dual, o, of, st, &sp); });
+                 [&] { return gemm(m, s, tA, tA2, W, W2, N, K, M, dual, o, of, st, &sp, tB); });
   };
   // row-parallel projection [d x K] whose partial sums the next residual + RMSNorm adds up: with
   // channel sharding it writes to the shared buffer of reduction `epoch` and signals the peers
   TpPartials parts{};
-  auto RP = [&](const CUtensorMap* tA, const void* W, int K) -> int {
+  auto RP = [&](const CUtensorMap* tA, const void* W, int K, const CUtensorMap* tB = nullptr) -> int {
     parts = TpPartials{};
     if (!tp) {
-      EVS_TRY(G(tA, nullptr, W, nullptr, d, K, 0));
+      EVS_TRY(G(tA, nullptr, W, nullptr, d, K, 0, nullptr, 0, tB));
       parts.R = 1;
       parts.buf[0] = s->ws;
       return EVS_OK;
@@ -142,7 +145,7 @@ int run_forward(const evs_model* m, evs_state* s, const int64_t* ids, int B, int
     const long long epoch = ++s->tp_epoch;
     const size_t boff = static_cast<size_t>(epoch & 1) * s->tp_buf_bytes;
     EVS_TRY(G(tA, nullptr, W, nullptr, d, K, 0, reinterpret_cast<float*>(s->tp_base[m->tp_rank] + boff),
-              s->tp_buf_bytes / sizeof(float)));
+              s->tp_buf_bytes / sizeof(float), tB));
     EVS_TRY(launch_tp_signal(s, epoch, st));
     parts.R = m->tp_world;
     parts.epoch = epoch;
@@ -178,9 +181,21 @@ int run_forward(const evs_model* m, evs_state* s, const int64_t* ids, int B, int
     EVS_TRY(timed(s, st, EVS_PROF_ROW, row_bytes + 4.0 * sp * M * d * parts.R, [&] {
       return launch_res_add_norm(m, s, M, sp, parts, static_cast<const float*>(L.post_norm), -1, T, st);
     }));
-    EVS_TRY(G(&L.tm_w1, &L.tm_w2, L.w1, L.w2, 2 * F, d, 1));
-    EVS_TRY(timed(s, st, EVS_PROF_ROW, 8.0 * sp * M * F + M * F * el, [&] { return launch_swiglu(m, s, M, sp, st); }));
-    EVS_TRY(RP(&L.tm_w3, L.w3, F));
+    if (c.dtype == EVS_DTYPE_BF16 && gemm_plan(m, 2 * F, d, M, 1).splits == 1) {
+      // one split: the w1/w2 projection applies the SwiGLU gate in its epilogue
+      const GemmPlan pl = gemm_plan(m, 2 * F, d, M, 1);
+      const double bytes = (2.0 * F * d + static_cast<double>(M) * d) * el + M * F * el;
+      EVS_TRY(timed(s, st, EVS_PROF_GEMM, bytes, [&] {
+        const CUtensorMap* tB = s->tm_act_d;
+        return launch_gemm_tc(&L.tm_w1, &L.tm_w2, tB, pl, s->ws, s->d_err, st, s->use_pdl(), s->gate, F);
+      }));
+      w3_act = s->tm_gate;
+    } else {
+      w3_act = nullptr;
+      EVS_TRY(G(&L.tm_w1, &L.tm_w2, L.w1, L.w2, 2 * F, d, 1));
+      EVS_TRY(timed(s, st, EVS_PROF_ROW, 8.0 * sp * M * F + M * F * el, [&] { return launch_swiglu(m, s, M, sp, st); }));
+    }
+    EVS_TRY(RP(&L.tm_w3, L.w3, F, w3_act));
     const float* next = static_cast<const float*>(i + 1 < c.n_layers ? m->L[i + 1].pre_norm : m->final_norm);
     EVS_TRY(timed(s, st, EVS_PROF_ROW, row_bytes + 4.0 * sp * M * d * parts.R,
                   [&] { return launch_res_add_norm(m, s, M, sp, parts, next, m->capture_slot(i), T, st); }));
@@ -458,6 +473,7 @@ int evs_state_create(const evs_model* m, int max_batch, int max_seqlen, int max_
   const size_t o_qrot = take(static_cast<size_t>(s->m_cap) * dl * el);
   const size_t o_part = any_mha ? take(B * H * s->attn_blocks * s->attn_tcap * (Dh + 2) * 4) : SIZE_MAX;
   const size_t o_ids = take(static_cast<size_t>(s->m_cap) * 8);
+  const size_t o_gate = c.dtype == EVS_DTYPE_BF16 ? take(static_cast<size_t>(s->m_cap) * F * 2) : SIZE_MAX;
   const size_t o_err = take(sizeof(EvsDevErr));
   void* scr = nullptr;
   if (cudaMalloc(&scr, off) != cudaSuccess) {
@@ -476,6 +492,7 @@ int evs_state_create(const evs_model* m, int max_batch, int max_seqlen, int max_
   s->qrot = base + o_qrot;
   if (o_part != SIZE_MAX) s->attn_part = reinterpret_cast<float*>(base + o_part);
   s->ids_scratch = reinterpret_cast<int64_t*>(base + o_ids);
+  if (o_gate != SIZE_MAX) s->gate = base + o_gate;
   s->d_err = reinterpret_cast<EvsDevErr*>(base + o_err);
   EVS_CUDA_TRY(cudaMemset(pers, 0, s->owned_bytes[0]));
   EVS_CUDA_TRY(cudaMemset(scr, 0, s->owned_bytes[1]));
@@ -498,6 +515,8 @@ int evs_state_create(const evs_model* m, int max_batch, int max_seqlen, int max_
       EVS_TRY(make_tmap_2d_bf16(&s->tm_act_d[t], s->act, d, s->m_cap, ld, GEMM_BK, GEMM_NT[t]));
       EVS_TRY(make_tmap_2d_bf16(&s->tm_act_f[t], s->act, F, s->m_cap, ld, GEMM_BK, GEMM_NT[t]));
       EVS_TRY(make_tmap_2d_bf16(&s->tm_act_l[t], s->act, dl, s->m_cap, ld, GEMM_BK, GEMM_NT[t]));
+      EVS_TRY(make_tmap_2d_bf16(&s->tm_gate[t], s->gate, F, s->m_cap, static_cast<uint64_t>(F) * 2, GEMM_BK,
+                                GEMM_NT[t]));
     }
   }
   EVS_CUDA_TRY(cudaDeviceSynchronize());

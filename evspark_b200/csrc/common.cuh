@@ -79,6 +79,9 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
+// SwiGLU gate silu(a) * c, one expression shared by every kernel that applies it
+__device__ __forceinline__ float swiglu_gate(float a, float c) { return a * (1.0f / (1.0f + expf(-a))) * c; }
+
 // ---------------------------------------------------------------------------
 // mbarrier / TMA / tcgen05 wrappers (inline PTX, sm_100a)
 // ---------------------------------------------------------------------------

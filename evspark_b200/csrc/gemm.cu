@@ -30,7 +30,7 @@ template <int NT>
 __global__ void __launch_bounds__(192, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmA2,
                    const __grid_constant__ CUtensorMap tmB, float* __restrict__ ws, int N, int K, int M, int splits,
-                   int dual, EvsDevErr* err) {
+                   int dual, __nv_bfloat16* __restrict__ act, int ld_act, EvsDevErr* err) {
   using C = TcCfg<NT>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -123,7 +123,32 @@ __global__ void __launch_bounds__(192, 1)
     const bool ok = mbar_wait_bounded(accum, 0, err, EVS_K_GEMM_TC, 3);
     tc_fence_after();
     pdl_wait();  // (already satisfied: the MMAs consumed activations loaded after the wait)
-    if (ok) {
+    if (ok && act != nullptr) {
+      // fused SwiGLU (dual tile, one split): TMEM lanes 0-63 hold w1 features tile*64 + r, lanes
+      // 64-127 the same w2 features; the w2 half goes through the idle stage memory to the w1 half,
+      // which writes silu(g1) * g2 as the bf16 activation of the w3 projection
+      float* g2s = reinterpret_cast<float*>(sA);  // [64][NT + 1]; every stage has been consumed
+      float v[NT];
+#pragma unroll
+      for (int c0 = 0; c0 < NT; c0 += 16)
+        tmem_ld_32x32b_x16(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + c0,
+                           *reinterpret_cast<float(*)[16]>(v + c0));
+      tmem_ld_wait();
+      if (q >= 2) {
+#pragma unroll
+        for (int j = 0; j < NT; ++j) g2s[((q - 2) * 32 + lane) * (NT + 1) + j] = v[j];
+      }
+      asm volatile("bar.sync 1, 128;" ::: "memory");  // the four epilogue warps
+      if (q < 2) {
+        const int f = tile * 64 + q * 32 + lane;
+#pragma unroll
+        for (int j = 0; j < NT; ++j) {
+          const int tok = ttile * NT + j;
+          if (tok < M)
+            act[static_cast<size_t>(tok) * ld_act + f] = __float2bfloat16_rn(swiglu_gate(v[j], g2s[(q * 32 + lane) * (NT + 1) + j]));
+        }
+      }
+    } else if (ok) {
       const int row = tile * GEMM_BM + q * 32 + lane;
 #pragma unroll
       for (int c0 = 0; c0 < NT; c0 += 16) {
@@ -267,7 +292,7 @@ PFN_encodeTiled get_encode() {
 
 template <int NT>
 int launch_tc(const CUtensorMap* tmA, const CUtensorMap* tmA2, const CUtensorMap* tmB, const GemmPlan& p, float* ws,
-              EvsDevErr* err, cudaStream_t st, bool pdl) {
+              EvsDevErr* err, cudaStream_t st, bool pdl, __nv_bfloat16* act, int ld_act) {
   static_assert(NT % 16 == 0 && NT <= 256, "UMMA N");
   using C = TcCfg<NT>;
   static bool attr_set = false;
@@ -277,7 +302,7 @@ int launch_tc(const CUtensorMap* tmA, const CUtensorMap* tmA2, const CUtensorMap
   }
   dim3 grid((p.M + NT - 1) / NT, p.N / GEMM_BM, p.splits);
   EVS_CUDA_TRY(evs_launch(gemm_tc_kernel<NT>, grid, dim3(192), C::SMEM, st, pdl, *tmA, tmA2 ? *tmA2 : *tmA, *tmB,
-                          ws, p.N, p.K, p.M, p.splits, p.dual, err));
+                          ws, p.N, p.K, p.M, p.splits, p.dual, act, ld_act, err));
   evs_count_launch(1);
   return EVS_OK;
 }
@@ -346,14 +371,15 @@ GemmPlan gemm_plan_f32_drafter(int N, int K, int M) {
 int gemm_tile_index(int M) { return M <= GEMM_NT[0] ? 0 : (M <= GEMM_NT[1] ? 1 : 2); }
 
 int launch_gemm_tc(const CUtensorMap* tmA, const CUtensorMap* tmA2, const CUtensorMap* tmB, const GemmPlan& p,
-                   float* ws, EvsDevErr* err, cudaStream_t st, bool pdl) {
+                   float* ws, EvsDevErr* err, cudaStream_t st, bool pdl, void* swiglu_act, int ld_act) {
+  EVS_CHECK_ARG(swiglu_act == nullptr || (p.dual && p.splits == 1), "fused SwiGLU needs the dual tile and one split");
   EVS_CHECK_ARG(p.N % GEMM_BM == 0 && p.K % GEMM_BK == 0, "tcgen05 GEMM needs N % 128 == 0 and K % 64 == 0");
   EVS_CHECK_ARG(p.splits >= 1 && p.splits <= p.K / GEMM_BK, "bad split count");
   if (p.M <= 0) return EVS_OK;
   switch (gemm_tile_index(p.M)) {
-    case 0: return launch_tc<GEMM_NT[0]>(tmA, tmA2, &tmB[0], p, ws, err, st, pdl);
-    case 1: return launch_tc<GEMM_NT[1]>(tmA, tmA2, &tmB[1], p, ws, err, st, pdl);
-    default: return launch_tc<GEMM_NT[2]>(tmA, tmA2, &tmB[2], p, ws, err, st, pdl);
+    case 0: return launch_tc<GEMM_NT[0]>(tmA, tmA2, &tmB[0], p, ws, err, st, pdl, static_cast<__nv_bfloat16*>(swiglu_act), ld_act);
+    case 1: return launch_tc<GEMM_NT[1]>(tmA, tmA2, &tmB[1], p, ws, err, st, pdl, static_cast<__nv_bfloat16*>(swiglu_act), ld_act);
+    default: return launch_tc<GEMM_NT[2]>(tmA, tmA2, &tmB[2], p, ws, err, st, pdl, static_cast<__nv_bfloat16*>(swiglu_act), ld_act);
   }
 }
 

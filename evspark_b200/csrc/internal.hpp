@@ -107,6 +107,10 @@ struct evs_state {
   long long tp_epoch = 0;  // row-parallel reductions issued so far (same count on every rank)
   // activation buffer as GEMM B operand, K = d, K = local F and K = local d, box rows GEMM_NT[i]
   CUtensorMap tm_act_d[3], tm_act_f[3], tm_act_l[3];
+  // bf16: the w1/w2 projection's fused SwiGLU output [m_cap][F] (its own buffer: the projection's
+  // other CTAs still read act while one CTA's epilogue writes), read by w3 through tm_gate
+  void* gate = nullptr;
+  CUtensorMap tm_gate[3];
   // profiling (evs_profile_start / evs_profile_stop)
   struct ProfRec {
     int kind;
@@ -138,8 +142,11 @@ int launch_reduce_splits(const float* ws, int splits, int M, int N, const float*
 // pdl: launch with programmatic stream serialization (see pdl_wait)
 // tmB: three maps of the activations with box rows GEMM_NT[0..2]; the tile is chosen from p.M
 int gemm_tile_index(int M);
+// swiglu_act: with the dual w1/w2 tile and one split, write silu(w1 x) * (w2 x) as bf16 rows of
+// stride ld_act there instead of partial sums to ws
 int launch_gemm_tc(const CUtensorMap* tmA, const CUtensorMap* tmA2, const CUtensorMap* tmB, const GemmPlan& p,
-                   float* ws, EvsDevErr* err, cudaStream_t st, bool pdl = false);
+                   float* ws, EvsDevErr* err, cudaStream_t st, bool pdl = false, void* swiglu_act = nullptr,
+                   int ld_act = 0);
 int launch_gemm_simt(const void* W, const void* W2, const void* X, int ldx, int dtype, const GemmPlan& p, float* ws,
                      cudaStream_t st, bool pdl = false);
 int make_tmap_2d_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t row_stride_bytes,

@@ -207,9 +207,9 @@ __global__ void __launch_bounds__(ROW_THREADS) swiglu_kernel(const float* __rest
     g2.z += c.z;
     g2.w += c.w;
   }
-  auto gate = [](float a, float c) { return a * (1.0f / (1.0f + expf(-a))) * c; };
   store4<TD>(act + static_cast<size_t>(row) * ld_act + f,
-             make_float4(gate(g1.x, g2.x), gate(g1.y, g2.y), gate(g1.z, g2.z), gate(g1.w, g2.w)));
+             make_float4(swiglu_gate(g1.x, g2.x), swiglu_gate(g1.y, g2.y), swiglu_gate(g1.z, g2.z),
+                         swiglu_gate(g1.w, g2.w)));
 }
 
 __global__ void logits_kernel(const float* __restrict__ ws, int splits, int M, int V, int T, int out_T, int t0,
