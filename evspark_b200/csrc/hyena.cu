@@ -20,7 +20,8 @@ constexpr int CH = 32;          // output channels per CTA (96 interleaved in-pr
 constexpr int C3 = 3 * CH;
 constexpr int TS = 32;          // chunk positions per pass
 constexpr int UW = 64;          // outer-FIR input window in shared memory (positions mod UW)
-constexpr int HY_THREADS = 128;
+constexpr int HY_THREADS = 128;      // IIR kernel: 32 channels x 4 pole groups
+constexpr int HY_FIR_THREADS = 512;  // FIR kernel: 16 warps, one chunk position per warp at a time
 
 template <typename TD>
 struct HyArgs {
@@ -166,9 +167,8 @@ __host__ __device__ constexpr int tap_stride(int K) {
 // grid (d / 32, B), 128 threads.  Shared memory: uw[UW][96] f32 | zs[TS][96] f32 | wo[96][K0] f32 |
 // taps[32][tap_stride(K)] f32 | hist[win][32] TD (x1v by position mod win) | x2s[TS][32] f32
 template <typename TD, bool FLIP>
-__global__ void __launch_bounds__(HY_THREADS) hyena_fir_kernel(HyArgs<TD> a, int win) {
+__global__ void __launch_bounds__(HY_FIR_THREADS) hyena_fir_kernel(HyArgs<TD> a, int win) {
   pdl_trigger();
-  pdl_wait();
   extern __shared__ __align__(16) float sm[];
   const int K = a.K, H = K - 1, KS = tap_stride(K), T = a.T;
   float* uw = sm;
@@ -179,9 +179,24 @@ __global__ void __launch_bounds__(HY_THREADS) hyena_fir_kernel(HyArgs<TD> a, int
   float* x2s = reinterpret_cast<float*>(hist + win * CH);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int h0 = blockIdx.x * CH, b = blockIdx.y;
-  const int L0 = a.len[b];
   const int wm = win - 1;
-  // asynchronous copies first: inner-FIR history rows and (K % 4 == 0) the tap rows
+  // the filter taps are weights (no earlier kernel writes them): fetch them before waiting for
+  // the in-projection, asynchronously when K % 4 == 0
+  const float* iw = a.inner_w + static_cast<size_t>(h0) * K;
+  if (K % 4 == 0) {
+    const int k4 = K / 4;
+    for (int i = threadIdx.x; i < CH * k4; i += blockDim.x) {
+      const int cc = i / k4, j = i - cc * k4;
+      cp_async16(taps + cc * KS + 4 * j, iw + cc * K + 4 * j);
+    }
+  } else {
+    batched_copy(CH * K, [&](int i) { return __ldg(iw + i); },
+                 [&](int i, float v) { taps[(i / K) * KS + i % K] = v; });
+  }
+  cp_async_commit();
+  pdl_wait();
+  const int L0 = a.len[b];
+  // inner-FIR history rows, asynchronously
   constexpr int EPC = 16 / sizeof(TD);
   constexpr int RC = CH / EPC;  // 16-byte chunks per history row
   for (int i = threadIdx.x; i < H * RC; i += blockDim.x) {
@@ -191,18 +206,7 @@ __global__ void __launch_bounds__(HY_THREADS) hyena_fir_kernel(HyArgs<TD> a, int
       cp_async16(hist + (P & wm) * CH + c * EPC,
                  a.inner_ring + (static_cast<size_t>(b) * a.cap_i + (P % a.cap_i)) * a.d + h0 + c * EPC);
   }
-  const float* iw = a.inner_w + static_cast<size_t>(h0) * K;
-  if (K % 4 == 0) {
-    const int k4 = K / 4;
-    for (int i = threadIdx.x; i < CH * k4; i += blockDim.x) {
-      const int cc = i / k4, j = i - cc * k4;
-      cp_async16(taps + cc * KS + 4 * j, iw + cc * K + 4 * j);
-    }
-  }
   cp_async_commit();
-  if (K % 4 != 0)
-    batched_copy(CH * K, [&](int i) { return __ldg(iw + i); },
-                 [&](int i, float v) { taps[(i / K) * KS + i % K] = v; });
   outer_stage(a, b, L0, h0, uw, wo);
   const float Dg = FLIP ? a.D[h0 + lane] : 0.f;
   const float* tp = taps + lane * KS;
@@ -225,7 +229,7 @@ __global__ void __launch_bounds__(HY_THREADS) hyena_fir_kernel(HyArgs<TD> a, int
     }
     __syncthreads();
     // inner FIR, lane = channel, one position per warp at a time, ages in descending order
-    for (int t = warp; t < ns; t += HY_THREADS / 32) {
+    for (int t = warp; t < ns; t += HY_FIR_THREADS / 32) {
       const int P = L0 + t0 + t;
       const int cs = min(P, H);
       float z = 0.f;
@@ -431,7 +435,7 @@ int launch_hyena_t(const evs_model* m, evs_state* s, int layer, int B, int T, in
     EVS_CHECK_RANGE(smem <= 220 * 1024, "FIR filter too long for the shared-memory window");
     auto launch = [&](auto kern) -> int {
       EVS_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
-      EVS_CUDA_TRY(evs_launch(kern, grid, dim3(HY_THREADS), smem, st, s->use_pdl(), a, win));
+      EVS_CUDA_TRY(evs_launch(kern, grid, dim3(HY_FIR_THREADS), smem, st, s->use_pdl(), a, win));
       return EVS_OK;
     };
     if (L.kind == EVS_LAYER_HCM)
