@@ -111,6 +111,42 @@ __device__ __forceinline__ void stage_kv(const AttnSmem<TD>& sm, const TD* kb, s
   cp_async_commit();
 }
 
+// nq query rows (head slice of Dh values, row stride ld elements) -> fp32 sm.qs[nq][Dh]: 16-byte
+// loads, up to four per thread in flight before the conversions
+template <typename TD>
+__device__ __forceinline__ void stage_q(const AttnSmem<TD>& sm, const TD* src, size_t ld, int nq, int Dh) {
+  constexpr int EPC = 16 / sizeof(TD);
+  const int cpr = Dh / EPC, n = nq * cpr;
+  for (int i0 = threadIdx.x; i0 < n; i0 += 4 * ATTN_THREADS) {
+    uint4 raw[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int i = i0 + k * ATTN_THREADS;
+      if (i < n) {
+        const int t = i / cpr, c = i - t * cpr;
+        raw[k] = *reinterpret_cast<const uint4*>(src + t * ld + c * EPC);
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int i = i0 + k * ATTN_THREADS;
+      if (i < n) {
+        const int t = i / cpr, c = i - t * cpr;
+        float* dst = sm.qs + t * Dh + c * EPC;
+        if constexpr (sizeof(TD) == 2) {
+          const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw[k]);
+          const float2 f0 = __bfloat1622float2(h2[0]), f1 = __bfloat1622float2(h2[1]);
+          const float2 f2 = __bfloat1622float2(h2[2]), f3 = __bfloat1622float2(h2[3]);
+          reinterpret_cast<float4*>(dst)[0] = make_float4(f0.x, f0.y, f1.x, f1.y);
+          reinterpret_cast<float4*>(dst)[1] = make_float4(f2.x, f2.y, f3.x, f3.y);
+        } else {
+          *reinterpret_cast<uint4*>(dst) = raw[k];
+        }
+      }
+    }
+  }
+}
+
 // scores of one key block: thread = one key x QK_Q queries; keys past a query's position -> -inf
 template <typename TD>
 __device__ __forceinline__ void block_scores(const AttnSmem<TD>& sm, int Dh, int nk, int nq, int k0, int P0,
@@ -264,10 +300,7 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_block_kernel(const TD* __re
   for (int tq0 = 0; tq0 < T; tq0 += QT) {
     const int nq = min(QT, T - tq0);
     if (L0 + tq0 + nq - 1 < k0) continue;  // every query of the group precedes the block
-    for (int i = threadIdx.x; i < nq * Dh; i += ATTN_THREADS) {
-      const int t = i / Dh, dd = i - t * Dh;
-      sm.qs[i] = to_f32(qrot[static_cast<size_t>(b * T + tq0 + t) * d + h * Dh + dd]);
-    }
+    stage_q(sm, qrot + static_cast<size_t>(b * T + tq0) * d + h * Dh, d, nq, Dh);
     if (!k_ready) {
       cp_async_wait<1>();
       k_ready = true;
@@ -358,10 +391,7 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_fused_kernel(const TD* __re
   const size_t HD = static_cast<size_t>(H) * Dh;
   const int npair = Dh / 2, groups = ATTN_THREADS / npair;
   const int pi = threadIdx.x % npair, g = threadIdx.x / npair;
-  for (int i = threadIdx.x; i < nq * Dh; i += ATTN_THREADS) {
-    const int t = i / Dh, dd = i - t * Dh;
-    sm.qs[i] = to_f32(qrot[static_cast<size_t>(b * T + tq0 + t) * d + h * Dh + dd]);
-  }
+  stage_q(sm, qrot + static_cast<size_t>(b * T + tq0) * d + h * Dh, d, nq, Dh);
   for (int t = threadIdx.x; t < QT; t += ATTN_THREADS) {
     sm.fold[4 * t] = -CUDART_INF_F;
     sm.fold[4 * t + 1] = 0.f;

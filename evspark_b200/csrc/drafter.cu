@@ -257,10 +257,22 @@ __global__ void __launch_bounds__(128) serial_head_warp_kernel(const float* U, c
                                                               const int64_t* forced, int64_t* tokens, double* qout,
                                                               int64_t* prev_ids) {
   pdl_trigger();
-  pdl_wait();
   constexpr int V = 128 * NL;
   constexpr int PT = V / 128;  // elements per thread in the elementwise phases
+  {
+    // the Markov table rows are read one dependent step at a time: pull the table into L2 first
+    constexpr unsigned TB = V * V * 4, CHUNK = 16384;
+    for (unsigned off = threadIdx.x * CHUNK; off < TB; off += blockDim.x * CHUNK)
+      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<const char*>(markov) + off),
+                   "r"(CHUNK)
+                   : "memory");
+  }
+  pdl_wait();
   __shared__ double row[V];
+  __shared__ double cval[V];  // sampling: nonzero weights (then their prefix sums) in index order
+  __shared__ int cidx[V];     // ... and their indices
+  __shared__ double su[EVS_RETAIN_MAX];
+  __shared__ long long sfo[EVS_RETAIN_MAX];
   __shared__ float fred[4];
   __shared__ double dsh[2];
   __shared__ int ish[1];
@@ -270,6 +282,12 @@ __global__ void __launch_bounds__(128) serial_head_warp_kernel(const float* U, c
   const int b = blockIdx.x;
   const unsigned full = 0xffffffffu;
   int prev = static_cast<int>(anchor[b]);
+  // per-step inputs up front: the uniforms and forced tokens of every step
+  for (int i = tid; i < g; i += blockDim.x) {
+    su[i] = (!greedy && u != nullptr) ? u[static_cast<size_t>(b) * g + i] : 0.0;
+    sfo[i] = forced != nullptr ? forced[static_cast<size_t>(b) * g + i] : -1;
+  }
+  __syncthreads();
   for (int k = 0; k < g; ++k) {
     const float* Ur = U + (static_cast<size_t>(b) * g + k) * V;
     const float* Br = markov + static_cast<size_t>(prev) * V;
@@ -388,27 +406,65 @@ __global__ void __launch_bounds__(128) serial_head_warp_kernel(const float* U, c
         const double s = warp_pw_sum<NL>(w, lane);
         const bool bad = !(s > 0.0) || !isfinite(s);
         __syncwarp();
+        // normalised weights in index order (0 / s is exactly 0: no division)
 #pragma unroll
         for (int t = 0; t < 16; ++t)
-          if (act) row[base + 8 * t] = bad ? 1.0 / V : w[t] / s;
+          if (act) row[base + 8 * t] = bad ? 1.0 / V : (w[t] != 0.0 ? w[t] / s : 0.0);
         __syncwarp();
-        if (lane == 0) seq_cumsum(row, V);
+        // cumsum + inverse CDF.  Adding a zero leaves the running sum unchanged, so the prefix
+        // sums are those of the nonzero weights in index order: lane L compacts indices
+        // [L*PL, (L+1)*PL), lane 0 sums the compacted weights in order, and since the prefixes never
+        // decrease, the count of prefix / last <= u is the index of the first nonzero that fails it
+        constexpr int PL = V / 32;
+        double cv[PL];
+        unsigned nzm = 0;
+#pragma unroll
+        for (int i = 0; i < PL; ++i) {
+          cv[i] = row[lane * PL + i];
+          if (cv[i] != 0.0) nzm |= 1u << i;
+        }
+        const int mine = __popc(nzm);
+        int incl = mine;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int nb = __shfl_up_sync(full, incl, o);
+          if (lane >= o) incl += nb;
+        }
+        const int nnz = __shfl_sync(full, incl, 31);
+        int pos = incl - mine;
+#pragma unroll
+        for (int i = 0; i < PL; ++i)
+          if (nzm >> i & 1u) {
+            cval[pos] = cv[i];
+            cidx[pos] = lane * PL + i;
+            ++pos;
+          }
         __syncwarp();
-        const double last = row[V - 1];
-        const double uu = u[static_cast<size_t>(b) * g + k];
-        int cnt = 0;
+        if (lane == 0) {
+          double c = 0.0;
+          for (int n = 0; n < nnz; ++n) {
+            c += cval[n];
+            cval[n] = c;
+          }
+        }
+        __syncwarp();
+        const double last = cval[nnz - 1];  // nnz >= 1: the normalised weights sum to about 1
+        const double uu = su[k];
+        int first = nnz;
+        for (int n = lane; n < nnz; n += 32)
+          if (!(cval[n] / last <= uu)) {
+            first = n;
+            break;
+          }
 #pragma unroll
-        for (int t = 0; t < 16; ++t)
-          if (act && row[base + 8 * t] / last <= uu) ++cnt;
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) cnt += __shfl_xor_sync(full, cnt, o);
+        for (int o = 16; o > 0; o >>= 1) first = min(first, __shfl_xor_sync(full, first, o));
+        const int cnt = first < nnz ? cidx[first] : V;
         if (lane == 0) ish[0] = cnt < V ? cnt : V - 1;
       }
       __syncthreads();
       tok = ish[0];
     }
-    if (forced != nullptr && forced[static_cast<size_t>(b) * g + k] >= 0)  // negative: not forced
-      tok = static_cast<int>(forced[static_cast<size_t>(b) * g + k]);
+    if (sfo[k] >= 0) tok = static_cast<int>(sfo[k]);  // negative: not forced
     if (tid == 0) {
       tokens[static_cast<size_t>(b) * g + k] = tok;
       prev_ids[static_cast<size_t>(b) * g + k] = prev;
@@ -742,7 +798,7 @@ int evs_draft_propose(evs_drafter* dr, const evs_state* s, const int64_t* anchor
   EVS_CUDA_TRY(evs_launch(scale_kernel, dim3(blocks_for(static_cast<size_t>(rows) * V, 256)), dim3(256), 0, st, true, 
       dr->U, 1.0f / sqrtf(static_cast<float>(H)), static_cast<size_t>(rows) * V));
   // ---- serial Markov head ----
-  if (V == 512 || V == 256 || V == 128) {
+  if ((V == 512 || V == 256 || V == 128) && g <= EVS_RETAIN_MAX) {  // per-step inputs held in shared memory
     auto head = V == 512 ? serial_head_warp_kernel<4> : (V == 256 ? serial_head_warp_kernel<2> : serial_head_warp_kernel<1>);
     EVS_CUDA_TRY(evs_launch(head, dim3(B), dim3(128), 0, st, true, dr->U, T[EVS_D_MARKOV], anchor, g, greedy,
                             temperature, top_k, u, forced, tokens, qrows, dr->prev));
