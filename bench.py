@@ -48,6 +48,9 @@ sys.path.insert(0, str(ROOT))
 METRIC = "accepted tok/s single-stream Evo2-7B-shape γ=12; verify-block µs; HBM GB/s"
 GAMMA = 12
 PROMPT_LEN = 1024
+# DRAM bytes per launch of the tcgen05 projection over its algorithmic bytes, from one ncu capture
+# of the w3, in- and out-projection shapes (1.033, 1.026, 0.971)
+GEMM_TRAFFIC_RATIO = 1.010
 E2E_TOKENS = 256
 
 
@@ -512,7 +515,12 @@ def run_ours(args) -> int:
             "verify_block_us": round(verify_block_us, 1),
             "roofline": {"bound": "hbm", "kernel": "gemm_tc (tcgen05 projections)", "achieved": round(achieved, 1),
                          "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
-                         "traffic": None, "launches": int(gemm_n),
+                         "traffic": round(gemm_bytes / max(gemm_n, 1) * GEMM_TRAFFIC_RATIO),
+                         "traffic_note": "ncu dram__bytes_read+write per launch / algorithmic bytes = "
+                                         f"{GEMM_TRAFFIC_RATIO} (mean over the w3, in- and out-projection "
+                                         "captures of profiles/gemm_tc_evo2_7b_shapes.md), times this run's "
+                                         "algorithmic bytes per launch",
+                         "launches": int(gemm_n),
                          "bytes_per_launch": round(gemm_bytes / max(gemm_n, 1)),
                          "avg_launch_us": round(gemm_ms / max(gemm_n, 1) * 1e3, 2),
                          "share_of_kernel_time": round(gemm_ms / kernel_ms, 4) if kernel_ms else None,
