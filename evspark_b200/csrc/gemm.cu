@@ -4,7 +4,7 @@
 // 64 K, TMA, 128-byte swizzle) is the MMA A operand, the activation tile (NT tokens x 64 K)
 // is the B operand, the fp32 accumulator [128 x NT] lives in TMEM.  One elected thread
 // issues TMA, one issues tcgen05.mma, four warps drain TMEM.  A fixed split of K (chosen
-// from N and K only, never from the token count) spreads each GEMM over >= 148 CTAs;
+// from N and K only, never from the token count) spreads each GEMM over up to 3 x 148 CTAs;
 // partial sums land in ws[split][token][row] and the consumer kernel adds them in split
 // order, so every token row is computed by the same arithmetic whatever the batch size.
 //
@@ -20,7 +20,8 @@ constexpr int A_STAGE_BYTES = GEMM_BM * GEMM_BK * 2;  // 16 KiB
 template <int NT>
 struct TcCfg {
   static constexpr int B_STAGE_BYTES = NT * GEMM_BK * 2;
-  static constexpr int STAGES = NT <= 16 ? 6 : (NT <= 64 ? 4 : 3);  // NT=16: 2 CTAs per SM
+  // NT = 16: 4 stages (~75 KB): three CTAs per SM, and room beside the next kernel's CTAs
+  static constexpr int STAGES = NT <= 16 ? 4 : (NT <= 64 ? 4 : 3);
   static constexpr int STAGE_BYTES = A_STAGE_BYTES + B_STAGE_BYTES;
   static constexpr int TMEM_COLS = NT < 32 ? 32 : NT;
   static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
@@ -338,8 +339,10 @@ GemmPlan gemm_plan(const evs_model* m, int N, int K, int M, int dual) {
   if (m->cfg.dtype != EVS_DTYPE_BF16) return gemm_plan_f32(N, K, M, dual);
   const int kblocks = K / GEMM_BK;
   const int tiles = N / GEMM_BM;
+  // as many splits as keep every CTA resident at once (three per SM at the 16-token tile): more
+  // CTAs streaming the same bytes, each over fewer k-blocks.  From N and K only (row invariance).
   int splits = 1;
-  while (tiles * splits < 148 && splits < kblocks) ++splits;
+  while (tiles * (splits + 1) <= 3 * 148 && splits < kblocks) ++splits;
   p.splits = splits;
   return p;
 }
