@@ -35,9 +35,7 @@ __global__ void rope_append_kernel(const float* __restrict__ ws, int splits, int
   }
   const int N = 3 * d;
   auto val = [&](int c) {
-    float acc = 0.f;
-    for (int sp = 0; sp < splits; ++sp) acc += ws[(static_cast<size_t>(sp) * M + row) * N + c];
-    return round_to<TD>(acc);
+    return round_to<TD>(split_sum(ws + static_cast<size_t>(row) * N + c, static_cast<size_t>(M) * N, splits));
   };
   const int c1 = h * Dh + j, c2 = c1 + half;
   const float q1 = val(c1), q2 = val(c2);

@@ -79,6 +79,42 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
+// Sum of n split partials src[0], src[stride], ... in split order (the order every consumer of a
+// split-K projection uses), with up to 8 loads in flight before the adds
+__device__ __forceinline__ float split_sum(const float* src, size_t stride, int n) {
+  float acc = 0.f;
+  for (int s0 = 0; s0 < n; s0 += 8) {
+    float v[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) v[k] = s0 + k < n ? src[static_cast<size_t>(s0 + k) * stride] : 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      if (s0 + k < n) acc += v[k];
+  }
+  return acc;
+}
+// the same over float4 (stride in floats); acc accumulates on top of its input value
+template <bool VOLATILE>
+__device__ __forceinline__ void split_sum4(float4& acc, const float* src, size_t stride, int n) {
+  for (int s0 = 0; s0 < n; s0 += 8) {
+    float4 v[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      if (s0 + k < n) {
+        const float4* p = reinterpret_cast<const float4*>(src + static_cast<size_t>(s0 + k) * stride);
+        v[k] = VOLATILE ? __ldcv(p) : *p;
+      }
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      if (s0 + k < n) {
+        acc.x += v[k].x;
+        acc.y += v[k].y;
+        acc.z += v[k].z;
+        acc.w += v[k].w;
+      }
+  }
+}
+
 // SwiGLU gate silu(a) * c, one expression shared by every kernel that applies it
 __device__ __forceinline__ float swiglu_gate(float a, float c) { return a * (1.0f / (1.0f + expf(-a))) * c; }
 

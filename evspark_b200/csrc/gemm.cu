@@ -270,8 +270,7 @@ __global__ void reduce_splits_kernel(const float* __restrict__ ws, int splits, i
   pdl_wait();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= MN) return;
-  float acc = 0.f;
-  for (int sp = 0; sp < splits; ++sp) acc += ws[static_cast<size_t>(sp) * MN + i];
+  float acc = split_sum(ws + i, MN, splits);
   out[i] = bias ? acc + bias[i % N] : acc;
 }
 
@@ -342,7 +341,7 @@ GemmPlan gemm_plan(const evs_model* m, int N, int K, int M, int dual) {
   // as many splits as keep every CTA resident at once (three per SM at the 16-token tile): more
   // CTAs streaming the same bytes, each over fewer k-blocks.  From N and K only (row invariance).
   int splits = 1;
-  while (tiles * (splits + 1) <= 3 * 148 && splits < kblocks) ++splits;
+  while (tiles * (splits + 1) <= 3 * 148 && splits < kblocks && splits < 16) ++splits;
   p.splits = splits;
   return p;
 }

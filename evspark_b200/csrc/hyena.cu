@@ -105,24 +105,30 @@ __device__ void outer_pass(const HyArgs<TD>& a, int b, int L0, int h0, int t0, i
     float4 acc[4];
 #pragma unroll
     for (int k = 0; k < 4; ++k) acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int sp = 0; sp < a.splits; ++sp) {
-      float4 v[4];
+    for (int s0 = 0; s0 < a.splits; s0 += 2) {  // two splits x four chunks of loads in flight
+      float4 v[2][4];
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const int i = i0 + k * blockDim.x;
-        if (i < n4) {
-          const int t = i / Q, q4 = i - t * Q;
-          v[k] = __ldg(reinterpret_cast<const float4*>(a.ws + sp * split_stride +
-                                                       static_cast<size_t>(b * a.T + t0 + t) * N3 + c0) + q4);
+      for (int u = 0; u < 2; ++u)
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int i = i0 + k * blockDim.x;
+          if (s0 + u < a.splits && i < n4) {
+            const int t = i / Q, q4 = i - t * Q;
+            v[u][k] = __ldg(reinterpret_cast<const float4*>(a.ws + (s0 + u) * split_stride +
+                                                            static_cast<size_t>(b * a.T + t0 + t) * N3 + c0) + q4);
+          }
         }
-      }
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        acc[k].x += v[k].x;
-        acc[k].y += v[k].y;
-        acc[k].z += v[k].z;
-        acc[k].w += v[k].w;
-      }
+      for (int u = 0; u < 2; ++u)
+        if (s0 + u < a.splits) {
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            acc[k].x += v[u][k].x;
+            acc[k].y += v[u][k].y;
+            acc[k].z += v[u][k].z;
+            acc[k].w += v[u][k].w;
+          }
+        }
     }
 #pragma unroll
     for (int k = 0; k < 4; ++k) {

@@ -130,15 +130,11 @@ __global__ void __cluster_dims__(NORM_CL, 1, 1) __launch_bounds__(NORM_THREADS)
       const int c = c_base + c4 * 4;
       float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
       for (int r = 0; r < parts.R; ++r) {  // ranks in rank order, each rank's splits in split order
-        const float* ws = parts.buf[r];
-        for (int sp = 0; sp < splits; ++sp) {
-          const float4* src = reinterpret_cast<const float4*>(ws + (static_cast<size_t>(sp) * M + row) * d + c);
-          const float4 w = parts.R > 1 ? __ldcv(src) : *src;
-          acc.x += w.x;
-          acc.y += w.y;
-          acc.z += w.z;
-          acc.w += w.w;
-        }
+        const float* src = parts.buf[r] + static_cast<size_t>(row) * d + c;
+        if (parts.R > 1)
+          split_sum4<true>(acc, src, static_cast<size_t>(M) * d, splits);
+        else
+          split_sum4<false>(acc, src, static_cast<size_t>(M) * d, splits);
       }
       float4* rp = reinterpret_cast<float4*>(resid + static_cast<size_t>(row) * d + c);
       float4 x = *rp;
@@ -194,19 +190,9 @@ __global__ void __launch_bounds__(ROW_THREADS) swiglu_kernel(const float* __rest
   const int N2 = 2 * F;
   const int v1 = (f / 64) * 128 + (f % 64), v2 = v1 + 64;
   float4 g1 = make_float4(0.f, 0.f, 0.f, 0.f), g2 = g1;
-  for (int sp = 0; sp < splits; ++sp) {
-    const float* r = ws + (static_cast<size_t>(sp) * M + row) * N2;
-    const float4 a = *reinterpret_cast<const float4*>(r + v1);
-    const float4 c = *reinterpret_cast<const float4*>(r + v2);
-    g1.x += a.x;
-    g1.y += a.y;
-    g1.z += a.z;
-    g1.w += a.w;
-    g2.x += c.x;
-    g2.y += c.y;
-    g2.z += c.z;
-    g2.w += c.w;
-  }
+  const float* r = ws + static_cast<size_t>(row) * N2;
+  split_sum4<false>(g1, r + v1, static_cast<size_t>(M) * N2, splits);
+  split_sum4<false>(g2, r + v2, static_cast<size_t>(M) * N2, splits);
   store4<TD>(act + static_cast<size_t>(row) * ld_act + f,
              make_float4(swiglu_gate(g1.x, g2.x), swiglu_gate(g1.y, g2.y), swiglu_gate(g1.z, g2.z),
                          swiglu_gate(g1.w, g2.w)));
@@ -221,8 +207,7 @@ __global__ void logits_kernel(const float* __restrict__ ws, int splits, int M, i
   if (v >= V) return;
   const int t = row % T;
   if (last_only && t != T - 1) return;
-  float acc = 0.f;
-  for (int sp = 0; sp < splits; ++sp) acc += ws[(static_cast<size_t>(sp) * M + row) * V + v];
+  const float acc = split_sum(ws + static_cast<size_t>(row) * V + v, static_cast<size_t>(M) * V, splits);
   const int b = row / T;
   const size_t orow = last_only ? static_cast<size_t>(b) : static_cast<size_t>(b) * out_T + t0 + t;
   out[orow * V + v] = acc;
