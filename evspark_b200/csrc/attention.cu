@@ -109,12 +109,27 @@ __device__ __forceinline__ void stage_kv(const AttnSmem<TD>& sm, const TD* kb, s
   cp_async_commit();
 }
 
-// nq query rows (head slice of Dh values, row stride ld elements) -> fp32 sm.qs[nq][Dh]: 16-byte
-// loads, up to four per thread in flight before the conversions
+// query rows per block pass and the bf16 query tile's padded row (272 B for Dh = 128: the MMA
+// fragment loads of 8 rows x 4 lanes hit 32 distinct banks)
+__host__ __device__ constexpr int qb_pad(int Dh) { return Dh + 8; }
+
+// nq query rows (head slice of Dh values, row stride ld elements) into shared memory with 16-byte
+// loads, up to four per thread in flight: fp32 sm.qs[nq][Dh] (fp32 data), or for bf16 data the
+// bf16 rows themselves in sm.qs viewed as bf16[QT][qb_pad(Dh)], rows nq..QT-1 zero
 template <typename TD>
 __device__ __forceinline__ void stage_q(const AttnSmem<TD>& sm, const TD* src, size_t ld, int nq, int Dh) {
   constexpr int EPC = 16 / sizeof(TD);
   const int cpr = Dh / EPC, n = nq * cpr;
+  if constexpr (sizeof(TD) == 2) {
+    TD* qb = reinterpret_cast<TD*>(sm.qs);
+    const int qp = qb_pad(Dh);
+    for (int i = threadIdx.x; i < QT * cpr; i += ATTN_THREADS) {
+      const int t = i / cpr, c = i - t * cpr;
+      *reinterpret_cast<uint4*>(qb + t * qp + c * EPC) =
+          t < nq ? *reinterpret_cast<const uint4*>(src + t * ld + c * EPC) : make_uint4(0u, 0u, 0u, 0u);
+    }
+    return;
+  }
   for (int i0 = threadIdx.x; i0 < n; i0 += 4 * ATTN_THREADS) {
     uint4 raw[4];
 #pragma unroll
@@ -146,9 +161,55 @@ __device__ __forceinline__ void stage_q(const AttnSmem<TD>& sm, const TD* src, s
 }
 
 // scores of one key block: thread = one key x QK_Q queries; keys past a query's position -> -inf
+// bf16 x bf16 -> fp32 tensor-core MMA, m16n8k16, A row-major, B column-major
+__device__ __forceinline__ void mma_bf16_16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                               uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
 template <typename TD>
 __device__ __forceinline__ void block_scores(const AttnSmem<TD>& sm, int Dh, int nk, int nq, int k0, int P0,
                                              float scale) {
+  if constexpr (sizeof(TD) == 2) {
+    // S[16 queries][64 keys] = Q K^T on the tensor cores (bf16 inputs are exact, fp32
+    // accumulation; a query row's result does not depend on the other rows).  Warp w: keys
+    // 16w .. 16w+15 as two 8-key tiles, Dh / 16 steps of K.
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
+    const TD* qb = reinterpret_cast<const TD*>(sm.qs);
+    const int qp = qb_pad(Dh);
+    float c[2][4];
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) c[nt][e] = 0.f;
+    for (int kc = tig * 2; kc < Dh; kc += 16) {
+      const uint32_t a0 = *reinterpret_cast<const uint32_t*>(qb + gid * qp + kc);
+      const uint32_t a1 = *reinterpret_cast<const uint32_t*>(qb + (gid + 8) * qp + kc);
+      const uint32_t a2 = *reinterpret_cast<const uint32_t*>(qb + gid * qp + kc + 8);
+      const uint32_t a3 = *reinterpret_cast<const uint32_t*>(qb + (gid + 8) * qp + kc + 8);
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+        const TD* kr = sm.Ks + (warp * 16 + nt * 8 + gid) * sm.kpad;
+        mma_bf16_16816(c[nt], a0, a1, a2, a3, *reinterpret_cast<const uint32_t*>(kr + kc),
+                       *reinterpret_cast<const uint32_t*>(kr + kc + 8));
+      }
+    }
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int t = gid + (e >> 1) * 8, key = warp * 16 + nt * 8 + tig * 2 + (e & 1);
+        if (t < nq) {
+          const bool vis = key < nk && k0 + key <= P0 + t;  // P0: position of query 0 of the pass
+          sm.S[t * ATTN_BLOCK + key] = vis ? c[nt][e] * scale : -CUDART_INF_F;
+        }
+      }
+    return;
+  }
   constexpr int EPC = 16 / sizeof(TD);
   const int key = threadIdx.x % ATTN_BLOCK, qh = threadIdx.x / ATTN_BLOCK;
   float acc[QK_Q];
@@ -233,24 +294,36 @@ __device__ __forceinline__ void block_pv(const AttnSmem<TD>& sm, int Dh, int nk,
   const int pi = threadIdx.x % npair, g = threadIdx.x / npair;
 #pragma unroll
   for (int q = 0; q < PV_QMAX; ++q) a0[q] = a1[q] = 0.f;
-  for (int i = 0; i < nk; ++i) {
-    float v0, v1;
-    if constexpr (sizeof(TD) == 2) {
-      const float2 f2 = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(sm.Vs + i * Dh)[pi]);
-      v0 = f2.x;
-      v1 = f2.y;
-    } else {
-      const float2 f2 = reinterpret_cast<const float2*>(sm.Vs + i * Dh)[pi];
-      v0 = f2.x;
-      v1 = f2.y;
-    }
+  for (int i0 = 0; i0 < nk; i0 += 4) {  // keys in order, four per float4 of P
+    float4 p4[PV_QMAX];
 #pragma unroll
     for (int q = 0; q < PV_QMAX; ++q) {
       const int t = g + q * groups;
-      if (t < nq) {
-        const float pv = sm.S[t * ATTN_BLOCK + i];
-        a0[q] = fmaf(pv, v0, a0[q]);
-        a1[q] = fmaf(pv, v1, a1[q]);
+      p4[q] = t < nq ? *reinterpret_cast<const float4*>(sm.S + t * ATTN_BLOCK + i0) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int i = i0 + k;
+      if (i < nk) {
+        float v0, v1;
+        if constexpr (sizeof(TD) == 2) {
+          const float2 f2 = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(sm.Vs + i * Dh)[pi]);
+          v0 = f2.x;
+          v1 = f2.y;
+        } else {
+          const float2 f2 = reinterpret_cast<const float2*>(sm.Vs + i * Dh)[pi];
+          v0 = f2.x;
+          v1 = f2.y;
+        }
+#pragma unroll
+        for (int q = 0; q < PV_QMAX; ++q) {
+          const int t = g + q * groups;
+          if (t < nq) {
+            const float pv = k == 0 ? p4[q].x : (k == 1 ? p4[q].y : (k == 2 ? p4[q].z : p4[q].w));
+            a0[q] = fmaf(pv, v0, a0[q]);
+            a1[q] = fmaf(pv, v1, a1[q]);
+          }
+        }
       }
     }
   }
