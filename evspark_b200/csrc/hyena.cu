@@ -294,7 +294,6 @@ __device__ __forceinline__ void store_vec(float* dst, const float* v) {
 template <typename TD, int SPT>
 __global__ void __launch_bounds__(HY_THREADS) hyena_iir_kernel(HyArgs<TD> a) {
   pdl_trigger();
-  pdl_wait();
   extern __shared__ __align__(16) float sm[];
   float* uw = sm;
   float* zs = uw + UW * C3;
@@ -303,18 +302,20 @@ __global__ void __launch_bounds__(HY_THREADS) hyena_iir_kernel(HyArgs<TD> a) {
   const int h0 = blockIdx.x * CH, h = h0 + hl;
   const int b = blockIdx.y;
   const int T = a.T, S = a.S, d = a.d;
-  const int L0 = a.len[b];
-  outer_stage(a, b, L0, h0, uw, wo);
+  // poles, residues and D are weights (no earlier kernel writes them): load before the wait
   float p[SPT], r[SPT], s[SPT];
   load_vec<SPT>(a.poles + static_cast<size_t>(h) * S + q * SPT, p);
   load_vec<SPT>(a.residues + static_cast<size_t>(h) * S + q * SPT, r);
+  const float Dg = a.D[h];
+  pdl_wait();
+  const int L0 = a.len[b];
+  outer_stage(a, b, L0, h0, uw, wo);
   if (L0 > 0) {
     load_vec<SPT>(a.s_all + ((static_cast<size_t>(b) * a.slots + a.iir_cur[b]) * d + h) * S + q * SPT, s);
   } else {
 #pragma unroll
     for (int j = 0; j < SPT; ++j) s[j] = 0.f;
   }
-  const float Dg = a.D[h];
   __syncthreads();
   for (int t0 = 0; t0 < T; t0 += TS) {
     const int ns = min(TS, T - t0);

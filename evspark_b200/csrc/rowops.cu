@@ -87,6 +87,17 @@ __global__ void __cluster_dims__(NORM_CL, 1, 1) __launch_bounds__(NORM_THREADS)
                         float* __restrict__ ring, int ring_len, const int32_t* __restrict__ len, int T,
                         EvsDevErr* err) {
   pdl_trigger();
+  cg::cluster_group cluster = cg::this_cluster();
+  const int rank = static_cast<int>(cluster.block_rank());
+  const int cpc = d / NORM_CL, n4 = cpc / 4;
+  const int c_base = rank * cpc;
+  // the norm weight is a weight (no earlier kernel writes it): load it before the wait
+  float4 sc[NORM_VPT];
+#pragma unroll
+  for (int v = 0; v < NORM_VPT; ++v) {
+    const int c4 = threadIdx.x + v * NORM_THREADS;
+    if (c4 < n4) sc[v] = __ldg(reinterpret_cast<const float4*>(scale + c_base + c4 * 4));
+  }
   pdl_wait();
   if (parts.R > 1) {
     // every rank's partial sums of this reduction are published once its flag reaches the epoch
@@ -110,8 +121,6 @@ __global__ void __cluster_dims__(NORM_CL, 1, 1) __launch_bounds__(NORM_THREADS)
   }
   __shared__ float red[NORM_THREADS / 32];
   __shared__ float cta_ss;
-  cg::cluster_group cluster = cg::this_cluster();
-  const int rank = static_cast<int>(cluster.block_rank());
   const int row = blockIdx.y;
   const int b = row / T, t = row % T;
   float* cap = nullptr;
@@ -119,10 +128,15 @@ __global__ void __cluster_dims__(NORM_CL, 1, 1) __launch_bounds__(NORM_THREADS)
     const int P = len[b] + t;
     cap = ring + (static_cast<size_t>(b) * ring_len + P % ring_len) * d;
   }
-  const int cpc = d / NORM_CL, n4 = cpc / 4;
-  const int c_base = rank * cpc;
   float4 r[NORM_VPT];
   float ss = 0.f;
+  // the residual values first, so that their loads are in flight with the partial sums'
+  float4 xr[NORM_VPT];
+#pragma unroll
+  for (int v = 0; v < NORM_VPT; ++v) {
+    const int c4 = threadIdx.x + v * NORM_THREADS;
+    if (c4 < n4) xr[v] = *reinterpret_cast<const float4*>(resid + static_cast<size_t>(row) * d + c_base + c4 * 4);
+  }
 #pragma unroll
   for (int v = 0; v < NORM_VPT; ++v) {
     const int c4 = threadIdx.x + v * NORM_THREADS;
@@ -137,7 +151,7 @@ __global__ void __cluster_dims__(NORM_CL, 1, 1) __launch_bounds__(NORM_THREADS)
           split_sum4<false>(acc, src, static_cast<size_t>(M) * d, splits);
       }
       float4* rp = reinterpret_cast<float4*>(resid + static_cast<size_t>(row) * d + c);
-      float4 x = *rp;
+      float4 x = xr[v];
       x.x += acc.x;
       x.y += acc.y;
       x.z += acc.z;
@@ -169,10 +183,9 @@ __global__ void __cluster_dims__(NORM_CL, 1, 1) __launch_bounds__(NORM_THREADS)
     const int c4 = threadIdx.x + v * NORM_THREADS;
     if (c4 < n4) {
       const int c = c_base + c4 * 4;
-      const float4 sc = *reinterpret_cast<const float4*>(scale + c);
       const float4 x = r[v];
       store4<TD>(act + static_cast<size_t>(row) * ld_act + c,
-                 make_float4(x.x * inv * sc.x, x.y * inv * sc.y, x.z * inv * sc.z, x.w * inv * sc.w));
+                 make_float4(x.x * inv * sc[v].x, x.y * inv * sc[v].y, x.z * inv * sc[v].z, x.w * inv * sc[v].w));
     }
   }
 }
