@@ -62,13 +62,13 @@ constexpr int ATTN_THREADS = 128;
 constexpr int QK_Q = QT / (ATTN_THREADS / ATTN_BLOCK);  // queries per thread in the score pass
 constexpr int PV_QMAX = 8;       // queries per thread in P.V (head_dim <= 128)
 
-// shared memory of both attention kernels: K rows padded by 16 bytes (conflict-free row-per-thread
-// reads), V rows dense, fp32 queries, scores and per-query stats (+ the running fold of the fused
-// kernel)
+// shared memory of both attention kernels: K and V rows padded by 16 bytes (conflict-free
+// row-per-thread reads and 8-row matrix loads), fp32 queries, scores, the P.V tile of the tensor-core
+// path and per-query stats (+ the running fold of the fused kernel)
 template <typename TD>
 __host__ __device__ constexpr size_t attn_smem_bytes(int Dh) {
-  return sizeof(TD) * (static_cast<size_t>(ATTN_BLOCK) * (Dh + 16 / sizeof(TD)) + static_cast<size_t>(ATTN_BLOCK) * Dh) +
-         sizeof(float) * (static_cast<size_t>(QT) * Dh + static_cast<size_t>(QT) * ATTN_BLOCK + 6 * QT);
+  return sizeof(TD) * (2 * static_cast<size_t>(ATTN_BLOCK) * (Dh + 16 / sizeof(TD))) +
+         sizeof(float) * (2 * static_cast<size_t>(QT) * Dh + static_cast<size_t>(QT) * ATTN_BLOCK + 6 * QT);
 }
 
 template <typename TD>
@@ -79,16 +79,18 @@ struct AttnSmem {
   float* S;
   float* stt;   // [2 QT]: block max, block sum
   float* fold;  // [4 QT]: running max, running sum, scale of the old accumulator, scale of the block
-  int kpad;
+  float* O;     // [QT][Dh]: P.V of the tensor-core path
+  int kpad;     // row stride of K and V (elements)
   __device__ AttnSmem(unsigned char* raw, int Dh) {
     constexpr int EPC = 16 / sizeof(TD);
     kpad = Dh + EPC;
     Ks = reinterpret_cast<TD*>(raw);
     Vs = Ks + ATTN_BLOCK * kpad;
-    qs = reinterpret_cast<float*>(Vs + ATTN_BLOCK * Dh);
+    qs = reinterpret_cast<float*>(Vs + ATTN_BLOCK * kpad);
     S = qs + QT * Dh;
     stt = S + QT * ATTN_BLOCK;
     fold = stt + 2 * QT;
+    O = fold + 4 * QT;
   }
 };
 
@@ -104,9 +106,14 @@ __device__ __forceinline__ void stage_kv(const AttnSmem<TD>& sm, const TD* kb, s
   cp_async_commit();
   for (int i = threadIdx.x; i < nk * cpr; i += ATTN_THREADS) {
     const int r = i / cpr, c = i - r * cpr;
-    cp_async16(sm.Vs + r * Dh + c * EPC, kb + static_cast<size_t>(r) * 2 * HD + HD + c * EPC);
+    cp_async16(sm.Vs + r * sm.kpad + c * EPC, kb + static_cast<size_t>(r) * 2 * HD + HD + c * EPC);
   }
   cp_async_commit();
+  // V rows past the block's keys are zero: P is zero there, and 0 times stale data could be NaN
+  for (int i = nk * cpr + threadIdx.x; i < ATTN_BLOCK * cpr; i += ATTN_THREADS) {
+    const int r = i / cpr, c = i - r * cpr;
+    *reinterpret_cast<uint4*>(sm.Vs + r * sm.kpad + c * EPC) = make_uint4(0u, 0u, 0u, 0u);
+  }
 }
 
 // query rows per block pass and the bf16 query tile's padded row (272 B for Dh = 128: the MMA
@@ -286,12 +293,76 @@ __device__ __forceinline__ void block_softmax(const AttnSmem<TD>& sm, int nq) {
   }
 }
 
+// two 8x8 bf16 matrices from shared memory, transposed (rows addressed by lanes 0-15)
+__device__ __forceinline__ void ldmatrix_x2_trans(uint32_t& r0, uint32_t& r1, const void* row_addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0, %1}, [%2];"
+               : "=r"(r0), "=r"(r1)
+               : "r"(smem_u32(row_addr)));
+}
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+
 // P.V of one key block: head columns 2*pi, 2*pi+1 for queries g, g+groups, ...
 template <typename TD>
 __device__ __forceinline__ void block_pv(const AttnSmem<TD>& sm, int Dh, int nk, int nq, float (&a0)[PV_QMAX],
                                          float (&a1)[PV_QMAX]) {
   const int npair = Dh / 2, groups = ATTN_THREADS / npair;
   const int pi = threadIdx.x % npair, g = threadIdx.x / npair;
+  if constexpr (sizeof(TD) == 2) {
+    // O[16][Dh] = P V on the tensor cores.  P (fp32) enters as two bf16 parts hi + lo (P = hi + lo
+    // to ~16 bits), V exactly; fp32 accumulation.  Warp w: head columns [w*Dh/4, (w+1)*Dh/4) as
+    // 8-column tiles, 16 keys per step (V^T fragments by transposed 8x8 matrix loads).
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
+    const int ntw = Dh / 32;  // 8-column tiles per warp (<= 4)
+    float c[4][4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) c[j][e] = 0.f;
+#pragma unroll
+    for (int ks = 0; ks < ATTN_BLOCK / 16; ++ks) {
+      const float* S0 = sm.S + gid * ATTN_BLOCK + ks * 16 + 2 * tig;
+      const float* S1 = S0 + 8 * ATTN_BLOCK;
+      const float p[8] = {S0[0], S0[1], S1[0], S1[1], S0[8], S0[9], S1[8], S1[9]};
+      uint32_t hi[4], lo[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const __nv_bfloat16 h0 = __float2bfloat16_rn(p[2 * e]), h1 = __float2bfloat16_rn(p[2 * e + 1]);
+        const __nv_bfloat162 hh = __halves2bfloat162(h0, h1);
+        hi[e] = *reinterpret_cast<const uint32_t*>(&hh);
+        lo[e] = pack_bf16x2(p[2 * e] - __bfloat162float(h0), p[2 * e + 1] - __bfloat162float(h1));
+      }
+      const TD* vrow = sm.Vs + (ks * 16 + (lane >> 3 & 1) * 8 + (lane & 7)) * sm.kpad;
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (j < ntw) {
+          uint32_t b0, b1;
+          ldmatrix_x2_trans(b0, b1, vrow + (warp * ntw + j) * 8);
+          mma_bf16_16816(c[j], hi[0], hi[1], hi[2], hi[3], b0, b1);
+          mma_bf16_16816(c[j], lo[0], lo[1], lo[2], lo[3], b0, b1);
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      if (j < ntw) {
+        const int col = (warp * ntw + j) * 8 + 2 * tig;
+        sm.O[gid * Dh + col] = c[j][0];
+        sm.O[gid * Dh + col + 1] = c[j][1];
+        sm.O[(gid + 8) * Dh + col] = c[j][2];
+        sm.O[(gid + 8) * Dh + col + 1] = c[j][3];
+      }
+    __syncthreads();
+#pragma unroll
+    for (int q = 0; q < PV_QMAX; ++q) {
+      const int t = g + q * groups;
+      a0[q] = t < QT ? sm.O[t * Dh + 2 * pi] : 0.f;
+      a1[q] = t < QT ? sm.O[t * Dh + 2 * pi + 1] : 0.f;
+    }
+    __syncthreads();  // O is rewritten by the next block
+    return;
+  }
 #pragma unroll
   for (int q = 0; q < PV_QMAX; ++q) a0[q] = a1[q] = 0.f;
   for (int i0 = 0; i0 < nk; i0 += 4) {  // keys in order, four per float4 of P
@@ -307,11 +378,11 @@ __device__ __forceinline__ void block_pv(const AttnSmem<TD>& sm, int Dh, int nk,
       if (i < nk) {
         float v0, v1;
         if constexpr (sizeof(TD) == 2) {
-          const float2 f2 = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(sm.Vs + i * Dh)[pi]);
+          const float2 f2 = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(sm.Vs + i * sm.kpad)[pi]);
           v0 = f2.x;
           v1 = f2.y;
         } else {
-          const float2 f2 = reinterpret_cast<const float2*>(sm.Vs + i * Dh)[pi];
+          const float2 f2 = reinterpret_cast<const float2*>(sm.Vs + i * sm.kpad)[pi];
           v0 = f2.x;
           v1 = f2.y;
         }
