@@ -269,24 +269,42 @@ __device__ __forceinline__ void block_scores(const AttnSmem<TD>& sm, int Dh, int
   }
 }
 
-// per query (one warp each): block max, p = exp(s - max) in place, block sum -> stt
+// per query: block max, p = exp(s - max) in place, block sum -> stt.  Eight lanes per query (keys
+// 8k8 .. 8k8+7 on lane k8, summed in key order, then across the eight lanes by butterfly), four
+// queries per warp: the 16 query rows of a pass in one round.
 template <typename TD>
 __device__ __forceinline__ void block_softmax(const AttnSmem<TD>& sm, int nq) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int t = warp; t < nq; t += ATTN_THREADS / 32) {
-    float* Sr = sm.S + t * ATTN_BLOCK;
-    float mx = -CUDART_INF_F;
-    for (int i = lane; i < ATTN_BLOCK; i += 32) mx = fmaxf(mx, Sr[i]);
-    mx = warp_max(mx);
-    float l = 0.f;
-    for (int i = lane; i < ATTN_BLOCK; i += 32) {
-      const float sv = Sr[i];
-      const float pv = (mx == -CUDART_INF_F || sv == -CUDART_INF_F) ? 0.f : expf(sv - mx);
-      Sr[i] = pv;
-      l += pv;
-    }
-    l = warp_sum(l);
-    if (lane == 0) {
+  static_assert(ATTN_BLOCK == 64 && QT == 16 && ATTN_THREADS == 128, "layout of the softmax pass");
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, k8 = lane & 7;
+  const int t = warp * 4 + (lane >> 3);
+  const bool live = t < nq;
+  float* Sr = sm.S + t * ATTN_BLOCK + 8 * k8;
+  float v[8];
+  if (live) {
+    const float4 x0 = reinterpret_cast<const float4*>(Sr)[0], x1 = reinterpret_cast<const float4*>(Sr)[1];
+    v[0] = x0.x; v[1] = x0.y; v[2] = x0.z; v[3] = x0.w;
+    v[4] = x1.x; v[5] = x1.y; v[6] = x1.z; v[7] = x1.w;
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = -CUDART_INF_F;
+  }
+  float mx = v[0];
+#pragma unroll
+  for (int i = 1; i < 8; ++i) mx = fmaxf(mx, v[i]);
+#pragma unroll
+  for (int o = 4; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  float l = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    v[i] = (mx == -CUDART_INF_F || v[i] == -CUDART_INF_F) ? 0.f : expf(v[i] - mx);
+    l += v[i];
+  }
+#pragma unroll
+  for (int o = 4; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+  if (live) {
+    reinterpret_cast<float4*>(Sr)[0] = make_float4(v[0], v[1], v[2], v[3]);
+    reinterpret_cast<float4*>(Sr)[1] = make_float4(v[4], v[5], v[6], v[7]);
+    if (k8 == 0) {
       sm.stt[2 * t] = mx;
       sm.stt[2 * t + 1] = l;
     }
