@@ -14,6 +14,8 @@
 // does not depend on how many other queries share the call (native T=1 == verify T=γ+1).
 #include <math_constants.h>
 
+#include <algorithm>
+
 #include "internal.hpp"
 
 namespace {
@@ -94,9 +96,9 @@ struct AttnSmem {
   }
 };
 
-// 16-byte asynchronous copies of K and V rows [0, nk) of one key block (two commit groups: K, V)
+// 16-byte asynchronous copies of the K rows [0, nk) of one key block (one commit group)
 template <typename TD>
-__device__ __forceinline__ void stage_kv(const AttnSmem<TD>& sm, const TD* kb, size_t HD, int Dh, int nk) {
+__device__ __forceinline__ void stage_k(const AttnSmem<TD>& sm, const TD* kb, size_t HD, int Dh, int nk) {
   constexpr int EPC = 16 / sizeof(TD);
   const int cpr = Dh / EPC;
   for (int i = threadIdx.x; i < nk * cpr; i += ATTN_THREADS) {
@@ -104,16 +106,27 @@ __device__ __forceinline__ void stage_kv(const AttnSmem<TD>& sm, const TD* kb, s
     cp_async16(sm.Ks + r * sm.kpad + c * EPC, kb + static_cast<size_t>(r) * 2 * HD + c * EPC);
   }
   cp_async_commit();
+}
+// ... and of its V rows (one commit group); V rows past the block's keys are zero: P is zero
+// there, and 0 times stale data could be NaN
+template <typename TD>
+__device__ __forceinline__ void stage_v(const AttnSmem<TD>& sm, const TD* kb, size_t HD, int Dh, int nk) {
+  constexpr int EPC = 16 / sizeof(TD);
+  const int cpr = Dh / EPC;
   for (int i = threadIdx.x; i < nk * cpr; i += ATTN_THREADS) {
     const int r = i / cpr, c = i - r * cpr;
     cp_async16(sm.Vs + r * sm.kpad + c * EPC, kb + static_cast<size_t>(r) * 2 * HD + HD + c * EPC);
   }
   cp_async_commit();
-  // V rows past the block's keys are zero: P is zero there, and 0 times stale data could be NaN
   for (int i = nk * cpr + threadIdx.x; i < ATTN_BLOCK * cpr; i += ATTN_THREADS) {
     const int r = i / cpr, c = i - r * cpr;
     *reinterpret_cast<uint4*>(sm.Vs + r * sm.kpad + c * EPC) = make_uint4(0u, 0u, 0u, 0u);
   }
+}
+template <typename TD>
+__device__ __forceinline__ void stage_kv(const AttnSmem<TD>& sm, const TD* kb, size_t HD, int Dh, int nk) {
+  stage_k(sm, kb, HD, Dh, nk);
+  stage_v(sm, kb, HD, Dh, nk);
 }
 
 // query rows per block pass and the bf16 query tile's padded row (272 B for Dh = 128: the MMA
@@ -431,56 +444,61 @@ __device__ __forceinline__ float fold_acc(float acc, float a, float accj, float 
   return fmaf(acc, a, __fmul_rn(accj, bj));
 }
 
-// Split-KV: grid (blocks, H, B), ATTN_THREADS threads.  One CTA stages one ATTN_BLOCK-key block
-// of one head (K and V in two asynchronous groups, so scores start while V is in flight) and
-// writes, for each query whose position reaches the block, the block's partial (acc, max, sum).
-// Keys past a query's position score -inf and contribute exact zeros, so a query's partial does
-// not depend on how many queries share the call.
+// Split-KV (chunks of at most QT queries, i.e. one pass): grid (block groups, H, B), ATTN_THREADS
+// threads.  A CTA walks bpc consecutive ATTN_BLOCK-key blocks of one head; for each it computes the
+// scores, softmax and P.V and writes, for each query whose position reaches the block, the block's
+// partial (acc, max, sum).  The next block's K is in flight while this block's softmax and P.V
+// run, its V while this block's partials are written.  Keys past a query's position score -inf
+// and contribute exact zeros, so a query's partial does not depend on how many queries share the
+// call, nor on bpc.
 template <typename TD>
 __global__ void __launch_bounds__(ATTN_THREADS) attn_block_kernel(const TD* __restrict__ qrot,
                                                                  const TD* __restrict__ kv,
                                                                  const int32_t* __restrict__ len, int T, int d,
                                                                  int H, int Dh, int Lmax, int nblk_cap, int tcap,
-                                                                 float scale, float* __restrict__ part) {
+                                                                 int bpc, float scale, float* __restrict__ part) {
   pdl_trigger();
   pdl_wait();
   extern __shared__ __align__(16) unsigned char attn_sm[];
-  const int j = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int h = blockIdx.y, b = blockIdx.z;
   const int L0 = len[b];
   const int Lend = L0 + T;
-  const int k0 = j * ATTN_BLOCK;
-  if (k0 >= Lend) return;
-  const int nk = min(ATTN_BLOCK, Lend - k0);
+  const int nq = T;  // T <= QT
+  const int j_begin = blockIdx.x * bpc;
+  const int j_end = min(j_begin + bpc, (Lend + ATTN_BLOCK - 1) / ATTN_BLOCK);
+  if (j_begin >= j_end) return;
   AttnSmem<TD> sm(attn_sm, Dh);
   const size_t HD = static_cast<size_t>(H) * Dh;
-  stage_kv(sm, kv + (static_cast<size_t>(b) * Lmax + k0) * 2 * HD + static_cast<size_t>(h) * Dh, HD, Dh, nk);
-  bool k_ready = false, v_ready = false;
+  const TD* kvb = kv + static_cast<size_t>(b) * Lmax * 2 * HD + static_cast<size_t>(h) * Dh;
+  auto nk_of = [&](int j) { return min(ATTN_BLOCK, Lend - j * ATTN_BLOCK); };
+  stage_k(sm, kvb + static_cast<size_t>(j_begin) * ATTN_BLOCK * 2 * HD, HD, Dh, nk_of(j_begin));
+  stage_v(sm, kvb + static_cast<size_t>(j_begin) * ATTN_BLOCK * 2 * HD, HD, Dh, nk_of(j_begin));
+  stage_q(sm, qrot + static_cast<size_t>(b * T) * d + h * Dh, d, nq, Dh);
   const int npair = Dh / 2, groups = ATTN_THREADS / npair;
   const int pi = threadIdx.x % npair, g = threadIdx.x / npair;
-  for (int tq0 = 0; tq0 < T; tq0 += QT) {
-    const int nq = min(QT, T - tq0);
-    if (L0 + tq0 + nq - 1 < k0) continue;  // every query of the group precedes the block
-    stage_q(sm, qrot + static_cast<size_t>(b * T + tq0) * d + h * Dh, d, nq, Dh);
-    if (!k_ready) {
-      cp_async_wait<1>();
-      k_ready = true;
-    }
+  for (int j = j_begin; j < j_end; ++j) {
+    const int k0 = j * ATTN_BLOCK, nk = nk_of(j);
+    const bool more = j + 1 < j_end;
+    cp_async_wait<1>();  // K of block j (its V may still be in flight)
     __syncthreads();
-    block_scores(sm, Dh, nk, nq, k0, L0 + tq0, scale);
-    __syncthreads();
+    block_scores(sm, Dh, nk, nq, k0, L0, scale);
+    __syncthreads();  // K of block j no longer read
+    if (more) stage_k(sm, kvb + static_cast<size_t>(j + 1) * ATTN_BLOCK * 2 * HD, HD, Dh, nk_of(j + 1));
     block_softmax(sm, nq);
-    if (!v_ready) {
+    if (more)
+      cp_async_wait<1>();  // V of block j (the next K may still be in flight)
+    else
       cp_async_wait<0>();
-      v_ready = true;
-    }
     __syncthreads();
     float a0[PV_QMAX], a1[PV_QMAX];
     block_pv(sm, Dh, nk, nq, a0, a1);
+    __syncthreads();  // V of block j no longer read
+    if (more) stage_v(sm, kvb + static_cast<size_t>(j + 1) * ATTN_BLOCK * 2 * HD, HD, Dh, nk_of(j + 1));
 #pragma unroll
     for (int q = 0; q < PV_QMAX; ++q) {
       const int t = g + q * groups;
-      if (t < nq && L0 + tq0 + t >= k0) {
-        float* pd = part + ((((static_cast<size_t>(b) * H + h) * nblk_cap + j) * tcap + tq0 + t) * (Dh + 2));
+      if (t < nq && L0 + t >= k0) {
+        float* pd = part + ((((static_cast<size_t>(b) * H + h) * nblk_cap + j) * tcap + t) * (Dh + 2));
         pd[2 * pi] = a0[q];
         pd[2 * pi + 1] = a1[q];
         if (pi == 0) {
@@ -489,9 +507,8 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_block_kernel(const TD* __re
         }
       }
     }
-    __syncthreads();
   }
-  if (!v_ready) cp_async_wait<0>();  // no copy may outlive the CTA
+  cp_async_wait<0>();  // no copy may outlive the CTA
 }
 
 template <typename TD>
@@ -637,10 +654,17 @@ int launch_attention_t(const evs_model* m, evs_state* s, int layer, int B, int T
   }
   EVS_CUDA_TRY(cudaFuncSetAttribute(attn_block_kernel<TD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     static_cast<int>(smem)));
-  EVS_CUDA_TRY(evs_launch(attn_block_kernel<TD>, dim3(kv_blocks, H, B), dim3(ATTN_THREADS), smem, st, pdl,
-                          static_cast<const TD*>(qrot), static_cast<const TD*>(kv),
+  // key blocks per CTA: one while the grid has fewer than ~16 CTAs per SM, more for long contexts
+  // (the arithmetic of a block does not depend on it)
+  EVS_CHECK_ARG(T <= QT, "split-KV attention takes at most QT queries per call");
+  static int n_sm = 0;
+  if (n_sm == 0) EVS_CUDA_TRY(cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, m->device));
+  const long long want = 16LL * n_sm;
+  const int bpc = static_cast<int>(std::max<long long>(1, (static_cast<long long>(kv_blocks) * H * B + want - 1) / want));
+  EVS_CUDA_TRY(evs_launch(attn_block_kernel<TD>, dim3((kv_blocks + bpc - 1) / bpc, H, B), dim3(ATTN_THREADS), smem, st,
+                          pdl, static_cast<const TD*>(qrot), static_cast<const TD*>(kv),
                           static_cast<const int32_t*>(s->d_len), T, d, H, Dh, s->max_seqlen, s->attn_blocks,
-                          s->attn_tcap, scale, s->attn_part));
+                          s->attn_tcap, bpc, scale, s->attn_part));
   EVS_CUDA_TRY(evs_launch(attn_combine_kernel<TD>, dim3(M, H), dim3(Dh), 0, st, pdl,
                           static_cast<const float*>(s->attn_part), static_cast<const int32_t*>(s->d_len), T, d, H,
                           Dh, s->attn_blocks, s->attn_tcap, static_cast<TD*>(s->act), s->ld_act));
