@@ -213,7 +213,7 @@ def run_streams(args) -> int:
     if world > 1:
         dist.barrier()
     clocks = ClockSampler(local)
-    n0 = N.lib().evs_launch_count()
+    n0 = N.launch_count()
     emitted0 = sum(len(e) for e in sb.emitted)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
@@ -222,7 +222,7 @@ def run_streams(args) -> int:
         sb.round()
     ev1.record()
     torch.cuda.synchronize()
-    launches = N.lib().evs_launch_count() - n0
+    launches = N.launch_count() - n0
     clk = clocks.stop()
     ms = ev0.elapsed_time(ev1)
     tokens = float(sum(len(e) for e in sb.emitted) - emitted0)
@@ -306,7 +306,7 @@ def run_tp(args) -> int:
     if world > 1:
         dist.barrier()
     clocks = ClockSampler(local)
-    n0 = N.lib().evs_launch_count()
+    n0 = N.launch_count()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
     ev0.record()
@@ -315,7 +315,7 @@ def run_tp(args) -> int:
         tokens += one_round()
     ev1.record()
     torch.cuda.synchronize()
-    launches = N.lib().evs_launch_count() - n0
+    launches = N.launch_count() - n0
     clk = clocks.stop()
     ms, _ = combine_timing(ev0.elapsed_time(ev1), 0.0, device)
     err = [C.c_int32(), C.c_int32(), C.c_int32()]
@@ -400,7 +400,7 @@ def run_ours(args) -> int:
     if world > 1:
         dist.barrier()
     clocks = ClockSampler(local)
-    n0 = N.lib().evs_launch_count()
+    n0 = N.launch_count()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
     ev0.record()
@@ -414,7 +414,7 @@ def run_ours(args) -> int:
         ks.append(out.log.k)
     ev1.record()
     torch.cuda.synchronize()
-    launches = N.lib().evs_launch_count() - n0
+    launches = N.launch_count() - n0
     clk = clocks.stop()
     ms = ev0.elapsed_time(ev1)
     # a separate profiled pass (events around every kernel group of the verify block) for the

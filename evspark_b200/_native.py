@@ -144,6 +144,21 @@ def call(name: str, *args) -> None:
     check(getattr(lib(), name)(*args), name)
 
 
+# kernels of this library launched by CUDA-graph replays (the library's own counter sees only the
+# launches its entry points issue): graph replays add the launch count of the captured call
+_replayed = 0
+
+
+def note_replayed(n: int) -> None:
+    global _replayed
+    _replayed += int(n)
+
+
+def launch_count() -> int:
+    """Kernels of this library launched so far: by its entry points and by graph replays."""
+    return int(lib().evs_launch_count()) + _replayed
+
+
 def ptr(t) -> int | None:
     """Device (or host) address of a torch tensor / None."""
     if t is None:

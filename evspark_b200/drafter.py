@@ -85,6 +85,22 @@ class DeviceDrafter:
                 "evs_draft_propose")
         return toks, q, conf, U
 
+    def propose_into(self, ip, anchors: torch.Tensor, gamma: int, greedy: bool, toks: torch.Tensor,
+                     q: torch.Tensor, conf: torch.Tensor, *, temperature: float = 1.0, top_k: int | None = 4,
+                     uniforms: torch.Tensor | None = None, forced: torch.Tensor | None = None) -> None:
+        """``propose`` into caller-owned outputs (tokens int64 [B,γ'], q fp64 [B,γ',V], conf fp32 [B,γ']):
+        a fixed sequence of launches over fixed buffers, which a CUDA graph can capture and replay."""
+        B = int(anchors.shape[0])
+        V = self.cfg.vocab_size
+        if (toks.shape != (B, gamma) or q.shape != (B, gamma, V) or conf.shape != (B, gamma)
+                or toks.dtype != torch.int64 or q.dtype != torch.float64 or conf.dtype != torch.float32):
+            raise ValueError("propose_into: outputs must be int64 [B,γ'], fp64 [B,γ',V] and fp32 [B,γ']")
+        k = 0 if top_k is None else int(top_k)
+        N.check(N.lib().evs_draft_propose(self._h, ip.handle, anchors.data_ptr(), B, int(gamma), int(greedy),
+                                          float(temperature), k, N.ptr(uniforms), N.ptr(forced), toks.data_ptr(),
+                                          q.data_ptr(), conf.data_ptr(), None, N.stream_ptr()),
+                "evs_draft_propose")
+
     def close(self):
         if getattr(self, "_h", None):
             N.lib().evs_drafter_destroy(self._h)

@@ -21,6 +21,7 @@ from dataclasses import dataclass, field
 import numpy as np
 import torch
 
+from evspark_b200 import _native as N
 from evspark_b200.specdec.block.driver import block_forward, prefill, step_forward_reference
 from evspark_b200.specdec.block.slice import slice_states_to_accept
 from evspark_b200.specdec.transforms import apply_transform, transform_rows
@@ -125,6 +126,10 @@ class _RoundBuffers:
         self.u_ver = torch.empty(gamma + 1, dtype=torch.float64, device=device)
         self.res_h = torch.empty(4 + gamma + 1, dtype=torch.int64, pin_memory=True)
         self.conf_h = torch.empty(gamma, dtype=torch.float32, pin_memory=True)
+        # drafter outputs of the round, and the drafter call captured as a CUDA graph per
+        # (state, sampling settings): the same launches, issued by one graph launch
+        self.toks = self.q = self.conf = None
+        self.draft_graphs: dict = {}
 
 
 def _spec_round_device(model, draft, ip, y: int, gamma: int, greedy: bool, rng, remaining: int, temperature,
@@ -144,8 +149,30 @@ def _spec_round_device(model, draft, ip, y: int, gamma: int, greedy: bool, rng, 
         bufs.u_draft_h.numpy()[:] = rng.random(int(gamma))
         bufs.u_draft.copy_(bufs.u_draft_h, non_blocking=True)
         u = bufs.u_draft[None]
-    toks_d, q_rows, conf_d, _ = draft.drafter.propose(ip, chunk[:, 0], int(gamma), greedy, temperature=temperature,
-                                                      top_k=top_k, uniforms=u)
+    dr = draft.drafter
+    if bufs.toks is None:
+        V = dr.cfg.vocab_size
+        bufs.toks = torch.empty(1, gamma, dtype=torch.int64, device=model.device)
+        bufs.q = torch.empty(1, gamma, V, dtype=torch.float64, device=model.device)
+        bufs.conf = torch.empty(1, gamma, dtype=torch.float32, device=model.device)
+    key = (ip.handle.value, dr._h.value, bool(greedy), float(temperature), None if top_k is None else int(top_k))
+    entry = bufs.draft_graphs.get(key)
+    call = lambda: dr.propose_into(ip, chunk[:, 0], int(gamma), greedy, bufs.toks, bufs.q, bufs.conf,
+                                   temperature=temperature, top_k=top_k, uniforms=u)
+    if entry is None:
+        call()  # this round's draft; then the same call is captured for the next rounds
+        graph = torch.cuda.CUDAGraph()
+        n0 = N.launch_count()
+        with torch.cuda.graph(graph):
+            call()
+        n_calls = N.launch_count() - n0
+        N.note_replayed(-n_calls)  # capturing issues nothing
+        bufs.draft_graphs[key] = (graph, n_calls)
+    else:
+        graph, n_calls = entry
+        graph.replay()
+        N.note_replayed(n_calls)
+    toks_d, q_rows, conf_d = bufs.toks, bufs.q, bufs.conf
     chunk[0, 1:] = toks_d[0]
     draft.capture_begin()
     logits = ip.forward(chunk, retain=True)
