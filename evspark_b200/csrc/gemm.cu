@@ -358,12 +358,13 @@ GemmPlan gemm_plan_f32(int N, int K, int M, int dual) {
   return p;
 }
 
-// drafter projections: one split (no reduction launch) unless the GEMM has fewer than 64 row tiles
+// drafter projections: one split (no reduction launch) when the GEMM has at least 128 row tiles;
+// otherwise K is split until about two CTAs per SM stream it (K chunks of at least 128 columns)
 GemmPlan gemm_plan_f32_drafter(int N, int K, int M) {
   GemmPlan p{N, K, M, 1, 0};
   const int tiles = (N + SK_ROWS - 1) / SK_ROWS;
   int splits = 1;
-  while (tiles * splits < 64 && (K + 128 * (splits + 1) - 1) / (128 * (splits + 1)) >= 1 && splits < K / 128) ++splits;
+  while (tiles < 128 && tiles * splits < 296 && splits < K / 128) ++splits;
   p.kchunk = (K + splits - 1) / splits;
   p.kchunk = (p.kchunk + 127) / 128 * 128;
   p.splits = (K + p.kchunk - 1) / p.kchunk;
