@@ -29,6 +29,13 @@ from evspark_b200.specdec.verifier import (draw_uniforms, rewind_uniforms, sampl
                                            verify_device_multicand)
 
 VOCAB_SIZE = 512
+# tokens per forward when a prompt is prefilled: the whole prompt up to this many per forward
+# (chunking does not change any result bit; fewer forwards stream the weights fewer times)
+PREFILL_CHUNK_MAX = 1024
+
+
+def _prefill_chunk(model, L: int) -> int:
+    return int(min(PREFILL_CHUNK_MAX, max(int(model.max_chunk), int(L))))
 
 
 @dataclass
@@ -411,7 +418,8 @@ def speculative_generate(model, draft, prompt_ids, n_tokens: int, gamma: int, gr
         return SpecGenerateResult(np.empty(0, dtype=np.int64), [], ip, anchor=y, rollback=rollback)
     seen = prompt_np.copy()
     if inference_params_dict is None:
-        ip = model.initialize_inference_params(max_seqlen=L + n_tokens + gamma + 2, max_batch=n_candidates)
+        ip = model.initialize_inference_params(max_seqlen=L + n_tokens + gamma + 2, max_batch=n_candidates,
+                                               max_chunk=_prefill_chunk(model, L))
         if has_capture:
             draft.capture_begin()
         prefill(model, prompt[:, :-1], ip)
@@ -456,7 +464,7 @@ def native_greedy_reference(model, prompt_ids, n_tokens: int, *, record_logits: 
     if n_tokens < 0:
         raise ValueError("n_tokens must be >= 0")
     L = int(prompt.shape[1])
-    ip = model.initialize_inference_params(max_seqlen=L + max(n_tokens, 0) + 2)
+    ip = model.initialize_inference_params(max_seqlen=L + max(n_tokens, 0) + 2, max_chunk=_prefill_chunk(model, L))
     if n_tokens == 0:
         return np.empty(0, dtype=np.int64), ip, None
     last = prefill(model, prompt, ip)[0, -1]
@@ -485,11 +493,10 @@ def native_sample_reference(model, prompt_ids, n_tokens: int, rng: np.random.Gen
     if n_tokens == 0:
         return np.empty(0, dtype=np.int64)
     L = int(prompt.shape[1])
-    ip = model.initialize_inference_params(max_seqlen=L + n_tokens + 2)
+    ip = model.initialize_inference_params(max_seqlen=L + n_tokens + 2, max_chunk=_prefill_chunk(model, L))
     last = prefill(model, prompt, ip)[0, -1]
     emitted = np.empty(n_tokens, dtype=np.int64)
     x = torch.empty(1, 1, dtype=torch.int64, device=device)
-    from evspark_b200 import _native as N
 
     for i in range(n_tokens):
         probs = transform_rows(last[None], temperature, top_k)
