@@ -58,11 +58,31 @@ class GenerateResult:
     extra: dict = field(default_factory=dict)
 
 
+def _init_graph_capture(device) -> None:
+    """The first CUDA-graph capture of a process initialises the runtime's graph machinery (tens of
+    milliseconds); do it once at load time, not inside the first generate call (whose rounds capture
+    the drafter call as a graph)."""
+    import torch
+
+    dev = torch.device(device)
+    if dev.type != "cuda" or not torch.cuda.is_available():
+        return
+    with torch.cuda.device(dev):
+        x = torch.zeros(1, device=dev)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            x.add_(1.0)
+        g.replay()
+        torch.cuda.synchronize(dev)
+        del g
+
+
 class EvSpark:
     def __init__(self, model, nd, device: str = "cuda:0"):
         self.model = model
         self._nd = nd
         self.device = device
+        _init_graph_capture(device)
 
     @classmethod
     def load(cls, ckpt: str | None = DEFAULT_CKPT, model_name: str = "evo2_7b", device: str = "cuda:0",
