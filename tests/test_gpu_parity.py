@@ -210,6 +210,33 @@ def test_prefill_chunking_invariant_bitwise(cuda, tiny, which):
         model.close()
 
 
+@pytest.mark.parametrize("which,L", [("tiny", 20000), ("7b_slice", 6000)])
+def test_long_context_multi_block_split_kv_bitwise(cuda, tiny, which, L):
+    """At contexts long enough that each split-KV CTA walks several key blocks (the grid keeps about
+    16 CTAs per SM), prefilling in 16-token chunks (split-KV + combine) and in 64-token chunks (fused
+    kernel) still gives the same bits at every position and for the verify block afterwards."""
+    if which == "tiny":
+        model, _ = tiny
+    else:
+        from evspark_b200.config import EVO2_7B_SLICE
+        from evspark_b200.model import TargetModel
+
+        model = TargetModel.random(EVO2_7B_SLICE, seed=9, device=cuda, init_on="cuda")
+    n_sm = torch.cuda.get_device_properties(cuda).multi_processor_count
+    kv_blocks = (L + 13 + 63) // 64
+    blocks_per_cta = -(-kv_blocks * model.cfg.n_heads // (16 * n_sm))
+    assert blocks_per_cta > 1, "the context must be long enough for several key blocks per CTA"
+    rng = np.random.default_rng(23)
+    prompt = rng.choice([65, 67, 71, 84], size=L)
+    chunk = rng.choice([65, 67, 71, 84], size=13)
+    pre16, blk16 = _prefill_then_block(model, prompt, chunk, 16)
+    pre64, blk64 = _prefill_then_block(model, prompt, chunk, 64)
+    assert torch.equal(pre16, pre64), (pre16 - pre64).abs().max().item()
+    assert torch.equal(blk16, blk64)
+    if which != "tiny":
+        model.close()
+
+
 def test_tiny_long_prefill_vs_oracle(tiny, oracle_tiny):
     """2048-token prompt prefilled in 256-token chunks (IIR over long chunks, MR tail carry across
     chunks, fused attention over 2 k keys), then a verify block: fp64 oracle agreement."""
