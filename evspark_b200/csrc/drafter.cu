@@ -61,36 +61,6 @@ __global__ void gather_ctx_kernel(RingPtrs rings, int n_inject, int ring_len, in
   }
 }
 
-// out = scale * (v / sqrt(mean(v²) + eps)), v = x (+ bias); one CTA per row
-__global__ void bias_rmsnorm_kernel(const float* x, const float* bias, const float* scale, float* out, int d,
-                                    float eps) {
-  pdl_trigger();
-  pdl_wait();
-  __shared__ float red[33];
-  const int row = blockIdx.x;
-  const float* xr = x + static_cast<size_t>(row) * d;
-  float ss = 0.f;
-  for (int c = threadIdx.x; c < d; c += blockDim.x) {
-    const float v = bias ? xr[c] + bias[c] : xr[c];
-    ss = fmaf(v, v, ss);
-  }
-  ss = warp_sum(ss);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    float s = 0.f;
-    for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) s += red[w];
-    red[32] = s;
-  }
-  __syncthreads();
-  const float rms = sqrtf(red[32] / static_cast<float>(d) + eps);
-  float* o = out + static_cast<size_t>(row) * d;
-  for (int c = threadIdx.x; c < d; c += blockDim.x) {
-    const float v = bias ? xr[c] + bias[c] : xr[c];
-    o[c] = scale[c] * (v / rms);
-  }
-}
-
 // rows b*g + t: embed[t == 0 ? anchor[b] : mask]  or embed[ids[b*g + t]] when ids is given
 __global__ void embed_rows_kernel(const float* embed, int H, const int64_t* anchor, const int64_t* ids, int g,
                                   int mask_id, float* out) {
@@ -104,42 +74,113 @@ __global__ void embed_rows_kernel(const float* embed, int H, const int64_t* anch
   for (int e = threadIdx.x; e < H; e += blockDim.x) dst[e] = src[e];
 }
 
-// x[row] = (x[row] + bias) + pos[t]   (pos may be null)
-__global__ void bias_pos_kernel(float* x, const float* bias, const float* pos, int g, int d, int rows) {
-  pdl_trigger();
-  pdl_wait();
-  const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (i >= static_cast<size_t>(rows) * d) return;
-  const int row = static_cast<int>(i / d), c = static_cast<int>(i % d);
-  float v = x[i] + bias[c];
-  if (pos) v = v + pos[(row % g) * d + c];
-  x[i] = v;
-}
+// Split-K partials of a projection summed in split order (reduce_splits_kernel's additions), then
+// the drafter's elementwise step after that projection (acc = the sum, t = row % g):
+//   EPI_BIAS_NORM   out = RMSNorm(acc + bias)                     context rows
+//   EPI_IN_NORM     h = (acc + bias) + pos[t]; out = RMSNorm(h)   in-projection and the first pre-norm
+//   EPI_RESID_NORM  h = h + (acc (+ bias)); out = RMSNorm(h)      attention / MLP output, next norm
+//   EPI_BIAS_SILU   out = silu(acc + bias)                        MLP hidden layer
+//   EPI_BIAS        out = acc + bias                              out-projection, conf in-projection
+//   EPI_SCALE       out = acc * s                                 logits scale H^-1/2
+// RMSNorm(v) = scale * (v / sqrt(mean(v²) + eps)), the sum of squares per thread over columns
+// tid, tid + 256, ..., then the warp butterfly and the warps in order.  The norm modes run one CTA
+// per row; the others one thread per element.
+enum DraftEpi { EPI_BIAS_NORM, EPI_IN_NORM, EPI_RESID_NORM, EPI_BIAS_SILU, EPI_BIAS, EPI_SCALE };
+constexpr int EPI_THREADS = 256;
+constexpr int EPI_VPT = 4;  // norm modes: columns per thread per pass
+constexpr int EPI_SB = 8;   // norm modes: splits per batch of loads
+struct DraftEpiArgs {
+  const float* ws;  // partials [splits][M][N]
+  int splits, M, N;
+  const float* bias;
+  const float* pos;  // EPI_IN_NORM: [g][N] position rows (t = row % g)
+  int g;
+  float* h;  // residual stream [M][N] (EPI_IN_NORM writes it, EPI_RESID_NORM updates it)
+  const float* scale;
+  float* out;
+  float eps, s;
+};
 
-// h += (x (+ bias))
-__global__ void residual_add_kernel(float* h, const float* x, const float* bias, int d, int rows) {
+template <int MODE>
+__global__ void __launch_bounds__(EPI_THREADS) draft_epi_kernel(DraftEpiArgs a) {
   pdl_trigger();
   pdl_wait();
-  const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (i >= static_cast<size_t>(rows) * d) return;
-  const float v = bias ? x[i] + bias[i % d] : x[i];
-  h[i] = h[i] + v;
-}
-
-__global__ void bias_silu_kernel(float* x, const float* bias, int n, int rows) {
-  pdl_trigger();
-  pdl_wait();
-  const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (i >= static_cast<size_t>(rows) * n) return;
-  const float v = x[i] + bias[i % n];
-  x[i] = v / (1.0f + expf(-v));
-}
-
-__global__ void scale_kernel(float* x, float s, size_t n) {
-  pdl_trigger();
-  pdl_wait();
-  const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (i < n) x[i] = x[i] * s;
+  const size_t MN = static_cast<size_t>(a.M) * a.N;
+  if constexpr (MODE == EPI_BIAS_NORM || MODE == EPI_IN_NORM || MODE == EPI_RESID_NORM) {
+    extern __shared__ float vrow[];  // the row before the norm
+    __shared__ float red[33];
+    const int row = blockIdx.x, N = a.N;
+    const size_t r0 = static_cast<size_t>(row) * N;
+    float ss = 0.f;
+    // EPI_VPT columns c = tid + 256 j per pass; the split loads of all of them are in flight together
+    for (int c0 = 0; c0 < N; c0 += EPI_THREADS * EPI_VPT) {
+      float acc[EPI_VPT], hv[EPI_VPT];
+#pragma unroll
+      for (int j = 0; j < EPI_VPT; ++j) {
+        acc[j] = 0.f;
+        const int c = c0 + threadIdx.x + j * EPI_THREADS;
+        if (MODE == EPI_RESID_NORM && c < N) hv[j] = a.h[r0 + c];
+      }
+      for (int s0 = 0; s0 < a.splits; s0 += EPI_SB) {
+        float v[EPI_VPT][EPI_SB];
+#pragma unroll
+        for (int j = 0; j < EPI_VPT; ++j)
+#pragma unroll
+          for (int k = 0; k < EPI_SB; ++k) {
+            const int c = c0 + threadIdx.x + j * EPI_THREADS;
+            if (c < N && s0 + k < a.splits) v[j][k] = __ldcg(a.ws + static_cast<size_t>(s0 + k) * MN + r0 + c);
+          }
+#pragma unroll
+        for (int j = 0; j < EPI_VPT; ++j)
+#pragma unroll
+          for (int k = 0; k < EPI_SB; ++k)
+            if (s0 + k < a.splits) acc[j] += v[j][k];
+      }
+#pragma unroll
+      for (int j = 0; j < EPI_VPT; ++j) {
+        const int c = c0 + threadIdx.x + j * EPI_THREADS;
+        if (c >= N) break;
+        float v;
+        if constexpr (MODE == EPI_BIAS_NORM) {
+          v = acc[j] + a.bias[c];
+        } else if constexpr (MODE == EPI_IN_NORM) {
+          v = acc[j] + a.bias[c];
+          v = v + a.pos[static_cast<size_t>(row % a.g) * N + c];
+          a.h[r0 + c] = v;
+        } else {
+          const float x = a.bias ? acc[j] + a.bias[c] : acc[j];
+          v = hv[j] + x;
+          a.h[r0 + c] = v;
+        }
+        vrow[c] = v;
+        ss = fmaf(v, v, ss);
+      }
+    }
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float t = 0.f;
+      for (int w = 0; w < EPI_THREADS / 32; ++w) t += red[w];
+      red[32] = t;
+    }
+    __syncthreads();
+    const float rms = sqrtf(red[32] / static_cast<float>(N) + a.eps);
+    float* o = a.out + r0;
+    for (int c = threadIdx.x; c < N; c += EPI_THREADS) o[c] = a.scale[c] * (vrow[c] / rms);
+  } else {
+    const size_t i = static_cast<size_t>(blockIdx.x) * EPI_THREADS + threadIdx.x;
+    if (i >= MN) return;
+    const float acc = split_sum(a.ws + i, MN, a.splits);
+    if constexpr (MODE == EPI_BIAS_SILU) {
+      const float v = acc + a.bias[i % a.N];
+      a.out[i] = v / (1.0f + expf(-v));
+    } else if constexpr (MODE == EPI_BIAS) {
+      a.out[i] = acc + a.bias[i % a.N];
+    } else {
+      a.out[i] = acc * a.s;
+    }
+  }
 }
 
 // kv_in[b] = [ctx[b] (CW rows) ; xb[b] (g rows)]
@@ -621,6 +662,46 @@ int sgemm(evs_drafter* dr, const float* W, const float* X, int ldx, float* out, 
 
 inline unsigned blocks_for(size_t n, int t) { return static_cast<unsigned>((n + t - 1) / t); }
 
+// projection partials into the workspace (no reduction), then the fused epilogue `mode` over them
+int sgemm_epi(evs_drafter* dr, const float* W, const float* X, int ldx, int N, int K, int M, int mode,
+              DraftEpiArgs e, cudaStream_t st) {
+  const GemmPlan p = gemm_plan_f32_drafter(N, K, M);
+  EVS_CHECK_RANGE(static_cast<size_t>(p.splits) * M * N <= dr->ws_floats, "drafter workspace too small");
+  EVS_TRY(launch_gemm_simt(W, nullptr, X, ldx, EVS_DTYPE_FP32, p, dr->ws, st, true));
+  e.ws = dr->ws;
+  e.splits = p.splits;
+  e.M = M;
+  e.N = N;
+  const bool norm = mode == EPI_BIAS_NORM || mode == EPI_IN_NORM || mode == EPI_RESID_NORM;
+  const dim3 grid = norm ? dim3(M) : dim3(blocks_for(static_cast<size_t>(M) * N, EPI_THREADS));
+  const size_t smem = norm ? sizeof(float) * N : 0;
+  EVS_CHECK_ARG(smem <= 48 * 1024, "drafter width too large for the fused norm");
+  switch (mode) {
+    case EPI_BIAS_NORM: EVS_CUDA_TRY(evs_launch(draft_epi_kernel<EPI_BIAS_NORM>, grid, dim3(EPI_THREADS), smem, st, true, e)); break;
+    case EPI_IN_NORM: EVS_CUDA_TRY(evs_launch(draft_epi_kernel<EPI_IN_NORM>, grid, dim3(EPI_THREADS), smem, st, true, e)); break;
+    case EPI_RESID_NORM: EVS_CUDA_TRY(evs_launch(draft_epi_kernel<EPI_RESID_NORM>, grid, dim3(EPI_THREADS), smem, st, true, e)); break;
+    case EPI_BIAS_SILU: EVS_CUDA_TRY(evs_launch(draft_epi_kernel<EPI_BIAS_SILU>, grid, dim3(EPI_THREADS), 0, st, true, e)); break;
+    case EPI_BIAS: EVS_CUDA_TRY(evs_launch(draft_epi_kernel<EPI_BIAS>, grid, dim3(EPI_THREADS), 0, st, true, e)); break;
+    default: EVS_CUDA_TRY(evs_launch(draft_epi_kernel<EPI_SCALE>, grid, dim3(EPI_THREADS), 0, st, true, e)); break;
+  }
+  evs_count_launch(1);
+  return EVS_OK;
+}
+
+DraftEpiArgs epi(const float* bias, float* out, const float* scale = nullptr, float* h = nullptr,
+                 const float* pos = nullptr, int g = 1, float eps = 1e-6f, float sc = 1.f) {
+  DraftEpiArgs e{};
+  e.bias = bias;
+  e.out = out;
+  e.scale = scale;
+  e.h = h;
+  e.pos = pos;
+  e.g = g;
+  e.eps = eps;
+  e.s = sc;
+  return e;
+}
+
 }  // namespace
 
 extern "C" {
@@ -756,8 +837,8 @@ int evs_draft_propose(evs_drafter* dr, const evs_state* s, const int64_t* anchor
     for (int k = 0; k < 4; ++k) rg.p[k] = s->cap_ring[k];
     EVS_CUDA_TRY(evs_launch(gather_ctx_kernel, dim3(dim3(CW, B)), dim3(256), 0, st, true, rg, c.n_inject, s->ring_len, H, s->d_len, CW, dr->ctx_in));
     EVS_CUDA_TRY(cudaGetLastError());
-    EVS_TRY(sgemm(dr, T[EVS_D_CTX_W], dr->ctx_in, c.n_inject * H, dr->kb, d, c.n_inject * H, B * CW, st));
-    EVS_CUDA_TRY(evs_launch(bias_rmsnorm_kernel, dim3(B * CW), dim3(256), 0, st, true, dr->kb, T[EVS_D_CTX_B], T[EVS_D_CTX_NORM], dr->ctx, d, eps));
+    EVS_TRY(sgemm_epi(dr, T[EVS_D_CTX_W], dr->ctx_in, c.n_inject * H, d, c.n_inject * H, B * CW, EPI_BIAS_NORM,
+                      epi(T[EVS_D_CTX_B], dr->ctx, T[EVS_D_CTX_NORM], nullptr, nullptr, 1, eps), st));
   } else {
     EVS_CUDA_TRY(cudaMemsetAsync(dr->ctx, 0, sizeof(float) * B * CW * d, st));
   }
@@ -766,37 +847,32 @@ int evs_draft_propose(evs_drafter* dr, const evs_state* s, const int64_t* anchor
   if (c.n_inject == 0) EVS_CUDA_TRY(cudaMemsetAsync(dr->prev, 0, sizeof(int32_t) * B, st));
   // ---- h = in_proj(embed([anchor, MASK...])) + pos ----
   EVS_CUDA_TRY(evs_launch(embed_rows_kernel, dim3(rows), dim3(256), 0, st, true, T[EVS_D_EMBED], H, anchor, nullptr, g, c.mask_id, dr->emb));
-  EVS_TRY(sgemm(dr, T[EVS_D_IN_W], dr->emb, H, dr->h, d, H, rows, st));
-  EVS_CUDA_TRY(evs_launch(bias_pos_kernel, dim3(blocks_for(static_cast<size_t>(rows) * d, 256)), dim3(256), 0, st, true, dr->h, T[EVS_D_IN_B], T[EVS_D_POS],
-                                                                                 g, d, rows));
+  // h = (in_proj + bias) + pos, and the first layer's pre-norm of h into xb
+  const float* ln1_0 = c.n_layers > 0 ? T[EVS_D_LAYER0 + EVS_D_LN1] : T[EVS_D_FINAL_LN];
+  EVS_TRY(sgemm_epi(dr, T[EVS_D_IN_W], dr->emb, H, d, H, rows, EPI_IN_NORM,
+                    epi(T[EVS_D_IN_B], dr->xb, ln1_0, dr->h, T[EVS_D_POS], g, eps), st));
   for (int l = 0; l < c.n_layers; ++l) {
     const float* const* L = T + EVS_D_LAYER0 + l * EVS_D_PER_LAYER;
-    EVS_CUDA_TRY(evs_launch(bias_rmsnorm_kernel, dim3(rows), dim3(256), 0, st, true, dr->h, nullptr, L[EVS_D_LN1], dr->xb, d, eps));
+    // the norm after this layer's MLP: the next layer's pre-norm, or the final norm
+    const float* next_ln = l + 1 < c.n_layers ? T[EVS_D_LAYER0 + (l + 1) * EVS_D_PER_LAYER + EVS_D_LN1] : T[EVS_D_FINAL_LN];
     EVS_TRY(sgemm(dr, L[EVS_D_Q], dr->xb, d, dr->q, d, d, rows, st));
     EVS_CUDA_TRY(evs_launch(build_kv_kernel, dim3(dim3(nk, B)), dim3(256), 0, st, true, dr->ctx, dr->xb, CW, g, d, dr->kv_in));
     EVS_TRY(sgemm(dr, L[EVS_D_K], dr->kv_in, d, dr->kb, d, d, B * nk, st));
     EVS_TRY(sgemm(dr, L[EVS_D_V], dr->kv_in, d, dr->vb, d, d, B * nk, st));
     EVS_CUDA_TRY(evs_launch(draft_attn_kernel, dim3(dim3(g, c.n_heads, B)), dim3(128), 0, st, true, dr->q, dr->kb, dr->vb, ctx_len, CW, g, d, c.n_heads,
                                                             dr->y));
-    EVS_TRY(sgemm(dr, L[EVS_D_O], dr->y, d, dr->tmp, d, d, rows, st));
-    EVS_CUDA_TRY(evs_launch(residual_add_kernel, dim3(blocks_for(static_cast<size_t>(rows) * d, 256)), dim3(256), 0, st, true, dr->h, dr->tmp, nullptr, d,
-                                                                                        rows));
-    EVS_CUDA_TRY(evs_launch(bias_rmsnorm_kernel, dim3(rows), dim3(256), 0, st, true, dr->h, nullptr, L[EVS_D_LN2], dr->xb, d, eps));
-    EVS_TRY(sgemm(dr, L[EVS_D_MLP0_W], dr->xb, d, dr->m1, hid, d, rows, st));
-    EVS_CUDA_TRY(evs_launch(bias_silu_kernel, dim3(blocks_for(static_cast<size_t>(rows) * hid, 256)), dim3(256), 0, st, true, dr->m1, L[EVS_D_MLP0_B], hid,
-                                                                                      rows));
-    EVS_TRY(sgemm(dr, L[EVS_D_MLP2_W], dr->m1, hid, dr->tmp, d, hid, rows, st));
-    EVS_CUDA_TRY(evs_launch(residual_add_kernel, dim3(blocks_for(static_cast<size_t>(rows) * d, 256)), dim3(256), 0, st, true, dr->h, dr->tmp,
-                                                                                        L[EVS_D_MLP2_B], d, rows));
+    // h += out_proj(y); xb = pre-MLP norm of h
+    EVS_TRY(sgemm_epi(dr, L[EVS_D_O], dr->y, d, d, d, rows, EPI_RESID_NORM,
+                      epi(nullptr, dr->xb, L[EVS_D_LN2], dr->h, nullptr, 1, eps), st));
+    EVS_TRY(sgemm_epi(dr, L[EVS_D_MLP0_W], dr->xb, d, hid, d, rows, EPI_BIAS_SILU, epi(L[EVS_D_MLP0_B], dr->m1), st));
+    // h += mlp2(m1) + bias; xb = next pre-norm (the final norm after the last layer)
+    EVS_TRY(sgemm_epi(dr, L[EVS_D_MLP2_W], dr->m1, hid, d, hid, rows, EPI_RESID_NORM,
+                      epi(L[EVS_D_MLP2_B], dr->xb, next_ln, dr->h, nullptr, 1, eps), st));
   }
-  // ---- U = (final_ln(h) out_proj) embedᵀ H^-1/2 ----
-  EVS_CUDA_TRY(evs_launch(bias_rmsnorm_kernel, dim3(rows), dim3(256), 0, st, true, dr->h, nullptr, T[EVS_D_FINAL_LN], dr->xb, d, eps));
-  EVS_TRY(sgemm(dr, T[EVS_D_OUT_W], dr->xb, d, dr->z, H, d, rows, st));
-  EVS_CUDA_TRY(evs_launch(bias_pos_kernel, dim3(blocks_for(static_cast<size_t>(rows) * H, 256)), dim3(256), 0, st, true, dr->z, T[EVS_D_OUT_B], nullptr, g,
-                                                                                 H, rows));
-  EVS_TRY(sgemm(dr, T[EVS_D_EMBED], dr->z, H, dr->U, V, H, rows, st));
-  EVS_CUDA_TRY(evs_launch(scale_kernel, dim3(blocks_for(static_cast<size_t>(rows) * V, 256)), dim3(256), 0, st, true, 
-      dr->U, 1.0f / sqrtf(static_cast<float>(H)), static_cast<size_t>(rows) * V));
+  // ---- U = (final_ln(h) out_proj) embedᵀ H^-1/2 (xb holds final_ln(h)) ----
+  EVS_TRY(sgemm_epi(dr, T[EVS_D_OUT_W], dr->xb, d, H, d, rows, EPI_BIAS, epi(T[EVS_D_OUT_B], dr->z), st));
+  EVS_TRY(sgemm_epi(dr, T[EVS_D_EMBED], dr->z, H, V, H, rows, EPI_SCALE,
+                    epi(nullptr, dr->U, nullptr, nullptr, nullptr, 1, eps, 1.0f / sqrtf(static_cast<float>(H))), st));
   // ---- serial Markov head ----
   if ((V == 512 || V == 256 || V == 128) && g <= EVS_RETAIN_MAX) {  // per-step inputs held in shared memory
     auto head = V == 512 ? serial_head_warp_kernel<4> : (V == 256 ? serial_head_warp_kernel<2> : serial_head_warp_kernel<1>);
@@ -808,13 +884,11 @@ int evs_draft_propose(evs_drafter* dr, const evs_state* s, const int64_t* anchor
   }
   // ---- confidence: σ(conf_w [final_ln(h) ; in_proj(embed(prev))]) ----
   EVS_CUDA_TRY(evs_launch(embed_rows_kernel, dim3(rows), dim3(256), 0, st, true, T[EVS_D_EMBED], H, nullptr, dr->prev, g, 0, dr->emb));
-  EVS_TRY(sgemm(dr, T[EVS_D_IN_W], dr->emb, H, dr->pe, d, H, rows, st));
-  EVS_CUDA_TRY(evs_launch(bias_pos_kernel, dim3(blocks_for(static_cast<size_t>(rows) * d, 256)), dim3(256), 0, st, true, dr->pe, T[EVS_D_IN_B], nullptr, g,
-                                                                                 d, rows));
+  EVS_TRY(sgemm_epi(dr, T[EVS_D_IN_W], dr->emb, H, d, H, rows, EPI_BIAS, epi(T[EVS_D_IN_B], dr->pe), st));
   EVS_CUDA_TRY(evs_launch(conf_kernel, dim3(blocks_for(rows, 4)), dim3(128), 0, st, true, dr->xb, dr->pe, T[EVS_D_CONF_W], T[EVS_D_CONF_B], d, rows, conf));
-  // non-GEMM kernels of this call (the projections count themselves): context gather + norm,
-  // embed + bias/pos, 7 per layer, final norm + bias + scale, serial head, conf embed + bias + dot
-  evs_count_launch((c.n_inject > 0 ? 2 : 0) + 2 + 7 * c.n_layers + 3 + 4);
+  // kernels of this call that count nowhere else (projections and their fused epilogues count
+  // themselves): context gather, embed, kv build + attention per layer, serial head, conf embed + dot
+  evs_count_launch((c.n_inject > 0 ? 1 : 0) + 1 + 2 * c.n_layers + 3);
   if (U_out != nullptr)
     EVS_CUDA_TRY(cudaMemcpyAsync(U_out, dr->U, sizeof(float) * rows * V, cudaMemcpyDeviceToDevice, st));
   EVS_CUDA_TRY(cudaGetLastError());
