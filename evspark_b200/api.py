@@ -78,11 +78,39 @@ def _init_graph_capture(device) -> None:
 
 
 class EvSpark:
-    def __init__(self, model, nd, device: str = "cuda:0"):
+    """state_seqlen: positions of the decode state allocated here and reused by every generate call
+    whose prompt + tokens + gamma fit (a serving engine's preallocated caches: a call then allocates
+    no device memory); a longer call allocates a larger state, which is kept instead.  0: allocate
+    the state on first use."""
+
+    def __init__(self, model, nd, device: str = "cuda:0", *, state_seqlen: int = 4096):
         self.model = model
         self._nd = nd
         self.device = device
+        self._state = None
         _init_graph_capture(device)
+        if state_seqlen > 0:
+            self._state = self._new_state(int(state_seqlen))
+
+    def _new_state(self, max_seqlen: int):
+        from evspark_b200.specdec.block.loop import PREFILL_CHUNK_MAX
+
+        # the largest prefill chunk, so that every prompt is prefilled in the chunks a fresh state of
+        # its own length would use (the results do not depend on the chunking either)
+        return self.model.initialize_inference_params(max_seqlen=max_seqlen, max_batch=1,
+                                                      max_chunk=PREFILL_CHUNK_MAX)
+
+    def _decode_state(self, need: int):
+        """The kept decode state, reset to length 0, or a new one when `need` positions do not fit."""
+        if self._state is not None and self._state.max_seqlen >= need:
+            self._state.batch = 1
+            self._state.set_offset(0)
+            return self._state
+        if self._state is not None:
+            self._state.close()
+            self._state = None
+        self._state = self._new_state(need)
+        return self._state
 
     @classmethod
     def load(cls, ckpt: str | None = DEFAULT_CKPT, model_name: str = "evo2_7b", device: str = "cuda:0",
@@ -135,17 +163,25 @@ class EvSpark:
 
         from evspark_b200.specdec.block.loop import speculative_generate
 
+        from evspark_b200.specdec.block.driver import prefill
+
         seq, ids = self._ids(prompt)
         g = int(gamma) if gamma else self.gamma
+        L = int(ids.shape[1])
         self._nd.capture_reset()
         torch.cuda.synchronize()
         t0 = time.perf_counter()
+        # prefill the prompt (all but its last token, the first anchor) into the kept decode state,
+        # with the drafter capturing its context, as speculative_generate does with a fresh state
+        ip = self._decode_state(L + int(n_tokens) + g + 2)
+        self._nd.capture_begin()
+        prefill(self.model, ids[:, :-1], ip)
+        self._nd.capture_commit(L - 1)
         spec = speculative_generate(self.model, self._nd, ids, int(n_tokens), g, greedy=greedy,
                                     rng=np.random.default_rng(seed), temperature=temperature, top_k=top_k,
-                                    rollback="slice", timing=False)
+                                    rollback="slice", timing=False, inference_params_dict=ip)
         torch.cuda.synchronize()
         wall = time.perf_counter() - t0
-        spec.inference_params_dict.close()
         ks = [int(r.k) for r in spec.rounds_log]
         out = np.asarray(spec.emitted_ids)
         return GenerateResult(text=ids_to_text(out), ids=out, mode="greedy" if greedy else "sampling",
@@ -178,6 +214,9 @@ class EvSpark:
                               extra={"seed": seed, "prompt_bp": len(seq)})
 
     def close(self) -> None:
+        if self._state is not None:
+            self._state.close()
+            self._state = None
         if self._nd is not None:
             self._nd.close()
             self._nd = None

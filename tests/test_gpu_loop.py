@@ -219,3 +219,35 @@ def test_single_sync_round_equals_general_round(tiny):
         assert k1 == k2 and o1 == o2
         assert torch.equal(f1, f2) and torch.equal(s1, s2)
     nd.close()
+
+
+def test_evspark_generate_reuses_its_decode_state(tiny):
+    """EvSpark keeps one decode state across generate calls: it resets it to length 0 and
+    allocates a larger one when a call needs more positions.  Every call emits exactly the tokens
+    that speculative_generate emits with a fresh state of its own, when sampling and greedy."""
+    from evspark_b200.api import EvSpark, ids_to_text
+    from evspark_b200.config import DRAFTERS
+    from evspark_b200.drafter import DeviceDrafter
+    from evspark_b200.specdec.block.loop import speculative_generate
+    from evspark_b200.specdec.block.neural_draft import NeuralDraftModel
+
+    model, w = tiny
+    dr = DeviceDrafter.random(DRAFTERS["tiny"], embed=w["embed"], device=model.device)
+    nd = NeuralDraftModel(model, dr, ("blocks.2",))
+    es = EvSpark(model, nd, str(model.device), state_seqlen=300)
+    rng = np.random.default_rng(7)
+    p1 = ids_to_text(rng.choice([65, 67, 71, 84], size=200))
+    p2 = ids_to_text(rng.choice([65, 67, 71, 84], size=260))  # 260 + 48 + 14 > 300: a larger state
+    state0 = es._state
+    for prompt, n, greedy, seed in ((p1, 48, False, 5), (p1, 48, False, 5), (p1, 40, True, 0), (p2, 48, False, 9)):
+        got = es.generate(prompt, n_tokens=n, greedy=greedy, seed=seed)
+        nd.capture_reset()
+        ids = torch.as_tensor(np.frombuffer(prompt.encode("ascii"), dtype=np.uint8).astype(np.int64))[None]
+        ref = speculative_generate(model, nd, ids, n, 12, greedy=greedy, rng=np.random.default_rng(seed),
+                                   temperature=1.0, top_k=4)
+        ref.inference_params_dict.close()
+        np.testing.assert_array_equal(got.ids, ref.emitted_ids)
+    assert es._state is not state0 and es._state.max_seqlen >= 260 + 48 + 14
+    es._state.close()  # not es.close(): the model belongs to the module fixture
+    es._state = None
+    nd.close()
