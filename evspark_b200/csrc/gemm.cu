@@ -72,14 +72,17 @@ __global__ void __launch_bounds__(192, 1)
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
     if (dual) prefetch_tmap(&tmA2);
+    // the weights stream through once per forward: evict them first, so that the states, caches
+    // and partial sums of the small kernels stay in L2
+    const uint64_t pol = l2_policy_evict_first();
     auto load_a = [&](int i, int s) {
       const int kx = (kb_begin + i) * GEMM_BK;
       uint8_t* a_dst = sA + s * A_STAGE_BYTES;
       if (dual) {
-        tma_load_2d(&tmA, &full[s], a_dst, kx, tile * (GEMM_BM / 2));
-        tma_load_2d(&tmA2, &full[s], a_dst + A_STAGE_BYTES / 2, kx, tile * (GEMM_BM / 2));
+        tma_load_2d_hint(&tmA, &full[s], a_dst, kx, tile * (GEMM_BM / 2), pol);
+        tma_load_2d_hint(&tmA2, &full[s], a_dst + A_STAGE_BYTES / 2, kx, tile * (GEMM_BM / 2), pol);
       } else {
-        tma_load_2d(&tmA, &full[s], a_dst, kx, tile * GEMM_BM);
+        tma_load_2d_hint(&tmA, &full[s], a_dst, kx, tile * GEMM_BM, pol);
       }
     };
     auto load_b = [&](int i, int s) {
