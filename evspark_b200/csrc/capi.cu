@@ -75,6 +75,10 @@ int gemm(const evs_model* m, evs_state* s, const CUtensorMap* tA, const CUtensor
   if (m->cfg.dtype == EVS_DTYPE_BF16) {
     const CUtensorMap* tB =
         tB_override ? tB_override : (K == m->cfg.d_model ? s->tm_act_d : (K == m->Fl ? s->tm_act_f : s->tm_act_l));
+    if (m->tp_world == 1 && gemm_serial(p)) {
+      *splits = 1;  // the splits' sum, stored as one split
+      return launch_gemm_tc_serial(tA, tA2, tB, p, out, s->d_err, st, s->use_pdl());
+    }
     return launch_gemm_tc(tA, tA2, tB, p, out, s->d_err, st, s->use_pdl());
   }
   return launch_gemm_simt(W, W2, s->act, s->ld_act, m->cfg.dtype, p, out, st, s->use_pdl());

@@ -175,6 +175,155 @@ __global__ void __launch_bounds__(192, 1)
   }
 }
 
+// Large token counts (prefill): the CTA of (token tile, weight tile) walks every split of the
+// fixed split plan in order.  Each split is accumulated from zero in its own TMEM buffer by the same
+// MMA sequence as in gemm_tc_kernel, and the epilogue adds the splits into a running fp32 sum
+// (0 + s0 + s1 + ..., the consumers' order of additions).  The sum is stored as the only split:
+// a consumer reading one split computes 0 + sum = sum, so every row gets the bits of the split-K
+// path without writing and re-reading the per-split partial sums.  Two TMEM buffers alternate:
+// the MMA of split s + 2 waits until the epilogue has read split s.
+constexpr int SER_NT = 128;
+// two CTAs per SM (registers <= 168): one CTA's epilogue and another's main loop overlap
+__global__ void __launch_bounds__(192, 2)
+    gemm_tc_serial_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmA2,
+                          const __grid_constant__ CUtensorMap tmB, float* __restrict__ ws, int N, int K, int M,
+                          int splits, int dual, EvsDevErr* err) {
+  constexpr int NT = SER_NT;
+  using C = TcCfg<NT>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + C::STAGES * A_STAGE_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
+  uint64_t* empty = full + C::STAGES;
+  uint64_t* accf = empty + C::STAGES;  // [2] split accumulated
+  uint64_t* acce = accf + 2;           // [2] split read by the epilogue
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acce + 2);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ttile = blockIdx.x, tile = blockIdx.y;
+  const int kblocks = K / GEMM_BK;
+  pdl_trigger();
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&accf[b], 1);
+      mbar_init(&acce[b], 128);
+    }
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 2 * NT);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // every k-block in order (the splits' ranges concatenated)
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+    if (dual) prefetch_tmap(&tmA2);
+    const uint64_t pol = l2_policy_evict_first();
+    auto load_a = [&](int kb, int s) {
+      const int kx = kb * GEMM_BK;
+      uint8_t* a_dst = sA + s * A_STAGE_BYTES;
+      if (dual) {
+        tma_load_2d_hint(&tmA, &full[s], a_dst, kx, tile * (GEMM_BM / 2), pol);
+        tma_load_2d_hint(&tmA2, &full[s], a_dst + A_STAGE_BYTES / 2, kx, tile * (GEMM_BM / 2), pol);
+      } else {
+        tma_load_2d_hint(&tmA, &full[s], a_dst, kx, tile * GEMM_BM, pol);
+      }
+    };
+    auto load_b = [&](int kb, int s) {
+      tma_load_2d(&tmB, &full[s], sB + s * C::B_STAGE_BYTES, kb * GEMM_BK, ttile * NT);
+    };
+    const int pre = kblocks < C::STAGES ? kblocks : C::STAGES;
+    for (int i = 0; i < pre; ++i) {
+      mbar_arrive_expect_tx(&full[i], C::STAGE_BYTES);
+      load_a(i, i);
+    }
+    pdl_wait();
+    for (int i = 0; i < pre; ++i) load_b(i, i);
+    for (int i = pre; i < kblocks; ++i) {
+      const int s = i % C::STAGES;
+      if (!mbar_wait_bounded(&empty[s], ((i / C::STAGES) & 1) ^ 1, err, EVS_K_GEMM_TC, 41)) break;
+      mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
+      load_a(i, s);
+      load_b(i, s);
+    }
+  } else if (warp == 1 && lane == 0) {
+    constexpr uint32_t idesc = umma_idesc_bf16(GEMM_BM, NT);
+    bool ok = true;
+    for (int sp = 0; sp < splits && ok; ++sp) {
+      const int kb0 = static_cast<int>(static_cast<long long>(kblocks) * sp / splits);
+      const int kb1 = static_cast<int>(static_cast<long long>(kblocks) * (sp + 1) / splits);
+      const int buf = sp & 1;
+      if (sp >= 2 && !mbar_wait_bounded(&acce[buf], ((sp >> 1) - 1) & 1, err, EVS_K_GEMM_TC, 42)) break;
+      tc_fence_after();
+      for (int kb = kb0; kb < kb1; ++kb) {
+        const int s = kb % C::STAGES;
+        if (!mbar_wait_bounded(&full[s], (kb / C::STAGES) & 1, err, EVS_K_GEMM_TC, 43)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t a0 = smem_u32(sA + s * A_STAGE_BYTES);
+        const uint32_t b0 = smem_u32(sB + s * C::B_STAGE_BYTES);
+#pragma unroll
+        for (int j = 0; j < GEMM_BK / 16; ++j)
+          tc_mma_f16(tmem_base + buf * NT, umma_desc_sw128(a0 + j * 32), umma_desc_sw128(b0 + j * 32), idesc,
+                     (kb != kb0 || j != 0) ? 1u : 0u);
+        tc_commit(&empty[s]);
+      }
+      if (ok) tc_commit(&accf[buf]);
+    }
+  } else if (warp >= 2) {
+    const int q = warp & 3;  // TMEM lane quadrant this warp may access
+    float sum[NT];
+#pragma unroll
+    for (int j = 0; j < NT; ++j) sum[j] = 0.f;
+    bool ok = true;
+    for (int sp = 0; sp < splits; ++sp) {
+      const int buf = sp & 1;
+      ok = mbar_wait_bounded(&accf[buf], (sp >> 1) & 1, err, EVS_K_GEMM_TC, 44);
+      if (!ok) break;
+      tc_fence_after();
+#pragma unroll
+      for (int c0 = 0; c0 < NT; c0 += 16) {
+        float v[16];
+        tmem_ld_32x32b_x16(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * NT + c0, v);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 16; ++j) sum[c0 + j] += v[j];
+      }
+      tc_fence_before();
+      asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&acce[buf])) : "memory");
+    }
+    pdl_wait();  // (already satisfied: the MMAs consumed activations loaded after the wait)
+    if (ok) {
+      const int row = tile * GEMM_BM + q * 32 + lane;
+#pragma unroll
+      for (int j = 0; j < NT; ++j) {
+        const int tok = ttile * NT + j;
+        if (tok < M) ws[static_cast<size_t>(tok) * N + row] = sum[j];
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 2 * NT);
+  }
+}
+
 // fp32 projection for few token rows (the drafter, fp32 targets): CTA = 8 warps x 4 weight rows,
 // one split of K (SK_KC <= 1024 columns) and up to 16 token rows.  The token rows of the split are
 // staged in shared memory with 16-byte asynchronous copies; each warp streams its 4 weight rows
@@ -372,6 +521,31 @@ GemmPlan gemm_plan_f32_drafter(int N, int K, int M) {
   p.kchunk = (p.kchunk + 127) / 128 * 128;
   p.splits = (K + p.kchunk - 1) / p.kchunk;
   return p;
+}
+
+// Whether a projection of M token rows runs gemm_tc_serial_kernel: many token rows (a prefill
+// chunk), and at least one wave of (token tile, weight tile) CTAs.  The choice changes no bit.
+bool gemm_serial(const GemmPlan& p) {
+  const long long ctas = static_cast<long long>((p.M + SER_NT - 1) / SER_NT) * (p.N / GEMM_BM);
+  return p.M >= 512 && p.splits > 1 && ctas >= 148;
+}
+
+int launch_gemm_tc_serial(const CUtensorMap* tmA, const CUtensorMap* tmA2, const CUtensorMap* tmB, const GemmPlan& p,
+                          float* ws, EvsDevErr* err, cudaStream_t st, bool pdl) {
+  EVS_CHECK_ARG(p.N % GEMM_BM == 0 && p.K % GEMM_BK == 0, "tcgen05 GEMM needs N % 128 == 0 and K % 64 == 0");
+  EVS_CHECK_ARG(p.splits >= 1 && p.splits <= p.K / GEMM_BK, "bad split count");
+  if (p.M <= 0) return EVS_OK;
+  using C = TcCfg<SER_NT>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    EVS_CUDA_TRY(cudaFuncSetAttribute(gemm_tc_serial_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+    attr_set = true;
+  }
+  dim3 grid((p.M + SER_NT - 1) / SER_NT, p.N / GEMM_BM, 1);
+  EVS_CUDA_TRY(evs_launch(gemm_tc_serial_kernel, grid, dim3(192), C::SMEM, st, pdl, *tmA, tmA2 ? *tmA2 : *tmA,
+                          tmB[gemm_tile_index(GEMM_NT[2])], ws, p.N, p.K, p.M, p.splits, p.dual, err));
+  evs_count_launch(1);
+  return EVS_OK;
 }
 
 int gemm_tile_index(int M) { return M <= GEMM_NT[0] ? 0 : (M <= GEMM_NT[1] ? 1 : 2); }

@@ -147,6 +147,11 @@ int gemm_tile_index(int M);
 int launch_gemm_tc(const CUtensorMap* tmA, const CUtensorMap* tmA2, const CUtensorMap* tmB, const GemmPlan& p,
                    float* ws, EvsDevErr* err, cudaStream_t st, bool pdl = false, void* swiglu_act = nullptr,
                    int ld_act = 0);
+// large token counts: every split in one CTA per (token tile, weight tile), the splits' sum stored
+// as the only split (the same bits as the split partials summed in order); see gemm_serial
+bool gemm_serial(const GemmPlan& p);
+int launch_gemm_tc_serial(const CUtensorMap* tmA, const CUtensorMap* tmA2, const CUtensorMap* tmB, const GemmPlan& p,
+                          float* ws, EvsDevErr* err, cudaStream_t st, bool pdl = false);
 int launch_gemm_simt(const void* W, const void* W2, const void* X, int ldx, int dtype, const GemmPlan& p, float* ws,
                      cudaStream_t st, bool pdl = false);
 int make_tmap_2d_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t row_stride_bytes,
