@@ -433,8 +433,29 @@ __global__ void __launch_bounds__(128) serial_head_warp_kernel(const float* U, c
             for (int t = 0; t < 16; ++t) m[t] = (keep >> t & 1u) ? p[t] : 0.0;
             const double ms = warp_pw_sum<NL>(m, lane);
             const bool bad2 = !(ms > 0.0) || !isfinite(ms);
+            // the kept weights / ms: at most top_k per warp and usually at most one per lane, so the
+            // lanes divide their r-th kept weight in round r (warp-uniform rounds, no per-slot branch)
+            int rounds = __popc(keep);
 #pragma unroll
-            for (int t = 0; t < 16; ++t) p[t] = (keep >> t & 1u) ? (bad2 ? 1.0 / top_k : m[t] / ms) : 0.0;
+            for (int o = 16; o > 0; o >>= 1) rounds = max(rounds, __shfl_xor_sync(full, rounds, o));
+            double pk[16];
+#pragma unroll
+            for (int t = 0; t < 16; ++t) pk[t] = 0.0;
+            unsigned rem = keep;
+            for (int r = 0; r < rounds; ++r) {
+              const int ts = rem != 0u ? __ffs(rem) - 1 : -1;
+              double x = 0.0;
+#pragma unroll
+              for (int t = 0; t < 16; ++t)
+                if (t == ts) x = m[t];
+              const double y = bad2 ? 1.0 / top_k : x / ms;
+#pragma unroll
+              for (int t = 0; t < 16; ++t)
+                if (t == ts) pk[t] = y;
+              rem &= rem - 1u;
+            }
+#pragma unroll
+            for (int t = 0; t < 16; ++t) p[t] = (keep >> t & 1u) ? pk[t] : 0.0;
           }
         }
         // the q' row out, then sample_categorical(q'): clip, normalise (pairwise), cumsum, inverse CDF
@@ -447,39 +468,33 @@ __global__ void __launch_bounds__(128) serial_head_warp_kernel(const float* U, c
         const double s = warp_pw_sum<NL>(w, lane);
         const bool bad = !(s > 0.0) || !isfinite(s);
         __syncwarp();
-        // normalised weights in index order (0 / s is exactly 0: no division)
+        // the weights in index order (1/V each when their sum is unusable)
 #pragma unroll
         for (int t = 0; t < 16; ++t)
-          if (act) row[base + 8 * t] = bad ? 1.0 / V : (w[t] != 0.0 ? w[t] / s : 0.0);
+          if (act) row[base + 8 * t] = bad ? 1.0 / V : w[t];
         __syncwarp();
         // cumsum + inverse CDF.  Adding a zero leaves the running sum unchanged, so the prefix
-        // sums are those of the nonzero weights in index order: lane L compacts indices
-        // [L*PL, (L+1)*PL), lane 0 sums the compacted weights in order, and since the prefixes never
-        // decrease, the count of prefix / last <= u is the index of the first nonzero that fails it
-        constexpr int PL = V / 32;
-        double cv[PL];
-        unsigned nzm = 0;
+        // sums are those of the nonzero weights in index order: the nonzero weights are compacted in
+        // index order (round i holds indices 32i .. 32i+31, a ballot gives each its place) and
+        // normalised there, one division per lane (an entry whose quotient underflows to 0 only
+        // repeats the prefix before it, which cannot be the first to exceed u); lane 0 sums them in
+        // order, and since the prefixes never decrease, the count of prefix / last <= u is the index
+        // of the first nonzero that fails it
+        int nnz = 0;
 #pragma unroll
-        for (int i = 0; i < PL; ++i) {
-          cv[i] = row[lane * PL + i];
-          if (cv[i] != 0.0) nzm |= 1u << i;
-        }
-        const int mine = __popc(nzm);
-        int incl = mine;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-          const int nb = __shfl_up_sync(full, incl, o);
-          if (lane >= o) incl += nb;
-        }
-        const int nnz = __shfl_sync(full, incl, 31);
-        int pos = incl - mine;
-#pragma unroll
-        for (int i = 0; i < PL; ++i)
-          if (nzm >> i & 1u) {
-            cval[pos] = cv[i];
-            cidx[pos] = lane * PL + i;
-            ++pos;
+        for (int i = 0; i < V / 32; ++i) {
+          const double v = row[i * 32 + lane];
+          const unsigned nzm = __ballot_sync(full, v != 0.0);
+          if (v != 0.0) {
+            const int pos = nnz + __popc(nzm & ((1u << lane) - 1u));
+            cval[pos] = v;
+            cidx[pos] = i * 32 + lane;
           }
+          nnz += __popc(nzm);
+        }
+        __syncwarp();
+        if (!bad)
+          for (int n = lane; n < nnz; n += 32) cval[n] = cval[n] / s;
         __syncwarp();
         if (lane == 0) {
           double c = 0.0;
