@@ -542,8 +542,10 @@ int launch_gemm_tc_serial(const CUtensorMap* tmA, const CUtensorMap* tmA2, const
     attr_set = true;
   }
   dim3 grid((p.M + SER_NT - 1) / SER_NT, p.N / GEMM_BM, 1);
+  // tmB[2]: the activation map with box rows GEMM_NT[2] = SER_NT
+  static_assert(GEMM_NT[2] == SER_NT, "the serial kernel's token tile is the widest tile");
   EVS_CUDA_TRY(evs_launch(gemm_tc_serial_kernel, grid, dim3(192), C::SMEM, st, pdl, *tmA, tmA2 ? *tmA2 : *tmA,
-                          tmB[gemm_tile_index(GEMM_NT[2])], ws, p.N, p.K, p.M, p.splits, p.dual, err));
+                          tmB[2], ws, p.N, p.K, p.M, p.splits, p.dual, err));
   evs_count_launch(1);
   return EVS_OK;
 }
