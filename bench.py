@@ -48,10 +48,12 @@ sys.path.insert(0, str(ROOT))
 METRIC = "accepted tok/s single-stream Evo2-7B-shape γ=12; verify-block µs; HBM GB/s"
 GAMMA = 12
 PROMPT_LEN = 1024
-# DRAM bytes per launch of the tcgen05 projection over its algorithmic bytes, from one ncu capture
-# of the w3, in- and out-projection shapes (1.033, 1.026, 0.971)
-GEMM_TRAFFIC_RATIO = 1.010
-E2E_TOKENS = 256
+# ncu dram__bytes_read.sum + dram__bytes_write.sum per launch of the tcgen05 projection, averaged
+# over one round's launches with this round's launch mix (None until captured)
+GEMM_TRAFFIC_PER_LAUNCH = None
+GEMM_TRAFFIC_NOTE = "not captured on the current kernels"
+E2E_TOKENS = 1024
+VERIFY_REPS = 32
 
 
 def peaks() -> tuple[float, str]:
@@ -100,54 +102,114 @@ def dist_setup():
     return world, rank, local
 
 
-def cpu_round_sample(n_threads: int, steps: int) -> dict:
-    """Reference path on CPU (the oracle port): one speculative round per step, bounded sample.
-
-    Sample: the verify block of 13 tokens through 4 blocks of the 7B shape (one SE, MR, LI, MHA,
-    d=4096, bf16-rounding fp32 compute) after a 16-token prefill, scaled to 32 blocks (x8), plus
-    the drafter round (d=1024 trunk + serial head, fp32) and the fp64 verification; τ=1 (the
-    random-init drafter's drafts are rejected)."""
+def _cpu_target_weights(cfg, seed: int) -> dict:
+    """The GPU arm's seeded weights drawn on the host, each GEMM weight rounded to bf16 and held in
+    fp32 (the bf16-emulating port computes in fp32), one tensor at a time."""
     import torch
 
-    from evspark_b200.config import DRAFTERS, EVO2_7B_SLICE
-    from evspark_b200.weights import init_drafter_weights, init_target_weights
+    from evspark_b200.weights import _draw, data_dtype, target_weight_specs
+
+    from concurrent.futures import ThreadPoolExecutor
+
+    def one(item):
+        idx, (name, shape, kind, storage) = item
+        gen = torch.Generator()
+        gen.manual_seed(int(seed) * 1_000_003 + idx)
+        t = _draw(kind, shape, gen, "cpu", cfg)
+        return name, (t.to(data_dtype(cfg)) if storage == "data" else t).to(torch.float32).contiguous()
+
+    # every tensor has its own generator, so drawing them on several threads gives the same bits
+    with ThreadPoolExecutor(max_workers=max(1, (os.cpu_count() or 1))) as ex:
+        return dict(ex.map(one, enumerate(target_weight_specs(cfg))))
+
+
+def cpu_reference_rounds(n_threads: int, steps: int, warmup: int, *, sampled: bool = False,
+                         prompt_len: int = PROMPT_LEN) -> dict:
+    """The reference path on the host cores (the CPU port in ``oracle/``), timed round by round.
+
+    Workload: the GPU arm's own (1024-token order-3 Markov prompt, Evo2-7B shape, 32 blocks, bf16
+    rounding points, fp32 arithmetic; neural drafter d=1024 from block 27; gamma=12, T=1.0,
+    top_k=4; fp64 transform + verification; slice rollback).  ``warmup`` untimed rounds, then
+    ``steps`` timed rounds; ``ms_per_step`` is their mean and ``value`` = tokens emitted / timed
+    seconds, so ``ms_per_step * steps`` is the timed region.  With ``sampled`` (a bounded sample), or
+    when the host has too little free memory for the 26 GB of fp32 weights, four 7B-width blocks
+    (SE, MR, LI, MHA) run instead and ``value`` is scaled from their measured time to 32 blocks
+    (reported as separate fields)."""
+    import torch
+
+    from evspark_b200.config import DRAFTERS, EVO2_7B, EVO2_7B_SLICE
+    from evspark_b200.weights import init_drafter_weights
+    from evspark_b200.workload import markov_prompt
     from oracle import specdec as sd
     from oracle.model import OracleTarget
 
     torch.set_num_threads(n_threads)
-    cfg = EVO2_7B_SLICE
-    w = init_target_weights(cfg, seed=20260820)
+    try:
+        import psutil
+
+        avail = psutil.virtual_memory().available
+    except Exception:  # noqa: BLE001
+        avail = 0
+    full = avail > 48 * 2**30 and not sampled
+    cfg = EVO2_7B if full else EVO2_7B_SLICE
+    inject = 27 if full else 2
+    t_init = time.perf_counter()
+    w = _cpu_target_weights(cfg, 20260820)
     o = OracleTarget(cfg, w, compute=torch.float32, emulate=True)
     dcfg = DRAFTERS["evo2_7b"]
     dw = init_drafter_weights(dcfg, seed=20260830, embed=w["embed"])
-    rng = np.random.default_rng(0)
-    from evspark_b200.workload import markov_prompt
-
-    prompt = markov_prompt(17, seed=1)
-    st = o.init_state(1, 512)
-    _, _, cap = o.forward(prompt[None, :-1], st, prefill=True, capture_layers=(2,))
-    ctx = cap[2][0]
+    init_s = time.perf_counter() - t_init
+    rng = np.random.default_rng(7)
+    prompt = markov_prompt(prompt_len, seed=20260821)
+    rounds = warmup + steps
+    st = o.init_state(1, prompt_len + (rounds + 2) * (GAMMA + 1))
+    t0 = time.perf_counter()
+    with torch.no_grad():
+        _, _, cap = o.forward(prompt[None, :-1], st, prefill=True, capture_layers=(inject,))
+    prefill_s = time.perf_counter() - t0
+    ctx = cap[inject][0][-dcfg.ctx_window:].float()
     y = int(prompt[-1])
-    times = []
-    for i in range(steps):
+    times, scaled, emitted = [], [], []
+    for r in range(rounds):
         t0 = time.perf_counter()
         with torch.no_grad():
-            U, h = sd.drafter_trunk(dw, dcfg, y, ctx[-dcfg.ctx_window:].float(), min(len(ctx), dcfg.ctx_window))
+            U, h = sd.drafter_trunk(dw, dcfg, y, ctx, int(ctx.shape[0]))
             toks, q, _ = sd.drafter_serial(dw, U, h, y, False, rng)
-        t1 = time.perf_counter()
-        lg, stash, _ = o.forward(np.concatenate([[y], toks])[None], st, retain=True)
-        t2 = time.perf_counter()
-        p = np.stack([sd.apply_transform(r, 1.0, 4) for r in lg[0].double().numpy()])
+            t1 = time.perf_counter()
+            lg, stash, capr = o.forward(np.concatenate([[y], toks])[None], st, retain=True, capture_layers=(inject,))
+            t2 = time.perf_counter()
+        p = np.stack([sd.apply_transform(row, 1.0, 4) for row in lg[0].double().numpy()])
         res = sd.verify_round(toks, q, p, rng)
-        o.slice(st, stash, res.accepted_len if res.accepted_len < GAMMA else GAMMA)
+        k = int(res.accepted_len)
+        o.slice(st, stash, k)
+        ctx = torch.cat([ctx, capr[inject][0][: k + 1].float()])[-dcfg.ctx_window:]
         y = int(res.tokens[-1])
         t3 = time.perf_counter()
-        times.append((t1 - t0) + (t2 - t1) * 8.0 + (t3 - t2))
-    t_round = float(np.median(times))
-    return {"t_round_s": t_round, "value": 1.0 / t_round, "cores": n_threads,
-            "sample": ("per step: drafter round + verify block of 13 tokens over 4 sampled 7B-width blocks "
-                       "(SE, MR, LI, MHA) x8 to 32 blocks + fp64 verification; 16-token prefill; tau=1 "
-                       "(random-init drafter); median of %d steps" % steps)}
+        times.append(t3 - t0)
+        scaled.append((t1 - t0) + (t2 - t1) * (32 / cfg.n_layers) + (t3 - t2))
+        emitted.append(k + 1)
+    t_timed = float(sum(times[warmup:]))
+    tokens = float(sum(emitted[warmup:]))
+    out = {"cores": n_threads, "init_s": round(init_s, 1), "prefill_s": round(prefill_s, 2),
+           "ms_per_step": t_timed / steps * 1e3, "timed_s": t_timed, "tokens": tokens,
+           "blocks_run": cfg.n_layers}
+    if full:
+        out["value"] = tokens / t_timed
+        out["sample"] = (f"{steps} timed rounds (after {warmup} untimed) of the full Evo2-7B-shaped round on the "
+                         f"host: neural drafter + 13-token verify through 32 blocks + fp64 verify + slice rollback, "
+                         f"after a {prompt_len - 1}-token prefill; tau from the random-init drafter")
+    else:
+        # the 32-block round from the 4 measured blocks: the verify forward x8, drafter and verify once
+        t_scaled = float(sum(scaled[warmup:]))
+        out["value"] = tokens / t_scaled
+        out["ms_per_step_scaled_to_32_blocks"] = round(t_scaled / steps * 1e3, 2)
+        out["block_scale"] = 32 / cfg.n_layers
+        why = ("a bounded sample" if sampled else
+               f"host memory {avail / 2**30:.0f} GiB free is short of the 26 GB of fp32 weights")
+        out["sample"] = (f"{steps} timed rounds (after {warmup} untimed) over 4 of the 32 blocks (SE, MR, LI, MHA; "
+                         f"{why}) after a {prompt_len - 1}-token prefill; value scales the measured verify forward "
+                         f"x8 to 32 blocks")
+    return out
 
 
 def run_reference(args) -> int:
@@ -156,21 +218,36 @@ def run_reference(args) -> int:
         return 0
     n = os.cpu_count() or 1
     t0 = time.perf_counter()
-    r = cpu_round_sample(n, args.warmup + args.steps)
+    r = cpu_reference_rounds(n, args.steps, args.warmup)
     wall = time.perf_counter() - t0
+    value = r["value"]
     line = {
-        "impl": "reference", "metric": METRIC, "value": round(r["value"], 4), "unit": "tok/s", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(r["t_round_s"] * 1e3, 2),
+        "impl": "reference", "metric": METRIC, "value": None if value is None else round(value, 4), "unit": "tok/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(r["ms_per_step"], 2),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": "evo2_7b single-stream speculative round (CPU port of the reference path)",
-                   "model": "evo2_7b-shaped random init", "gamma": GAMMA, "parallelism": "cpu"},
-        "cpu_baseline": {"value": round(r["value"], 4), "unit": "tok/s", "cores": r["cores"], "kind": "port",
-                         "sample": r["sample"]},
-        "e2e": {"value": round(r["value"], 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-        "wall_s": round(wall, 1),
+        "config": headline_config(1),
+        "cpu_baseline": {"value": None if value is None else round(value, 4), "unit": "tok/s", "cores": r["cores"],
+                         "kind": "port", "sample": r["sample"]},
+        "e2e": {"value": None if value is None else round(value, 4), "unit": "tok/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+        "tau": round(r["tokens"] / args.steps, 4), "blocks_run": r["blocks_run"], "init_s": r["init_s"],
+        "prefill_s": r["prefill_s"], "wall_s": round(wall, 1),
     }
+    for k in ("ms_per_step_scaled_to_32_blocks", "block_scale"):
+        if k in r:
+            line[k] = r[k]
     print(json.dumps(line), flush=True)
     return 0
+
+
+def headline_config(world: int) -> dict:
+    return {"workload": "evo2_7b-shaped single-stream speculative round: neural drafter + gamma=12 verify "
+                        "block + fp64 verify + slice rollback, T=1.0 top_k=4",
+            "prompt": f"{PROMPT_LEN}-token order-3 Markov ACGT, GC~0.5, seed per rank",
+            "gamma": GAMMA, "d_model": 4096, "n_layers": 32,
+            "drafter": "d=1024, 2 layers, ctx 64 from block 27",
+            "l2": "inputs larger than L2: 12.95 GB of bf16 weights streamed per step",
+            "parallelism": f"independent streams x{world}, no collectives"}
 
 
 def run_streams(args) -> int:
@@ -219,7 +296,9 @@ def run_streams(args) -> int:
     torch.cuda.synchronize()
     ev0.record()
     for _ in range(args.steps):
+        torch.cuda.nvtx.range_push("evs_round")  # lets a profiler select the timed rounds
         sb.round()
+        torch.cuda.nvtx.range_pop()
     ev1.record()
     torch.cuda.synchronize()
     launches = N.launch_count() - n0
@@ -377,7 +456,7 @@ def run_ours(args) -> int:
     nd = NeuralDraftModel(model, drafter, dcfg.inject_layers)
     prompt = markov_prompt(PROMPT_LEN, seed=20260821 + rank)
     rounds_total = args.warmup + args.steps + min(args.steps, 8)
-    ip = model.initialize_inference_params(PROMPT_LEN + (rounds_total + 4) * (GAMMA + 1) + 64)
+    ip = model.initialize_inference_params(PROMPT_LEN + (rounds_total + 4) * (GAMMA + 1) + VERIFY_REPS + 64)
     nd.capture_begin()
     prefill(model, torch.as_tensor(prompt[:-1], device=device)[None], ip)
     nd.capture_commit(PROMPT_LEN - 1)
@@ -417,6 +496,22 @@ def run_ours(args) -> int:
     launches = N.launch_count() - n0
     clk = clocks.stop()
     ms = ev0.elapsed_time(ev1)
+    # verify-block latency: CUDA events around the retained verify forward alone (unprofiled, the
+    # same kernels and launch overlap as in the rounds), each followed by a rollback to k = 0
+    vb_chunk = torch.as_tensor(np.concatenate([[y], markov_prompt(GAMMA, seed=5)]), device=device)[None]
+    ipv = ip.clone()
+    vb_ms = []
+    for i in range(VERIFY_REPS + 2):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        ipv.forward(vb_chunk, retain=True)
+        e1.record()
+        ipv.rollback(np.zeros(1, dtype=np.int64))
+        torch.cuda.synchronize()
+        if i >= 2:
+            vb_ms.append(e0.elapsed_time(e1))
+    ipv.close()
+    verify_block_us = float(np.median(vb_ms)) * 1e3
     # a separate profiled pass (events around every kernel group of the verify block) for the
     # per-kernel roofline; its event overhead stays out of the headline number above
     import ctypes as C
@@ -442,9 +537,7 @@ def run_ours(args) -> int:
     gemm_ms, gemm_bytes, gemm_n = pms[0], pb[0], pl[0]
     achieved = gemm_bytes / (gemm_ms / 1e3) / 1e9 if gemm_ms > 0 else 0.0
     kernel_ms = sum(pms[i] for i in range(4))
-    verify_block_us = kernel_ms / prof_steps * 1e3
 
-    # ---- e2e through the public API: host prompt -> EvSpark.generate -> host tokens ----
     if args.no_extras:
         if rank == 0:
             print(json.dumps({"metric": METRIC, "value": round(value, 3), "unit": "tok/s", "config": args.config,
@@ -454,16 +547,30 @@ def run_ours(args) -> int:
         nd.close()
         model.close()
         return 0
-    es = EvSpark(model, nd, str(device))
+
+    # ---- e2e through the public API: host prompt string -> EvSpark.generate -> host tokens, the
+    # prompt staged from pinned memory, every round's uniforms up and result down (counted) ----
+    from evspark_b200.ranks import combine_timing
+
+    es = EvSpark(model, nd, str(device), state_seqlen=PROMPT_LEN + E2E_TOKENS + 64)
     text = to_text(prompt)
-    e2e_res = es.generate(text, n_tokens=E2E_TOKENS, seed=11 + rank)
-    rounds_e2e = e2e_res.n_rounds
-    h2d = (PROMPT_LEN * 8 + rounds_e2e * ((2 * GAMMA + 1) * 8 + 8)) / rounds_e2e
-    d2h = (4 + GAMMA + 1) * 8
-    e2e = {"value": round(e2e_res.tok_s * (world if world > 1 else 1), 3), "unit": "tok/s",
-           "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
-           "n_tokens": E2E_TOKENS, "rounds": rounds_e2e, "mean_tau": round(e2e_res.mean_tau, 3),
-           "prefill_included": True}
+    es.generate(text, n_tokens=32, seed=3 + rank)  # first call: drafter graph capture, lazy set-up
+    e2e = {}
+    for mode, greedy in (("sampled", False), ("greedy", True)):
+        x0 = N.transfer_count()
+        res = es.generate(text, n_tokens=E2E_TOKENS, seed=11 + rank, greedy=greedy)
+        x1 = N.transfer_count()
+        wall_ms, toks = combine_timing(res.wall_s * 1e3, float(res.n_tokens), device)
+        e2e[mode] = {"value": round(toks / (wall_ms / 1e3), 3), "rounds": int(res.n_rounds),
+                     "mean_tau": round(res.mean_tau, 3), "h2d_bytes": int(x1[0] - x0[0]),
+                     "d2h_bytes": int(x1[1] - x0[1]), "wall_ms": round(wall_ms, 1)}
+    es_s = e2e["sampled"]
+    e2e_line = {"value": es_s["value"], "unit": "tok/s",
+                "h2d_bytes_per_step": round(es_s["h2d_bytes"] / es_s["rounds"], 1),
+                "d2h_bytes_per_step": round(es_s["d2h_bytes"] / es_s["rounds"], 1),
+                "n_tokens": E2E_TOKENS, "rounds": es_s["rounds"], "mean_tau": es_s["mean_tau"],
+                "prefill_included": True, "aggregate": f"tokens of all {world} rank(s) / slowest rank's wall time",
+                "greedy": e2e["greedy"]}
 
     extra = {}
     if rank == 0 and world == 1:
@@ -493,51 +600,56 @@ def run_ours(args) -> int:
         extra["oracle_drafter_tok_s"] = round(13 * 8 / (time.perf_counter() - t0), 2)
         extra["oracle_drafter_greedy_identical"] = bool(np.array_equal(spec.emitted_ids, cont))
         spec.inference_params_dict.close()
-        cpu = cpu_round_sample(os.cpu_count() or 1, args.cpu_steps)
+    es._state.close()
+    es._state = None
+    ip.close()
+    nd.close()
+    model.close()
+    del es, model
+    torch.cuda.empty_cache()
+    cpu_baseline = None
+    if rank == 0 and world == 1:
+        cpu = cpu_reference_rounds(os.cpu_count() or 1, args.cpu_steps, 1, sampled=True, prompt_len=256)
         cpu_baseline = {"value": round(cpu["value"], 4), "unit": "tok/s", "cores": cpu["cores"], "kind": "port",
-                        "sample": cpu["sample"]}
-    else:
-        cpu_baseline = None
+                        "sample": cpu["sample"], "ms_per_step_measured": round(cpu["ms_per_step"], 1),
+                        "ms_per_step_scaled_to_32_blocks": cpu.get("ms_per_step_scaled_to_32_blocks"),
+                        "blocks_run": cpu["blocks_run"]}
 
     if rank == 0:
+        hy_ms, hy_bytes = pms[1], pb[1]
+        hy_gbs = hy_bytes / (hy_ms / 1e3) / 1e9 if hy_ms > 0 else 0.0
         line = {
             "metric": METRIC, "value": round(value, 3), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "evo2_7b-shaped single-stream speculative round: neural drafter + gamma=12 verify "
-                                   "block + fp64 verify + slice rollback, T=1.0 top_k=4",
-                       "prompt": f"{PROMPT_LEN}-token order-3 Markov ACGT, GC~0.5, seed per rank",
-                       "gamma": GAMMA, "d_model": cfg.d_model, "n_layers": cfg.n_layers,
-                       "drafter": "d=1024, 2 layers, ctx 64 from block 27",
-                       "l2": "inputs larger than L2: 12.95 GB of bf16 weights streamed per step",
-                       "parallelism": f"independent streams x{world}, no collectives"},
+            "config": headline_config(world),
             "tau": round(total_accepted / (args.steps * max(world, 1)), 4),
             "verify_block_us": round(verify_block_us, 1),
+            "verify_block_note": f"median of {VERIFY_REPS} CUDA-event timings of the retained 13-token verify "
+                                 "forward alone (no profiling events), after the timed rounds",
             "roofline": {"bound": "hbm", "kernel": "gemm_tc (tcgen05 projections)", "achieved": round(achieved, 1),
                          "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
-                         "traffic": round(gemm_bytes / max(gemm_n, 1) * GEMM_TRAFFIC_RATIO),
-                         "traffic_note": "ncu dram__bytes_read+write per launch / algorithmic bytes = "
-                                         f"{GEMM_TRAFFIC_RATIO} (mean over the w3, in- and out-projection "
-                                         "captures of profiles/gemm_tc_evo2_7b_shapes.md), times this run's "
-                                         "algorithmic bytes per launch",
+                         "traffic": GEMM_TRAFFIC_PER_LAUNCH,
+                         "traffic_note": GEMM_TRAFFIC_NOTE,
                          "launches": int(gemm_n),
                          "bytes_per_launch": round(gemm_bytes / max(gemm_n, 1)),
                          "avg_launch_us": round(gemm_ms / max(gemm_n, 1) * 1e3, 2),
                          "share_of_kernel_time": round(gemm_ms / kernel_ms, 4) if kernel_ms else None,
+                         "timing_note": "per-launch CUDA events around every kernel group of a separate "
+                                        f"{prof_steps}-round pass (serialises the kernels of a forward)",
                          "groups_ms_per_step": {k: round(pms[i] / prof_steps, 4)
                                                 for i, k in enumerate(("gemm", "hyena", "attn", "row"))},
                          "groups_gbs": {k: round(pb[i] / (pms[i] / 1e3) / 1e9, 1) if pms[i] else None
-                                        for i, k in enumerate(("gemm", "hyena", "attn", "row"))}},
+                                        for i, k in enumerate(("gemm", "hyena", "attn", "row"))},
+                         "hyena": {"achieved": round(hy_gbs, 1), "frac": round(hy_gbs / peak, 4),
+                                   "unit": "GB/s"}},
             "cpu_baseline": cpu_baseline,
-            "e2e": e2e,
+            "e2e": e2e_line,
             "clocks": clk,
             "gpu_launches": int(launches),
             **extra,
         }
         print(json.dumps(line), flush=True)
-    ip.close()
-    nd.close()
-    model.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

@@ -159,6 +159,23 @@ def launch_count() -> int:
     return int(lib().evs_launch_count()) + _replayed
 
 
+# host <-> device bytes copied by the decode loop and the facade (the tensors they copy, counted
+# where the copy is issued): what one generate call moves across PCIe
+_h2d = 0
+_d2h = 0
+
+
+def note_transfer(h2d: int = 0, d2h: int = 0) -> None:
+    global _h2d, _d2h
+    _h2d += int(h2d)
+    _d2h += int(d2h)
+
+
+def transfer_count() -> tuple[int, int]:
+    """(host-to-device, device-to-host) bytes noted so far."""
+    return _h2d, _d2h
+
+
 def ptr(t) -> int | None:
     """Device (or host) address of a torch tensor / None."""
     if t is None:

@@ -157,6 +157,18 @@ class EvSpark:
         seq = clean_prompt(prompt)
         return seq, torch.as_tensor(tokenize(seq)[None], device=self.model.device)
 
+    def _ids_pinned(self, prompt: str):
+        """The prompt's ids on the host (pinned) and on the device: one host-to-device copy."""
+        import torch
+
+        from evspark_b200 import _native as N
+
+        seq = clean_prompt(prompt)
+        host = torch.from_numpy(tokenize(seq)[None]).pin_memory()
+        dev = host.to(self.model.device, non_blocking=True)
+        N.note_transfer(h2d=host.nbytes)
+        return seq, host, dev
+
     def generate(self, prompt: str, n_tokens: int = 256, *, greedy: bool = False, gamma: int | None = None,
                  seed: int = 0, temperature: float = 1.0, top_k: int = 4) -> GenerateResult:
         import torch
@@ -165,19 +177,19 @@ class EvSpark:
 
         from evspark_b200.specdec.block.driver import prefill
 
-        seq, ids = self._ids(prompt)
         g = int(gamma) if gamma else self.gamma
-        L = int(ids.shape[1])
         self._nd.capture_reset()
         torch.cuda.synchronize()
         t0 = time.perf_counter()
+        seq, host_ids, ids = self._ids_pinned(prompt)
+        L = int(ids.shape[1])
         # prefill the prompt (all but its last token, the first anchor) into the kept decode state,
         # with the drafter capturing its context, as speculative_generate does with a fresh state
         ip = self._decode_state(L + int(n_tokens) + g + 2)
         self._nd.capture_begin()
         prefill(self.model, ids[:, :-1], ip)
         self._nd.capture_commit(L - 1)
-        spec = speculative_generate(self.model, self._nd, ids, int(n_tokens), g, greedy=greedy,
+        spec = speculative_generate(self.model, self._nd, host_ids, int(n_tokens), g, greedy=greedy,
                                     rng=np.random.default_rng(seed), temperature=temperature, top_k=top_k,
                                     rollback="slice", timing=False, inference_params_dict=ip)
         torch.cuda.synchronize()

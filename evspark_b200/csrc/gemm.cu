@@ -447,11 +447,8 @@ int launch_tc(const CUtensorMap* tmA, const CUtensorMap* tmA2, const CUtensorMap
               EvsDevErr* err, cudaStream_t st, bool pdl, __nv_bfloat16* act, int ld_act) {
   static_assert(NT % 16 == 0 && NT <= 256, "UMMA N");
   using C = TcCfg<NT>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    EVS_CUDA_TRY(cudaFuncSetAttribute(gemm_tc_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
-    attr_set = true;
-  }
+  static std::atomic<unsigned long long> attr_devs{0};
+  EVS_TRY(smem_attr_once(attr_devs, reinterpret_cast<const void*>(gemm_tc_kernel<NT>), C::SMEM));
   dim3 grid((p.M + NT - 1) / NT, p.N / GEMM_BM, p.splits);
   EVS_CUDA_TRY(evs_launch(gemm_tc_kernel<NT>, grid, dim3(192), C::SMEM, st, pdl, *tmA, tmA2 ? *tmA2 : *tmA, *tmB,
                           ws, p.N, p.K, p.M, p.splits, p.dual, act, ld_act, err));
@@ -536,11 +533,8 @@ int launch_gemm_tc_serial(const CUtensorMap* tmA, const CUtensorMap* tmA2, const
   EVS_CHECK_ARG(p.splits >= 1 && p.splits <= p.K / GEMM_BK, "bad split count");
   if (p.M <= 0) return EVS_OK;
   using C = TcCfg<SER_NT>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    EVS_CUDA_TRY(cudaFuncSetAttribute(gemm_tc_serial_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
-    attr_set = true;
-  }
+  static std::atomic<unsigned long long> attr_devs{0};
+  EVS_TRY(smem_attr_once(attr_devs, reinterpret_cast<const void*>(gemm_tc_serial_kernel), C::SMEM));
   dim3 grid((p.M + SER_NT - 1) / SER_NT, p.N / GEMM_BM, 1);
   // tmB[2]: the activation map with box rows GEMM_NT[2] = SER_NT
   static_assert(GEMM_NT[2] == SER_NT, "the serial kernel's token tile is the widest tile");
@@ -573,12 +567,8 @@ int launch_gemm_simt(const void* W, const void* W2, const void* X, int ldx, int 
                     reinterpret_cast<uintptr_t>(W) % 16 == 0,
                 "fp32 projection needs K and the row stride multiples of 4 and 16-byte aligned operands");
   EVS_CHECK_ARG(p.kchunk > 0 && p.kchunk % 128 == 0 && p.splits * p.kchunk >= p.K, "bad fp32 projection plan");
-  static bool attr_set = false;
-  if (!attr_set) {
-    EVS_CUDA_TRY(cudaFuncSetAttribute(gemm_skinny_f32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      static_cast<int>(SK_SMEM)));
-    attr_set = true;
-  }
+  static std::atomic<unsigned long long> attr_devs{0};
+  EVS_TRY(smem_attr_once(attr_devs, reinterpret_cast<const void*>(gemm_skinny_f32_kernel), static_cast<int>(SK_SMEM)));
   const size_t smem = SK_SMEM;
   dim3 grid((p.N + SK_ROWS - 1) / SK_ROWS, p.splits, (p.M + SK_TOK - 1) / SK_TOK);
   EVS_CUDA_TRY(evs_launch(gemm_skinny_f32_kernel, grid, dim3(SK_WARPS * 32), smem, st, pdl,

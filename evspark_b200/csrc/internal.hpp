@@ -1,9 +1,22 @@
 // Internal structures of libevspark_sm100 (not part of the C ABI).
 #pragma once
 
+#include <atomic>
 #include <vector>
 
 #include "common.cuh"
+
+// A kernel's dynamic shared-memory opt-in (cudaFuncSetAttribute) belongs to one device context:
+// each launch site keeps a bit per device that has it, set once per device, any thread.
+inline int smem_attr_once(std::atomic<unsigned long long>& done, const void* kern, int bytes) {
+  int dev = 0;
+  EVS_CUDA_TRY(cudaGetDevice(&dev));
+  const unsigned long long bit = dev < 64 ? (1ull << dev) : 0ull;
+  if (bit != 0 && (done.load(std::memory_order_acquire) & bit) != 0) return EVS_OK;
+  EVS_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+  done.fetch_or(bit, std::memory_order_acq_rel);
+  return EVS_OK;
+}
 
 // GEMM tile geometry (tcgen05 path): 128 weight rows x 64 K per stage, tokens per MMA = NT
 constexpr int GEMM_BM = 128;

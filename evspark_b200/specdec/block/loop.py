@@ -79,6 +79,15 @@ def _as_prompt_ids(prompt_ids, device) -> torch.Tensor:
     return t.to(device)
 
 
+def _prompt_host(prompt_ids) -> np.ndarray:
+    """The prompt's ids on the host (read back from the device only when given there)."""
+    if isinstance(prompt_ids, torch.Tensor) and prompt_ids.device.type != "cpu":
+        out = prompt_ids.reshape(-1).cpu().numpy().astype(np.int64)
+        N.note_transfer(d2h=out.nbytes)
+        return out
+    return np.asarray(prompt_ids, dtype=np.int64).reshape(-1)
+
+
 def _q_prime_from_raw(q: np.ndarray, temperature: float, top_k: int | None) -> np.ndarray:
     """Draft distribution -> the target's sampling transform applied to log(q) (loop.py:111-128)."""
     q = np.asarray(q, dtype=np.float64).ravel()
@@ -150,11 +159,13 @@ def _spec_round_device(model, draft, ip, y: int, gamma: int, greedy: bool, rng, 
         bufs = ip._round_bufs = _RoundBuffers(model.device, gamma)
     draft._check_gamma(gamma)
     chunk = bufs.chunk
-    chunk[0, 0] = int(y)
+    chunk[0, 0] = int(y)  # the anchor travels as a kernel argument
+    h2d = chunk.element_size()
     u = None
     if not greedy:
         bufs.u_draft_h.numpy()[:] = rng.random(int(gamma))
         bufs.u_draft.copy_(bufs.u_draft_h, non_blocking=True)
+        h2d += bufs.u_draft_h.nbytes
         u = bufs.u_draft[None]
     dr = draft.drafter
     if bufs.toks is None:
@@ -192,10 +203,12 @@ def _spec_round_device(model, draft, ip, y: int, gamma: int, greedy: bool, rng, 
         uv, state = draw_uniforms(rng, gamma + 1)
         bufs.u_ver_h.numpy()[:] = uv
         bufs.u_ver.copy_(bufs.u_ver_h, non_blocking=True)
+        h2d += bufs.u_ver_h.nbytes
         acc, toks_v, info = verify_device(p, q_rows, x, bufs.u_ver[None], greedy=False)
     ip.rollback_launch(torch.clamp(acc, max=int(remaining) - 1))
     bufs.res_h.copy_(torch.cat([acc.to(torch.int64), info[0].to(torch.int64), toks_v[0]]), non_blocking=True)
     bufs.conf_h.copy_(conf_d[0], non_blocking=True)
+    N.note_transfer(h2d=h2d, d2h=bufs.res_h.nbytes + bufs.conf_h.nbytes)
     torch.cuda.current_stream(model.device).synchronize()
     res = bufs.res_h.numpy()
     k = int(res[0])
@@ -389,7 +402,9 @@ def speculative_generate(model, draft, prompt_ids, n_tokens: int, gamma: int, gr
                          inference_params_dict=None, record_logits: bool = False, rollback: str = "slice",
                          n_candidates: int = 1, timing: bool = True) -> SpecGenerateResult:
     device = model.device
-    prompt = _as_prompt_ids(prompt_ids, device)
+    pt = torch.as_tensor(prompt_ids)
+    if not (pt.ndim == 1 or (pt.ndim == 2 and pt.shape[0] == 1)):
+        raise ValueError(f"prompt_ids must be [1, L] (independent streams use the batched API), got {tuple(pt.shape)}")
     n_candidates = int(n_candidates)
     if n_candidates < 1:
         raise ValueError(f"n_candidates must be >= 1, got {n_candidates}")
@@ -408,10 +423,10 @@ def speculative_generate(model, draft, prompt_ids, n_tokens: int, gamma: int, gr
         raise ValueError("the neural drafter needs rollback='slice' (rejected positions are trimmed at j*)")
     if has_device_draft and int(gamma) > draft.gamma:
         raise ValueError(f"decode γ={gamma} > drafter training γ={draft.gamma}")
-    L = int(prompt.shape[1])
+    prompt_np = _prompt_host(prompt_ids)
+    L = int(prompt_np.shape[0])
     if L < 2:
         raise ValueError(f"prompt length must be >= 2 (the first round needs an anchor), got {L}")
-    prompt_np = prompt[0].cpu().numpy().astype(np.int64)
     y = int(prompt_np[-1])
     if n_tokens == 0:
         ip = inference_params_dict or model.initialize_inference_params(max_seqlen=L + gamma + 2)
@@ -422,6 +437,7 @@ def speculative_generate(model, draft, prompt_ids, n_tokens: int, gamma: int, gr
                                                max_chunk=_prefill_chunk(model, L))
         if has_capture:
             draft.capture_begin()
+        prompt = _as_prompt_ids(prompt_ids, device)
         prefill(model, prompt[:, :-1], ip)
         if has_capture:
             draft.capture_commit(L - 1)

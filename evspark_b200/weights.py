@@ -5,12 +5,15 @@ random-init weights of the configured shape.  Each tensor is drawn from its own
 ``torch.Generator`` (seed derived from the model seed and the tensor index), so
 a given (config, seed, device type) always yields the same weights.
 
-Distributions (documented model convention): input projections
-N(0, 0.25/fan_in), residual out-projections N(0, 0.64/fan_in), embedding
-N(0, 0.64/d); norm scales 1 + N(0, 0.1²) (final norm ×4, so the logits are
-sharp enough for top-k sampling and argmax gaps are well above bf16 noise);
-FIR taps N(0, 1/K); IIR real poles |p| ~ U(0.9, 0.999) stored as
-``log_poles``; residues N(0, 1/S); D N(0, 0.5²).
+Distributions: dense input projections and the (tied) embedding N(0, 0.02²);
+residual out-projections (Hyena ``w_out``, attention ``w_o``, MLP ``w3``)
+N(0, 1/fan_in); norm scales 1 + N(0, 0.1²) (the final norm included); FIR taps
+N(0, 1/K); IIR real poles |p| ~ U(0.9, 0.999) stored as ``log_poles``;
+residues N(0, 1/S); D N(0, 0.5²).  The logits have a standard deviation of
+0.02 * sqrt(d) (1.3 at Evo2-7B width).  Out-projections of N(0, 1/fan_in)
+keep the blocks' contributions well above the embedding row in the residual
+stream; with the GPT-style 0.02 / sqrt(2 n_layers) instead, the 4-block
+tiny model's greedy argmax repeats its input token at 92 % of positions.
 """
 
 from __future__ import annotations
@@ -59,16 +62,12 @@ def target_weight_specs(cfg: TargetConfig) -> list[tuple[str, tuple[int, ...], s
 
 def _draw(kind: str, shape, gen: torch.Generator, device, cfg: TargetConfig) -> torch.Tensor:
     f32 = torch.float32
-    if kind == "dense":
-        return torch.randn(shape, generator=gen, device=device, dtype=f32) * (0.5 / math.sqrt(shape[1]))
+    if kind in ("dense", "embed"):
+        return torch.randn(shape, generator=gen, device=device, dtype=f32) * 0.02
     if kind == "dense_out":
-        return torch.randn(shape, generator=gen, device=device, dtype=f32) * (0.8 / math.sqrt(shape[1]))
-    if kind == "embed":
-        return torch.randn(shape, generator=gen, device=device, dtype=f32) * (0.8 / math.sqrt(cfg.d_model))
-    if kind == "norm":
+        return torch.randn(shape, generator=gen, device=device, dtype=f32) / math.sqrt(shape[1])
+    if kind in ("norm", "final_norm"):
         return 1.0 + 0.1 * torch.randn(shape, generator=gen, device=device, dtype=f32)
-    if kind == "final_norm":
-        return 4.0 * (1.0 + 0.1 * torch.randn(shape, generator=gen, device=device, dtype=f32))
     if kind == "fir":
         return torch.randn(shape, generator=gen, device=device, dtype=f32) / math.sqrt(shape[-1])
     if kind == "dvec":
@@ -91,6 +90,18 @@ def init_target_weights(cfg: TargetConfig, seed: int = 20260820, device="cpu") -
         t = _draw(kind, shape, gen, device, cfg)
         out[name] = t.to(data_dtype(cfg) if storage == "data" else torch.float32).contiguous()
     return out
+
+
+def init_target_tensor(cfg: TargetConfig, name: str, seed: int = 20260820, device="cpu") -> torch.Tensor:
+    """One named tensor of ``init_target_weights(cfg, seed, device)``, drawn alone (same bits)."""
+    device = torch.device(device)
+    for idx, (nm, shape, kind, storage) in enumerate(target_weight_specs(cfg)):
+        if nm == name:
+            gen = torch.Generator(device=device)
+            gen.manual_seed(int(seed) * 1_000_003 + idx)
+            t = _draw(kind, shape, gen, device, cfg)
+            return t.to(data_dtype(cfg) if storage == "data" else torch.float32).contiguous()
+    raise KeyError(name)
 
 
 def drafter_weight_specs(dcfg: DrafterConfig) -> list[tuple[str, tuple[int, ...], str]]:

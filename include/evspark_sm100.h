@@ -204,10 +204,12 @@ EVS_API int evs_gemm_bf16(const void* W, const void* X, float* out, int N, int K
  * (a host that has handed all device memory to its own pool, code running during stream capture,
  * plugins barred from allocating after start-up).  No counterpart in the reference.  Partial sums
  * go to one fixed 4 MiB file-scope device array (1,048,576 fp32; each GPU that loads the library
- * holds it until exit) instead of allocated scratch; calls needing more than that (splits*M*N,
- * splits chosen as in evs_forward) fail with EVS_ERANGE.  No cudaMalloc/cudaFree.  The first call
- * on a device looks up the array's address — make it before any stream capture.  All calls share
- * the array (last call's contents remain): calls that may overlap on the GPU race. */
+ * holds it until exit) instead of allocated scratch.  The K split is the smallest `splits` with
+ * (N / 128) * splits >= 148, at most K / 64; calls whose splits * M * N exceeds 1,048,576 fail with
+ * EVS_ERANGE.  No cudaMalloc/cudaFree.  The first call on a device looks up the array's address —
+ * make it before any stream capture.  All calls share the array (last call's contents remain):
+ * calls that may overlap on the GPU race.  If a wait inside the projection times out, every output
+ * value is NaN. */
 EVS_API int evs_gemm_bf16_noalloc(const void* W, const void* X, float* out, int N, int K, int M,
                                   cudaStream_t stream);
 

@@ -265,6 +265,38 @@ class OracleTarget:
             y = self.q(x2 * self.r32(res + D[None, :, None] * x1v))
         return y.transpose(1, 2)
 
+    def embed(self, ids) -> torch.Tensor:
+        """Embedding lookup: the residual stream entering block 0, ``[B, T, d]``."""
+        ids = torch.as_tensor(np.asarray(ids), dtype=torch.long)
+        return self.w["embed"][ids[None] if ids.dim() == 1 else ids]
+
+    def block(self, i: int, x: torch.Tensor, st: OracleState, *, prefill: bool = False,
+              stash: OracleStash | None = None) -> torch.Tensor:
+        """Block ``i`` on the residual stream ``x [B, T, d]`` (returned updated).
+
+        Advances the layer's FIR/IIR/KV state; ``st.lengths`` (the tokens consumed before this
+        chunk) is read, not advanced.
+        """
+        kind = self.cfg.layer_types[i]
+        a = self.q(self.rmsnorm(x, self.w[f"blocks.{i}.pre_norm"]))
+        if kind == MHA:
+            o = self._mha(i, a, st)
+            x = self.r32(x + o @ self.w[f"blocks.{i}.w_o"].T)
+        else:
+            u = self.q(a @ self.w[f"blocks.{i}.w_in"].T)
+            y = self._hyena(i, kind, u, st, prefill, stash)
+            x = self.r32(x + y @ self.w[f"blocks.{i}.w_out"].T)
+        bn = self.q(self.rmsnorm(x, self.w[f"blocks.{i}.post_norm"]))
+        g1 = bn @ self.w[f"blocks.{i}.w1"].T
+        g2 = bn @ self.w[f"blocks.{i}.w2"].T
+        g = self.q(g1 * torch.sigmoid(g1) * g2)
+        return self.r32(x + g @ self.w[f"blocks.{i}.w3"].T)
+
+    def head(self, x: torch.Tensor) -> torch.Tensor:
+        """Final RMSNorm and tied unembedding: fp32 logits ``[B, T, V]``."""
+        h = self.q(self.rmsnorm(x, self.w["final_norm"]))
+        return self.r32(h @ self.w["embed"].T)
+
     def forward(self, ids, st: OracleState, *, prefill: bool = False, retain: bool = False,
                 capture_layers: tuple[int, ...] = ()):
         """Run ``ids [B,T]`` through the model from ``st`` (advanced in place).
@@ -273,35 +305,19 @@ class OracleTarget:
         stash or None, captured {layer: [B,T,d]})``.
         """
         cfg = self.cfg
-        ids = torch.as_tensor(np.asarray(ids), dtype=torch.long)
-        if ids.dim() == 1:
-            ids = ids[None]
-        B, T = ids.shape
+        x = self.embed(ids)
+        B, T = x.shape[:2]
         if B != st.batch:
             raise ValueError(f"batch {B} != state batch {st.batch}")
         if prefill and np.any(st.lengths != 0):
             raise ValueError("prefill requires an empty state")
         stash = OracleStash(L0=st.lengths.copy(), chunk_len=T) if retain else None
-        x = self.w["embed"][ids]
         captured = {}
-        for i, kind in enumerate(cfg.layer_types):
-            a = self.q(self.rmsnorm(x, self.w[f"blocks.{i}.pre_norm"]))
-            if kind == MHA:
-                o = self._mha(i, a, st)
-                x = self.r32(x + o @ self.w[f"blocks.{i}.w_o"].T)
-            else:
-                u = self.q(a @ self.w[f"blocks.{i}.w_in"].T)
-                y = self._hyena(i, kind, u, st, prefill, stash)
-                x = self.r32(x + y @ self.w[f"blocks.{i}.w_out"].T)
-            bn = self.q(self.rmsnorm(x, self.w[f"blocks.{i}.post_norm"]))
-            g1 = bn @ self.w[f"blocks.{i}.w1"].T
-            g2 = bn @ self.w[f"blocks.{i}.w2"].T
-            g = self.q(g1 * torch.sigmoid(g1) * g2)
-            x = self.r32(x + g @ self.w[f"blocks.{i}.w3"].T)
+        for i in range(cfg.n_layers):
+            x = self.block(i, x, st, prefill=prefill, stash=stash)
             if i in capture_layers:
                 captured[i] = x.clone()
-        h = self.q(self.rmsnorm(x, self.w["final_norm"]))
-        logits = self.r32(h @ self.w["embed"].T)
+        logits = self.head(x)
         st.lengths = st.lengths + T
         return logits, stash, captured
 
@@ -333,3 +349,25 @@ class OracleTarget:
         for i, s_all in stash.s_all.items():
             st.iir[i] = torch.stack([s_all[b, ..., int(ks[b])] for b in range(st.batch)], 0)
         st.lengths = stash.L0 + ks + 1
+
+
+def block_over_segments(cfg: TargetConfig, i: int, layer_weights: dict, xs: list, *, compute=torch.float64,
+                        emulate: bool = False) -> list:
+    """Block ``i`` alone, from an empty state, over consecutive chunks of its input stream.
+
+    ``layer_weights`` maps the block's slot names (``w_in``, ``pre_norm``, ...) to tensors and
+    ``xs`` is a list of residual-stream chunks ``[B, T_j, d]``: the first is prefilled (the
+    parallel path of an empty state), each later one runs as a chunk forward on the state the
+    earlier ones left.  Returns the block's output for every chunk.  One block's weights are held
+    at a time, so models of any depth fit host memory when run block by block.
+    """
+    kind = cfg.layer_types[i]
+    sub = cfg.with_(name=f"{cfg.name}.block{i}", n_layers=1, layer_types=(kind,))
+    o = OracleTarget(sub, {f"blocks.0.{k}": v for k, v in layer_weights.items()}, compute=compute, emulate=emulate)
+    B = xs[0].shape[0]
+    st = o.init_state(B, sum(int(x.shape[1]) for x in xs))
+    outs = []
+    for j, x in enumerate(xs):
+        outs.append(o.block(0, x.to(compute), st, prefill=(j == 0)))
+        st.lengths = st.lengths + int(x.shape[1])
+    return outs

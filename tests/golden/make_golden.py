@@ -1,14 +1,14 @@
 """Generate the golden fixtures that pin the CPU oracle to the reference.
 
-Runs the reference's OWN implementation (EvSpark, read-only checkout at
-/root/reference) unmodified on CPU: its block path (``block_forward``,
+Runs the reference's OWN implementation (an EvSpark checkout, read-only)
+unmodified on CPU: its block path (``block_forward``,
 ``slice_states_to_accept``, ``speculative_generate``, ``native_*_reference``)
 drives the oracle StripedHyena2 through ``oracle/vortex_stub``; its verifier,
 sampling transform and ``Drafter`` / ``trunk_forward`` / ``serial_sample`` run
 directly.  Outputs go to ``tests/golden/*.npz``.  Only this build container has
 the reference; the GPU box uses the committed fixtures.
 
-    python tests/golden/make_golden.py [--reference /root/reference]
+    python tests/golden/make_golden.py --reference <path of the EvSpark checkout>
 """
 
 from __future__ import annotations
@@ -48,7 +48,7 @@ def state_arrays(ip, prefix: str, out: dict) -> None:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True, help="root of the EvSpark checkout (read-only)")
     args = ap.parse_args()
     sys.path[:0] = [str(REPO), str(REPO / "oracle" / "vortex_stub"), args.reference]
     torch.set_num_threads(8)
@@ -227,7 +227,35 @@ def main() -> None:
         dr[f"ctx{T}/greedy_tokens"], dr[f"ctx{T}/greedy_q"], dr[f"ctx{T}/greedy_conf"] = tg, qg, cg
         dr[f"ctx{T}/sample_tokens"], dr[f"ctx{T}/sample_q"], dr[f"ctx{T}/sample_conf"] = ts, qsx, cs
     np.savez_compressed(HERE / "drafter_tiny.npz", **dr)
-    for f in ("tiny_model.npz", "verify_kat.npz", "drafter_tiny.npz"):
+
+    # ---- 6. drafter at Evo2-7B width (d=1024, 16 heads, context of block-27 outputs, d_target 4096) ----
+    from evspark_b200.config import EVO2_7B
+    from evspark_b200.weights import init_target_tensor
+
+    dcfg = DRAFTERS["evo2_7b"]
+    emb7 = init_target_tensor(EVO2_7B, "embed", seed=MODEL_SEED)
+    dw = init_drafter_weights(dcfg, seed=DRAFTER_SEED, embed=emb7)
+    drafter = Drafter(d_model=dcfg.d_model, n_layers=dcfg.n_layers, gamma=dcfg.gamma, n_inject=dcfg.n_inject,
+                      target_hidden=dcfg.target_hidden, ctx_window=dcfg.ctx_window)
+    drafter.load_state_dict(dw)
+    drafter.eval()
+    dr7: dict = {"drafter_sha256": np.array(weights_digest(dw))}
+    g = torch.Generator().manual_seed(DRAFTER_SEED + 7)
+    for T in (0, 64):
+        h_raw = torch.randn(T, dcfg.n_inject * dcfg.target_hidden, generator=g)
+        anchor = 67
+        with torch.no_grad():
+            U, h = trunk_forward(drafter, torch.tensor([anchor]), h_raw if T else None, torch.tensor([T]))
+            tg, qg, cg = serial_sample(drafter, U, h, anchor, True, np.random.default_rng(0))
+            ts, qsx, cs = serial_sample(drafter, U, h, anchor, False, np.random.default_rng(11),
+                                        temperature=1.0, top_k=4)
+        dr7[f"ctx{T}/h_raw"] = h_raw.numpy()
+        dr7[f"ctx{T}/U"] = U[0].numpy()
+        dr7[f"ctx{T}/h"] = h[0].numpy()
+        dr7[f"ctx{T}/greedy_tokens"], dr7[f"ctx{T}/greedy_q"], dr7[f"ctx{T}/greedy_conf"] = tg, qg, cg
+        dr7[f"ctx{T}/sample_tokens"], dr7[f"ctx{T}/sample_q"], dr7[f"ctx{T}/sample_conf"] = ts, qsx, cs
+    np.savez_compressed(HERE / "drafter_7b.npz", **dr7)
+    for f in ("tiny_model.npz", "verify_kat.npz", "drafter_tiny.npz", "drafter_7b.npz"):
         print(f, (HERE / f).stat().st_size, "bytes")
 
 

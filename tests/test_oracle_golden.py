@@ -186,3 +186,31 @@ def test_oracle_drafter_matches_reference(golden, tiny_weights, T):
     ts, qs, cs = sd.drafter_serial(dw, U_ref, h_ref, 71, False, np.random.default_rng(11))
     np.testing.assert_array_equal(ts, d[f"ctx{T}/sample_tokens"])
     np.testing.assert_allclose(qs, d[f"ctx{T}/sample_q"], atol=1e-7)
+
+
+@pytest.mark.parametrize("T", [0, 64])
+def test_oracle_drafter_7b_width_matches_reference(golden, T):
+    """The drafter at Evo2-7B width (d=1024, 16 heads, 4096-wide context rows from block 27) against
+    the reference ``Drafter`` / ``trunk_forward`` / ``serial_sample`` (evspark/train/drafter.py:54-409,
+    evspark/specdec/block/neural_draft.py:157-259)."""
+    from evspark_b200.config import EVO2_7B
+    from evspark_b200.weights import init_target_tensor
+    from tests.golden.make_golden import weights_digest
+
+    d = golden("drafter_7b.npz")
+    dcfg = DRAFTERS["evo2_7b"]
+    dw = init_drafter_weights(dcfg, seed=20260830, embed=init_target_tensor(EVO2_7B, "embed", seed=20260820))
+    assert str(d["drafter_sha256"]) == weights_digest(dw)
+    h_raw = torch.from_numpy(d[f"ctx{T}/h_raw"])
+    with torch.no_grad():
+        U, h = sd.drafter_trunk(dw, dcfg, 67, h_raw if T else None, T)
+    np.testing.assert_allclose(U.numpy(), d[f"ctx{T}/U"], atol=2e-5, rtol=1e-4)
+    np.testing.assert_allclose(h.numpy(), d[f"ctx{T}/h"], atol=2e-5, rtol=1e-4)
+    U_ref, h_ref = torch.from_numpy(d[f"ctx{T}/U"]), torch.from_numpy(d[f"ctx{T}/h"])
+    tg, qg, cg = sd.drafter_serial(dw, U_ref, h_ref, 67, True, np.random.default_rng(0))
+    np.testing.assert_array_equal(tg, d[f"ctx{T}/greedy_tokens"])
+    np.testing.assert_allclose(qg, d[f"ctx{T}/greedy_q"], atol=1e-7)
+    np.testing.assert_allclose(cg, d[f"ctx{T}/greedy_conf"], atol=1e-6)
+    ts, qs, cs = sd.drafter_serial(dw, U_ref, h_ref, 67, False, np.random.default_rng(11))
+    np.testing.assert_array_equal(ts, d[f"ctx{T}/sample_tokens"])
+    np.testing.assert_allclose(qs, d[f"ctx{T}/sample_q"], atol=1e-7)

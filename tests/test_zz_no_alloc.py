@@ -43,11 +43,45 @@ def test_noalloc_matches_regular_entry_point_twice(cuda, N_, K, M):
         torch.cuda.synchronize()
         outs.append(out)
     scale = ref.abs().max().item()
+    exact = X.float() @ W.float().T
     for out in outs:
         assert torch.isfinite(out).all()
         err = (out - ref).abs().max().item()
         assert err <= TOL_REL * scale, (err, scale)
+        err = (out - exact).abs().max().item()
+        assert err <= TOL_REL * exact.abs().max().item(), err
+    # the partial sums are added in fixed split order: the same bits on every call
     assert torch.equal(outs[0], outs[1])
+
+
+def _noalloc_splits(N_, K):
+    """The entry point's K split: the smallest count that gives at least 148 CTAs, at most K / 64."""
+    tiles, splits = N_ // 128, 1
+    while tiles * splits < 148 and splits < K // 64:
+        splits += 1
+    return splits
+
+
+def test_noalloc_at_the_scratch_limit(cuda):
+    """splits * M * N exactly at the 1,048,576-value limit runs and matches the fp32 product; one
+    token row more is rejected."""
+    from evspark_b200 import _native as N
+
+    N_, K, M = 16384, 512, 32
+    splits = _noalloc_splits(N_, K)
+    assert splits * M * N_ == 1 << 20
+    g = torch.Generator(device=cuda).manual_seed(5)
+    W = torch.randn(N_, K, device=cuda, generator=g).to(torch.bfloat16)
+    X = torch.randn(M + 1, K, device=cuda, generator=g).to(torch.bfloat16)
+    out = torch.full((M, N_), float("nan"), device=cuda)
+    N.call("evs_gemm_bf16_noalloc", W.data_ptr(), X.data_ptr(), out.data_ptr(), N_, K, M, N.stream_ptr())
+    exact = X[:M].float() @ W.float().T
+    torch.cuda.synchronize()
+    assert torch.isfinite(out).all()
+    assert (out - exact).abs().max().item() <= TOL_REL * exact.abs().max().item()
+    out1 = torch.empty(M + 1, N_, device=cuda)
+    with pytest.raises(ValueError, match="scratch"):
+        N.call("evs_gemm_bf16_noalloc", W.data_ptr(), X.data_ptr(), out1.data_ptr(), N_, K, M + 1, N.stream_ptr())
 
 
 def test_noalloc_rejects_sizes_beyond_the_fixed_scratch(cuda):
