@@ -397,6 +397,30 @@ def run_tp(args) -> int:
     launches = N.launch_count() - n0
     clk = clocks.stop()
     ms, _ = combine_timing(ev0.elapsed_time(ev1), 0.0, device)
+    # the verify forward alone (every rank issues the same calls: the forward is collective over the
+    # ranks' shared partial sums), on a clone of the state, each followed by a rollback to k = 0
+    vb_chunk = torch.as_tensor(np.concatenate([[state["y"]], markov_prompt(GAMMA, seed=5)]), device=device)[None]
+    ipv = state["ip"].clone()
+    vb_ms = []
+    for i in range(VERIFY_REPS + 2):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        ipv.forward(vb_chunk, retain=True)
+        e1.record()
+        ipv.rollback(np.zeros(1, dtype=np.int64))
+        torch.cuda.synchronize()
+        if i >= 2:
+            vb_ms.append(e0.elapsed_time(e1))
+    ipv.close()
+    vb_us, _ = combine_timing(float(np.median(vb_ms)) * 1e3, 0.0, device)
+    # per kernel group of the target forward (a profiled pass: events around every group)
+    prof_steps = 4
+    N.call("evs_profile_start", state["ip"].handle)
+    for _ in range(prof_steps):
+        one_round()
+    torch.cuda.synchronize()
+    pl, pms, pb = (C.c_int64 * 4)(), (C.c_double * 4)(), (C.c_double * 4)()
+    N.call("evs_profile_stop", state["ip"].handle, pl, pms, pb)
     err = [C.c_int32(), C.c_int32(), C.c_int32()]
     N.check(N.lib().evs_get_device_error(state["ip"].handle, *[C.byref(e) for e in err]), "evs_get_device_error")
     if rank == 0:
@@ -414,6 +438,14 @@ def run_tp(args) -> int:
                        "l2": "inputs larger than L2: the bf16 weight shards are streamed every round"},
             "tau": round(tokens / args.steps, 4), "prefill_s": round(prefill_s, 3),
             "prefill_tok_s": round((L - 1) / prefill_s, 1), "prefill_chunk": int(ip.max_chunk),
+            "verify_block_us": round(vb_us, 1),
+            "groups_ms_per_step": {k: round(pms[i] / prof_steps, 4)
+                                   for i, k in enumerate(("gemm", "hyena", "attn", "row"))},
+            "groups_launches_per_step": {k: int(pl[i] // prof_steps)
+                                         for i, k in enumerate(("gemm", "hyena", "attn", "row"))},
+            "groups_note": "rank 0, a separate profiled pass with CUDA events around every kernel group of the "
+                           "target forward (serialises them); row = embedding, residual + RMSNorm with the "
+                           "cross-rank partial sums, SwiGLU, logits",
             "device_error": int(err[0].value), "clocks": clk, "gpu_launches": int(launches),
         }
         print(json.dumps(line), flush=True)

@@ -148,9 +148,11 @@ int run_forward(const evs_model* m, evs_state* s, const int64_t* ids, int B, int
     }
     const long long epoch = ++s->tp_epoch;
     const size_t boff = static_cast<size_t>(epoch & 1) * s->tp_buf_bytes;
-    EVS_TRY(G(tA, nullptr, W, nullptr, d, K, 0, reinterpret_cast<float*>(s->tp_base[m->tp_rank] + boff),
-              s->tp_buf_bytes / sizeof(float), tB));
-    EVS_TRY(launch_tp_signal(s, epoch, st));
+    float* mine = reinterpret_cast<float*>(s->tp_base[m->tp_rank] + boff);
+    EVS_TRY(G(tA, nullptr, W, nullptr, d, K, 0, mine, s->tp_buf_bytes / sizeof(float), tB));
+    // this rank's splits summed into split 0, then published: the consumer reads one partial per rank
+    EVS_TRY(launch_tp_reduce_signal(s, mine, sp, M, epoch, st));
+    sp = 1;
     parts.R = m->tp_world;
     parts.epoch = epoch;
     for (int r = 0; r < m->tp_world; ++r) {

@@ -24,9 +24,13 @@ struct evs_drafter {
   bool finalized = false;
   const float* t[EVS_D_LAYER0 + EVS_D_MAX_LAYERS * EVS_D_PER_LAYER] = {nullptr};
   int64_t numel[EVS_D_LAYER0 + EVS_D_MAX_LAYERS * EVS_D_PER_LAYER] = {0};
-  float *ctx_in = nullptr, *ctx = nullptr, *emb = nullptr, *h = nullptr, *xb = nullptr, *q = nullptr;
+  float *ctx_in = nullptr, *ctx = nullptr, *h = nullptr, *xb = nullptr, *q = nullptr;
   float *kv_in = nullptr, *kb = nullptr, *vb = nullptr, *y = nullptr, *tmp = nullptr, *m1 = nullptr;
-  float *z = nullptr, *U = nullptr, *pe = nullptr;
+  float *z = nullptr, *U = nullptr;
+  // in_proj(embed[v]) + in_proj.bias for every token v [V][d], formed once at finalize by the same
+  // projection and epilogue as a round's rows (a token's row does not depend on the other rows), so
+  // the draft rows [anchor, MASK...] and the confidence head's in_proj(embed(prev)) are gathers
+  float* tok_in = nullptr;
   int64_t* prev = nullptr;
   float* ws = nullptr;  // split-K partials of the projections
   size_t ws_floats = 0;
@@ -61,19 +65,6 @@ __global__ void gather_ctx_kernel(RingPtrs rings, int n_inject, int ring_len, in
   }
 }
 
-// rows b*g + t: embed[t == 0 ? anchor[b] : mask]  or embed[ids[b*g + t]] when ids is given
-__global__ void embed_rows_kernel(const float* embed, int H, const int64_t* anchor, const int64_t* ids, int g,
-                                  int mask_id, float* out) {
-  pdl_trigger();
-  pdl_wait();
-  const int row = blockIdx.x;
-  const int b = row / g, t = row % g;
-  const int64_t id = ids ? ids[row] : (t == 0 ? anchor[b] : mask_id);
-  const float* src = embed + static_cast<size_t>(id) * H;
-  float* dst = out + static_cast<size_t>(row) * H;
-  for (int e = threadIdx.x; e < H; e += blockDim.x) dst[e] = src[e];
-}
-
 // Split-K partials of a projection summed in split order (reduce_splits_kernel's additions), then
 // the drafter's elementwise step after that projection (acc = the sum, t = row % g):
 //   EPI_BIAS_NORM   out = RMSNorm(acc + bias)                     context rows
@@ -85,7 +76,9 @@ __global__ void embed_rows_kernel(const float* embed, int H, const int64_t* anch
 // RMSNorm(v) = scale * (v / sqrt(mean(v²) + eps)), the sum of squares per thread over columns
 // tid, tid + 256, ..., then the warp butterfly and the warps in order.  The norm modes run one CTA
 // per row; the others one thread per element.
-enum DraftEpi { EPI_BIAS_NORM, EPI_IN_NORM, EPI_RESID_NORM, EPI_BIAS_SILU, EPI_BIAS, EPI_SCALE };
+//   EPI_TOK_IN_NORM h = tok_in[id] + pos[t]; out = RMSNorm(h)     EPI_IN_NORM from the token table
+//                   (id = anchor[b] at t = 0, mask_id after it): the same values, no projection
+enum DraftEpi { EPI_BIAS_NORM, EPI_IN_NORM, EPI_RESID_NORM, EPI_BIAS_SILU, EPI_BIAS, EPI_SCALE, EPI_TOK_IN_NORM };
 constexpr int EPI_THREADS = 256;
 constexpr int EPI_VPT = 4;  // norm modes: columns per thread per pass
 constexpr int EPI_SB = 8;   // norm modes: splits per batch of loads
@@ -99,6 +92,9 @@ struct DraftEpiArgs {
   const float* scale;
   float* out;
   float eps, s;
+  const float* tok_in;      // EPI_TOK_IN_NORM: the token table [V][N]
+  const int64_t* anchor;    // ... the anchor of each batch row
+  int mask_id;
 };
 
 template <int MODE>
@@ -106,7 +102,7 @@ __global__ void __launch_bounds__(EPI_THREADS) draft_epi_kernel(DraftEpiArgs a) 
   pdl_trigger();
   pdl_wait();
   const size_t MN = static_cast<size_t>(a.M) * a.N;
-  if constexpr (MODE == EPI_BIAS_NORM || MODE == EPI_IN_NORM || MODE == EPI_RESID_NORM) {
+  if constexpr (MODE == EPI_BIAS_NORM || MODE == EPI_IN_NORM || MODE == EPI_RESID_NORM || MODE == EPI_TOK_IN_NORM) {
     extern __shared__ float vrow[];  // the row before the norm
     __shared__ float red[33];
     const int row = blockIdx.x, N = a.N;
@@ -121,7 +117,16 @@ __global__ void __launch_bounds__(EPI_THREADS) draft_epi_kernel(DraftEpiArgs a) 
         const int c = c0 + threadIdx.x + j * EPI_THREADS;
         if (MODE == EPI_RESID_NORM && c < N) hv[j] = a.h[r0 + c];
       }
-      for (int s0 = 0; s0 < a.splits; s0 += EPI_SB) {
+      if constexpr (MODE == EPI_TOK_IN_NORM) {
+        const int t = row % a.g;
+        const int64_t id = t == 0 ? a.anchor[row / a.g] : a.mask_id;
+#pragma unroll
+        for (int j = 0; j < EPI_VPT; ++j) {
+          const int c = c0 + threadIdx.x + j * EPI_THREADS;
+          if (c < N) acc[j] = a.tok_in[static_cast<size_t>(id) * N + c];
+        }
+      }
+      for (int s0 = 0; s0 < (MODE == EPI_TOK_IN_NORM ? 0 : a.splits); s0 += EPI_SB) {
         float v[EPI_VPT][EPI_SB];
 #pragma unroll
         for (int j = 0; j < EPI_VPT; ++j)
@@ -146,6 +151,9 @@ __global__ void __launch_bounds__(EPI_THREADS) draft_epi_kernel(DraftEpiArgs a) 
         } else if constexpr (MODE == EPI_IN_NORM) {
           v = acc[j] + a.bias[c];
           v = v + a.pos[static_cast<size_t>(row % a.g) * N + c];
+          a.h[r0 + c] = v;
+        } else if constexpr (MODE == EPI_TOK_IN_NORM) {
+          v = acc[j] + a.pos[static_cast<size_t>(row % a.g) * N + c];  // acc = in_proj(embed) + bias
           a.h[r0 + c] = v;
         } else {
           const float x = a.bias ? acc[j] + a.bias[c] : acc[j];
@@ -612,17 +620,18 @@ __global__ void __launch_bounds__(256) serial_head_kernel(const float* U, const 
   }
 }
 
-// conf[row] = sigmoid([h ; pe] · w + bias); one warp per row
-__global__ void conf_kernel(const float* h, const float* pe, const float* w, const float* bias, int d, int rows,
-                            float* conf) {
+// conf[row] = sigmoid([h ; tok_in[prev[row]]] · w + bias); one warp per row
+__global__ void conf_kernel(const float* h, const float* tok_in, const int64_t* prev, const float* w,
+                            const float* bias, int d, int rows, float* conf) {
   pdl_trigger();
   pdl_wait();
   const int row = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
+  const float* pe = tok_in + static_cast<size_t>(prev[row]) * d;
   float acc = 0.f;
   for (int c = lane; c < 2 * d; c += 32) {
-    const float x = c < d ? h[static_cast<size_t>(row) * d + c] : pe[static_cast<size_t>(row) * d + c - d];
+    const float x = c < d ? h[static_cast<size_t>(row) * d + c] : pe[c - d];
     acc = fmaf(x, w[c], acc);
   }
   acc = warp_sum(acc);
@@ -687,7 +696,7 @@ int sgemm_epi(evs_drafter* dr, const float* W, const float* X, int ldx, int N, i
   e.splits = p.splits;
   e.M = M;
   e.N = N;
-  const bool norm = mode == EPI_BIAS_NORM || mode == EPI_IN_NORM || mode == EPI_RESID_NORM;
+  const bool norm = mode == EPI_BIAS_NORM || mode == EPI_IN_NORM || mode == EPI_RESID_NORM || mode == EPI_TOK_IN_NORM;
   const dim3 grid = norm ? dim3(M) : dim3(blocks_for(static_cast<size_t>(M) * N, EPI_THREADS));
   const size_t smem = norm ? sizeof(float) * N : 0;
   EVS_CHECK_ARG(smem <= 48 * 1024, "drafter width too large for the fused norm");
@@ -695,6 +704,7 @@ int sgemm_epi(evs_drafter* dr, const float* W, const float* X, int ldx, int N, i
     case EPI_BIAS_NORM: EVS_CUDA_TRY(evs_launch(draft_epi_kernel<EPI_BIAS_NORM>, grid, dim3(EPI_THREADS), smem, st, true, e)); break;
     case EPI_IN_NORM: EVS_CUDA_TRY(evs_launch(draft_epi_kernel<EPI_IN_NORM>, grid, dim3(EPI_THREADS), smem, st, true, e)); break;
     case EPI_RESID_NORM: EVS_CUDA_TRY(evs_launch(draft_epi_kernel<EPI_RESID_NORM>, grid, dim3(EPI_THREADS), smem, st, true, e)); break;
+    case EPI_TOK_IN_NORM: EVS_CUDA_TRY(evs_launch(draft_epi_kernel<EPI_TOK_IN_NORM>, grid, dim3(EPI_THREADS), smem, st, true, e)); break;
     case EPI_BIAS_SILU: EVS_CUDA_TRY(evs_launch(draft_epi_kernel<EPI_BIAS_SILU>, grid, dim3(EPI_THREADS), 0, st, true, e)); break;
     case EPI_BIAS: EVS_CUDA_TRY(evs_launch(draft_epi_kernel<EPI_BIAS>, grid, dim3(EPI_THREADS), 0, st, true, e)); break;
     default: EVS_CUDA_TRY(evs_launch(draft_epi_kernel<EPI_SCALE>, grid, dim3(EPI_THREADS), 0, st, true, e)); break;
@@ -745,12 +755,12 @@ int evs_drafter_create(const evs_drafter_config* cfg, int max_batch, evs_drafter
     off = (off + bytes + 255) & ~size_t(255);
     return o;
   };
-  const size_t o_ctx_in = take(4 * B * CW * nI * H), o_ctx = take(4 * B * CW * d), o_emb = take(4 * B * g * H);
+  const size_t o_ctx_in = take(4 * B * CW * nI * H), o_ctx = take(4 * B * CW * d);
   const size_t o_h = take(4 * B * g * d), o_xb = take(4 * B * g * d), o_q = take(4 * B * g * d);
   const size_t o_kv = take(4 * B * (CW + g) * d), o_kb = take(4 * B * (CW + g) * d), o_vb = take(4 * B * (CW + g) * d);
   const size_t o_y = take(4 * B * g * d), o_tmp = take(4 * B * g * d), o_m1 = take(4 * B * g * hid);
-  const size_t o_z = take(4 * B * g * H), o_U = take(4 * B * g * V), o_pe = take(4 * B * g * d);
-  const size_t o_prev = take(8 * B * g);
+  const size_t o_z = take(4 * B * g * H), o_U = take(4 * B * g * V);
+  const size_t o_prev = take(8 * B * g), o_tok = take(4 * V * d);
   // largest split-K partial buffer over the drafter's projections
   size_t wsf = 0;
   auto need = [&](size_t M_, size_t N_, size_t K_) {
@@ -765,6 +775,7 @@ int evs_drafter_create(const evs_drafter_config* cfg, int max_batch, evs_drafter
   need(B * g, d, hid);
   need(B * g, H, d);
   need(B * g, V, H);
+  need(V, d, H);  // the token table
   const size_t o_ws = take(4 * wsf);
   if (cudaMalloc(&dr->block, off) != cudaSuccess) {
     cudaGetLastError();
@@ -775,7 +786,6 @@ int evs_drafter_create(const evs_drafter_config* cfg, int max_batch, evs_drafter
   char* base = static_cast<char*>(dr->block);
   dr->ctx_in = reinterpret_cast<float*>(base + o_ctx_in);
   dr->ctx = reinterpret_cast<float*>(base + o_ctx);
-  dr->emb = reinterpret_cast<float*>(base + o_emb);
   dr->h = reinterpret_cast<float*>(base + o_h);
   dr->xb = reinterpret_cast<float*>(base + o_xb);
   dr->q = reinterpret_cast<float*>(base + o_q);
@@ -787,8 +797,8 @@ int evs_drafter_create(const evs_drafter_config* cfg, int max_batch, evs_drafter
   dr->m1 = reinterpret_cast<float*>(base + o_m1);
   dr->z = reinterpret_cast<float*>(base + o_z);
   dr->U = reinterpret_cast<float*>(base + o_U);
-  dr->pe = reinterpret_cast<float*>(base + o_pe);
   dr->prev = reinterpret_cast<int64_t*>(base + o_prev);
+  dr->tok_in = reinterpret_cast<float*>(base + o_tok);
   dr->ws = reinterpret_cast<float*>(base + o_ws);
   dr->ws_floats = wsf;
   EVS_CUDA_TRY(cudaMemset(dr->block, 0, off));
@@ -815,6 +825,16 @@ int evs_drafter_finalize(evs_drafter* dr) {
       return EVS_EINVAL;
     }
   }
+  // the token table: every embedding row through in_proj (+ bias), the rows a round would form
+  const evs_drafter_config& c = dr->cfg;
+  cudaStream_t st = nullptr;
+  EVS_CUDA_TRY(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
+  const int r = sgemm_epi(dr, dr->t[EVS_D_IN_W], dr->t[EVS_D_EMBED], c.target_hidden, c.d_model, c.target_hidden,
+                          c.vocab_size, EPI_BIAS, epi(dr->t[EVS_D_IN_B], dr->tok_in), st);
+  const cudaError_t e = cudaStreamSynchronize(st);
+  cudaStreamDestroy(st);
+  EVS_TRY(r);
+  EVS_CUDA_TRY(e);
   dr->finalized = true;
   return EVS_OK;
 }
@@ -860,12 +880,20 @@ int evs_draft_propose(evs_drafter* dr, const evs_state* s, const int64_t* anchor
   // the draft attention reads the context length from the state; without injection it is empty
   const int32_t* ctx_len = c.n_inject > 0 ? s->d_len : reinterpret_cast<const int32_t*>(dr->prev);
   if (c.n_inject == 0) EVS_CUDA_TRY(cudaMemsetAsync(dr->prev, 0, sizeof(int32_t) * B, st));
-  // ---- h = in_proj(embed([anchor, MASK...])) + pos ----
-  EVS_CUDA_TRY(evs_launch(embed_rows_kernel, dim3(rows), dim3(256), 0, st, true, T[EVS_D_EMBED], H, anchor, nullptr, g, c.mask_id, dr->emb));
-  // h = (in_proj + bias) + pos, and the first layer's pre-norm of h into xb
+  // ---- h = in_proj(embed([anchor, MASK...])) + pos (rows of the token table), and the first
+  // layer's pre-norm of h into xb ----
   const float* ln1_0 = c.n_layers > 0 ? T[EVS_D_LAYER0 + EVS_D_LN1] : T[EVS_D_FINAL_LN];
-  EVS_TRY(sgemm_epi(dr, T[EVS_D_IN_W], dr->emb, H, d, H, rows, EPI_IN_NORM,
-                    epi(T[EVS_D_IN_B], dr->xb, ln1_0, dr->h, T[EVS_D_POS], g, eps), st));
+  {
+    DraftEpiArgs e = epi(nullptr, dr->xb, ln1_0, dr->h, T[EVS_D_POS], g, eps);
+    e.tok_in = dr->tok_in;
+    e.anchor = anchor;
+    e.mask_id = c.mask_id;
+    e.M = rows;
+    e.N = d;
+    e.splits = 0;
+    EVS_CUDA_TRY(evs_launch(draft_epi_kernel<EPI_TOK_IN_NORM>, dim3(rows), dim3(EPI_THREADS), sizeof(float) * d, st,
+                            true, e));
+  }
   for (int l = 0; l < c.n_layers; ++l) {
     const float* const* L = T + EVS_D_LAYER0 + l * EVS_D_PER_LAYER;
     // the norm after this layer's MLP: the next layer's pre-norm, or the final norm
@@ -897,13 +925,12 @@ int evs_draft_propose(evs_drafter* dr, const evs_state* s, const int64_t* anchor
     EVS_CUDA_TRY(evs_launch(serial_head_kernel, dim3(B), dim3(256), 0, st, true, dr->U, T[EVS_D_MARKOV], anchor, g, V,
                             greedy, temperature, top_k, u, forced, tokens, qrows, dr->prev));
   }
-  // ---- confidence: σ(conf_w [final_ln(h) ; in_proj(embed(prev))]) ----
-  EVS_CUDA_TRY(evs_launch(embed_rows_kernel, dim3(rows), dim3(256), 0, st, true, T[EVS_D_EMBED], H, nullptr, dr->prev, g, 0, dr->emb));
-  EVS_TRY(sgemm_epi(dr, T[EVS_D_IN_W], dr->emb, H, d, H, rows, EPI_BIAS, epi(T[EVS_D_IN_B], dr->pe), st));
-  EVS_CUDA_TRY(evs_launch(conf_kernel, dim3(blocks_for(rows, 4)), dim3(128), 0, st, true, dr->xb, dr->pe, T[EVS_D_CONF_W], T[EVS_D_CONF_B], d, rows, conf));
+  // ---- confidence: σ(conf_w [final_ln(h) ; in_proj(embed(prev))]), the second half from the table ----
+  EVS_CUDA_TRY(evs_launch(conf_kernel, dim3(blocks_for(rows, 4)), dim3(128), 0, st, true, dr->xb, dr->tok_in, dr->prev,
+                          T[EVS_D_CONF_W], T[EVS_D_CONF_B], d, rows, conf));
   // kernels of this call that count nowhere else (projections and their fused epilogues count
-  // themselves): context gather, embed, kv build + attention per layer, serial head, conf embed + dot
-  evs_count_launch((c.n_inject > 0 ? 1 : 0) + 1 + 2 * c.n_layers + 3);
+  // themselves): context gather, draft rows, kv build + attention per layer, serial head, conf
+  evs_count_launch((c.n_inject > 0 ? 1 : 0) + 1 + 2 * c.n_layers + 2);
   if (U_out != nullptr)
     EVS_CUDA_TRY(cudaMemcpyAsync(U_out, dr->U, sizeof(float) * rows * V, cudaMemcpyDeviceToDevice, st));
   EVS_CUDA_TRY(cudaGetLastError());

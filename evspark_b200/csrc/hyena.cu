@@ -343,6 +343,270 @@ __global__ void __launch_bounds__(HY_THREADS) hyena_iir_kernel(HyArgs<TD> a) {
   if (!a.retain) store_vec<SPT>(a.s_all + ((static_cast<size_t>(b) * a.slots + 0) * d + h) * S + q * SPT, s);
 }
 
+// ---------------------------------------------------------------------------------------------
+// Decode kernels (chunks of at most DEC_T tokens: verify blocks and native steps of any batch).
+// One thread owns one output channel h of one row b for every position of the chunk, so the
+// in-projection sum, the outer FIR, the de-interleave, x1v and the inner FIR / IIR run in the
+// thread's registers with no block barrier between them, and a launch has d x B threads (warps of
+// 32 consecutive channels, coalesced on every buffer).  Every value is formed by the same float
+// operations in the same order as in hyena_fir_kernel / hyena_iir_kernel (in-projection splits in
+// split order; FIR ages oldest first, one fmaf each; the IIR residue sum over four groups of four
+// poles, added pairwise), so the two paths give the same bits and the chunking of a sequence
+// still changes no result.
+// ---------------------------------------------------------------------------------------------
+constexpr int DEC_T = 16;     // chunk positions held in registers
+constexpr int DEC_ROWS = 4;   // rows per CTA (one warp each); the taps are staged once per CTA
+constexpr int DEC_K0 = 3;     // outer short filter length of the decode path
+// batches from this many rows take the decode path: with fewer, its d x B threads leave the GPU
+// idle and the general kernels (16 warps per 32 channels) finish sooner; the bits are the same
+constexpr int DEC_MIN_ROWS = 4;
+
+// Outer pass of one channel h of row b: u (three interleaved in-projection channels 3h+j, splits
+// summed in split order, rounded) into the outer ring, outer FIR (oldest age first) rounded, then
+// x2 = z[3h] and x1v = round(z[3h+1] * z[3h+2]) for positions L0 .. L0+T-1.  The partial sums are
+// loaded split by split, every position's at once, so a split costs one memory round trip.
+template <typename TD>
+__device__ __forceinline__ void dec_outer(const HyArgs<TD>& a, int b, int h, int L0, const float (&wo)[3 * DEC_K0],
+                                          float (&x2)[DEC_T], float (&x1v)[DEC_T]) {
+  const size_t N3 = 3 * static_cast<size_t>(a.d);
+  const size_t split_stride = static_cast<size_t>(a.M) * N3;
+  TD* ring = a.outer_ring + static_cast<size_t>(b) * a.cap_o * N3 + 3 * h;
+  const int T = a.T;
+  // u window: uw[j][0..1] = u at positions P-2, P-1 (history from the ring, zero before position 0)
+  float uw[3][DEC_K0 - 1];
+#pragma unroll
+  for (int r = 0; r < DEC_K0 - 1; ++r) {
+    const int P = L0 - (DEC_K0 - 1) + r;
+#pragma unroll
+    for (int j = 0; j < 3; ++j) uw[j][r] = P >= 0 ? to_f32(ring[static_cast<size_t>(P % a.cap_o) * N3 + j]) : 0.f;
+  }
+  float u[DEC_T][3];
+#pragma unroll
+  for (int t = 0; t < DEC_T; ++t)
+#pragma unroll
+    for (int j = 0; j < 3; ++j) u[t][j] = 0.f;
+  // positions t >= T load row T-1 again (unconditional loads stay in one block, all in flight)
+  // and are never used
+  const float* src = a.ws + static_cast<size_t>(b) * T * N3 + 3 * h;
+  for (int sp = 0; sp < a.splits; sp += 2) {  // two splits' loads in flight, added in split order
+    const float* s0 = src + sp * split_stride;
+    const float* s1 = src + min(sp + 1, a.splits - 1) * split_stride;
+    float v0[DEC_T][3], v1[DEC_T][3];
+#pragma unroll
+    for (int t = 0; t < DEC_T; ++t) {
+      const size_t o = static_cast<size_t>(min(t, T - 1)) * N3;
+#pragma unroll
+      for (int j = 0; j < 3; ++j) {
+        v0[t][j] = __ldg(s0 + o + j);
+        v1[t][j] = __ldg(s1 + o + j);
+      }
+    }
+    const bool two = sp + 1 < a.splits;
+#pragma unroll
+    for (int t = 0; t < DEC_T; ++t)
+#pragma unroll
+      for (int j = 0; j < 3; ++j) {
+        u[t][j] += v0[t][j];
+        if (two) u[t][j] += v1[t][j];
+      }
+  }
+#pragma unroll
+  for (int t = 0; t < DEC_T; ++t) {
+    x2[t] = 0.f;
+    x1v[t] = 0.f;
+    if (t < T) {
+      const int P = L0 + t;
+      float zq[3];
+      const int cs = min(P, DEC_K0 - 1);
+      const int base = a.prefill ? DEC_K0 - 1 : cs;
+#pragma unroll
+      for (int j = 0; j < 3; ++j) {
+        const float un = round_to<TD>(u[t][j]);
+        ring[static_cast<size_t>(P % a.cap_o) * N3 + j] = from_f32<TD>(un);
+        // the weights of ages 2, 1, 0 are w[base-2], w[base-1], w[base] (selected, not indexed, so
+        // that they stay in registers); age 2 appears only when cs = 2, where base = 2
+        const float w0 = wo[j * DEC_K0], w1 = wo[j * DEC_K0 + 1], w2 = wo[j * DEC_K0 + 2];
+        const float wb = base == 2 ? w1 : w0;
+        const float wc = base == 2 ? w2 : (base == 1 ? w1 : w0);
+        float z = 0.f;
+        if (cs >= 2) z = fmaf(w0, uw[j][0], z);
+        if (cs >= 1) z = fmaf(wb, uw[j][1], z);
+        z = fmaf(wc, un, z);
+        zq[j] = round_to<TD>(z);
+        uw[j][0] = uw[j][1];
+        uw[j][1] = un;
+      }
+      x2[t] = zq[0];
+      x1v[t] = round_to<TD>(zq[1] * zq[2]);
+    }
+  }
+}
+
+// grid (d / 32, ceil(B / DEC_ROWS)), block (32, DEC_ROWS).  KI = inner filter length (7 or 128).
+// Shared memory: taps[32][tap_stride(KI)] f32 (channel c's weight of age a at taps[c][a]) | per
+// warp hist[KI-1+DEC_T][32] TD (x1v by position, the oldest history position first).
+template <typename TD, bool FLIP, int KI>
+__global__ void __launch_bounds__(32 * DEC_ROWS) hyena_fir_dec_kernel(HyArgs<TD> a) {
+  pdl_trigger();
+  constexpr int H = KI - 1, WROWS = H + DEC_T, KS = tap_stride(KI);
+  extern __shared__ __align__(16) float sm[];
+  float* taps = sm;
+  TD* hist = reinterpret_cast<TD*>(taps + 32 * KS) + threadIdx.y * WROWS * 32;
+  const int lane = threadIdx.x, h0 = blockIdx.x * 32, h = h0 + lane;
+  const int b = blockIdx.y * DEC_ROWS + threadIdx.y;
+  // the taps are weights: stage them before waiting for the in-projection.  The full-window weight
+  // of age a is w[a] for the flipped filter (the rows as they are: asynchronous 16-byte copies) and
+  // w[K-1-a] otherwise (reversed rows)
+  const float* iw = a.inner_w + static_cast<size_t>(h0) * KI;
+  if constexpr (FLIP && KI % 4 == 0) {
+    for (int i = threadIdx.y * 32 + lane; i < 32 * (KI / 4); i += 32 * DEC_ROWS) {
+      const int c = i / (KI / 4), j = i - c * (KI / 4);
+      cp_async16(taps + c * KS + 4 * j, iw + c * KI + 4 * j);
+    }
+    cp_async_commit();
+  } else {
+    for (int i = threadIdx.y * 32 + lane; i < 32 * KI; i += 32 * DEC_ROWS) {
+      const int c = i / KI, k = i - c * KI;
+      taps[c * KS + (FLIP ? k : H - k)] = __ldg(iw + i);
+    }
+  }
+  for (int i = threadIdx.y * 32 + lane; i < 32 * (KS - KI); i += 32 * DEC_ROWS)
+    taps[(i / (KS - KI)) * KS + KI + i % (KS - KI)] = 0.f;  // the padding a float4 read may touch
+  float wo[3 * DEC_K0];
+#pragma unroll
+  for (int i = 0; i < 3 * DEC_K0; ++i) wo[i] = __ldg(a.short_w + static_cast<size_t>(3 * h) * DEC_K0 + i);
+  const float Dg = FLIP ? __ldg(a.D + h) : 0.f;
+  pdl_wait();
+  if constexpr (FLIP && KI % 4 == 0) cp_async_wait<0>();
+  __syncthreads();  // taps staged
+  if (b >= a.M / a.T) return;
+  const int L0 = a.len[b];
+  const int T = a.T;
+  // x1v history of the warp's 32 channels, positions L0-H .. L0-1 (zero before position 0), copied
+  // asynchronously while the outer pass runs: one 16-byte chunk per copy, every copy in flight
+  constexpr int CPR = 32 * static_cast<int>(sizeof(TD)) / 16;  // 16-byte chunks per history row
+  const TD* ring_row = a.inner_ring + static_cast<size_t>(b) * a.cap_i * a.d + h0;
+  for (int i = lane; i < H * CPR; i += 32) {
+    const int r = i / CPR, c = i - r * CPR;
+    const int P = L0 - H + r;
+    TD* dst = hist + r * 32 + c * (16 / sizeof(TD));
+    if (P >= 0)
+      cp_async16(dst, ring_row + static_cast<size_t>(P % a.cap_i) * a.d + c * (16 / sizeof(TD)));
+    else
+      *reinterpret_cast<int4*>(dst) = make_int4(0, 0, 0, 0);
+  }
+  cp_async_commit();
+  float x2[DEC_T], x1v[DEC_T];
+  dec_outer(a, b, h, L0, wo, x2, x1v);
+  TD* ring_w = a.inner_ring + static_cast<size_t>(b) * a.cap_i * a.d + h;
+#pragma unroll
+  for (int t = 0; t < DEC_T; ++t) {
+    hist[(H + t) * 32 + lane] = from_f32<TD>(x1v[t]);
+    if (t < T) ring_w[static_cast<size_t>((L0 + t) % a.cap_i) * a.d] = from_f32<TD>(x1v[t]);
+  }
+  cp_async_wait<0>();
+  __syncwarp();  // the history rows the other lanes copied
+  float acc[DEC_T];
+#pragma unroll
+  for (int t = 0; t < DEC_T; ++t) acc[t] = 0.f;
+  if (FLIP || a.prefill || L0 >= H) {
+    // every position uses the full window (positions before 0 hold zeros, which add nothing):
+    // acc[t] += w(age) * x(L0 + t - age) for age = H .. 0, the window rotating one position a step
+    float win[DEC_T];
+#pragma unroll
+    for (int t = 0; t < DEC_T; ++t) win[t] = to_f32(hist[t * 32 + lane]);
+    const float* tp = taps + lane * KS;
+#pragma unroll
+    for (int a4 = H / 4; a4 >= 0; --a4) {
+      const float4 w4 = *reinterpret_cast<const float4*>(tp + 4 * a4);
+      const float wv[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+      for (int e = 3; e >= 0; --e) {
+        const int age = 4 * a4 + e;
+        if (age > H) continue;
+#pragma unroll
+        for (int t = 0; t < DEC_T; ++t) acc[t] = fmaf(wv[e], win[t], acc[t]);
+        if (age > 0) {
+#pragma unroll
+          for (int t = 0; t < DEC_T - 1; ++t) win[t] = win[t + 1];
+          win[DEC_T - 1] = to_f32(hist[(H + DEC_T - age) * 32 + lane]);
+        }
+      }
+    }
+  } else {
+    // unflipped filter on a history shorter than K-1 (a sequence's first positions outside
+    // prefill): position P weights age a by w[min(P, K-1) - a]
+    const float* wr = a.inner_w + static_cast<size_t>(h) * KI;
+#pragma unroll
+    for (int t = 0; t < DEC_T; ++t) {
+      if (t < T) {
+        const int P = L0 + t, cs = min(P, H);
+        float z = 0.f;
+        for (int age = cs; age >= 0; --age) z = fmaf(__ldg(wr + cs - age), to_f32(hist[(H + t - age) * 32 + lane]), z);
+        acc[t] = z;
+      }
+    }
+  }
+#pragma unroll
+  for (int t = 0; t < DEC_T; ++t) {
+    if (t < T) {
+      float z = acc[t];
+      if (FLIP) z = fmaf(Dg, x1v[t], z);
+      const float yv = round_to<TD>(x2[t] * round_to<TD>(z));
+      a.y[static_cast<size_t>(b * T + t) * a.ld_y + h] = from_f32<TD>(yv);
+    }
+  }
+}
+
+// grid (d / 32, ceil(B / DEC_ROWS)), block (32, DEC_ROWS): one thread per channel and row, all 16
+// poles in registers (four groups of four, as the four pole-group threads of hyena_iir_kernel).
+template <typename TD>
+__global__ void __launch_bounds__(32 * DEC_ROWS) hyena_iir_dec_kernel(HyArgs<TD> a) {
+  pdl_trigger();
+  constexpr int S = 16;
+  const int h = blockIdx.x * 32 + threadIdx.x;
+  const int b = blockIdx.y * DEC_ROWS + threadIdx.y;
+  const int d = a.d;
+  float p[S], r[S], s[S];
+  load_vec<S>(a.poles + static_cast<size_t>(h) * S, p);
+  load_vec<S>(a.residues + static_cast<size_t>(h) * S, r);
+  float wo[3 * DEC_K0];
+#pragma unroll
+  for (int i = 0; i < 3 * DEC_K0; ++i) wo[i] = __ldg(a.short_w + static_cast<size_t>(3 * h) * DEC_K0 + i);
+  const float Dg = a.D[h];
+  pdl_wait();
+  if (b >= a.M / a.T) return;
+  const int L0 = a.len[b];
+  if (L0 > 0) {
+    load_vec<S>(a.s_all + ((static_cast<size_t>(b) * a.slots + a.iir_cur[b]) * d + h) * S, s);
+  } else {
+#pragma unroll
+    for (int j = 0; j < S; ++j) s[j] = 0.f;
+  }
+  float x2[DEC_T], x1v[DEC_T];
+  dec_outer(a, b, h, L0, wo, x2, x1v);
+#pragma unroll
+  for (int t = 0; t < DEC_T; ++t) {
+    if (t < a.T) {
+      float part[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        part[q] = 0.f;
+#pragma unroll
+        for (int j = 4 * q; j < 4 * q + 4; ++j) {
+          s[j] = fmaf(p[j], s[j], x1v[t]);
+          part[q] = fmaf(r[j], s[j], part[q]);
+        }
+      }
+      const float tot = (part[0] + part[1]) + (part[2] + part[3]);
+      const float yv = round_to<TD>(x2[t] * (tot + Dg * x1v[t]));
+      a.y[static_cast<size_t>(b * a.T + t) * a.ld_y + h] = from_f32<TD>(yv);
+      if (a.retain) store_vec<S>(a.s_all + ((static_cast<size_t>(b) * a.slots + t) * d + h) * S, s);
+    }
+  }
+  if (!a.retain) store_vec<S>(a.s_all + ((static_cast<size_t>(b) * a.slots + 0) * d + h) * S, s);
+}
+
 __global__ void rollback_kernel(int32_t* len, const int32_t* len0, int32_t* iir_cur, const int32_t* chunk,
                                 const int32_t* k, int B, EvsDevErr* err) {
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
@@ -418,6 +682,34 @@ int launch_hyena_t(const evs_model* m, evs_state* s, int layer, int B, int T, in
   a.y = static_cast<TD*>(s->act);
   a.ld_y = s->ld_act;
   EVS_CHECK_ARG(a.K0 >= 1 && a.K0 - 1 + TS <= UW, "short filter too long for the outer-FIR window");
+  // chunks of at most DEC_T tokens with the Evo2 filter shapes: the register-resident decode path
+  // (same bits as the general kernels below)
+  const bool dec_shape = B >= DEC_MIN_ROWS && T <= DEC_T && a.K0 == DEC_K0 &&
+                         (L.kind == EVS_LAYER_HCL ? a.S == 16 : (a.K == 7 || a.K == 128));
+  if (dec_shape) {
+    const dim3 dgrid(d / 32, (B + DEC_ROWS - 1) / DEC_ROWS), dblock(32, DEC_ROWS);
+    if (L.kind == EVS_LAYER_HCL) {
+      EVS_CUDA_TRY(evs_launch(hyena_iir_dec_kernel<TD>, dgrid, dblock, 0, st, s->use_pdl(), a));
+    } else {
+      auto launch = [&](auto kern, int KI) -> int {
+        const size_t smem = sizeof(float) * 32 * tap_stride(KI) + sizeof(TD) * DEC_ROWS * (KI - 1 + DEC_T) * 32;
+        EVS_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+        EVS_CUDA_TRY(evs_launch(kern, dgrid, dblock, smem, st, s->use_pdl(), a));
+        return EVS_OK;
+      };
+      if (L.kind == EVS_LAYER_HCM && a.K == 128)
+        EVS_TRY(launch(hyena_fir_dec_kernel<TD, true, 128>, 128));
+      else if (L.kind == EVS_LAYER_HCM)
+        EVS_TRY(launch(hyena_fir_dec_kernel<TD, true, 7>, 7));
+      else if (a.K == 128)
+        EVS_TRY(launch(hyena_fir_dec_kernel<TD, false, 128>, 128));
+      else
+        EVS_TRY(launch(hyena_fir_dec_kernel<TD, false, 7>, 7));
+    }
+    EVS_CUDA_TRY(cudaGetLastError());
+    evs_count_launch(1);
+    return EVS_OK;
+  }
   dim3 grid(d / CH, B);
   const size_t outer_floats = static_cast<size_t>(UW) * C3 + TS * C3 + C3 * a.K0;
   if (L.kind == EVS_LAYER_HCL) {

@@ -184,7 +184,7 @@ struct TpPartials {
 int launch_res_add_norm(const evs_model* m, evs_state* s, int M, int splits, const TpPartials& parts,
                         const float* scale, int capture_slot, int T, cudaStream_t st);
 // publish this rank's partial sums of reduction `epoch` to the peers (after the producing kernel)
-int launch_tp_signal(evs_state* s, long long epoch, cudaStream_t st);
+int launch_tp_reduce_signal(evs_state* s, float* buf, int splits, int M, long long epoch, cudaStream_t st);
 int launch_swiglu(const evs_model* m, evs_state* s, int M, int splits, cudaStream_t st);
 // logits rows go to out[(b * out_T + t0 + t) * V] (or out[b * V] for the last row when last_only)
 int launch_logits(const evs_model* m, evs_state* s, int M, int T, int splits, float* logits, int out_T, int t0,

@@ -3,6 +3,8 @@
 // Every reduction runs in a fixed order that does not depend on the number of token rows.
 #include <cooperative_groups.h>
 
+#include <algorithm>
+
 #include "internal.hpp"
 
 namespace cg = cooperative_groups;
@@ -241,11 +243,34 @@ __global__ void bookkeeping_kernel(int32_t* len, int32_t* len0, int32_t* iir_cur
 }
 
 // publish this rank's partial sums (written by the preceding projection) to the peers
-__global__ void tp_signal_kernel(long long* flag, long long epoch) {
+// This rank's split partials of a row-parallel projection summed in split order into split 0
+// (in place, float4 per thread), then the epoch published: each CTA fences its sums at system
+// scope and counts itself in; the last one resets the counter and stores the epoch with a
+// system-scope release.  The peers then read one partial buffer per rank instead of every split.
+__global__ void tp_reduce_signal_kernel(float4* __restrict__ buf, int splits, int n4, unsigned* counter,
+                                        long long* flag, long long epoch) {
   pdl_trigger();
   pdl_wait();
+  if (splits > 1) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += gridDim.x * blockDim.x) {
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int sp = 0; sp < splits; ++sp) {
+        const float4 v = buf[static_cast<size_t>(sp) * n4 + i];
+        acc.x += v.x;
+        acc.y += v.y;
+        acc.z += v.z;
+        acc.w += v.w;
+      }
+      buf[i] = acc;
+    }
+  }
   __threadfence_system();
-  st_release_sys(flag, epoch);
+  __syncthreads();
+  if (threadIdx.x == 0 && atomicAdd(counter, 1u) == gridDim.x - 1) {
+    *counter = 0u;
+    __threadfence_system();
+    st_release_sys(flag, epoch);
+  }
 }
 
 __global__ void poles_kernel(const float* lp, float* p, int n) {
@@ -323,9 +348,16 @@ int launch_bookkeeping(evs_state* s, int B, int T, int retain, cudaStream_t st) 
   return EVS_OK;
 }
 
-int launch_tp_signal(evs_state* s, long long epoch, cudaStream_t st) {
-  long long* flag = reinterpret_cast<long long*>(s->tp_base[s->m->tp_rank] + 2 * s->tp_buf_bytes);
-  EVS_CUDA_TRY(evs_launch(tp_signal_kernel, dim3(1), dim3(1), 0, st, s->use_pdl(), flag, epoch));
+int launch_tp_reduce_signal(evs_state* s, float* buf, int splits, int M, long long epoch, cudaStream_t st) {
+  char* tail = s->tp_base[s->m->tp_rank] + 2 * s->tp_buf_bytes;  // [epoch flag | ... | arrival counter]
+  long long* flag = reinterpret_cast<long long*>(tail);
+  unsigned* counter = reinterpret_cast<unsigned*>(tail + 64);
+  const int d = s->m->cfg.d_model;
+  EVS_CHECK_ARG(d % 4 == 0, "d_model must be a multiple of 4");
+  const int n4 = M * d / 4;
+  const int blocks = splits > 1 ? std::min((n4 + 255) / 256, 2 * 148) : 1;
+  EVS_CUDA_TRY(evs_launch(tp_reduce_signal_kernel, dim3(blocks), dim3(256), 0, st, s->use_pdl(),
+                          reinterpret_cast<float4*>(buf), splits, n4, counter, flag, epoch));
   evs_count_launch(1);
   return EVS_OK;
 }
