@@ -124,7 +124,7 @@ def _cpu_target_weights(cfg, seed: int) -> dict:
 
 
 def cpu_reference_rounds(n_threads: int, steps: int, warmup: int, *, sampled: bool = False,
-                         prompt_len: int = PROMPT_LEN) -> dict:
+                         prompt_len: int = PROMPT_LEN, synthetic_context: int = 0) -> dict:
     """The reference path on the host cores (the CPU port in ``oracle/``), timed round by round.
 
     Workload: the GPU arm's own (1024-token order-3 Markov prompt, Evo2-7B shape, 32 blocks, bf16
@@ -134,7 +134,9 @@ def cpu_reference_rounds(n_threads: int, steps: int, warmup: int, *, sampled: bo
     seconds, so ``ms_per_step * steps`` is the timed region.  With ``sampled`` (a bounded sample), or
     when the host has too little free memory for the 26 GB of fp32 weights, four 7B-width blocks
     (SE, MR, LI, MHA) run instead and ``value`` is scaled from their measured time to 32 blocks
-    (reported as separate fields)."""
+    (reported as separate fields).  ``synthetic_context`` = L > 0 replaces the prefill (infeasible on
+    the host at long context) by a synthetically filled state of L consumed tokens: random KV rows,
+    FIR histories and IIR states of the right sizes, and random drafter context rows."""
     import torch
 
     from evspark_b200.config import DRAFTERS, EVO2_7B, EVO2_7B_SLICE
@@ -160,15 +162,34 @@ def cpu_reference_rounds(n_threads: int, steps: int, warmup: int, *, sampled: bo
     dw = init_drafter_weights(dcfg, seed=20260830, embed=w["embed"])
     init_s = time.perf_counter() - t_init
     rng = np.random.default_rng(7)
-    prompt = markov_prompt(prompt_len, seed=20260821)
     rounds = warmup + steps
-    st = o.init_state(1, prompt_len + (rounds + 2) * (GAMMA + 1))
-    t0 = time.perf_counter()
-    with torch.no_grad():
-        _, _, cap = o.forward(prompt[None, :-1], st, prefill=True, capture_layers=(inject,))
-    prefill_s = time.perf_counter() - t0
-    ctx = cap[inject][0][-dcfg.ctx_window:].float()
-    y = int(prompt[-1])
+    if synthetic_context:
+        L = int(synthetic_context)
+        st = o.init_state(1, L + (rounds + 2) * (GAMMA + 1))
+        t0 = time.perf_counter()
+        g = torch.Generator().manual_seed(5)
+        for i in st.kv:
+            st.kv[i][:, :L].normal_(generator=g)
+        K0, S = cfg.short_filter_length, cfg.state_size
+        for i in st.outer:
+            st.outer[i] = torch.randn(1, 3 * cfg.d_model, K0 - 1, generator=g)
+        for i in st.inner:
+            st.inner[i] = torch.randn(1, cfg.d_model, cfg.filter_length(cfg.layer_types[i]) - 1, generator=g)
+        for i in st.iir:
+            st.iir[i] = torch.randn(1, cfg.d_model, S, generator=g)
+        st.lengths[:] = L
+        ctx = torch.randn(dcfg.ctx_window, cfg.d_model, generator=g)
+        prefill_s = time.perf_counter() - t0
+        y = 71
+    else:
+        prompt = markov_prompt(prompt_len, seed=20260821)
+        st = o.init_state(1, prompt_len + (rounds + 2) * (GAMMA + 1))
+        t0 = time.perf_counter()
+        with torch.no_grad():
+            _, _, cap = o.forward(prompt[None, :-1], st, prefill=True, capture_layers=(inject,))
+        prefill_s = time.perf_counter() - t0
+        ctx = cap[inject][0][-dcfg.ctx_window:].float()
+        y = int(prompt[-1])
     times, scaled, emitted = [], [], []
     for r in range(rounds):
         t0 = time.perf_counter()
@@ -206,9 +227,11 @@ def cpu_reference_rounds(n_threads: int, steps: int, warmup: int, *, sampled: bo
         out["block_scale"] = 32 / cfg.n_layers
         why = ("a bounded sample" if sampled else
                f"host memory {avail / 2**30:.0f} GiB free is short of the 26 GB of fp32 weights")
+        ctx_desc = (f"on a synthetically filled state of {synthetic_context} tokens (random KV rows, FIR "
+                    f"histories, IIR states and drafter context)" if synthetic_context else
+                    f"after a {prompt_len - 1}-token prefill")
         out["sample"] = (f"{steps} timed rounds (after {warmup} untimed) over 4 of the 32 blocks (SE, MR, LI, MHA; "
-                         f"{why}) after a {prompt_len - 1}-token prefill; value scales the measured verify forward "
-                         f"x8 to 32 blocks")
+                         f"{why}) {ctx_desc}; value scales the measured verify forward x8 to 32 blocks")
     return out
 
 
@@ -391,7 +414,9 @@ def run_tp(args) -> int:
     ev0.record()
     tokens = 0
     for _ in range(args.steps):
+        torch.cuda.nvtx.range_push("evs_round")  # lets a profiler select the timed rounds
         tokens += one_round()
+        torch.cuda.nvtx.range_pop()
     ev1.record()
     torch.cuda.synchronize()
     launches = N.launch_count() - n0
@@ -423,6 +448,17 @@ def run_tp(args) -> int:
     N.call("evs_profile_stop", state["ip"].handle, pl, pms, pb)
     err = [C.c_int32(), C.c_int32(), C.c_int32()]
     N.check(N.lib().evs_get_device_error(state["ip"].handle, *[C.byref(e) for e in err]), "evs_get_device_error")
+    cpu_baseline = None
+    if rank == 0 and world == 1 and args.config == "evo2_7b" and args.cpu_steps > 0:
+        state["ip"].close()
+        state["ip"] = None
+        nd.close()
+        model.close()
+        torch.cuda.empty_cache()
+        cpu = cpu_reference_rounds(os.cpu_count() or 1, args.cpu_steps, 1, sampled=True, synthetic_context=L - 1)
+        cpu_baseline = {"value": round(cpu["value"], 5), "unit": "tok/s", "cores": cpu["cores"], "kind": "port",
+                        "sample": cpu["sample"], "ms_per_step_measured": round(cpu["ms_per_step"], 1),
+                        "ms_per_step_scaled_to_32_blocks": cpu.get("ms_per_step_scaled_to_32_blocks")}
     if rank == 0:
         line = {
             "metric": (f"accepted tok/s single-stream {args.config} γ=12, channel-sharded" if world > 1 else
@@ -448,10 +484,13 @@ def run_tp(args) -> int:
                            "cross-rank partial sums, SwiGLU, logits",
             "device_error": int(err[0].value), "clocks": clk, "gpu_launches": int(launches),
         }
+        if cpu_baseline is not None:
+            line["cpu_baseline"] = cpu_baseline
         print(json.dumps(line), flush=True)
-    state["ip"].close()
-    nd.close()
-    model.close()
+    if state["ip"] is not None:
+        state["ip"].close()
+        nd.close()
+        model.close()
     if world > 1:
         dist.destroy_process_group()
     return 0

@@ -429,6 +429,8 @@ int evs_state_create(const evs_model* m, int max_batch, int max_seqlen, int max_
   }
   size_t o_ring[4];
   for (int k = 0; k < m->n_capture; ++k) o_ring[k] = take(B * s->ring_len * d * sizeof(float));
+  const size_t o_tag = m->n_capture > 0 ? take(B * s->ring_len * sizeof(unsigned long long)) : SIZE_MAX;
+  const size_t o_seq = take(sizeof(unsigned long long));
   void* pers = nullptr;
   if (cudaMalloc(&pers, off) != cudaSuccess) {
     cudaGetLastError();
@@ -450,6 +452,13 @@ int evs_state_create(const evs_model* m, int max_batch, int max_seqlen, int max_
     if (o_kv[i] != SIZE_MAX) s->kv[i] = base + o_kv[i];
   }
   for (int k = 0; k < m->n_capture; ++k) s->cap_ring[k] = reinterpret_cast<float*>(base + o_ring[k]);
+  if (o_tag != SIZE_MAX) s->cap_tag = reinterpret_cast<unsigned long long*>(base + o_tag);
+  s->d_fwd_seq = reinterpret_cast<unsigned long long*>(base + o_seq);
+  {
+    static std::atomic<unsigned long long> next_id{1};
+    const unsigned long long id = next_id.fetch_add(1) & ((1ull << (64 - EVS_TAG_SEQ_BITS - EVS_TAG_ROW_BITS)) - 1);
+    s->tag_hi = (id == 0 ? 1ull : id) << (EVS_TAG_SEQ_BITS + EVS_TAG_ROW_BITS);
+  }
 
   // ---- scratch ----
   size_t ws_cols = 0;
@@ -668,6 +677,10 @@ int copy_row(evs_state* s, int src, int dst, cudaStream_t st) {
   for (int k = 0; k < m->n_capture; ++k) {
     const size_t rb = static_cast<size_t>(s->ring_len) * c.d_model * 4;
     EVS_TRY(cp(s->cap_ring[k], rb, rb));
+  }
+  if (s->cap_tag) {
+    const size_t rb = static_cast<size_t>(s->ring_len) * sizeof(unsigned long long);
+    EVS_TRY(cp(s->cap_tag, rb, rb));
   }
   EVS_TRY(cp(s->d_len, 4, 4));
   EVS_TRY(cp(s->d_len0, 4, 4));

@@ -31,6 +31,14 @@ struct evs_drafter {
   // projection and epilogue as a round's rows (a token's row does not depend on the other rows), so
   // the draft rows [anchor, MASK...] and the confidence head's in_proj(embed(prev)) are gathers
   float* tok_in = nullptr;
+  // context rows are projected once per position: the k and v rows of every layer ([n_layers][B]
+  // [DR_CR][d], slot = position % DR_CR), with the position and the capture tag of the ring row they
+  // came from; a call projects only the rows whose slot does not hold the current (position, tag)
+  float *ck = nullptr, *cv = nullptr;
+  int32_t* cpos = nullptr;              // [B][DR_CR], -1 = empty
+  unsigned long long* ctag = nullptr;   // [B][DR_CR]
+  int32_t* cmap = nullptr;              // [B * CW][2]: (row, position) of this call's rows to project
+  int32_t* ccount = nullptr;            // [2]: those rows; plus the B * g draft rows
   int64_t* prev = nullptr;
   float* ws = nullptr;  // split-K partials of the projections
   size_t ws_floats = 0;
@@ -45,23 +53,82 @@ struct RingPtrs {
   const float* p[4];
 };
 
-__global__ void gather_ctx_kernel(RingPtrs rings, int n_inject, int ring_len, int H, const int32_t* len, int CW,
-                                  float* out) {
+constexpr int DR_CR = 128;  // cache slots per row: covers the ctx_window (<= 64) positions a call reads
+
+// Which context rows of a call lack a current projection: row b reads positions L-n .. L-1
+// (n = min(CW, L)); position P is current when its slot holds P with the capture tag that the
+// state's ring row at P carries now.  One CTA: the flags, an exclusive scan in (row, position)
+// order, the map of rows to project, and the counts [rows, rows + B*g].
+__global__ void __launch_bounds__(1024) ctx_plan_kernel(const int32_t* __restrict__ len, int B, int CW, int g,
+                                                        const unsigned long long* __restrict__ cap_tag, int ring_len,
+                                                        const int32_t* __restrict__ cpos,
+                                                        const unsigned long long* __restrict__ ctag,
+                                                        int32_t* __restrict__ cmap, int32_t* __restrict__ ccount) {
   pdl_trigger();
   pdl_wait();
-  const int j = blockIdx.x, b = blockIdx.y;
-  const int L = len[b];
-  const int n = min(CW, L);
-  const int K = n_inject * H;
-  float* dst = out + (static_cast<size_t>(b) * CW + j) * K;
-  if (j >= n) {
-    for (int e = threadIdx.x; e < K; e += blockDim.x) dst[e] = 0.f;
-    return;
+  __shared__ int wsum[32];
+  __shared__ int base, pass_total;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  if (threadIdx.x == 0) base = 0;
+  __syncthreads();
+  const int items = B * CW;
+  for (int i0 = 0; i0 < items; i0 += blockDim.x) {
+    const int i = i0 + threadIdx.x;
+    int need = 0, b = 0, P = 0;
+    if (i < items) {
+      b = i / CW;
+      const int j = i - b * CW, L = len[b], n = min(CW, L);
+      if (j < n) {
+        P = L - n + j;
+        const int slot = P % DR_CR;
+        need = !(cpos[b * DR_CR + slot] == P &&
+                 ctag[b * DR_CR + slot] == cap_tag[static_cast<size_t>(b) * ring_len + P % ring_len]);
+      }
+    }
+    const unsigned bal = __ballot_sync(0xffffffffu, need);
+    if (lane == 0) wsum[warp] = __popc(bal);
+    __syncthreads();
+    if (warp == 0) {
+      const int v = lane < nw ? wsum[lane] : 0;
+      int x = v;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+      }
+      if (lane < nw) wsum[lane] = x - v;  // exclusive prefix of the warps
+      if (lane == 31) pass_total = x;
+    }
+    __syncthreads();
+    if (need) {
+      const int idx = base + wsum[warp] + __popc(bal & ((1u << lane) - 1u));
+      cmap[2 * idx] = b;
+      cmap[2 * idx + 1] = P;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) base += pass_total;
+    __syncthreads();
   }
-  const int P = L - n + j;
+  if (threadIdx.x == 0) {
+    ccount[0] = base;
+    ccount[1] = base + B * g;
+  }
+}
+
+// the ring rows (injection-layer outputs, n_inject rings concatenated) of the rows to project
+__global__ void gather_ctx_rows_kernel(RingPtrs rings, int n_inject, int ring_len, int H,
+                                       const int32_t* __restrict__ cmap, const int32_t* __restrict__ ccount,
+                                       float* __restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
+  const int r = blockIdx.x;
+  if (r >= ccount[0]) return;
+  const int b = cmap[2 * r], P = cmap[2 * r + 1];
+  float* dst = out + static_cast<size_t>(r) * n_inject * H;
   for (int c = 0; c < n_inject; ++c) {
-    const float* src = rings.p[c] + (static_cast<size_t>(b) * ring_len + P % ring_len) * H;
-    for (int e = threadIdx.x; e < H; e += blockDim.x) dst[c * H + e] = src[e];
+    const float4* src = reinterpret_cast<const float4*>(rings.p[c] + (static_cast<size_t>(b) * ring_len + P % ring_len) * H);
+    float4* d4 = reinterpret_cast<float4*>(dst + c * H);
+    for (int e = threadIdx.x; e < H / 4; e += blockDim.x) d4[e] = src[e];
   }
 }
 
@@ -95,6 +162,7 @@ struct DraftEpiArgs {
   const float* tok_in;      // EPI_TOK_IN_NORM: the token table [V][N]
   const int64_t* anchor;    // ... the anchor of each batch row
   int mask_id;
+  const int32_t* m_dev;     // optional device-side row count (rows past it are skipped)
 };
 
 template <int MODE>
@@ -106,6 +174,7 @@ __global__ void __launch_bounds__(EPI_THREADS) draft_epi_kernel(DraftEpiArgs a) 
     extern __shared__ float vrow[];  // the row before the norm
     __shared__ float red[33];
     const int row = blockIdx.x, N = a.N;
+    if (a.m_dev != nullptr && row >= *a.m_dev) return;
     const size_t r0 = static_cast<size_t>(row) * N;
     float ss = 0.f;
     // EPI_VPT columns c = tid + 256 j per pass; the split loads of all of them are in flight together
@@ -191,35 +260,72 @@ __global__ void __launch_bounds__(EPI_THREADS) draft_epi_kernel(DraftEpiArgs a) 
   }
 }
 
-// kv_in[b] = [ctx[b] (CW rows) ; xb[b] (g rows)]
-__global__ void build_kv_kernel(const float* ctx, const float* xb, int CW, int g, int d, float* out) {
+// rows of the k / v projections: [the B*g draft rows (xb) ; the context rows to project]
+__global__ void build_kv_kernel(const float* __restrict__ xb, const float* __restrict__ ctx, int Bg,
+                                const int32_t* __restrict__ ccount, int d, float* __restrict__ out) {
   pdl_trigger();
   pdl_wait();
-  const int j = blockIdx.x, b = blockIdx.y;
-  const float* src = j < CW ? ctx + (static_cast<size_t>(b) * CW + j) * d : xb + (static_cast<size_t>(b) * g + j - CW) * d;
-  float* dst = out + (static_cast<size_t>(b) * (CW + g) + j) * d;
+  const int r = blockIdx.x;
+  const float* src;
+  if (r < Bg) {
+    src = xb + static_cast<size_t>(r) * d;
+  } else {
+    if (ccount == nullptr || r - Bg >= ccount[0]) return;
+    src = ctx + static_cast<size_t>(r - Bg) * d;
+  }
+  float* dst = out + static_cast<size_t>(r) * d;
   for (int c = threadIdx.x; c < d; c += blockDim.x) dst[c] = src[c];
 }
 
-// one CTA per (query t, head, row b); 128 threads; keys = ctx rows j < n_ctx(b) and drafts <= t
-__global__ void __launch_bounds__(128) draft_attn_kernel(const float* q, const float* kb, const float* vb,
-                                                         const int32_t* len, int CW, int g, int d, int heads,
-                                                         float* y) {
+// the projected context rows of one layer into their cache slots; after the last layer, the slots'
+// positions and tags (the rows are then current for later calls)
+__global__ void ctx_kv_store_kernel(const float* __restrict__ kb, const float* __restrict__ vb, int Bg,
+                                    const int32_t* __restrict__ cmap, const int32_t* __restrict__ ccount, int d,
+                                    float* __restrict__ ck, float* __restrict__ cv, int last,
+                                    const unsigned long long* __restrict__ cap_tag, int ring_len,
+                                    int32_t* __restrict__ cpos, unsigned long long* __restrict__ ctag) {
+  pdl_trigger();
+  pdl_wait();
+  const int r = blockIdx.x;
+  if (r >= ccount[0]) return;
+  const int b = cmap[2 * r], P = cmap[2 * r + 1];
+  const int slot = P % DR_CR;
+  const size_t src = static_cast<size_t>(Bg + r) * d, dst = (static_cast<size_t>(b) * DR_CR + slot) * d;
+  for (int c = threadIdx.x; c < d; c += blockDim.x) {
+    ck[dst + c] = kb[src + c];
+    cv[dst + c] = vb[src + c];
+  }
+  if (last && threadIdx.x == 0) {
+    cpos[b * DR_CR + slot] = P;
+    ctag[b * DR_CR + slot] = cap_tag[static_cast<size_t>(b) * ring_len + P % ring_len];
+  }
+}
+
+// one CTA per (query t, head, row b); 128 threads; keys = the row's context positions L-n .. L-1
+// (n = min(CW, L), their k/v from the cache slots) and the drafts <= t, in that order
+__global__ void __launch_bounds__(128) draft_attn_kernel(const float* q, const float* kd, const float* vd,
+                                                         const float* ck, const float* cv, const int32_t* len,
+                                                         int with_ctx, int CW, int g, int d, int heads, float* y) {
   pdl_trigger();
   pdl_wait();
   __shared__ float sc[256];
   __shared__ float red[8];
   const int t = blockIdx.x, hh = blockIdx.y, b = blockIdx.z;
   const int hd = d / heads;
-  const int nctx = min(CW, len[b]);
+  const int L = len[b];
+  const int nctx = with_ctx ? min(CW, L) : 0;
   const int nk = CW + g;
   const float scale = rsqrtf(static_cast<float>(hd));
   const float* qr = q + (static_cast<size_t>(b) * g + t) * d + hh * hd;
+  auto krow = [&](const float* cbuf, const float* dbuf, int j) -> const float* {
+    return j < CW ? cbuf + (static_cast<size_t>(b) * DR_CR + (L - nctx + j) % DR_CR) * d + hh * hd
+                  : dbuf + (static_cast<size_t>(b) * g + j - CW) * d + hh * hd;
+  };
   for (int j = threadIdx.x; j < nk; j += blockDim.x) {
     const bool vis = j < CW ? j < nctx : (j - CW) <= t;
     float s = -CUDART_INF_F;
     if (vis) {
-      const float* kr = kb + (static_cast<size_t>(b) * nk + j) * d + hh * hd;
+      const float* kr = krow(ck, kd, j);
       float acc = 0.f;
       for (int e = 0; e < hd; ++e) acc = fmaf(qr[e], kr[e], acc);
       s = acc * scale;
@@ -246,7 +352,9 @@ __global__ void __launch_bounds__(128) draft_attn_kernel(const float* q, const f
   l = (red[4] + red[5]) + (red[6] + red[7]);
   for (int e = threadIdx.x; e < hd; e += blockDim.x) {
     float acc = 0.f;
-    for (int j = 0; j < nk; ++j) acc = fmaf(sc[j], vb[(static_cast<size_t>(b) * nk + j) * d + hh * hd + e], acc);
+    // a key with p = 0 (invisible, or underflowed) adds exactly nothing: its row is not read
+    for (int j = 0; j < nk; ++j)
+      if (sc[j] != 0.f) acc = fmaf(sc[j], krow(cv, vd, j)[e], acc);
     y[(static_cast<size_t>(b) * g + t) * d + hh * hd + e] = acc / l;
   }
 }
@@ -674,14 +782,15 @@ int64_t drafter_numel(const evs_drafter_config& c, int id) {
   }
 }
 
-// out[M][N] = X W^T (fp32, split-K partials reduced in split order)
+// out[M][N] = X W^T (fp32, split-K partials reduced in split order); m_dev: optional device-side
+// row count at most M
 int sgemm(evs_drafter* dr, const float* W, const float* X, int ldx, float* out, int N, int K, int M,
-          cudaStream_t st) {
+          cudaStream_t st, const int32_t* m_dev = nullptr) {
   const GemmPlan p = gemm_plan_f32_drafter(N, K, M);
   EVS_CHECK_RANGE(static_cast<size_t>(p.splits) * M * N <= dr->ws_floats, "drafter workspace too small");
-  if (p.splits == 1) return launch_gemm_simt(W, nullptr, X, ldx, EVS_DTYPE_FP32, p, out, st, true);
-  EVS_TRY(launch_gemm_simt(W, nullptr, X, ldx, EVS_DTYPE_FP32, p, dr->ws, st, true));
-  return launch_reduce_splits(dr->ws, p.splits, M, N, nullptr, out, st, true);
+  if (p.splits == 1) return launch_gemm_simt(W, nullptr, X, ldx, EVS_DTYPE_FP32, p, out, st, true, m_dev);
+  EVS_TRY(launch_gemm_simt(W, nullptr, X, ldx, EVS_DTYPE_FP32, p, dr->ws, st, true, m_dev));
+  return launch_reduce_splits(dr->ws, p.splits, M, N, nullptr, out, st, true, m_dev);
 }
 
 inline unsigned blocks_for(size_t n, int t) { return static_cast<unsigned>((n + t - 1) / t); }
@@ -691,7 +800,7 @@ int sgemm_epi(evs_drafter* dr, const float* W, const float* X, int ldx, int N, i
               DraftEpiArgs e, cudaStream_t st) {
   const GemmPlan p = gemm_plan_f32_drafter(N, K, M);
   EVS_CHECK_RANGE(static_cast<size_t>(p.splits) * M * N <= dr->ws_floats, "drafter workspace too small");
-  EVS_TRY(launch_gemm_simt(W, nullptr, X, ldx, EVS_DTYPE_FP32, p, dr->ws, st, true));
+  EVS_TRY(launch_gemm_simt(W, nullptr, X, ldx, EVS_DTYPE_FP32, p, dr->ws, st, true, e.m_dev));
   e.ws = dr->ws;
   e.splits = p.splits;
   e.M = M;
@@ -761,6 +870,10 @@ int evs_drafter_create(const evs_drafter_config* cfg, int max_batch, evs_drafter
   const size_t o_y = take(4 * B * g * d), o_tmp = take(4 * B * g * d), o_m1 = take(4 * B * g * hid);
   const size_t o_z = take(4 * B * g * H), o_U = take(4 * B * g * V);
   const size_t o_prev = take(8 * B * g), o_tok = take(4 * V * d);
+  const size_t nL = c.n_layers, cache_rows = B * DR_CR;
+  const size_t o_ck = take(4 * nL * cache_rows * d), o_cv = take(4 * nL * cache_rows * d);
+  const size_t o_cpos = take(4 * cache_rows), o_ctag = take(8 * cache_rows), o_cmap = take(8 * B * CW),
+               o_ccount = take(8);
   // largest split-K partial buffer over the drafter's projections
   size_t wsf = 0;
   auto need = [&](size_t M_, size_t N_, size_t K_) {
@@ -799,9 +912,16 @@ int evs_drafter_create(const evs_drafter_config* cfg, int max_batch, evs_drafter
   dr->U = reinterpret_cast<float*>(base + o_U);
   dr->prev = reinterpret_cast<int64_t*>(base + o_prev);
   dr->tok_in = reinterpret_cast<float*>(base + o_tok);
+  dr->ck = reinterpret_cast<float*>(base + o_ck);
+  dr->cv = reinterpret_cast<float*>(base + o_cv);
+  dr->cpos = reinterpret_cast<int32_t*>(base + o_cpos);
+  dr->ctag = reinterpret_cast<unsigned long long*>(base + o_ctag);
+  dr->cmap = reinterpret_cast<int32_t*>(base + o_cmap);
+  dr->ccount = reinterpret_cast<int32_t*>(base + o_ccount);
   dr->ws = reinterpret_cast<float*>(base + o_ws);
   dr->ws_floats = wsf;
   EVS_CUDA_TRY(cudaMemset(dr->block, 0, off));
+  EVS_CUDA_TRY(cudaMemset(dr->cpos, 0xff, 4 * cache_rows));  // every slot empty (-1)
   *out = dr;
   return EVS_OK;
 }
@@ -863,23 +983,30 @@ int evs_draft_propose(evs_drafter* dr, const evs_state* s, const int64_t* anchor
   EVS_CHECK_ARG(c.n_inject == 0 || c.target_hidden == s->m->cfg.d_model, "drafter target_hidden != model d_model");
   EVS_CHECK_RANGE(s->ring_len - s->max_chunk >= dr->CW, "capture ring shorter than the drafter context window");
   const int B = batch, g = gamma, d = c.d_model, H = c.target_hidden, V = c.vocab_size, CW = dr->CW;
-  const int hid = c.mlp_mult * d, nk = CW + g, rows = B * g;
+  const int hid = c.mlp_mult * d, rows = B * g;
+  const size_t B_cap = static_cast<size_t>(dr->max_batch);  // the cache's row stride
   const float eps = 1e-6f;
   const float* const* T = dr->t;
-  // ---- context: H_ctx = RMSNorm(ctx_proj(last rows of the capture ring)) ----
+  // ---- context: H_ctx = RMSNorm(ctx_proj(the injection-layer outputs at the last n positions)),
+  // projected here only for positions whose k/v rows are not cached yet (the plan's rows, compacted)
+  const int Bg = B * g;
   if (c.n_inject > 0) {
+    EVS_CHECK_ARG(s->cap_tag != nullptr, "state has no capture tags");
+    EVS_CUDA_TRY(evs_launch(ctx_plan_kernel, dim3(1), dim3(1024), 0, st, true, static_cast<const int32_t*>(s->d_len), B,
+                            CW, g, static_cast<const unsigned long long*>(s->cap_tag), s->ring_len,
+                            static_cast<const int32_t*>(dr->cpos), static_cast<const unsigned long long*>(dr->ctag),
+                            dr->cmap, dr->ccount));
     RingPtrs rg;
     for (int k = 0; k < 4; ++k) rg.p[k] = s->cap_ring[k];
-    EVS_CUDA_TRY(evs_launch(gather_ctx_kernel, dim3(dim3(CW, B)), dim3(256), 0, st, true, rg, c.n_inject, s->ring_len, H, s->d_len, CW, dr->ctx_in));
-    EVS_CUDA_TRY(cudaGetLastError());
-    EVS_TRY(sgemm_epi(dr, T[EVS_D_CTX_W], dr->ctx_in, c.n_inject * H, d, c.n_inject * H, B * CW, EPI_BIAS_NORM,
-                      epi(T[EVS_D_CTX_B], dr->ctx, T[EVS_D_CTX_NORM], nullptr, nullptr, 1, eps), st));
-  } else {
-    EVS_CUDA_TRY(cudaMemsetAsync(dr->ctx, 0, sizeof(float) * B * CW * d, st));
+    EVS_CHECK_ARG(H % 4 == 0, "target_hidden must be a multiple of 4");
+    EVS_CUDA_TRY(evs_launch(gather_ctx_rows_kernel, dim3(B * CW), dim3(256), 0, st, true, rg, c.n_inject, s->ring_len,
+                            H, static_cast<const int32_t*>(dr->cmap), static_cast<const int32_t*>(dr->ccount),
+                            dr->ctx_in));
+    DraftEpiArgs e = epi(T[EVS_D_CTX_B], dr->ctx, T[EVS_D_CTX_NORM], nullptr, nullptr, 1, eps);
+    e.m_dev = dr->ccount;
+    EVS_TRY(sgemm_epi(dr, T[EVS_D_CTX_W], dr->ctx_in, c.n_inject * H, d, c.n_inject * H, B * CW, EPI_BIAS_NORM, e,
+                      st));
   }
-  // the draft attention reads the context length from the state; without injection it is empty
-  const int32_t* ctx_len = c.n_inject > 0 ? s->d_len : reinterpret_cast<const int32_t*>(dr->prev);
-  if (c.n_inject == 0) EVS_CUDA_TRY(cudaMemsetAsync(dr->prev, 0, sizeof(int32_t) * B, st));
   // ---- h = in_proj(embed([anchor, MASK...])) + pos (rows of the token table), and the first
   // layer's pre-norm of h into xb ----
   const float* ln1_0 = c.n_layers > 0 ? T[EVS_D_LAYER0 + EVS_D_LN1] : T[EVS_D_FINAL_LN];
@@ -899,11 +1026,29 @@ int evs_draft_propose(evs_drafter* dr, const evs_state* s, const int64_t* anchor
     // the norm after this layer's MLP: the next layer's pre-norm, or the final norm
     const float* next_ln = l + 1 < c.n_layers ? T[EVS_D_LAYER0 + (l + 1) * EVS_D_PER_LAYER + EVS_D_LN1] : T[EVS_D_FINAL_LN];
     EVS_TRY(sgemm(dr, L[EVS_D_Q], dr->xb, d, dr->q, d, d, rows, st));
-    EVS_CUDA_TRY(evs_launch(build_kv_kernel, dim3(dim3(nk, B)), dim3(256), 0, st, true, dr->ctx, dr->xb, CW, g, d, dr->kv_in));
-    EVS_TRY(sgemm(dr, L[EVS_D_K], dr->kv_in, d, dr->kb, d, d, B * nk, st));
-    EVS_TRY(sgemm(dr, L[EVS_D_V], dr->kv_in, d, dr->vb, d, d, B * nk, st));
-    EVS_CUDA_TRY(evs_launch(draft_attn_kernel, dim3(dim3(g, c.n_heads, B)), dim3(128), 0, st, true, dr->q, dr->kb, dr->vb, ctx_len, CW, g, d, c.n_heads,
-                                                            dr->y));
+    // k and v of [the draft rows ; the context rows to project], then those context rows' k/v
+    // into the cache
+    const bool ctxr = c.n_inject > 0;
+    const int kv_rows = ctxr ? Bg + B * CW : Bg;
+    const int32_t* kv_m = ctxr ? dr->ccount + 1 : nullptr;
+    EVS_CUDA_TRY(evs_launch(build_kv_kernel, dim3(kv_rows), dim3(256), 0, st, true, static_cast<const float*>(dr->xb),
+                            static_cast<const float*>(dr->ctx), Bg, ctxr ? static_cast<const int32_t*>(dr->ccount) : nullptr,
+                            d, dr->kv_in));
+    EVS_TRY(sgemm(dr, L[EVS_D_K], dr->kv_in, d, dr->kb, d, d, kv_rows, st, kv_m));
+    EVS_TRY(sgemm(dr, L[EVS_D_V], dr->kv_in, d, dr->vb, d, d, kv_rows, st, kv_m));
+    float* ckl = dr->ck + static_cast<size_t>(l) * B_cap * DR_CR * d;
+    float* cvl = dr->cv + static_cast<size_t>(l) * B_cap * DR_CR * d;
+    if (ctxr)
+      EVS_CUDA_TRY(evs_launch(ctx_kv_store_kernel, dim3(B * CW), dim3(256), 0, st, true,
+                              static_cast<const float*>(dr->kb), static_cast<const float*>(dr->vb), Bg,
+                              static_cast<const int32_t*>(dr->cmap), static_cast<const int32_t*>(dr->ccount), d, ckl,
+                              cvl, static_cast<int>(l == c.n_layers - 1),
+                              static_cast<const unsigned long long*>(s->cap_tag), s->ring_len, dr->cpos, dr->ctag));
+    EVS_CUDA_TRY(evs_launch(draft_attn_kernel, dim3(dim3(g, c.n_heads, B)), dim3(128), 0, st, true,
+                            static_cast<const float*>(dr->q), static_cast<const float*>(dr->kb),
+                            static_cast<const float*>(dr->vb), static_cast<const float*>(ckl),
+                            static_cast<const float*>(cvl), static_cast<const int32_t*>(s->d_len),
+                            static_cast<int>(ctxr), CW, g, d, c.n_heads, dr->y));
     // h += out_proj(y); xb = pre-MLP norm of h
     EVS_TRY(sgemm_epi(dr, L[EVS_D_O], dr->y, d, d, d, rows, EPI_RESID_NORM,
                       epi(nullptr, dr->xb, L[EVS_D_LN2], dr->h, nullptr, 1, eps), st));
@@ -929,8 +1074,9 @@ int evs_draft_propose(evs_drafter* dr, const evs_state* s, const int64_t* anchor
   EVS_CUDA_TRY(evs_launch(conf_kernel, dim3(blocks_for(rows, 4)), dim3(128), 0, st, true, dr->xb, dr->tok_in, dr->prev,
                           T[EVS_D_CONF_W], T[EVS_D_CONF_B], d, rows, conf));
   // kernels of this call that count nowhere else (projections and their fused epilogues count
-  // themselves): context gather, draft rows, kv build + attention per layer, serial head, conf
-  evs_count_launch((c.n_inject > 0 ? 1 : 0) + 1 + 2 * c.n_layers + 2);
+  // themselves): context plan + gather, draft rows, kv build (+ cache store) + attention per layer,
+  // serial head, conf
+  evs_count_launch((c.n_inject > 0 ? 2 : 0) + 1 + (c.n_inject > 0 ? 3 : 2) * c.n_layers + 2);
   if (U_out != nullptr)
     EVS_CUDA_TRY(cudaMemcpyAsync(U_out, dr->U, sizeof(float) * rows * V, cudaMemcpyDeviceToDevice, st));
   EVS_CUDA_TRY(cudaGetLastError());

@@ -338,13 +338,18 @@ __global__ void __launch_bounds__(SK_WARPS * 32) gemm_skinny_f32_kernel(const fl
                                                                         const float* __restrict__ W2,
                                                                         const float* __restrict__ X, int ldx,
                                                                         float* __restrict__ ws, int N, int K, int M,
-                                                                        int kc, int dual) {
+                                                                        int kc, int dual,
+                                                                        const int32_t* __restrict__ m_dev) {
   extern __shared__ __align__(16) float sk_sm[];
   pdl_trigger();
   pdl_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n0 = blockIdx.x * SK_ROWS, sp = blockIdx.y, m0 = blockIdx.z * SK_TOK;
-  const int mt = min(SK_TOK, M - m0);
+  // a device-side row count (rows decided by an earlier kernel): token groups past it have no work
+  // (M stays the partial buffers' row stride)
+  const int M_rows = m_dev != nullptr ? min(M, *m_dev) : M;
+  if (m0 >= M_rows) return;
+  const int mt = min(SK_TOK, M_rows - m0);
   const int kb = sp * kc, ke = min(K, kb + kc);  // this CTA's K range, staged SK_KC_MAX columns at a time
   const float* wr[SK_R];
 #pragma unroll
@@ -417,11 +422,11 @@ __global__ void __launch_bounds__(SK_WARPS * 32) gemm_skinny_f32_kernel(const fl
 }
 
 __global__ void reduce_splits_kernel(const float* __restrict__ ws, int splits, int MN, const float* __restrict__ bias,
-                                     int N, float* __restrict__ out) {
+                                     int N, float* __restrict__ out, const int32_t* __restrict__ m_dev) {
   pdl_trigger();
   pdl_wait();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= MN) return;
+  if (i >= MN || (m_dev != nullptr && i / N >= *m_dev)) return;
   float acc = split_sum(ws + i, MN, splits);
   out[i] = bias ? acc + bias[i % N] : acc;
 }
@@ -560,7 +565,7 @@ int launch_gemm_tc(const CUtensorMap* tmA, const CUtensorMap* tmA2, const CUtens
 }
 
 int launch_gemm_simt(const void* W, const void* W2, const void* X, int ldx, int dtype, const GemmPlan& p, float* ws,
-                     cudaStream_t st, bool pdl) {
+                     cudaStream_t st, bool pdl, const int32_t* m_dev) {
   if (p.M <= 0) return EVS_OK;
   EVS_CHECK_ARG(dtype == EVS_DTYPE_FP32, "CUDA-core projection is fp32 only");
   EVS_CHECK_ARG(p.K % 4 == 0 && ldx % 4 == 0 && reinterpret_cast<uintptr_t>(X) % 16 == 0 &&
@@ -573,17 +578,17 @@ int launch_gemm_simt(const void* W, const void* W2, const void* X, int ldx, int 
   dim3 grid((p.N + SK_ROWS - 1) / SK_ROWS, p.splits, (p.M + SK_TOK - 1) / SK_TOK);
   EVS_CUDA_TRY(evs_launch(gemm_skinny_f32_kernel, grid, dim3(SK_WARPS * 32), smem, st, pdl,
                           static_cast<const float*>(W), static_cast<const float*>(W2 ? W2 : W),
-                          static_cast<const float*>(X), ldx, ws, p.N, p.K, p.M, p.kchunk, p.dual));
+                          static_cast<const float*>(X), ldx, ws, p.N, p.K, p.M, p.kchunk, p.dual, m_dev));
   evs_count_launch(1);
   return EVS_OK;
 }
 
 int launch_reduce_splits(const float* ws, int splits, int M, int N, const float* bias, float* out, cudaStream_t st,
-                         bool pdl) {
+                         bool pdl, const int32_t* m_dev) {
   const int MN = M * N;
   if (MN <= 0) return EVS_OK;
   EVS_CUDA_TRY(evs_launch(reduce_splits_kernel, dim3((MN + 255) / 256), dim3(256), 0, st, pdl, ws, splits, MN, bias,
-                          N, out));
+                          N, out, m_dev));
   evs_count_launch(1);
   return EVS_OK;
 }

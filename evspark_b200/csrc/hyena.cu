@@ -361,55 +361,72 @@ constexpr int DEC_K0 = 3;     // outer short filter length of the decode path
 // idle and the general kernels (16 warps per 32 channels) finish sooner; the bits are the same
 constexpr int DEC_MIN_ROWS = 4;
 
-// Outer pass of one channel h of row b: u (three interleaved in-projection channels 3h+j, splits
-// summed in split order, rounded) into the outer ring, outer FIR (oldest age first) rounded, then
-// x2 = z[3h] and x1v = round(z[3h+1] * z[3h+2]) for positions L0 .. L0+T-1.  The partial sums are
-// loaded split by split, every position's at once, so a split costs one memory round trip.
+// 4-element stores of rounded values (bf16: one 8-byte store)
 template <typename TD>
-__device__ __forceinline__ void dec_outer(const HyArgs<TD>& a, int b, int h, int L0, const float (&wo)[3 * DEC_K0],
-                                          float (&x2)[DEC_T], float (&x1v)[DEC_T]) {
-  const size_t N3 = 3 * static_cast<size_t>(a.d);
+__device__ __forceinline__ void store4_td(TD* dst, float a, float b, float c, float d) {
+  if constexpr (sizeof(TD) == 2) {
+    const __nv_bfloat162 lo = __floats2bfloat162_rn(a, b), hi = __floats2bfloat162_rn(c, d);
+    uint2 u;
+    u.x = *reinterpret_cast<const uint32_t*>(&lo);
+    u.y = *reinterpret_cast<const uint32_t*>(&hi);
+    *reinterpret_cast<uint2*>(dst) = u;
+  } else {
+    *reinterpret_cast<float4*>(dst) = make_float4(a, b, c, d);
+  }
+}
+
+// Outer pass of the warp's 32 output channels h0 .. h0+31 of row b (lane = channel h0 + lane):
+// u (the 96 interleaved in-projection channels 3h0 .. 3h0+95, splits summed in split order,
+// rounded) into the outer ring, then per lane the outer FIR (oldest age first) of its channels
+// 3h+j, rounded, x2 = z[3h] and x1v = round(z[3h+1] * z[3h+2]) for positions L0 .. L0+T-1.  The
+// split partials are loaded as float4s by lanes 0..23 (one 16-byte chunk of the 96 channels each,
+// every position of a split in flight) and handed to the channel lanes through `ub` (the warp's
+// [DEC_T][96] TD buffer in shared memory: the rounded values are exact in TD).
+template <typename TD>
+__device__ __forceinline__ void dec_outer(const HyArgs<TD>& a, int b, int h0, int lane, int L0,
+                                          const float (&wo)[3 * DEC_K0], TD* ub, float (&x2)[DEC_T],
+                                          float (&x1v)[DEC_T]) {
+  const int N3 = 3 * a.d;
   const size_t split_stride = static_cast<size_t>(a.M) * N3;
-  TD* ring = a.outer_ring + static_cast<size_t>(b) * a.cap_o * N3 + 3 * h;
   const int T = a.T;
-  // u window: uw[j][0..1] = u at positions P-2, P-1 (history from the ring, zero before position 0)
+  const int cmask = a.cap_o - 1;  // the ring capacity is a power of two
+  TD* ring = a.outer_ring + static_cast<size_t>(b) * a.cap_o * N3 + 3 * h0;
+  // u window of the lane's channels: uw[j][0..1] = u at positions P-2, P-1 (zero before position 0)
   float uw[3][DEC_K0 - 1];
 #pragma unroll
   for (int r = 0; r < DEC_K0 - 1; ++r) {
     const int P = L0 - (DEC_K0 - 1) + r;
 #pragma unroll
-    for (int j = 0; j < 3; ++j) uw[j][r] = P >= 0 ? to_f32(ring[static_cast<size_t>(P % a.cap_o) * N3 + j]) : 0.f;
+    for (int j = 0; j < 3; ++j)
+      uw[j][r] = P >= 0 ? to_f32(ring[static_cast<size_t>(P & cmask) * N3 + 3 * lane + j]) : 0.f;
   }
-  float u[DEC_T][3];
+  if (lane < 24) {
+    // positions t >= T load row T-1 again (unconditional loads stay in one block, all in flight)
+    // and are never used
+    float4 u4[DEC_T];
 #pragma unroll
-  for (int t = 0; t < DEC_T; ++t)
+    for (int t = 0; t < DEC_T; ++t) u4[t] = make_float4(0.f, 0.f, 0.f, 0.f);
+    const float* src = a.ws + static_cast<size_t>(b) * T * N3 + 3 * h0 + 4 * lane;
+    for (int sp = 0; sp < a.splits; ++sp) {
+      const float* ss = src + sp * split_stride;
 #pragma unroll
-    for (int j = 0; j < 3; ++j) u[t][j] = 0.f;
-  // positions t >= T load row T-1 again (unconditional loads stay in one block, all in flight)
-  // and are never used
-  const float* src = a.ws + static_cast<size_t>(b) * T * N3 + 3 * h;
-  for (int sp = 0; sp < a.splits; sp += 2) {  // two splits' loads in flight, added in split order
-    const float* s0 = src + sp * split_stride;
-    const float* s1 = src + min(sp + 1, a.splits - 1) * split_stride;
-    float v0[DEC_T][3], v1[DEC_T][3];
-#pragma unroll
-    for (int t = 0; t < DEC_T; ++t) {
-      const size_t o = static_cast<size_t>(min(t, T - 1)) * N3;
-#pragma unroll
-      for (int j = 0; j < 3; ++j) {
-        v0[t][j] = __ldg(s0 + o + j);
-        v1[t][j] = __ldg(s1 + o + j);
+      for (int t = 0; t < DEC_T; ++t) {
+        const float4 v = __ldg(reinterpret_cast<const float4*>(ss + static_cast<size_t>(min(t, T - 1)) * N3));
+        u4[t].x += v.x;
+        u4[t].y += v.y;
+        u4[t].z += v.z;
+        u4[t].w += v.w;
       }
     }
-    const bool two = sp + 1 < a.splits;
 #pragma unroll
-    for (int t = 0; t < DEC_T; ++t)
-#pragma unroll
-      for (int j = 0; j < 3; ++j) {
-        u[t][j] += v0[t][j];
-        if (two) u[t][j] += v1[t][j];
-      }
+    for (int t = 0; t < DEC_T; ++t) {
+      const float r0 = round_to<TD>(u4[t].x), r1 = round_to<TD>(u4[t].y), r2 = round_to<TD>(u4[t].z),
+                  r3 = round_to<TD>(u4[t].w);
+      store4_td<TD>(ub + t * 96 + 4 * lane, r0, r1, r2, r3);
+      if (t < T) store4_td<TD>(ring + static_cast<size_t>((L0 + t) & cmask) * N3 + 4 * lane, r0, r1, r2, r3);
+    }
   }
+  __syncwarp();
 #pragma unroll
   for (int t = 0; t < DEC_T; ++t) {
     x2[t] = 0.f;
@@ -421,8 +438,7 @@ __device__ __forceinline__ void dec_outer(const HyArgs<TD>& a, int b, int h, int
       const int base = a.prefill ? DEC_K0 - 1 : cs;
 #pragma unroll
       for (int j = 0; j < 3; ++j) {
-        const float un = round_to<TD>(u[t][j]);
-        ring[static_cast<size_t>(P % a.cap_o) * N3 + j] = from_f32<TD>(un);
+        const float un = to_f32(ub[t * 96 + 3 * lane + j]);
         // the weights of ages 2, 1, 0 are w[base-2], w[base-1], w[base] (selected, not indexed, so
         // that they stay in registers); age 2 appears only when cs = 2, where base = 2
         const float w0 = wo[j * DEC_K0], w1 = wo[j * DEC_K0 + 1], w2 = wo[j * DEC_K0 + 2];
@@ -444,7 +460,8 @@ __device__ __forceinline__ void dec_outer(const HyArgs<TD>& a, int b, int h, int
 
 // grid (d / 32, ceil(B / DEC_ROWS)), block (32, DEC_ROWS).  KI = inner filter length (7 or 128).
 // Shared memory: taps[32][tap_stride(KI)] f32 (channel c's weight of age a at taps[c][a]) | per
-// warp hist[KI-1+DEC_T][32] TD (x1v by position, the oldest history position first).
+// warp hist[KI-1+DEC_T][32] TD (x1v by position, the oldest history position first) | per warp
+// ub[DEC_T][96] TD (the outer pass's exchange).
 template <typename TD, bool FLIP, int KI>
 __global__ void __launch_bounds__(32 * DEC_ROWS) hyena_fir_dec_kernel(HyArgs<TD> a) {
   pdl_trigger();
@@ -452,6 +469,7 @@ __global__ void __launch_bounds__(32 * DEC_ROWS) hyena_fir_dec_kernel(HyArgs<TD>
   extern __shared__ __align__(16) float sm[];
   float* taps = sm;
   TD* hist = reinterpret_cast<TD*>(taps + 32 * KS) + threadIdx.y * WROWS * 32;
+  TD* ub = reinterpret_cast<TD*>(taps + 32 * KS) + DEC_ROWS * WROWS * 32 + threadIdx.y * DEC_T * 96;
   const int lane = threadIdx.x, h0 = blockIdx.x * 32, h = h0 + lane;
   const int b = blockIdx.y * DEC_ROWS + threadIdx.y;
   // the taps are weights: stage them before waiting for the in-projection.  The full-window weight
@@ -491,18 +509,18 @@ __global__ void __launch_bounds__(32 * DEC_ROWS) hyena_fir_dec_kernel(HyArgs<TD>
     const int P = L0 - H + r;
     TD* dst = hist + r * 32 + c * (16 / sizeof(TD));
     if (P >= 0)
-      cp_async16(dst, ring_row + static_cast<size_t>(P % a.cap_i) * a.d + c * (16 / sizeof(TD)));
+      cp_async16(dst, ring_row + static_cast<size_t>(P & (a.cap_i - 1)) * a.d + c * (16 / sizeof(TD)));
     else
       *reinterpret_cast<int4*>(dst) = make_int4(0, 0, 0, 0);
   }
   cp_async_commit();
   float x2[DEC_T], x1v[DEC_T];
-  dec_outer(a, b, h, L0, wo, x2, x1v);
+  dec_outer(a, b, h0, lane, L0, wo, ub, x2, x1v);
   TD* ring_w = a.inner_ring + static_cast<size_t>(b) * a.cap_i * a.d + h;
 #pragma unroll
   for (int t = 0; t < DEC_T; ++t) {
     hist[(H + t) * 32 + lane] = from_f32<TD>(x1v[t]);
-    if (t < T) ring_w[static_cast<size_t>((L0 + t) % a.cap_i) * a.d] = from_f32<TD>(x1v[t]);
+    if (t < T) ring_w[static_cast<size_t>((L0 + t) & (a.cap_i - 1)) * a.d] = from_f32<TD>(x1v[t]);
   }
   cp_async_wait<0>();
   __syncwarp();  // the history rows the other lanes copied
@@ -560,23 +578,35 @@ __global__ void __launch_bounds__(32 * DEC_ROWS) hyena_fir_dec_kernel(HyArgs<TD>
 
 // grid (d / 32, ceil(B / DEC_ROWS)), block (32, DEC_ROWS): one thread per channel and row, all 16
 // poles in registers (four groups of four, as the four pole-group threads of hyena_iir_kernel).
+// Shared memory: poles and residues of the 32 channels [2][32][16] f32 (staged before the wait) |
+// per warp ub[DEC_T][96] TD.
 template <typename TD>
 __global__ void __launch_bounds__(32 * DEC_ROWS) hyena_iir_dec_kernel(HyArgs<TD> a) {
   pdl_trigger();
   constexpr int S = 16;
-  const int h = blockIdx.x * 32 + threadIdx.x;
+  extern __shared__ __align__(16) float sm[];
+  const int lane = threadIdx.x, h0 = blockIdx.x * 32, h = h0 + lane;
   const int b = blockIdx.y * DEC_ROWS + threadIdx.y;
   const int d = a.d;
-  float p[S], r[S], s[S];
-  load_vec<S>(a.poles + static_cast<size_t>(h) * S, p);
-  load_vec<S>(a.residues + static_cast<size_t>(h) * S, r);
+  float* pr = sm;  // [2][32 * S]: poles, then residues
+  TD* ub = reinterpret_cast<TD*>(sm + 2 * 32 * S) + threadIdx.y * DEC_T * 96;
+  // the poles and residues are weights: staged (16-byte copies) before waiting for the in-projection
+  for (int i = threadIdx.y * 32 + lane; i < 2 * 32 * S / 4; i += 32 * DEC_ROWS) {
+    const int w = i / (32 * S / 4), k = i - w * (32 * S / 4);
+    cp_async16(pr + w * 32 * S + 4 * k, (w == 0 ? a.poles : a.residues) + static_cast<size_t>(h0) * S + 4 * k);
+  }
+  cp_async_commit();
   float wo[3 * DEC_K0];
 #pragma unroll
   for (int i = 0; i < 3 * DEC_K0; ++i) wo[i] = __ldg(a.short_w + static_cast<size_t>(3 * h) * DEC_K0 + i);
   const float Dg = a.D[h];
   pdl_wait();
+  cp_async_wait<0>();
+  __syncthreads();  // poles and residues staged
   if (b >= a.M / a.T) return;
   const int L0 = a.len[b];
+  // the carried state first, so that its loads are in flight with the outer pass
+  float s[S];
   if (L0 > 0) {
     load_vec<S>(a.s_all + ((static_cast<size_t>(b) * a.slots + a.iir_cur[b]) * d + h) * S, s);
   } else {
@@ -584,7 +614,10 @@ __global__ void __launch_bounds__(32 * DEC_ROWS) hyena_iir_dec_kernel(HyArgs<TD>
     for (int j = 0; j < S; ++j) s[j] = 0.f;
   }
   float x2[DEC_T], x1v[DEC_T];
-  dec_outer(a, b, h, L0, wo, x2, x1v);
+  dec_outer(a, b, h0, lane, L0, wo, ub, x2, x1v);
+  float p[S], r[S];
+  load_vec<S>(pr + lane * S, p);
+  load_vec<S>(pr + 32 * S + lane * S, r);
 #pragma unroll
   for (int t = 0; t < DEC_T; ++t) {
     if (t < a.T) {
@@ -688,11 +721,14 @@ int launch_hyena_t(const evs_model* m, evs_state* s, int layer, int B, int T, in
                          (L.kind == EVS_LAYER_HCL ? a.S == 16 : (a.K == 7 || a.K == 128));
   if (dec_shape) {
     const dim3 dgrid(d / 32, (B + DEC_ROWS - 1) / DEC_ROWS), dblock(32, DEC_ROWS);
+    const size_t ub_bytes = sizeof(TD) * DEC_ROWS * DEC_T * 96;
     if (L.kind == EVS_LAYER_HCL) {
-      EVS_CUDA_TRY(evs_launch(hyena_iir_dec_kernel<TD>, dgrid, dblock, 0, st, s->use_pdl(), a));
+      const size_t smem = sizeof(float) * 2 * 32 * 16 + ub_bytes;
+      EVS_CUDA_TRY(evs_launch(hyena_iir_dec_kernel<TD>, dgrid, dblock, smem, st, s->use_pdl(), a));
     } else {
       auto launch = [&](auto kern, int KI) -> int {
-        const size_t smem = sizeof(float) * 32 * tap_stride(KI) + sizeof(TD) * DEC_ROWS * (KI - 1 + DEC_T) * 32;
+        const size_t smem =
+            sizeof(float) * 32 * tap_stride(KI) + sizeof(TD) * DEC_ROWS * (KI - 1 + DEC_T) * 32 + ub_bytes;
         EVS_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
         EVS_CUDA_TRY(evs_launch(kern, dgrid, dblock, smem, st, s->use_pdl(), a));
         return EVS_OK;

@@ -103,6 +103,12 @@ struct evs_state {
   HyenaDev hy[EVS_MAX_LAYERS];
   void* kv[EVS_MAX_LAYERS] = {nullptr};
   float* cap_ring[4] = {nullptr, nullptr, nullptr, nullptr};
+  // capture tags [B][ring_len]: which forward wrote each capture-ring row (state id, row, forward
+  // sequence number; every capture layer of a forward gets the same tag), so that a consumer that
+  // keeps values derived from ring rows (the drafter's projected context) can tell them current
+  unsigned long long* cap_tag = nullptr;
+  unsigned long long* d_fwd_seq = nullptr;  // [1] forwards run on this state (device counter)
+  unsigned long long tag_hi = 0;            // this state's id, in the tag's top bits
   // scratch
   float* resid = nullptr;      // [m_cap][d] fp32 residual stream
   void* act = nullptr;         // [m_cap][ld_act] data dtype: GEMM B operand
@@ -151,7 +157,7 @@ GemmPlan gemm_plan_f32(int N, int K, int M, int dual);
 GemmPlan gemm_plan_f32_drafter(int N, int K, int M);
 // out[m][n] = sum of the split partials (in split order) + bias[n]
 int launch_reduce_splits(const float* ws, int splits, int M, int N, const float* bias, float* out, cudaStream_t st,
-                         bool pdl = false);
+                         bool pdl = false, const int32_t* m_dev = nullptr);
 // pdl: launch with programmatic stream serialization (see pdl_wait)
 // tmB: three maps of the activations with box rows GEMM_NT[0..2]; the tile is chosen from p.M
 int gemm_tile_index(int M);
@@ -165,8 +171,9 @@ int launch_gemm_tc(const CUtensorMap* tmA, const CUtensorMap* tmA2, const CUtens
 bool gemm_serial(const GemmPlan& p);
 int launch_gemm_tc_serial(const CUtensorMap* tmA, const CUtensorMap* tmA2, const CUtensorMap* tmB, const GemmPlan& p,
                           float* ws, EvsDevErr* err, cudaStream_t st, bool pdl = false);
+// m_dev: optional device-side row count (at most p.M, which sizes the grid)
 int launch_gemm_simt(const void* W, const void* W2, const void* X, int ldx, int dtype, const GemmPlan& p, float* ws,
-                     cudaStream_t st, bool pdl = false);
+                     cudaStream_t st, bool pdl = false, const int32_t* m_dev = nullptr);
 int make_tmap_2d_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t row_stride_bytes,
                       uint32_t box_inner, uint32_t box_outer);
 
@@ -183,6 +190,13 @@ struct TpPartials {
 };
 int launch_res_add_norm(const evs_model* m, evs_state* s, int M, int splits, const TpPartials& parts,
                         const float* scale, int capture_slot, int T, cudaStream_t st);
+// capture tag of row b: state id | row | forward sequence number
+constexpr int EVS_TAG_SEQ_BITS = 34, EVS_TAG_ROW_BITS = 10;
+__host__ __device__ inline unsigned long long evs_capture_tag(unsigned long long tag_hi, int b,
+                                                              unsigned long long seq) {
+  return tag_hi | (static_cast<unsigned long long>(b) << EVS_TAG_SEQ_BITS) |
+         (seq & ((1ull << EVS_TAG_SEQ_BITS) - 1));
+}
 // publish this rank's partial sums of reduction `epoch` to the peers (after the producing kernel)
 int launch_tp_reduce_signal(evs_state* s, float* buf, int splits, int M, long long epoch, cudaStream_t st);
 int launch_swiglu(const evs_model* m, evs_state* s, int M, int splits, cudaStream_t st);

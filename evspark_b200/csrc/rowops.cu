@@ -87,7 +87,8 @@ __global__ void __cluster_dims__(NORM_CL, 1, 1) __launch_bounds__(NORM_THREADS)
     res_add_norm_kernel(TpPartials parts, int splits, int M, float* __restrict__ resid,
                         const float* __restrict__ scale, TD* __restrict__ act, int ld_act, int d, float eps,
                         float* __restrict__ ring, int ring_len, const int32_t* __restrict__ len, int T,
-                        EvsDevErr* err) {
+                        unsigned long long* __restrict__ tags, const unsigned long long* __restrict__ fwd_seq,
+                        unsigned long long tag_hi, EvsDevErr* err) {
   pdl_trigger();
   cg::cluster_group cluster = cg::this_cluster();
   const int rank = static_cast<int>(cluster.block_rank());
@@ -129,6 +130,8 @@ __global__ void __cluster_dims__(NORM_CL, 1, 1) __launch_bounds__(NORM_THREADS)
   if (ring != nullptr && t >= T - ring_len) {
     const int P = len[b] + t;
     cap = ring + (static_cast<size_t>(b) * ring_len + P % ring_len) * d;
+    if (tags != nullptr && rank == 0 && threadIdx.x == 0)
+      tags[static_cast<size_t>(b) * ring_len + P % ring_len] = evs_capture_tag(tag_hi, b, *fwd_seq);
   }
   float4 r[NORM_VPT];
   float ss = 0.f;
@@ -229,7 +232,7 @@ __global__ void logits_kernel(const float* __restrict__ ws, int splits, int M, i
 }
 
 __global__ void bookkeeping_kernel(int32_t* len, int32_t* len0, int32_t* iir_cur, int32_t* chunk, int B, int T,
-                                   int retain) {
+                                   int retain, unsigned long long* fwd_seq) {
   pdl_trigger();
   pdl_wait();
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
@@ -239,7 +242,10 @@ __global__ void bookkeeping_kernel(int32_t* len, int32_t* len0, int32_t* iir_cur
     len[b] = old + T;
     iir_cur[b] = retain ? T - 1 : 0;
   }
-  if (b == 0) chunk[0] = retain ? T : 0;
+  if (b == 0) {
+    chunk[0] = retain ? T : 0;
+    *fwd_seq += 1;  // the next forward's capture rows get a new tag
+  }
 }
 
 // publish this rank's partial sums (written by the preceding projection) to the peers
@@ -307,11 +313,13 @@ int launch_res_add_norm(const evs_model* m, evs_state* s, int M, int splits, con
     EVS_CUDA_TRY(evs_launch(res_add_norm_kernel<__nv_bfloat16>, dim3(NORM_CL, M), dim3(NORM_THREADS), 0, st,
                             s->use_pdl(), parts, splits, M, s->resid, scale, static_cast<__nv_bfloat16*>(s->act),
                             s->ld_act, d, m->cfg.eps, ring, s->ring_len, static_cast<const int32_t*>(s->d_len), T,
-                            s->d_err));
+                            ring ? s->cap_tag : nullptr, static_cast<const unsigned long long*>(s->d_fwd_seq),
+                            s->tag_hi, s->d_err));
   else
     EVS_CUDA_TRY(evs_launch(res_add_norm_kernel<float>, dim3(NORM_CL, M), dim3(NORM_THREADS), 0, st, s->use_pdl(),
                             parts, splits, M, s->resid, scale, static_cast<float*>(s->act), s->ld_act, d, m->cfg.eps,
-                            ring, s->ring_len, static_cast<const int32_t*>(s->d_len), T, s->d_err));
+                            ring, s->ring_len, static_cast<const int32_t*>(s->d_len), T, ring ? s->cap_tag : nullptr,
+                            static_cast<const unsigned long long*>(s->d_fwd_seq), s->tag_hi, s->d_err));
   evs_count_launch(1);
   return EVS_OK;
 }
@@ -343,7 +351,7 @@ int launch_logits(const evs_model* m, evs_state* s, int M, int T, int splits, fl
 
 int launch_bookkeeping(evs_state* s, int B, int T, int retain, cudaStream_t st) {
   EVS_CUDA_TRY(evs_launch(bookkeeping_kernel, dim3((B + 127) / 128), dim3(128), 0, st, s->use_pdl(), s->d_len,
-                          s->d_len0, s->d_iir_cur, s->d_chunk, B, T, retain));
+                          s->d_len0, s->d_iir_cur, s->d_chunk, B, T, retain, s->d_fwd_seq));
   evs_count_launch(1);
   return EVS_OK;
 }

@@ -23,7 +23,7 @@ convolution and stores the last ``min(L, K-1)`` inputs as the FIR state.
 The dense conventions (pre-norm blocks, SwiGLU, rotate-half RoPE, tied
 unembedding) are the ones documented in ``evspark_b200.config``.
 
-Modes: ``compute=torch.float64, emulate=False`` is the judge; ``emulate=True``
+Modes: ``compute=torch.float64, emulate=False`` is the reference arithmetic; ``emulate=True``
 rounds at every point where the device stores the data dtype (bf16 / fp32)
 and keeps the residual stream in fp32, like the CUDA path.
 """

@@ -251,3 +251,49 @@ def test_evspark_generate_reuses_its_decode_state(tiny):
     es._state.close()  # not es.close(): the model belongs to the module fixture
     es._state = None
     nd.close()
+
+
+def test_drafter_context_cache_equals_a_fresh_drafter(tiny):
+    """The drafter projects each context position once and keeps its k/v rows for later calls
+    (valid while the capture ring row it came from is unchanged).  Every proposal of a speculative
+    run, with rollbacks that rewrite positions, and of a second run on a reset state, equals the
+    proposal of a freshly built drafter (no cached rows) on the same state, bit for bit."""
+    from evspark_b200.config import DRAFTERS
+    from evspark_b200.drafter import DeviceDrafter
+    from evspark_b200.specdec.block.loop import speculative_generate
+    from evspark_b200.specdec.block.neural_draft import NeuralDraftModel
+    from evspark_b200.weights import init_drafter_weights
+
+    model, w = tiny
+    dcfg = DRAFTERS["tiny"]
+    dw = init_drafter_weights(dcfg, seed=20260830, embed=w["embed"])
+
+    class CheckedDraft(NeuralDraftModel):
+        checked = 0
+
+        def propose_device(self, anchor, gamma, greedy, rng, *, temperature=1.0, top_k=4,
+                           inference_params_dict=None):
+            ip = inference_params_dict
+            u = None if greedy else torch.as_tensor(rng.random(int(gamma)), device=model.device)[None]
+            got = self.drafter.propose(ip, anchor.reshape(1), int(gamma), greedy, temperature=temperature,
+                                       top_k=top_k, uniforms=u)
+            fresh = DeviceDrafter(dcfg, dw, device=model.device)
+            ref = fresh.propose(ip, anchor.reshape(1), int(gamma), greedy, temperature=temperature, top_k=top_k,
+                                uniforms=u)
+            torch.cuda.synchronize()
+            fresh.close()
+            for a, b in zip(got[:3], ref[:3]):
+                assert torch.equal(a, b)
+            CheckedDraft.checked += 1
+            return got[0], got[1], got[2]
+
+    nd = CheckedDraft(model, DeviceDrafter(dcfg, dw, device=model.device), ("blocks.2",))
+    rng = np.random.default_rng(41)
+    for L, greedy, seed in ((150, False, 3), (90, True, 0), (200, False, 8)):
+        prompt = torch.tensor(rng.choice([65, 67, 71, 84], size=L))[None]
+        nd.capture_reset()
+        spec = speculative_generate(model, nd, prompt, 30, 12, greedy=greedy, rng=np.random.default_rng(seed))
+        assert any(r.k < 12 for r in spec.rounds_log)
+        spec.inference_params_dict.close()
+    assert CheckedDraft.checked >= 30
+    nd.close()

@@ -1,7 +1,7 @@
 """CPU: the block-by-block bf16 parity harness (tests/_parity.py) is exact and has teeth.
 
 The oracle itself stands in for the device: its fp32-compute run plays the device, its fp64
-run is the judge, and a copy with one planted mistake must fail the bounds.
+run is the reference, and a copy with one planted mistake must fail the bounds.
 """
 
 from __future__ import annotations
@@ -43,7 +43,7 @@ def test_block_over_segments_equals_full_forward_bitwise(setup):
     xs, pre, blk = _stand_in_device(w, prompt, chunk, torch.float64)
     rep = _parity.teacher_forced_report(CFG, w, np.concatenate([prompt, chunk]), len(prompt), xs, pre, blk,
                                         free_running=True)
-    # fp64 judge on the fp64 run's own residual streams: the same arithmetic, block by block
+    # fp64 reference on the fp64 run's own residual streams: the same arithmetic, block by block
     assert all(b["rel_max"] == 0.0 for b in rep["blocks"]), rep["blocks"]
     assert rep["logits_err"] < 1e-6 and rep["free_running_err"] < 1e-6
 
