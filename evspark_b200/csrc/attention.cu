@@ -15,6 +15,7 @@
 #include <math_constants.h>
 
 #include <algorithm>
+#include <cmath>
 
 #include "internal.hpp"
 
@@ -61,50 +62,101 @@ __global__ void rope_append_kernel(const float* __restrict__ ws, int splits, int
 
 constexpr int QT = 16;           // queries per pass over the staged keys
 constexpr int ATTN_THREADS = 128;
-constexpr int QK_Q = QT / (ATTN_THREADS / ATTN_BLOCK);  // queries per thread in the score pass
-constexpr int PV_QMAX = 8;       // queries per thread in P.V (head_dim <= 128)
+constexpr int QK_Q = QT / (ATTN_THREADS / ATTN_BLOCK);  // queries per thread in the fp32 score pass
+constexpr int PV_QMAX = 8;       // queries per thread in the fp32 P.V (head_dim <= 128)
+constexpr int ACC_N = 16;        // P.V accumulators per thread (both paths)
+// row stride of the scores (floats): 4 floats of padding keep the softmax's quarter-warp float4
+// loads and the 8-row matrix loads of P on distinct banks.  For bf16 data the softmax pass
+// overwrites each score row with P's bf16 parts, hi in bytes 0-127 and lo in bytes 128-255 of the
+// row (PLD bf16 elements per row).
+constexpr int SLD = ATTN_BLOCK + 4;
+constexpr int PLD = 2 * SLD;
+
+// query rows per block pass and the bf16 query tile's padded row (272 B for Dh = 128: the MMA
+// fragment loads of 8 rows x 4 lanes hit 32 distinct banks)
+__host__ __device__ constexpr int qb_pad(int Dh) { return Dh + 8; }
 
 // shared memory of both attention kernels: K and V rows padded by 16 bytes (conflict-free
-// row-per-thread reads and 8-row matrix loads), fp32 queries, scores, the P.V tile of the tensor-core
-// path and per-query stats (+ the running fold of the fused kernel)
+// row-per-thread reads and 8-row matrix loads); the queries (fp32 rows, or bf16 rows padded to
+// qb_pad); the scores; for bf16 data the bf16 hi and lo parts of P; per-query stats (+ the running
+// folds of the fused kernel)
+template <typename TD>
+__host__ __device__ constexpr size_t attn_q_bytes(int Dh) {
+  return sizeof(TD) == 2 ? 2 * static_cast<size_t>(QT) * qb_pad(Dh) : 4 * static_cast<size_t>(QT) * Dh;
+}
 template <typename TD>
 __host__ __device__ constexpr size_t attn_smem_bytes(int Dh) {
-  return sizeof(TD) * (2 * static_cast<size_t>(ATTN_BLOCK) * (Dh + 16 / sizeof(TD))) +
-         sizeof(float) * (2 * static_cast<size_t>(QT) * Dh + static_cast<size_t>(QT) * ATTN_BLOCK + 6 * QT);
+  return sizeof(TD) * (2 * static_cast<size_t>(ATTN_BLOCK) * (Dh + 16 / sizeof(TD))) + attn_q_bytes<TD>(Dh) +
+         4 * static_cast<size_t>(QT) * SLD + sizeof(float) * 10 * QT;
 }
 
 template <typename TD>
 struct AttnSmem {
   TD* Ks;
   TD* Vs;
-  float* qs;
-  float* S;
-  float* stt;   // [2 QT]: block max, block sum
-  float* fold;  // [4 QT]: running max, running sum, scale of the old accumulator, scale of the block
-  float* O;     // [QT][Dh]: P.V of the tensor-core path
-  int kpad;     // row stride of K and V (elements)
+  float* qs;            // fp32 queries [QT][Dh], or bf16 query rows [QT][qb_pad(Dh)]
+  float* S;             // [QT][SLD]: scores; after the softmax pass p = 2^(s - max) (fp32 path)
+  __nv_bfloat16* Ph;    // [QT][PLD] over S: bf16 parts of p, p = hi + lo to ~16 bits (bf16 path)
+  __nv_bfloat16* Pl;    // Ph + 64
+  float* stt;    // [2 QT]: block max, block sum
+  float* fold;   // [4 QT]: running max, running sum, scale of the old accumulator, scale of the block
+  float* gfold;  // [4 QT]: the same for the current fold group (fused kernel)
+  int kpad;      // row stride of K and V (elements)
   __device__ AttnSmem(unsigned char* raw, int Dh) {
     constexpr int EPC = 16 / sizeof(TD);
     kpad = Dh + EPC;
     Ks = reinterpret_cast<TD*>(raw);
     Vs = Ks + ATTN_BLOCK * kpad;
-    qs = reinterpret_cast<float*>(Vs + ATTN_BLOCK * kpad);
-    S = qs + QT * Dh;
-    stt = S + QT * ATTN_BLOCK;
+    unsigned char* q = reinterpret_cast<unsigned char*>(Vs + ATTN_BLOCK * kpad);
+    qs = reinterpret_cast<float*>(q);
+    q += attn_q_bytes<TD>(Dh);
+    S = reinterpret_cast<float*>(q);
+    q += 4 * QT * SLD;
+    Ph = reinterpret_cast<__nv_bfloat16*>(S);
+    Pl = Ph + ATTN_BLOCK;
+    stt = reinterpret_cast<float*>(q);
     fold = stt + 2 * QT;
-    O = fold + 4 * QT;
+    gfold = fold + 4 * QT;
   }
 };
 
+// The P.V accumulators of a thread: ACC_N values, pairs (i, i + 1) of one query row and two
+// adjacent head columns.  bf16 path: the m16n8k16 fragments, i = 4 j + e -> row gid + 8 (e / 2),
+// column (warp ntw + j) 8 + 2 tig + e % 2 (ntw = Dh / 32 tiles per warp).  fp32 path: i = 2 q + e
+// -> row g + q groups, column 2 pi + e.
+template <typename TD>
+__device__ __forceinline__ int acc_row(int i, int Dh) {
+  if constexpr (sizeof(TD) == 2) {
+    return ((threadIdx.x & 31) >> 2) + 8 * ((i & 3) >> 1);
+  } else {
+    const int npair = Dh / 2, groups = ATTN_THREADS / npair;
+    return static_cast<int>(threadIdx.x) / npair + (i >> 1) * groups;
+  }
+}
+template <typename TD>
+__device__ __forceinline__ int acc_col(int i, int Dh) {
+  if constexpr (sizeof(TD) == 2) {
+    const int warp = threadIdx.x >> 5, tig = threadIdx.x & 3, ntw = Dh / 32;
+    return (warp * ntw + (i >> 2)) * 8 + 2 * tig + (i & 1);
+  } else {
+    return 2 * (static_cast<int>(threadIdx.x) % (Dh / 2)) + (i & 1);
+  }
+}
+template <typename TD>
+__device__ __forceinline__ bool acc_live(int i, int Dh) {
+  if constexpr (sizeof(TD) == 2) return (i >> 2) < Dh / 32;
+  return acc_row<TD>(i, Dh) < QT;
+}
+
 // 16-byte asynchronous copies of the K rows [0, nk) of one key block (one commit group)
+// (a thread copies chunk c of rows r0, r0 + rs, ...: 16-byte chunks per row divide ATTN_THREADS)
 template <typename TD>
 __device__ __forceinline__ void stage_k(const AttnSmem<TD>& sm, const TD* kb, size_t HD, int Dh, int nk) {
   constexpr int EPC = 16 / sizeof(TD);
-  const int cpr = Dh / EPC;
-  for (int i = threadIdx.x; i < nk * cpr; i += ATTN_THREADS) {
-    const int r = i / cpr, c = i - r * cpr;
+  const int cpr = Dh / EPC, rs = ATTN_THREADS / cpr;
+  const int r0 = threadIdx.x / cpr, c = threadIdx.x - r0 * cpr;
+  for (int r = r0; r < nk; r += rs)
     cp_async16(sm.Ks + r * sm.kpad + c * EPC, kb + static_cast<size_t>(r) * 2 * HD + c * EPC);
-  }
   cp_async_commit();
 }
 // ... and of its V rows (one commit group); V rows past the block's keys are zero: P is zero
@@ -112,26 +164,18 @@ __device__ __forceinline__ void stage_k(const AttnSmem<TD>& sm, const TD* kb, si
 template <typename TD>
 __device__ __forceinline__ void stage_v(const AttnSmem<TD>& sm, const TD* kb, size_t HD, int Dh, int nk) {
   constexpr int EPC = 16 / sizeof(TD);
-  const int cpr = Dh / EPC;
-  for (int i = threadIdx.x; i < nk * cpr; i += ATTN_THREADS) {
-    const int r = i / cpr, c = i - r * cpr;
-    cp_async16(sm.Vs + r * sm.kpad + c * EPC, kb + static_cast<size_t>(r) * 2 * HD + HD + c * EPC);
-  }
+  const int cpr = Dh / EPC, rs = ATTN_THREADS / cpr;
+  const int r0 = threadIdx.x / cpr, c = threadIdx.x - r0 * cpr;
+  int r = r0;
+  for (; r < nk; r += rs) cp_async16(sm.Vs + r * sm.kpad + c * EPC, kb + static_cast<size_t>(r) * 2 * HD + HD + c * EPC);
   cp_async_commit();
-  for (int i = nk * cpr + threadIdx.x; i < ATTN_BLOCK * cpr; i += ATTN_THREADS) {
-    const int r = i / cpr, c = i - r * cpr;
-    *reinterpret_cast<uint4*>(sm.Vs + r * sm.kpad + c * EPC) = make_uint4(0u, 0u, 0u, 0u);
-  }
+  for (; r < ATTN_BLOCK; r += rs) *reinterpret_cast<uint4*>(sm.Vs + r * sm.kpad + c * EPC) = make_uint4(0u, 0u, 0u, 0u);
 }
 template <typename TD>
 __device__ __forceinline__ void stage_kv(const AttnSmem<TD>& sm, const TD* kb, size_t HD, int Dh, int nk) {
   stage_k(sm, kb, HD, Dh, nk);
   stage_v(sm, kb, HD, Dh, nk);
 }
-
-// query rows per block pass and the bf16 query tile's padded row (272 B for Dh = 128: the MMA
-// fragment loads of 8 rows x 4 lanes hit 32 distinct banks)
-__host__ __device__ constexpr int qb_pad(int Dh) { return Dh + 8; }
 
 // nq query rows (head slice of Dh values, row stride ld elements) into shared memory with 16-byte
 // loads, up to four per thread in flight: fp32 sm.qs[nq][Dh] (fp32 data), or for bf16 data the
@@ -180,6 +224,11 @@ __device__ __forceinline__ void stage_q(const AttnSmem<TD>& sm, const TD* src, s
   }
 }
 
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+
 // scores of one key block: thread = one key x QK_Q queries; keys past a query's position -> -inf
 // bf16 x bf16 -> fp32 tensor-core MMA, m16n8k16, A row-major, B column-major
 __device__ __forceinline__ void mma_bf16_16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
@@ -221,11 +270,12 @@ __device__ __forceinline__ void block_scores(const AttnSmem<TD>& sm, int Dh, int
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int t = gid + (e >> 1) * 8, key = warp * 16 + nt * 8 + tig * 2 + (e & 1);
-        if (t < nq) {
-          const bool vis = key < nk && k0 + key <= P0 + t;  // P0: position of query 0 of the pass
-          sm.S[t * ATTN_BLOCK + key] = vis ? c[nt][e] * scale : -CUDART_INF_F;
+      for (int hh = 0; hh < 2; ++hh) {
+        const int t = gid + hh * 8, key = warp * 16 + nt * 8 + tig * 2;
+        if (t < nq) {  // P0: position of query 0 of the pass
+          const bool v0 = key < nk && k0 + key <= P0 + t, v1 = key + 1 < nk && k0 + key + 1 <= P0 + t;
+          *reinterpret_cast<float2*>(sm.S + t * SLD + key) =
+              make_float2(v0 ? c[nt][2 * hh] * scale : -CUDART_INF_F, v1 ? c[nt][2 * hh + 1] * scale : -CUDART_INF_F);
         }
       }
     return;
@@ -277,24 +327,27 @@ __device__ __forceinline__ void block_scores(const AttnSmem<TD>& sm, int Dh, int
     const int t = u0 + u;
     if (t < nq) {
       const bool vis = key < nk && k0 + key <= P0 + t;  // P0: position of query 0 of the pass
-      sm.S[t * ATTN_BLOCK + key] = vis ? acc[u] * scale : -CUDART_INF_F;
+      sm.S[t * SLD + key] = vis ? acc[u] * scale : -CUDART_INF_F;
     }
   }
 }
 
-// per query: block max, p = exp(s - max) in place, block sum -> stt.  Eight lanes per query (keys
-// 8k8 .. 8k8+7 on lane k8, summed in key order, then across the eight lanes by butterfly), four
-// queries per warp: the 16 query rows of a pass in one round.
+// per query: block max, p = 2^(s - max), block sum -> stt.  Eight lanes per query: lane k8
+// takes keys 4 k8 .. 4 k8 + 3 and 32 + 4 k8 .. 32 + 4 k8 + 3 (two float4, a quarter-warp on distinct
+// banks) and sums its eight p in that order, then the eight lanes are summed by butterfly; four
+// queries per warp, the 16 query rows of a pass in one round.  p goes back in place (fp32 path)
+// or as its bf16 parts hi = bf16(p), lo = bf16(p - hi) (bf16 path, the P.V operand).  Rows past
+// nq get p = 0.
 template <typename TD>
 __device__ __forceinline__ void block_softmax(const AttnSmem<TD>& sm, int nq) {
   static_assert(ATTN_BLOCK == 64 && QT == 16 && ATTN_THREADS == 128, "layout of the softmax pass");
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, k8 = lane & 7;
   const int t = warp * 4 + (lane >> 3);
   const bool live = t < nq;
-  float* Sr = sm.S + t * ATTN_BLOCK + 8 * k8;
+  float* Sr = sm.S + t * SLD + 4 * k8;
   float v[8];
   if (live) {
-    const float4 x0 = reinterpret_cast<const float4*>(Sr)[0], x1 = reinterpret_cast<const float4*>(Sr)[1];
+    const float4 x0 = *reinterpret_cast<const float4*>(Sr), x1 = *reinterpret_cast<const float4*>(Sr + 32);
     v[0] = x0.x; v[1] = x0.y; v[2] = x0.z; v[3] = x0.w;
     v[4] = x1.x; v[5] = x1.y; v[6] = x1.z; v[7] = x1.w;
   } else {
@@ -309,18 +362,35 @@ __device__ __forceinline__ void block_softmax(const AttnSmem<TD>& sm, int nq) {
   float l = 0.f;
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
-    v[i] = (mx == -CUDART_INF_F || v[i] == -CUDART_INF_F) ? 0.f : expf(v[i] - mx);
+    v[i] = (mx == -CUDART_INF_F || v[i] == -CUDART_INF_F) ? 0.f : exp2f(v[i] - mx);
     l += v[i];
   }
 #pragma unroll
   for (int o = 4; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
-  if (live) {
-    reinterpret_cast<float4*>(Sr)[0] = make_float4(v[0], v[1], v[2], v[3]);
-    reinterpret_cast<float4*>(Sr)[1] = make_float4(v[4], v[5], v[6], v[7]);
-    if (k8 == 0) {
-      sm.stt[2 * t] = mx;
-      sm.stt[2 * t + 1] = l;
+  if constexpr (sizeof(TD) == 2) {
+#pragma unroll
+    for (int hq = 0; hq < 2; ++hq) {
+      uint32_t hi[2], lo[2];
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const float p0 = v[4 * hq + 2 * e], p1 = v[4 * hq + 2 * e + 1];
+        const __nv_bfloat16 h0 = __float2bfloat16_rn(p0), h1 = __float2bfloat16_rn(p1);
+        const __nv_bfloat162 hh = __halves2bfloat162(h0, h1);
+        hi[e] = *reinterpret_cast<const uint32_t*>(&hh);
+        lo[e] = pack_bf16x2(p0 - __bfloat162float(h0), p1 - __bfloat162float(h1));
+      }
+      // (row t of P overlays row t of S, read by this warp only, before the shuffles above)
+      const int off = t * PLD + 4 * k8 + 32 * hq;
+      *reinterpret_cast<uint2*>(sm.Ph + off) = make_uint2(hi[0], hi[1]);
+      *reinterpret_cast<uint2*>(sm.Pl + off) = make_uint2(lo[0], lo[1]);
     }
+  } else if (live) {
+    *reinterpret_cast<float4*>(Sr) = make_float4(v[0], v[1], v[2], v[3]);
+    *reinterpret_cast<float4*>(Sr + 32) = make_float4(v[4], v[5], v[6], v[7]);
+  }
+  if (live && k8 == 0) {
+    sm.stt[2 * t] = mx;
+    sm.stt[2 * t + 1] = l;
   }
 }
 
@@ -330,41 +400,37 @@ __device__ __forceinline__ void ldmatrix_x2_trans(uint32_t& r0, uint32_t& r1, co
                : "=r"(r0), "=r"(r1)
                : "r"(smem_u32(row_addr)));
 }
-__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
-  const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
-  return *reinterpret_cast<const uint32_t*>(&v);
+
+// four 8x8 bf16 matrices from shared memory (rows addressed by lanes 0-31): the A fragment of
+// one m16n8k16 step
+__device__ __forceinline__ void ldmatrix_x4(uint32_t (&r)[4], const void* row_addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_u32(row_addr)));
 }
 
-// P.V of one key block: head columns 2*pi, 2*pi+1 for queries g, g+groups, ...
+// P.V of one key block into the thread's ACC_N accumulators (layout: acc_row / acc_col)
 template <typename TD>
-__device__ __forceinline__ void block_pv(const AttnSmem<TD>& sm, int Dh, int nk, int nq, float (&a0)[PV_QMAX],
-                                         float (&a1)[PV_QMAX]) {
-  const int npair = Dh / 2, groups = ATTN_THREADS / npair;
-  const int pi = threadIdx.x % npair, g = threadIdx.x / npair;
+__device__ __forceinline__ void block_pv(const AttnSmem<TD>& sm, int Dh, int nk, int nq, float (&acc)[ACC_N]) {
   if constexpr (sizeof(TD) == 2) {
-    // O[16][Dh] = P V on the tensor cores.  P (fp32) enters as two bf16 parts hi + lo (P = hi + lo
-    // to ~16 bits), V exactly; fp32 accumulation.  Warp w: head columns [w*Dh/4, (w+1)*Dh/4) as
-    // 8-column tiles, 16 keys per step (V^T fragments by transposed 8x8 matrix loads).
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
+    // O[16][Dh] = P V on the tensor cores.  P enters as its bf16 parts hi + lo (written by the
+    // softmax pass), V exactly; fp32 accumulation.  Warp w: head columns [w Dh/4, (w+1) Dh/4) as
+    // 8-column tiles, 16 keys per step (P by 8x8 matrix loads, V^T by transposed ones).
+    (void)nk;
+    (void)nq;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int ntw = Dh / 32;  // 8-column tiles per warp (<= 4)
     float c[4][4];
 #pragma unroll
     for (int j = 0; j < 4; ++j)
 #pragma unroll
       for (int e = 0; e < 4; ++e) c[j][e] = 0.f;
+    const int prow = (lane & 7) + ((lane >> 3) & 1) * 8, pcol = (lane >> 4) * 8;
 #pragma unroll
     for (int ks = 0; ks < ATTN_BLOCK / 16; ++ks) {
-      const float* S0 = sm.S + gid * ATTN_BLOCK + ks * 16 + 2 * tig;
-      const float* S1 = S0 + 8 * ATTN_BLOCK;
-      const float p[8] = {S0[0], S0[1], S1[0], S1[1], S0[8], S0[9], S1[8], S1[9]};
       uint32_t hi[4], lo[4];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const __nv_bfloat16 h0 = __float2bfloat16_rn(p[2 * e]), h1 = __float2bfloat16_rn(p[2 * e + 1]);
-        const __nv_bfloat162 hh = __halves2bfloat162(h0, h1);
-        hi[e] = *reinterpret_cast<const uint32_t*>(&hh);
-        lo[e] = pack_bf16x2(p[2 * e] - __bfloat162float(h0), p[2 * e + 1] - __bfloat162float(h1));
-      }
+      ldmatrix_x4(hi, sm.Ph + prow * PLD + ks * 16 + pcol);
+      ldmatrix_x4(lo, sm.Pl + prow * PLD + ks * 16 + pcol);
       const TD* vrow = sm.Vs + (ks * 16 + (lane >> 3 & 1) * 8 + (lane & 7)) * sm.kpad;
 #pragma unroll
       for (int j = 0; j < 4; ++j)
@@ -377,23 +443,13 @@ __device__ __forceinline__ void block_pv(const AttnSmem<TD>& sm, int Dh, int nk,
     }
 #pragma unroll
     for (int j = 0; j < 4; ++j)
-      if (j < ntw) {
-        const int col = (warp * ntw + j) * 8 + 2 * tig;
-        sm.O[gid * Dh + col] = c[j][0];
-        sm.O[gid * Dh + col + 1] = c[j][1];
-        sm.O[(gid + 8) * Dh + col] = c[j][2];
-        sm.O[(gid + 8) * Dh + col + 1] = c[j][3];
-      }
-    __syncthreads();
 #pragma unroll
-    for (int q = 0; q < PV_QMAX; ++q) {
-      const int t = g + q * groups;
-      a0[q] = t < QT ? sm.O[t * Dh + 2 * pi] : 0.f;
-      a1[q] = t < QT ? sm.O[t * Dh + 2 * pi + 1] : 0.f;
-    }
-    __syncthreads();  // O is rewritten by the next block
+      for (int e = 0; e < 4; ++e) acc[4 * j + e] = c[j][e];
     return;
   }
+  const int npair = Dh / 2, groups = ATTN_THREADS / npair;
+  const int pi = threadIdx.x % npair, g = threadIdx.x / npair;
+  float a0[PV_QMAX], a1[PV_QMAX];
 #pragma unroll
   for (int q = 0; q < PV_QMAX; ++q) a0[q] = a1[q] = 0.f;
   for (int i0 = 0; i0 < nk; i0 += 4) {  // keys in order, four per float4 of P
@@ -401,33 +457,29 @@ __device__ __forceinline__ void block_pv(const AttnSmem<TD>& sm, int Dh, int nk,
 #pragma unroll
     for (int q = 0; q < PV_QMAX; ++q) {
       const int t = g + q * groups;
-      p4[q] = t < nq ? *reinterpret_cast<const float4*>(sm.S + t * ATTN_BLOCK + i0) : make_float4(0.f, 0.f, 0.f, 0.f);
+      p4[q] = t < nq ? *reinterpret_cast<const float4*>(sm.S + t * SLD + i0) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
       const int i = i0 + k;
       if (i < nk) {
-        float v0, v1;
-        if constexpr (sizeof(TD) == 2) {
-          const float2 f2 = __bfloat1622float2(reinterpret_cast<const __nv_bfloat162*>(sm.Vs + i * sm.kpad)[pi]);
-          v0 = f2.x;
-          v1 = f2.y;
-        } else {
-          const float2 f2 = reinterpret_cast<const float2*>(sm.Vs + i * sm.kpad)[pi];
-          v0 = f2.x;
-          v1 = f2.y;
-        }
+        const float2 f2 = reinterpret_cast<const float2*>(sm.Vs + i * sm.kpad)[pi];
 #pragma unroll
         for (int q = 0; q < PV_QMAX; ++q) {
           const int t = g + q * groups;
           if (t < nq) {
             const float pv = k == 0 ? p4[q].x : (k == 1 ? p4[q].y : (k == 2 ? p4[q].z : p4[q].w));
-            a0[q] = fmaf(pv, v0, a0[q]);
-            a1[q] = fmaf(pv, v1, a1[q]);
+            a0[q] = fmaf(pv, f2.x, a0[q]);
+            a1[q] = fmaf(pv, f2.y, a1[q]);
           }
         }
       }
     }
+  }
+#pragma unroll
+  for (int q = 0; q < PV_QMAX; ++q) {
+    acc[2 * q] = a0[q];
+    acc[2 * q + 1] = a1[q];
   }
 }
 
@@ -435,8 +487,8 @@ __device__ __forceinline__ void block_pv(const AttnSmem<TD>& sm, int Dh, int nk,
 // (a) and of the block (bj); acc' = acc * a + acc_j * bj.  Blocks with mj = -inf are skipped.
 __device__ __forceinline__ void fold_stats(float& m, float& l, float mj, float lj, float& a, float& bj) {
   const float mn = fmaxf(m, mj);
-  a = m == -CUDART_INF_F ? 0.f : expf(m - mn);
-  bj = expf(mj - mn);
+  a = m == -CUDART_INF_F ? 0.f : exp2f(m - mn);
+  bj = exp2f(mj - mn);
   l = fmaf(l, a, __fmul_rn(lj, bj));
   m = mn;
 }
@@ -444,19 +496,29 @@ __device__ __forceinline__ float fold_acc(float acc, float a, float accj, float 
   return fmaf(acc, a, __fmul_rn(accj, bj));
 }
 
-// Split-KV (chunks of at most QT queries, i.e. one pass): grid (block groups, H, B), ATTN_THREADS
+// The fold order of a query's key blocks (the same in the split-KV combine and the fused kernel):
+// the blocks of each group of ATTN_GROUP consecutive blocks (aligned at absolute block indices) in
+// block order, from an empty accumulator; then the groups in group order.  Folding one group's
+// result into the empty accumulator is exact, so contexts of one group fold block by block.
+constexpr int ATTN_GROUP = 16;
+
+// Split-KV (chunks of at most QT queries, i.e. one pass): grid (block ranges, H, B), ATTN_THREADS
 // threads.  A CTA walks bpc consecutive ATTN_BLOCK-key blocks of one head; for each it computes the
-// scores, softmax and P.V and writes, for each query whose position reaches the block, the block's
-// partial (acc, max, sum).  The next block's K is in flight while this block's softmax and P.V
-// run, its V while this block's partials are written.  Keys past a query's position score -inf
-// and contribute exact zeros, so a query's partial does not depend on how many queries share the
-// call, nor on bpc.
+// scores, softmax and P.V.  The next block's K is in flight while this block's softmax and P.V
+// run, its V while this block's results are stored.  Keys past a query's position score -inf and
+// contribute exact zeros, so a query's result does not depend on how many queries share the call,
+// nor on bpc.  Stored per query whose position reaches the block:
+//   group_fold = 0: every block's partial (acc, max, sum) in its slot;
+//   group_fold = 1 (bpc a multiple of ATTN_GROUP, so the range covers whole groups): the blocks of
+//     each group folded in block order from an empty accumulator, the group's (acc, max, sum) in
+//     the slot of its first block, which is what attn_group_fold_kernel makes of the partials.
 template <typename TD>
-__global__ void __launch_bounds__(ATTN_THREADS) attn_block_kernel(const TD* __restrict__ qrot,
+__global__ void __launch_bounds__(ATTN_THREADS, 5) attn_block_kernel(const TD* __restrict__ qrot,
                                                                  const TD* __restrict__ kv,
                                                                  const int32_t* __restrict__ len, int T, int d,
                                                                  int H, int Dh, int Lmax, int nblk_cap, int tcap,
-                                                                 int bpc, float scale, float* __restrict__ part) {
+                                                                 int bpc, int group_fold, float scale,
+                                                                 float* __restrict__ part) {
   pdl_trigger();
   pdl_wait();
   extern __shared__ __align__(16) unsigned char attn_sm[];
@@ -474,8 +536,13 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_block_kernel(const TD* __re
   stage_k(sm, kvb + static_cast<size_t>(j_begin) * ATTN_BLOCK * 2 * HD, HD, Dh, nk_of(j_begin));
   stage_v(sm, kvb + static_cast<size_t>(j_begin) * ATTN_BLOCK * 2 * HD, HD, Dh, nk_of(j_begin));
   stage_q(sm, qrot + static_cast<size_t>(b * T) * d + h * Dh, d, nq, Dh);
-  const int npair = Dh / 2, groups = ATTN_THREADS / npair;
-  const int pi = threadIdx.x % npair, g = threadIdx.x / npair;
+  float gc[ACC_N];  // group_fold: the running accumulator of the current group
+#pragma unroll
+  for (int i = 0; i < ACC_N; ++i) gc[i] = 0.f;
+  for (int t = threadIdx.x; t < QT; t += ATTN_THREADS) {
+    sm.gfold[4 * t] = -CUDART_INF_F;
+    sm.gfold[4 * t + 1] = 0.f;
+  }
   for (int j = j_begin; j < j_end; ++j) {
     const int k0 = j * ATTN_BLOCK, nk = nk_of(j);
     const bool more = j + 1 < j_end;
@@ -490,30 +557,134 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_block_kernel(const TD* __re
     else
       cp_async_wait<0>();
     __syncthreads();
-    float a0[PV_QMAX], a1[PV_QMAX];
-    block_pv(sm, Dh, nk, nq, a0, a1);
-    __syncthreads();  // V of block j no longer read
-    if (more) stage_v(sm, kvb + static_cast<size_t>(j + 1) * ATTN_BLOCK * 2 * HD, HD, Dh, nk_of(j + 1));
-#pragma unroll
-    for (int q = 0; q < PV_QMAX; ++q) {
-      const int t = g + q * groups;
-      if (t < nq && L0 + t >= k0) {
-        float* pd = part + ((((static_cast<size_t>(b) * H + h) * nblk_cap + j) * tcap + t) * (Dh + 2));
-        pd[2 * pi] = a0[q];
-        pd[2 * pi + 1] = a1[q];
-        if (pi == 0) {
-          pd[Dh] = sm.stt[2 * t];
-          pd[Dh + 1] = sm.stt[2 * t + 1];
+    if (group_fold) {  // the block's stats folded into the group's (as the fused kernel does)
+      for (int t = threadIdx.x; t < nq; t += ATTN_THREADS) {
+        const float mj = sm.stt[2 * t];
+        float* f = sm.gfold + 4 * t;
+        if (mj == -CUDART_INF_F) {
+          f[2] = 1.f;
+          f[3] = 0.f;
+          continue;
         }
+        float m = f[0], l = f[1], a, bj;
+        fold_stats(m, l, mj, sm.stt[2 * t + 1], a, bj);
+        f[0] = m;
+        f[1] = l;
+        f[2] = a;
+        f[3] = bj;
+      }
+    }
+    float acc[ACC_N];
+    block_pv(sm, Dh, nk, nq, acc);
+    __syncthreads();  // V of block j no longer read; the group stats updated
+    if (more) stage_v(sm, kvb + static_cast<size_t>(j + 1) * ATTN_BLOCK * 2 * HD, HD, Dh, nk_of(j + 1));
+    if (!group_fold) {
+#pragma unroll
+      for (int i = 0; i < ACC_N; i += 2) {
+        const int t = acc_row<TD>(i, Dh), col = acc_col<TD>(i, Dh);
+        if (acc_live<TD>(i, Dh) && t < nq && L0 + t >= k0) {
+          float* pd = part + ((((static_cast<size_t>(b) * H + h) * nblk_cap + j) * tcap + t) * (Dh + 2));
+          *reinterpret_cast<float2*>(pd + col) = make_float2(acc[i], acc[i + 1]);
+          if (col == 0) {
+            pd[Dh] = sm.stt[2 * t];
+            pd[Dh + 1] = sm.stt[2 * t + 1];
+          }
+        }
+      }
+      continue;
+    }
+#pragma unroll
+    for (int i = 0; i < ACC_N; i += 2) {
+      const int t = acc_row<TD>(i, Dh);
+      if (acc_live<TD>(i, Dh) && t < nq && sm.stt[2 * t] != -CUDART_INF_F) {
+        const float a = sm.gfold[4 * t + 2], bj = sm.gfold[4 * t + 3];
+        gc[i] = fold_acc(gc[i], a, acc[i], bj);
+        gc[i + 1] = fold_acc(gc[i + 1], a, acc[i + 1], bj);
+      }
+    }
+    if (j % ATTN_GROUP == ATTN_GROUP - 1 || j + 1 == j_end) {
+      // the group's result into the slot of its first block (queries the group reaches), then the
+      // group emptied
+      const int jg = j - j % ATTN_GROUP;
+#pragma unroll
+      for (int i = 0; i < ACC_N; i += 2) {
+        const int t = acc_row<TD>(i, Dh), col = acc_col<TD>(i, Dh);
+        if (acc_live<TD>(i, Dh) && t < nq && L0 + t >= jg * ATTN_BLOCK) {
+          float* pd = part + ((((static_cast<size_t>(b) * H + h) * nblk_cap + jg) * tcap + t) * (Dh + 2));
+          *reinterpret_cast<float2*>(pd + col) = make_float2(gc[i], gc[i + 1]);
+          if (col == 0) {
+            pd[Dh] = sm.gfold[4 * t];
+            pd[Dh + 1] = sm.gfold[4 * t + 1];
+          }
+        }
+        gc[i] = gc[i + 1] = 0.f;
+      }
+      __syncthreads();  // the group stats are read
+      for (int t = threadIdx.x; t < QT; t += ATTN_THREADS) {
+        sm.gfold[4 * t] = -CUDART_INF_F;
+        sm.gfold[4 * t + 1] = 0.f;
       }
     }
   }
   cp_async_wait<0>();  // no copy may outlive the CTA
 }
 
+// partials of blocks jb, jb + jstep, jb + 2 jstep, ... <= jend folded in that order (eight loads
+// in flight); blocks with max -inf (past the query) are skipped
+__device__ __forceinline__ void fold_blocks(const float* pb, size_t jstride, int Dh, int dd, int jb, int jend,
+                                            int jstep, float& m, float& l, float& acc) {
+  for (int j0 = jb; j0 <= jend; j0 += 8 * jstep) {
+    float mj[8], lj[8], aj[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int j = j0 + k * jstep;
+      if (j <= jend) {
+        const float* pj = pb + j * jstride;
+        mj[k] = pj[Dh];
+        lj[k] = pj[Dh + 1];
+        aj[k] = pj[dd];
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      if (j0 + k * jstep > jend || mj[k] == -CUDART_INF_F) continue;
+      float a, bj;
+      fold_stats(m, l, mj[k], lj[k], a, bj);
+      acc = fold_acc(acc, a, aj[k], bj);
+    }
+  }
+}
+
+// Contexts of more than one group: group g's blocks folded in block order, in place, into the
+// partial slot of its first block.  grid (M, H, groups), Dh threads.
+__global__ void attn_group_fold_kernel(float* __restrict__ part, const int32_t* __restrict__ len, int T, int H,
+                                       int Dh, int nblk_cap, int tcap) {
+  pdl_trigger();
+  pdl_wait();
+  const int row = blockIdx.x, h = blockIdx.y, grp = blockIdx.z, dd = threadIdx.x;
+  const int b = row / T, t = row % T;
+  const int jmax = (len[b] + t) / ATTN_BLOCK;
+  const int jb = grp * ATTN_GROUP;
+  if (jb > jmax) return;  // the whole group lies past this query
+  float* pb = part + ((static_cast<size_t>(b) * H + h) * nblk_cap * tcap + t) * (Dh + 2);
+  const size_t jstride = static_cast<size_t>(tcap) * (Dh + 2);
+  float m = -CUDART_INF_F, l = 0.f, acc = 0.f;
+  if (dd < Dh) fold_blocks(pb, jstride, Dh, dd, jb, min(jmax, jb + ATTN_GROUP - 1), 1, m, l, acc);
+  __syncthreads();  // every thread has read the group's statistics
+  float* pg = pb + jb * jstride;
+  if (dd < Dh) pg[dd] = acc;
+  if (dd == 0) {
+    pg[Dh] = m;
+    pg[Dh + 1] = l;
+  }
+}
+
+// grid (M, H), Dh threads: the query's partial slots j = 0, jstep, 2 jstep, ... <= its last block
+// folded in order (jstep = 1: the blocks of a one-group context; ATTN_GROUP: the group results)
 template <typename TD>
 __global__ void attn_combine_kernel(const float* __restrict__ part, const int32_t* __restrict__ len, int T, int d,
-                                    int H, int Dh, int nblk_cap, int tcap, TD* __restrict__ out, int ld_out) {
+                                    int H, int Dh, int nblk_cap, int tcap, int jstep, TD* __restrict__ out,
+                                    int ld_out) {
   pdl_trigger();
   pdl_wait();
   const int row = blockIdx.x, h = blockIdx.y, dd = threadIdx.x;
@@ -524,25 +695,7 @@ __global__ void attn_combine_kernel(const float* __restrict__ part, const int32_
   float m = -CUDART_INF_F, l = 0.f, acc = 0.f;
   const float* pb = part + ((static_cast<size_t>(b) * H + h) * nblk_cap * tcap + t) * (Dh + 2);
   const size_t jstride = static_cast<size_t>(tcap) * (Dh + 2);
-  for (int j0 = 0; j0 <= jmax; j0 += 4) {  // four blocks' loads in flight, folded in block order
-    float mj[4], lj[4], aj[4];
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      if (j0 + k <= jmax) {
-        const float* pj = pb + (j0 + k) * jstride;
-        mj[k] = pj[Dh];
-        lj[k] = pj[Dh + 1];
-        aj[k] = pj[dd];
-      }
-    }
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      if (j0 + k > jmax || mj[k] == -CUDART_INF_F) continue;
-      float a, bj;
-      fold_stats(m, l, mj[k], lj[k], a, bj);
-      acc = fold_acc(acc, a, aj[k], bj);
-    }
-  }
+  fold_blocks(pb, jstride, Dh, dd, 0, jmax, jstep, m, l, acc);
   out[static_cast<size_t>(row) * ld_out + h * Dh + dd] = from_f32<TD>(acc / l);
 }
 
@@ -552,7 +705,7 @@ __global__ void attn_combine_kernel(const float* __restrict__ part, const int32_
 // then folds it as the combine kernel does (fold_stats / fold_acc), so every query's output equals
 // the split-KV + combine result bit for bit, with no partial buffer and any chunk length.
 template <typename TD>
-__global__ void __launch_bounds__(ATTN_THREADS) attn_fused_kernel(const TD* __restrict__ qrot,
+__global__ void __launch_bounds__(ATTN_THREADS, 4) attn_fused_kernel(const TD* __restrict__ qrot,
                                                                  const TD* __restrict__ kv,
                                                                  const int32_t* __restrict__ len, int T, int d,
                                                                  int H, int Dh, int Lmax, float scale,
@@ -566,16 +719,15 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_fused_kernel(const TD* __re
   const int Lend = L0 + T;
   AttnSmem<TD> sm(attn_sm, Dh);
   const size_t HD = static_cast<size_t>(H) * Dh;
-  const int npair = Dh / 2, groups = ATTN_THREADS / npair;
-  const int pi = threadIdx.x % npair, g = threadIdx.x / npair;
   stage_q(sm, qrot + static_cast<size_t>(b * T + tq0) * d + h * Dh, d, nq, Dh);
   for (int t = threadIdx.x; t < QT; t += ATTN_THREADS) {
-    sm.fold[4 * t] = -CUDART_INF_F;
-    sm.fold[4 * t + 1] = 0.f;
+    sm.fold[4 * t] = sm.gfold[4 * t] = -CUDART_INF_F;
+    sm.fold[4 * t + 1] = sm.gfold[4 * t + 1] = 0.f;
   }
-  float c0[PV_QMAX], c1[PV_QMAX];  // running accumulators (the combine kernel's acc)
+  // running accumulators: of the whole fold (cc) and of the current fold group (gc)
+  float cc[ACC_N], gc[ACC_N];
 #pragma unroll
-  for (int q = 0; q < PV_QMAX; ++q) c0[q] = c1[q] = 0.f;
+  for (int i = 0; i < ACC_N; ++i) cc[i] = gc[i] = 0.f;
   const int jlast = (L0 + tq0 + nq - 1) / ATTN_BLOCK;
   for (int j = 0; j <= jlast; ++j) {
     const int k0 = j * ATTN_BLOCK;
@@ -590,7 +742,7 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_fused_kernel(const TD* __re
     __syncthreads();
     for (int t = threadIdx.x; t < nq; t += ATTN_THREADS) {
       const float mj = sm.stt[2 * t];
-      float* f = sm.fold + 4 * t;
+      float* f = sm.gfold + 4 * t;
       if (mj == -CUDART_INF_F) {  // the block lies past this query: the combine skips it
         f[2] = 1.f;
         f[3] = 0.f;
@@ -604,26 +756,59 @@ __global__ void __launch_bounds__(ATTN_THREADS) attn_fused_kernel(const TD* __re
       f[3] = bj;
     }
     __syncthreads();
-    float a0[PV_QMAX], a1[PV_QMAX];
-    block_pv(sm, Dh, nk, nq, a0, a1);
+    float acc[ACC_N];
+    block_pv(sm, Dh, nk, nq, acc);
 #pragma unroll
-    for (int q = 0; q < PV_QMAX; ++q) {
-      const int t = g + q * groups;
-      if (t < nq && sm.stt[2 * t] != -CUDART_INF_F) {
-        const float a = sm.fold[4 * t + 2], bj = sm.fold[4 * t + 3];
-        c0[q] = fold_acc(c0[q], a, a0[q], bj);
-        c1[q] = fold_acc(c1[q], a, a1[q], bj);
+    for (int i = 0; i < ACC_N; i += 2) {
+      const int t = acc_row<TD>(i, Dh);
+      if (acc_live<TD>(i, Dh) && t < nq && sm.stt[2 * t] != -CUDART_INF_F) {
+        const float a = sm.gfold[4 * t + 2], bj = sm.gfold[4 * t + 3];
+        gc[i] = fold_acc(gc[i], a, acc[i], bj);
+        gc[i + 1] = fold_acc(gc[i + 1], a, acc[i + 1], bj);
+      }
+    }
+    if (j % ATTN_GROUP == ATTN_GROUP - 1 || j == jlast) {
+      // the group's result folded into the whole fold (a group past a query is skipped, as the
+      // combine skips it), then the group accumulator emptied
+      __syncthreads();
+      for (int t = threadIdx.x; t < nq; t += ATTN_THREADS) {
+        float* f = sm.fold + 4 * t;
+        float* gf = sm.gfold + 4 * t;
+        const float gm = gf[0], gl = gf[1];
+        gf[0] = -CUDART_INF_F;
+        gf[1] = 0.f;
+        if (gm == -CUDART_INF_F) {
+          f[3] = -1.f;  // no fold for this query
+          continue;
+        }
+        float m = f[0], l = f[1], a, bg;
+        fold_stats(m, l, gm, gl, a, bg);
+        f[0] = m;
+        f[1] = l;
+        f[2] = a;
+        f[3] = bg;
+      }
+      __syncthreads();
+#pragma unroll
+      for (int i = 0; i < ACC_N; i += 2) {
+        const int t = acc_row<TD>(i, Dh);
+        if (acc_live<TD>(i, Dh) && t < nq && sm.fold[4 * t + 3] >= 0.f) {
+          const float a = sm.fold[4 * t + 2], bg = sm.fold[4 * t + 3];
+          cc[i] = fold_acc(cc[i], a, gc[i], bg);
+          cc[i + 1] = fold_acc(cc[i + 1], a, gc[i + 1], bg);
+        }
+        gc[i] = gc[i + 1] = 0.f;
       }
     }
   }
 #pragma unroll
-  for (int q = 0; q < PV_QMAX; ++q) {
-    const int t = g + q * groups;
-    if (t < nq) {
+  for (int i = 0; i < ACC_N; i += 2) {
+    const int t = acc_row<TD>(i, Dh);
+    if (acc_live<TD>(i, Dh) && t < nq) {
       const float l = sm.fold[4 * t + 1];
-      TD* o = out + static_cast<size_t>(b * T + tq0 + t) * ld_out + h * Dh + 2 * pi;
-      o[0] = from_f32<TD>(c0[q] / l);
-      o[1] = from_f32<TD>(c1[q] / l);
+      TD* o = out + static_cast<size_t>(b * T + tq0 + t) * ld_out + h * Dh + acc_col<TD>(i, Dh);
+      o[0] = from_f32<TD>(cc[i] / l);
+      o[1] = from_f32<TD>(cc[i + 1] / l);
     }
   }
 }
@@ -641,7 +826,8 @@ int launch_attention_t(const evs_model* m, evs_state* s, int layer, int B, int T
                           static_cast<const int32_t*>(s->d_len), s->max_seqlen, qrot, kv, s->d_err));
   const size_t smem = attn_smem_bytes<TD>(Dh);
   EVS_CHECK_RANGE(smem <= 227 * 1024, "head_dim too large for the staged attention block");
-  const float scale = 1.0f / sqrtf(static_cast<float>(Dh));
+  // scores in the base-2 domain: s = (q.k / sqrt(Dh)) log2(e), p = 2^(s - max), the same softmax
+  const float scale = static_cast<float>(1.4426950408889634 / std::sqrt(static_cast<double>(Dh)));
   if (T > s->attn_tcap) {
     EVS_CUDA_TRY(cudaFuncSetAttribute(attn_fused_kernel<TD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       static_cast<int>(smem)));
@@ -660,14 +846,28 @@ int launch_attention_t(const evs_model* m, evs_state* s, int layer, int B, int T
   static int n_sm = 0;
   if (n_sm == 0) EVS_CUDA_TRY(cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, m->device));
   const long long want = 16LL * n_sm;
-  const int bpc = static_cast<int>(std::max<long long>(1, (static_cast<long long>(kv_blocks) * H * B + want - 1) / want));
+  int bpc = static_cast<int>(std::max<long long>(1, (static_cast<long long>(kv_blocks) * H * B + want - 1) / want));
+  // long contexts: whole groups per CTA, folded in the CTA (no per-block partials, no group fold
+  // kernel); the bits are those of the per-block path
+  const int group_fold = bpc >= ATTN_GROUP / 2 ? 1 : 0;
+  if (group_fold) bpc = (bpc + ATTN_GROUP - 1) / ATTN_GROUP * ATTN_GROUP;
   EVS_CUDA_TRY(evs_launch(attn_block_kernel<TD>, dim3((kv_blocks + bpc - 1) / bpc, H, B), dim3(ATTN_THREADS), smem, st,
                           pdl, static_cast<const TD*>(qrot), static_cast<const TD*>(kv),
                           static_cast<const int32_t*>(s->d_len), T, d, H, Dh, s->max_seqlen, s->attn_blocks,
-                          s->attn_tcap, bpc, scale, s->attn_part));
+                          s->attn_tcap, bpc, group_fold, scale, s->attn_part));
+  int jstep = 1;
+  if (group_fold) {
+    jstep = ATTN_GROUP;
+  } else if (kv_blocks > ATTN_GROUP) {
+    const int ngroups = (kv_blocks + ATTN_GROUP - 1) / ATTN_GROUP;
+    EVS_CUDA_TRY(evs_launch(attn_group_fold_kernel, dim3(M, H, ngroups), dim3(Dh), 0, st, pdl, s->attn_part,
+                            static_cast<const int32_t*>(s->d_len), T, H, Dh, s->attn_blocks, s->attn_tcap));
+    evs_count_launch(1);
+    jstep = ATTN_GROUP;
+  }
   EVS_CUDA_TRY(evs_launch(attn_combine_kernel<TD>, dim3(M, H), dim3(Dh), 0, st, pdl,
                           static_cast<const float*>(s->attn_part), static_cast<const int32_t*>(s->d_len), T, d, H,
-                          Dh, s->attn_blocks, s->attn_tcap, static_cast<TD*>(s->act), s->ld_act));
+                          Dh, s->attn_blocks, s->attn_tcap, jstep, static_cast<TD*>(s->act), s->ld_act));
   evs_count_launch(3);
   return EVS_OK;
 }

@@ -578,8 +578,8 @@ __global__ void __launch_bounds__(32 * DEC_ROWS) hyena_fir_dec_kernel(HyArgs<TD>
 
 // grid (d / 32, ceil(B / DEC_ROWS)), block (32, DEC_ROWS): one thread per channel and row, all 16
 // poles in registers (four groups of four, as the four pole-group threads of hyena_iir_kernel).
-// Shared memory: poles and residues of the 32 channels [2][32][16] f32 (staged before the wait) |
-// per warp ub[DEC_T][96] TD.
+// The poles and residues (weights) are loaded into registers before the dependency wait.  Shared
+// memory: per warp ub[DEC_T][96] TD.
 template <typename TD>
 __global__ void __launch_bounds__(32 * DEC_ROWS) hyena_iir_dec_kernel(HyArgs<TD> a) {
   pdl_trigger();
@@ -588,21 +588,15 @@ __global__ void __launch_bounds__(32 * DEC_ROWS) hyena_iir_dec_kernel(HyArgs<TD>
   const int lane = threadIdx.x, h0 = blockIdx.x * 32, h = h0 + lane;
   const int b = blockIdx.y * DEC_ROWS + threadIdx.y;
   const int d = a.d;
-  float* pr = sm;  // [2][32 * S]: poles, then residues
-  TD* ub = reinterpret_cast<TD*>(sm + 2 * 32 * S) + threadIdx.y * DEC_T * 96;
-  // the poles and residues are weights: staged (16-byte copies) before waiting for the in-projection
-  for (int i = threadIdx.y * 32 + lane; i < 2 * 32 * S / 4; i += 32 * DEC_ROWS) {
-    const int w = i / (32 * S / 4), k = i - w * (32 * S / 4);
-    cp_async16(pr + w * 32 * S + 4 * k, (w == 0 ? a.poles : a.residues) + static_cast<size_t>(h0) * S + 4 * k);
-  }
-  cp_async_commit();
+  TD* ub = reinterpret_cast<TD*>(sm) + threadIdx.y * DEC_T * 96;
+  float p[S], r[S];
+  load_vec<S>(a.poles + static_cast<size_t>(h) * S, p);
+  load_vec<S>(a.residues + static_cast<size_t>(h) * S, r);
   float wo[3 * DEC_K0];
 #pragma unroll
   for (int i = 0; i < 3 * DEC_K0; ++i) wo[i] = __ldg(a.short_w + static_cast<size_t>(3 * h) * DEC_K0 + i);
   const float Dg = a.D[h];
   pdl_wait();
-  cp_async_wait<0>();
-  __syncthreads();  // poles and residues staged
   if (b >= a.M / a.T) return;
   const int L0 = a.len[b];
   // the carried state first, so that its loads are in flight with the outer pass
@@ -615,9 +609,6 @@ __global__ void __launch_bounds__(32 * DEC_ROWS) hyena_iir_dec_kernel(HyArgs<TD>
   }
   float x2[DEC_T], x1v[DEC_T];
   dec_outer(a, b, h0, lane, L0, wo, ub, x2, x1v);
-  float p[S], r[S];
-  load_vec<S>(pr + lane * S, p);
-  load_vec<S>(pr + 32 * S + lane * S, r);
 #pragma unroll
   for (int t = 0; t < DEC_T; ++t) {
     if (t < a.T) {
@@ -723,8 +714,7 @@ int launch_hyena_t(const evs_model* m, evs_state* s, int layer, int B, int T, in
     const dim3 dgrid(d / 32, (B + DEC_ROWS - 1) / DEC_ROWS), dblock(32, DEC_ROWS);
     const size_t ub_bytes = sizeof(TD) * DEC_ROWS * DEC_T * 96;
     if (L.kind == EVS_LAYER_HCL) {
-      const size_t smem = sizeof(float) * 2 * 32 * 16 + ub_bytes;
-      EVS_CUDA_TRY(evs_launch(hyena_iir_dec_kernel<TD>, dgrid, dblock, smem, st, s->use_pdl(), a));
+      EVS_CUDA_TRY(evs_launch(hyena_iir_dec_kernel<TD>, dgrid, dblock, ub_bytes, st, s->use_pdl(), a));
     } else {
       auto launch = [&](auto kern, int KI) -> int {
         const size_t smem =

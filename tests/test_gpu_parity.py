@@ -233,6 +233,39 @@ def test_long_context_multi_block_split_kv_bitwise(cuda, tiny, which, L):
         model.close()
 
 
+def test_long_context_group_fold_in_cta_bitwise(cuda):
+    """Eight rows of 6,000 keys give the split-KV kernel enough key blocks per CTA to walk whole
+    16-block groups and fold them in the CTA; one row alone gives per-block partials, the group
+    fold kernel and the combine.  Every row's verify block agrees bit for bit between the two."""
+    from evspark_b200.config import EVO2_7B_SLICE
+    from evspark_b200.model import TargetModel
+    from evspark_b200.specdec.block import block_forward, prefill
+
+    model = TargetModel.random(EVO2_7B_SLICE, seed=9, device=cuda, init_on="cuda")
+    n_sm = torch.cuda.get_device_properties(cuda).multi_processor_count
+    B, L, H = 8, 6000, model.cfg.n_heads
+    kv_blocks = (L + 13 + 63) // 64
+
+    def blocks_per_cta(rows):
+        return -(-kv_blocks * H * rows // (16 * n_sm))
+
+    assert blocks_per_cta(B) >= 8 > blocks_per_cta(1), "one path each: in-CTA group fold, per-block partials"
+    rng = np.random.default_rng(29)
+    prompts = rng.choice([65, 67, 71, 84], size=(B, L))
+    chunks = rng.choice([65, 67, 71, 84], size=(B, 13))
+    ip = model.initialize_inference_params(L + 64, max_batch=B, max_chunk=1024)
+    prefill(model, torch.tensor(prompts), ip)
+    blk = block_forward(model, torch.tensor(chunks), ip)
+    ip.close()
+    for r in range(B):
+        ip1 = model.initialize_inference_params(L + 64, max_chunk=1024)
+        prefill(model, torch.tensor(prompts[r])[None], ip1)
+        one = block_forward(model, torch.tensor(chunks[r])[None], ip1)
+        ip1.close()
+        assert torch.equal(blk[r], one[0]), (r, (blk[r] - one[0]).abs().max().item())
+    model.close()
+
+
 TOL_FP32_2K = 2e-5  # max-abs logits after a 2048-token context (8x the 256-token prompt of the tiny
                     # workload): the fp32 recurrences over 2048 positions (poles up to 0.999) and the
                     # softmax over 2k keys grow fp32 rounding noise; the oracle itself, run in fp32,
