@@ -54,6 +54,7 @@ struct RingPtrs {
 };
 
 constexpr int DR_CR = 128;  // cache slots per row: covers the ctx_window (<= 64) positions a call reads
+constexpr int DRAFT_ATTN_ROWS_MIN_B = 4;  // rows from which one attention CTA per (head, row) serves all queries
 
 // Which context rows of a call lack a current projection: row b reads positions L-n .. L-1
 // (n = min(CW, L)); position P is current when its slot holds P with the capture tag that the
@@ -356,6 +357,105 @@ __global__ void __launch_bounds__(128) draft_attn_kernel(const float* q, const f
     for (int j = 0; j < nk; ++j)
       if (sc[j] != 0.f) acc = fmaf(sc[j], krow(cv, vd, j)[e], acc);
     y[(static_cast<size_t>(b) * g + t) * d + hh * hd + e] = acc / l;
+  }
+}
+
+// Many rows: one CTA per (head, row b) for all g queries, with the row's visible k/v rows staged
+// once in shared memory (K rows padded to hd + 1 floats: a thread per key reads its own row without
+// bank conflicts).  Each query runs draft_attn_kernel's arithmetic, thread for thread (same key per
+// thread, same reductions, same add order), so the two kernels give the same bits.
+__global__ void __launch_bounds__(128) draft_attn_rows_kernel(const float* q, const float* kd, const float* vd,
+                                                              const float* ck, const float* cv, const int32_t* len,
+                                                              int with_ctx, int CW, int g, int d, int heads,
+                                                              float* y) {
+  pdl_trigger();
+  pdl_wait();
+  extern __shared__ __align__(16) float da_sm[];
+  __shared__ float red[8];
+  const int hh = blockIdx.x, b = blockIdx.y;
+  const int hd = d / heads;
+  const int L = len[b];
+  const int nctx = with_ctx ? min(CW, L) : 0;
+  const int nk = CW + g;
+  const float scale = rsqrtf(static_cast<float>(hd));
+  float* Ks = da_sm;                                // [nk][hd + 1]
+  float* Vs = Ks + (nk * (hd + 1) + 3) / 4 * 4;     // [nk][hd], 16-byte aligned
+  float* Qs = Vs + nk * hd;           // [g][hd]
+  float* sc = Qs + g * hd;            // [nk]
+  auto krow = [&](const float* cbuf, const float* dbuf, int j) -> const float* {
+    return j < CW ? cbuf + (static_cast<size_t>(b) * DR_CR + (L - nctx + j) % DR_CR) * d + hh * hd
+                  : dbuf + (static_cast<size_t>(b) * g + j - CW) * d + hh * hd;
+  };
+  // 16-byte loads, eight per thread in flight (context slots before position 0 are never visible
+  // and never read)
+  const int h4 = hd / 4, n4 = nk * h4;
+  for (int i0 = threadIdx.x; i0 < n4; i0 += 8 * blockDim.x) {
+    float4 kx[8], vx[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int i = i0 + u * blockDim.x, j = i / h4, e4 = i - j * h4;
+      if (i < n4 && !(j < CW && j >= nctx)) {
+        kx[u] = *reinterpret_cast<const float4*>(krow(ck, kd, j) + 4 * e4);
+        vx[u] = *reinterpret_cast<const float4*>(krow(cv, vd, j) + 4 * e4);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int i = i0 + u * blockDim.x, j = i / h4, e4 = i - j * h4;
+      if (i < n4 && !(j < CW && j >= nctx)) {
+        float* kd4 = Ks + j * (hd + 1) + 4 * e4;
+        kd4[0] = kx[u].x;
+        kd4[1] = kx[u].y;
+        kd4[2] = kx[u].z;
+        kd4[3] = kx[u].w;
+        *reinterpret_cast<float4*>(Vs + j * hd + 4 * e4) = vx[u];
+      }
+    }
+  }
+  for (int i = threadIdx.x; i < g * h4; i += blockDim.x) {
+    const int t = i / h4, e4 = i - t * h4;
+    *reinterpret_cast<float4*>(Qs + 4 * i) =
+        *reinterpret_cast<const float4*>(q + (static_cast<size_t>(b) * g + t) * d + hh * hd + 4 * e4);
+  }
+  __syncthreads();
+  for (int t = 0; t < g; ++t) {
+    const float* qr = Qs + t * hd;
+    for (int j = threadIdx.x; j < nk; j += blockDim.x) {
+      const bool vis = j < CW ? j < nctx : (j - CW) <= t;
+      float s = -CUDART_INF_F;
+      if (vis) {
+        const float* kr = Ks + j * (hd + 1);
+        float acc = 0.f;
+        for (int e = 0; e < hd; ++e) acc = fmaf(qr[e], kr[e], acc);
+        s = acc * scale;
+      }
+      sc[j] = s;
+    }
+    __syncthreads();
+    float m = -CUDART_INF_F;
+    for (int j = threadIdx.x; j < nk; j += blockDim.x) m = fmaxf(m, sc[j]);
+    m = warp_max(m);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+    __syncthreads();
+    m = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+    __syncthreads();
+    float l = 0.f;
+    for (int j = threadIdx.x; j < nk; j += blockDim.x) {
+      const float p = sc[j] == -CUDART_INF_F ? 0.f : expf(sc[j] - m);
+      sc[j] = p;
+      l += p;
+    }
+    l = warp_sum(l);
+    if ((threadIdx.x & 31) == 0) red[4 + (threadIdx.x >> 5)] = l;
+    __syncthreads();
+    l = (red[4] + red[5]) + (red[6] + red[7]);
+    for (int e = threadIdx.x; e < hd; e += blockDim.x) {
+      float acc = 0.f;
+      for (int j = 0; j < nk; ++j)
+        if (sc[j] != 0.f) acc = fmaf(sc[j], Vs[j * hd + e], acc);
+      y[(static_cast<size_t>(b) * g + t) * d + hh * hd + e] = acc / l;
+    }
+    __syncthreads();  // sc and red are rewritten by the next query
   }
 }
 
@@ -1044,11 +1144,22 @@ int evs_draft_propose(evs_drafter* dr, const evs_state* s, const int64_t* anchor
                               static_cast<const int32_t*>(dr->cmap), static_cast<const int32_t*>(dr->ccount), d, ckl,
                               cvl, static_cast<int>(l == c.n_layers - 1),
                               static_cast<const unsigned long long*>(s->cap_tag), s->ring_len, dr->cpos, dr->ctag));
-    EVS_CUDA_TRY(evs_launch(draft_attn_kernel, dim3(dim3(g, c.n_heads, B)), dim3(128), 0, st, true,
-                            static_cast<const float*>(dr->q), static_cast<const float*>(dr->kb),
-                            static_cast<const float*>(dr->vb), static_cast<const float*>(ckl),
-                            static_cast<const float*>(cvl), static_cast<const int32_t*>(s->d_len),
-                            static_cast<int>(ctxr), CW, g, d, c.n_heads, dr->y));
+    const int hd = d / c.n_heads, nk = CW + g;
+    const size_t rows_smem =
+        sizeof(float) * ((static_cast<size_t>(nk) * (hd + 1) + 3) / 4 * 4 + static_cast<size_t>(nk) * hd + g * hd + nk);
+    if (B >= DRAFT_ATTN_ROWS_MIN_B && rows_smem <= 48 * 1024 && hd % 4 == 0 && d % 4 == 0) {
+      EVS_CUDA_TRY(evs_launch(draft_attn_rows_kernel, dim3(c.n_heads, B), dim3(128), rows_smem, st, true,
+                              static_cast<const float*>(dr->q), static_cast<const float*>(dr->kb),
+                              static_cast<const float*>(dr->vb), static_cast<const float*>(ckl),
+                              static_cast<const float*>(cvl), static_cast<const int32_t*>(s->d_len),
+                              static_cast<int>(ctxr), CW, g, d, c.n_heads, dr->y));
+    } else {
+      EVS_CUDA_TRY(evs_launch(draft_attn_kernel, dim3(dim3(g, c.n_heads, B)), dim3(128), 0, st, true,
+                              static_cast<const float*>(dr->q), static_cast<const float*>(dr->kb),
+                              static_cast<const float*>(dr->vb), static_cast<const float*>(ckl),
+                              static_cast<const float*>(cvl), static_cast<const int32_t*>(s->d_len),
+                              static_cast<int>(ctxr), CW, g, d, c.n_heads, dr->y));
+    }
     // h += out_proj(y); xb = pre-MLP norm of h
     EVS_TRY(sgemm_epi(dr, L[EVS_D_O], dr->y, d, d, d, rows, EPI_RESID_NORM,
                       epi(nullptr, dr->xb, L[EVS_D_LN2], dr->h, nullptr, 1, eps), st));
