@@ -576,59 +576,142 @@ __global__ void __launch_bounds__(32 * DEC_ROWS) hyena_fir_dec_kernel(HyArgs<TD>
   }
 }
 
-// grid (d / 32, ceil(B / DEC_ROWS)), block (32, DEC_ROWS): one thread per channel and row, all 16
-// poles in registers (four groups of four, as the four pole-group threads of hyena_iir_kernel).
-// The poles and residues (weights) are loaded into registers before the dependency wait.  Shared
-// memory: per warp ub[DEC_T][96] TD.
+// Outer pass of the IIR decode kernel: the warp's 8 output channels h0 .. h0+7 of row b, four
+// lanes per channel (lane = 4 ch + q).  The 24 interleaved in-projection channels 3h0 .. 3h0+23 of
+// every position are loaded as float4s spread over all lanes (three per lane and split, splits
+// summed in split order), rounded, written to the outer ring and handed over through `ub` (the
+// warp's [DEC_T][24] TD buffer); then every lane runs its channel's outer FIR with the arithmetic of
+// dec_outer (the four lanes of a channel compute the same values).
+template <typename TD>
+__device__ __forceinline__ void dec_outer8(const HyArgs<TD>& a, int b, int h0, int ch, int lane, int L0,
+                                           const float (&wo)[3 * DEC_K0], TD* ub, float (&x2)[DEC_T],
+                                           float (&x1v)[DEC_T]) {
+  constexpr int C4 = 6;  // float4 chunks of the 24 channels
+  const int N3 = 3 * a.d;
+  const size_t split_stride = static_cast<size_t>(a.M) * N3;
+  const int T = a.T;
+  const int cmask = a.cap_o - 1;  // the ring capacity is a power of two
+  TD* ring = a.outer_ring + static_cast<size_t>(b) * a.cap_o * N3 + 3 * h0;
+  float uw[3][DEC_K0 - 1];
+#pragma unroll
+  for (int r = 0; r < DEC_K0 - 1; ++r) {
+    const int P = L0 - (DEC_K0 - 1) + r;
+#pragma unroll
+    for (int j = 0; j < 3; ++j)
+      uw[j][r] = P >= 0 ? to_f32(ring[static_cast<size_t>(P & cmask) * N3 + 3 * ch + j]) : 0.f;
+  }
+  {
+    // item i = t * C4 + c (position t, chunk c); lane takes i = lane, lane + 32, lane + 64; positions
+    // t >= T load row T-1 again (all loads in flight) and are never used
+    float4 u4[3];
+#pragma unroll
+    for (int k = 0; k < 3; ++k) u4[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+    const float* src = a.ws + static_cast<size_t>(b) * T * N3 + 3 * h0;
+    for (int sp = 0; sp < a.splits; ++sp) {
+      const float* ss = src + sp * split_stride;
+#pragma unroll
+      for (int k = 0; k < 3; ++k) {
+        const int i = lane + 32 * k, t = i / C4, c = i - t * C4;
+        const float4 v = __ldg(reinterpret_cast<const float4*>(ss + static_cast<size_t>(min(t, T - 1)) * N3 + 4 * c));
+        u4[k].x += v.x;
+        u4[k].y += v.y;
+        u4[k].z += v.z;
+        u4[k].w += v.w;
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+      const int i = lane + 32 * k, t = i / C4, c = i - t * C4;
+      const float r0 = round_to<TD>(u4[k].x), r1 = round_to<TD>(u4[k].y), r2 = round_to<TD>(u4[k].z),
+                  r3 = round_to<TD>(u4[k].w);
+      store4_td<TD>(ub + t * 24 + 4 * c, r0, r1, r2, r3);
+      if (t < T) store4_td<TD>(ring + static_cast<size_t>((L0 + t) & cmask) * N3 + 4 * c, r0, r1, r2, r3);
+    }
+  }
+  __syncwarp();
+#pragma unroll
+  for (int t = 0; t < DEC_T; ++t) {
+    x2[t] = 0.f;
+    x1v[t] = 0.f;
+    if (t < T) {
+      const int P = L0 + t;
+      float zq[3];
+      const int cs = min(P, DEC_K0 - 1);
+      const int base = a.prefill ? DEC_K0 - 1 : cs;
+#pragma unroll
+      for (int j = 0; j < 3; ++j) {
+        const float un = to_f32(ub[t * 24 + 3 * ch + j]);
+        const float w0 = wo[j * DEC_K0], w1 = wo[j * DEC_K0 + 1], w2 = wo[j * DEC_K0 + 2];
+        const float wb = base == 2 ? w1 : w0;
+        const float wc = base == 2 ? w2 : (base == 1 ? w1 : w0);
+        float z = 0.f;
+        if (cs >= 2) z = fmaf(w0, uw[j][0], z);
+        if (cs >= 1) z = fmaf(wb, uw[j][1], z);
+        z = fmaf(wc, un, z);
+        zq[j] = round_to<TD>(z);
+        uw[j][0] = uw[j][1];
+        uw[j][1] = un;
+      }
+      x2[t] = zq[0];
+      x1v[t] = round_to<TD>(zq[1] * zq[2]);
+    }
+  }
+}
+
+// grid (d / 8, ceil(B / DEC_ROWS)), block (32, DEC_ROWS): four lanes per channel and row, lane q
+// holding poles 4q .. 4q+3 (the four pole-group threads of hyena_iir_kernel); the residue sum is
+// ((group 0 + group 1) + (group 2 + group 3)) by two butterfly steps, as in the general kernel.
+// The poles and residues (weights) are loaded before the dependency wait.  Shared memory: per warp
+// ub[DEC_T][24] TD.
 template <typename TD>
 __global__ void __launch_bounds__(32 * DEC_ROWS) hyena_iir_dec_kernel(HyArgs<TD> a) {
   pdl_trigger();
   constexpr int S = 16;
   extern __shared__ __align__(16) float sm[];
-  const int lane = threadIdx.x, h0 = blockIdx.x * 32, h = h0 + lane;
+  const int lane = threadIdx.x, ch = lane >> 2, q = lane & 3;
+  const int h0 = blockIdx.x * 8, h = h0 + ch;
   const int b = blockIdx.y * DEC_ROWS + threadIdx.y;
   const int d = a.d;
-  TD* ub = reinterpret_cast<TD*>(sm) + threadIdx.y * DEC_T * 96;
-  float p[S], r[S];
-  load_vec<S>(a.poles + static_cast<size_t>(h) * S, p);
-  load_vec<S>(a.residues + static_cast<size_t>(h) * S, r);
+  TD* ub = reinterpret_cast<TD*>(sm) + threadIdx.y * DEC_T * 24;
+  float p[4], r[4];
+  load_vec<4>(a.poles + static_cast<size_t>(h) * S + 4 * q, p);
+  load_vec<4>(a.residues + static_cast<size_t>(h) * S + 4 * q, r);
   float wo[3 * DEC_K0];
 #pragma unroll
   for (int i = 0; i < 3 * DEC_K0; ++i) wo[i] = __ldg(a.short_w + static_cast<size_t>(3 * h) * DEC_K0 + i);
   const float Dg = a.D[h];
   pdl_wait();
-  if (b >= a.M / a.T) return;
+  if (b >= a.M / a.T) return;  // (whole warps: b is the warp's row)
   const int L0 = a.len[b];
   // the carried state first, so that its loads are in flight with the outer pass
-  float s[S];
+  float st[4];
   if (L0 > 0) {
-    load_vec<S>(a.s_all + ((static_cast<size_t>(b) * a.slots + a.iir_cur[b]) * d + h) * S, s);
+    load_vec<4>(a.s_all + ((static_cast<size_t>(b) * a.slots + a.iir_cur[b]) * d + h) * S + 4 * q, st);
   } else {
 #pragma unroll
-    for (int j = 0; j < S; ++j) s[j] = 0.f;
+    for (int j = 0; j < 4; ++j) st[j] = 0.f;
   }
   float x2[DEC_T], x1v[DEC_T];
-  dec_outer(a, b, h0, lane, L0, wo, ub, x2, x1v);
+  dec_outer8(a, b, h0, ch, lane, L0, wo, ub, x2, x1v);
 #pragma unroll
   for (int t = 0; t < DEC_T; ++t) {
     if (t < a.T) {
-      float part[4];
+      float part = 0.f;
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        part[q] = 0.f;
-#pragma unroll
-        for (int j = 4 * q; j < 4 * q + 4; ++j) {
-          s[j] = fmaf(p[j], s[j], x1v[t]);
-          part[q] = fmaf(r[j], s[j], part[q]);
-        }
+      for (int j = 0; j < 4; ++j) {
+        st[j] = fmaf(p[j], st[j], x1v[t]);
+        part = fmaf(r[j], st[j], part);
       }
-      const float tot = (part[0] + part[1]) + (part[2] + part[3]);
-      const float yv = round_to<TD>(x2[t] * (tot + Dg * x1v[t]));
-      a.y[static_cast<size_t>(b * a.T + t) * a.ld_y + h] = from_f32<TD>(yv);
-      if (a.retain) store_vec<S>(a.s_all + ((static_cast<size_t>(b) * a.slots + t) * d + h) * S, s);
+      const float pair = part + __shfl_xor_sync(0xffffffffu, part, 1);
+      const float tot = pair + __shfl_xor_sync(0xffffffffu, pair, 2);
+      if (q == 0) {
+        const float yv = round_to<TD>(x2[t] * (tot + Dg * x1v[t]));
+        a.y[static_cast<size_t>(b * a.T + t) * a.ld_y + h] = from_f32<TD>(yv);
+      }
+      if (a.retain) store_vec<4>(a.s_all + ((static_cast<size_t>(b) * a.slots + t) * d + h) * S + 4 * q, st);
     }
   }
-  if (!a.retain) store_vec<S>(a.s_all + ((static_cast<size_t>(b) * a.slots + 0) * d + h) * S, s);
+  if (!a.retain) store_vec<4>(a.s_all + ((static_cast<size_t>(b) * a.slots + 0) * d + h) * S + 4 * q, st);
 }
 
 __global__ void rollback_kernel(int32_t* len, const int32_t* len0, int32_t* iir_cur, const int32_t* chunk,
@@ -714,7 +797,9 @@ int launch_hyena_t(const evs_model* m, evs_state* s, int layer, int B, int T, in
     const dim3 dgrid(d / 32, (B + DEC_ROWS - 1) / DEC_ROWS), dblock(32, DEC_ROWS);
     const size_t ub_bytes = sizeof(TD) * DEC_ROWS * DEC_T * 96;
     if (L.kind == EVS_LAYER_HCL) {
-      EVS_CUDA_TRY(evs_launch(hyena_iir_dec_kernel<TD>, dgrid, dblock, ub_bytes, st, s->use_pdl(), a));
+      EVS_CHECK_ARG(d % 8 == 0, "IIR channels must be a multiple of 8");
+      EVS_CUDA_TRY(evs_launch(hyena_iir_dec_kernel<TD>, dim3(d / 8, (B + DEC_ROWS - 1) / DEC_ROWS), dblock,
+                              sizeof(TD) * DEC_ROWS * DEC_T * 24, st, s->use_pdl(), a));
     } else {
       auto launch = [&](auto kern, int KI) -> int {
         const size_t smem =
