@@ -525,7 +525,7 @@ int evs_state_create(const evs_model* m, int max_batch, int max_seqlen, int max_
     s->tp_base[m->tp_rank] = static_cast<char*>(s->tp_region);
   }
   if (c.dtype == EVS_DTYPE_BF16) {
-    for (int t = 0; t < 3; ++t) {
+    for (int t = 0; t < GEMM_NMAPS; ++t) {
       const uint64_t ld = static_cast<uint64_t>(s->ld_act) * 2;
       EVS_TRY(make_tmap_2d_bf16(&s->tm_act_d[t], s->act, d, s->m_cap, ld, GEMM_BK, GEMM_NT[t]));
       EVS_TRY(make_tmap_2d_bf16(&s->tm_act_f[t], s->act, F, s->m_cap, ld, GEMM_BK, GEMM_NT[t]));

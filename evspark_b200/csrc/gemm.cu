@@ -182,14 +182,16 @@ __global__ void __launch_bounds__(192, 1)
 // a consumer reading one split computes 0 + sum = sum, so every row gets the bits of the split-K
 // path without writing and re-reading the per-split partial sums.  Two TMEM buffers alternate:
 // the MMA of split s + 2 waits until the epilogue has read split s.
-constexpr int SER_NT = 128;
+constexpr int SER_NT = 128;   // wide token tile (GEMM_NT[2])
+constexpr int SER_NT_N = 96;  // narrow token tile (GEMM_NT[3])
 // two CTAs per SM (registers <= 168): one CTA's epilogue and another's main loop overlap
+template <int NT>
 __global__ void __launch_bounds__(192, 2)
     gemm_tc_serial_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmA2,
                           const __grid_constant__ CUtensorMap tmB, float* __restrict__ ws, int N, int K, int M,
                           int splits, int dual, EvsDevErr* err) {
-  constexpr int NT = SER_NT;
   using C = TcCfg<NT>;
+  constexpr uint32_t TMEM_SER = 2 * NT <= 128 ? 128 : 256;  // two accumulators, a power of two
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -217,7 +219,7 @@ __global__ void __launch_bounds__(192, 2)
     fence_barrier_init();
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, 2 * NT);
+    tmem_alloc(tmem_slot, TMEM_SER);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -320,7 +322,7 @@ __global__ void __launch_bounds__(192, 2)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, 2 * NT);
+    tmem_dealloc(tmem_base, TMEM_SER);
   }
 }
 
@@ -537,16 +539,26 @@ int launch_gemm_tc_serial(const CUtensorMap* tmA, const CUtensorMap* tmA2, const
   EVS_CHECK_ARG(p.N % GEMM_BM == 0 && p.K % GEMM_BK == 0, "tcgen05 GEMM needs N % 128 == 0 and K % 64 == 0");
   EVS_CHECK_ARG(p.splits >= 1 && p.splits <= p.K / GEMM_BK, "bad split count");
   if (p.M <= 0) return EVS_OK;
-  using C = TcCfg<SER_NT>;
-  static std::atomic<unsigned long long> attr_devs{0};
-  EVS_TRY(smem_attr_once(attr_devs, reinterpret_cast<const void*>(gemm_tc_serial_kernel), C::SMEM));
-  dim3 grid((p.M + SER_NT - 1) / SER_NT, p.N / GEMM_BM, 1);
-  // tmB[2]: the activation map with box rows GEMM_NT[2] = SER_NT
-  static_assert(GEMM_NT[2] == SER_NT, "the serial kernel's token tile is the widest tile");
-  EVS_CUDA_TRY(evs_launch(gemm_tc_serial_kernel, grid, dim3(192), C::SMEM, st, pdl, *tmA, tmA2 ? *tmA2 : *tmA,
-                          tmB[2], ws, p.N, p.K, p.M, p.splits, p.dual, err));
-  evs_count_launch(1);
-  return EVS_OK;
+  static_assert(GEMM_NT[2] == SER_NT && GEMM_NT[3] == SER_NT_N, "the serial kernel's token tiles");
+  // the narrow token tile when its CTAs take no more rounds (two CTAs per SM) than the wide tile's:
+  // each CTA then does three quarters of the work (measured at 832 rows: -4 % on the in-, out- and
+  // w3 projections; the w1/w2 projection, one round more with it, +8 %).  The tile changes no bit
+  // (every token row runs the same MMA sequence and the same additions).
+  const long long tiles = p.N / GEMM_BM, slots = 2LL * 148;
+  auto rounds = [&](int nt) { return (static_cast<long long>((p.M + nt - 1) / nt) * tiles + slots - 1) / slots; };
+  const bool narrow = rounds(SER_NT_N) <= rounds(SER_NT);
+  auto launch = [&](auto kern, int nt, size_t smem, const CUtensorMap* tb, std::atomic<unsigned long long>& attr) -> int {
+    EVS_TRY(smem_attr_once(attr, reinterpret_cast<const void*>(kern), static_cast<int>(smem)));
+    dim3 grid((p.M + nt - 1) / nt, p.N / GEMM_BM, 1);
+    EVS_CUDA_TRY(evs_launch(kern, grid, dim3(192), smem, st, pdl, *tmA, tmA2 ? *tmA2 : *tmA, *tb, ws, p.N, p.K, p.M,
+                            p.splits, p.dual, err));
+    evs_count_launch(1);
+    return EVS_OK;
+  };
+  static std::atomic<unsigned long long> attr_w{0}, attr_n{0};
+  if (narrow)
+    return launch(gemm_tc_serial_kernel<SER_NT_N>, SER_NT_N, TcCfg<SER_NT_N>::SMEM, &tmB[3], attr_n);
+  return launch(gemm_tc_serial_kernel<SER_NT>, SER_NT, TcCfg<SER_NT>::SMEM, &tmB[2], attr_w);
 }
 
 int gemm_tile_index(int M) { return M <= GEMM_NT[0] ? 0 : (M <= GEMM_NT[1] ? 1 : 2); }

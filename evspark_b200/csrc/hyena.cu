@@ -382,10 +382,10 @@ __device__ __forceinline__ void store4_td(TD* dst, float a, float b, float c, fl
 // split partials are loaded as float4s by lanes 0..23 (one 16-byte chunk of the 96 channels each,
 // every position of a split in flight) and handed to the channel lanes through `ub` (the warp's
 // [DEC_T][96] TD buffer in shared memory: the rounded values are exact in TD).
-template <typename TD>
+template <typename TD, int DT>
 __device__ __forceinline__ void dec_outer(const HyArgs<TD>& a, int b, int h0, int lane, int L0,
-                                          const float (&wo)[3 * DEC_K0], TD* ub, float (&x2)[DEC_T],
-                                          float (&x1v)[DEC_T]) {
+                                          const float (&wo)[3 * DEC_K0], TD* ub, float (&x2)[DT],
+                                          float (&x1v)[DT]) {
   const int N3 = 3 * a.d;
   const size_t split_stride = static_cast<size_t>(a.M) * N3;
   const int T = a.T;
@@ -403,14 +403,14 @@ __device__ __forceinline__ void dec_outer(const HyArgs<TD>& a, int b, int h0, in
   if (lane < 24) {
     // positions t >= T load row T-1 again (unconditional loads stay in one block, all in flight)
     // and are never used
-    float4 u4[DEC_T];
+    float4 u4[DT];
 #pragma unroll
-    for (int t = 0; t < DEC_T; ++t) u4[t] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int t = 0; t < DT; ++t) u4[t] = make_float4(0.f, 0.f, 0.f, 0.f);
     const float* src = a.ws + static_cast<size_t>(b) * T * N3 + 3 * h0 + 4 * lane;
     for (int sp = 0; sp < a.splits; ++sp) {
       const float* ss = src + sp * split_stride;
 #pragma unroll
-      for (int t = 0; t < DEC_T; ++t) {
+      for (int t = 0; t < DT; ++t) {
         const float4 v = __ldg(reinterpret_cast<const float4*>(ss + static_cast<size_t>(min(t, T - 1)) * N3));
         u4[t].x += v.x;
         u4[t].y += v.y;
@@ -419,7 +419,7 @@ __device__ __forceinline__ void dec_outer(const HyArgs<TD>& a, int b, int h0, in
       }
     }
 #pragma unroll
-    for (int t = 0; t < DEC_T; ++t) {
+    for (int t = 0; t < DT; ++t) {
       const float r0 = round_to<TD>(u4[t].x), r1 = round_to<TD>(u4[t].y), r2 = round_to<TD>(u4[t].z),
                   r3 = round_to<TD>(u4[t].w);
       store4_td<TD>(ub + t * 96 + 4 * lane, r0, r1, r2, r3);
@@ -428,7 +428,7 @@ __device__ __forceinline__ void dec_outer(const HyArgs<TD>& a, int b, int h0, in
   }
   __syncwarp();
 #pragma unroll
-  for (int t = 0; t < DEC_T; ++t) {
+  for (int t = 0; t < DT; ++t) {
     x2[t] = 0.f;
     x1v[t] = 0.f;
     if (t < T) {
@@ -458,18 +458,26 @@ __device__ __forceinline__ void dec_outer(const HyArgs<TD>& a, int b, int h0, in
   }
 }
 
-// grid (d / 32, ceil(B / DEC_ROWS)), block (32, DEC_ROWS).  KI = inner filter length (7 or 128).
-// Shared memory: taps[32][tap_stride(KI)] f32 (channel c's weight of age a at taps[c][a]) | per
-// warp hist[KI-1+DEC_T][32] TD (x1v by position, the oldest history position first) | per warp
-// ub[DEC_T][96] TD (the outer pass's exchange).
-template <typename TD, bool FLIP, int KI>
+// grid (d / 32, ceil(B / DEC_ROWS)), block (32, DEC_ROWS).  KI = inner filter length (7 or 128);
+// DT = positions held in registers (the chunk length 13 of a verify block, or DT).  Shared
+// memory: taps[32][tap_stride(KI)] f32 (channel c's weight of age a at taps[c][a]) | per warp
+// x2s[DT][32] f32 (the gates, kept out of registers during the inner FIR) | per warp
+// hist[KI-1+DT][32] TD (x1v by position, the oldest history position first) | per warp
+// ub[DT][96] TD (the outer pass's exchange).
+template <int KI, int DT, typename TD>
+constexpr size_t fir_dec_smem() {
+  return sizeof(float) * 32 * tap_stride(KI) + sizeof(float) * DEC_ROWS * DT * 32 +
+         sizeof(TD) * DEC_ROWS * (KI - 1 + DT) * 32 + sizeof(TD) * DEC_ROWS * DT * 96;
+}
+template <typename TD, bool FLIP, int KI, int DT>
 __global__ void __launch_bounds__(32 * DEC_ROWS) hyena_fir_dec_kernel(HyArgs<TD> a) {
   pdl_trigger();
-  constexpr int H = KI - 1, WROWS = H + DEC_T, KS = tap_stride(KI);
+  constexpr int H = KI - 1, WROWS = H + DT, KS = tap_stride(KI);
   extern __shared__ __align__(16) float sm[];
   float* taps = sm;
-  TD* hist = reinterpret_cast<TD*>(taps + 32 * KS) + threadIdx.y * WROWS * 32;
-  TD* ub = reinterpret_cast<TD*>(taps + 32 * KS) + DEC_ROWS * WROWS * 32 + threadIdx.y * DEC_T * 96;
+  float* x2s = taps + 32 * KS + threadIdx.y * DT * 32;
+  TD* hist = reinterpret_cast<TD*>(taps + 32 * KS + DEC_ROWS * DT * 32) + threadIdx.y * WROWS * 32;
+  TD* ub = reinterpret_cast<TD*>(taps + 32 * KS + DEC_ROWS * DT * 32) + DEC_ROWS * WROWS * 32 + threadIdx.y * DT * 96;
   const int lane = threadIdx.x, h0 = blockIdx.x * 32, h = h0 + lane;
   const int b = blockIdx.y * DEC_ROWS + threadIdx.y;
   // the taps are weights: stage them before waiting for the in-projection.  The full-window weight
@@ -514,25 +522,29 @@ __global__ void __launch_bounds__(32 * DEC_ROWS) hyena_fir_dec_kernel(HyArgs<TD>
       *reinterpret_cast<int4*>(dst) = make_int4(0, 0, 0, 0);
   }
   cp_async_commit();
-  float x2[DEC_T], x1v[DEC_T];
-  dec_outer(a, b, h0, lane, L0, wo, ub, x2, x1v);
-  TD* ring_w = a.inner_ring + static_cast<size_t>(b) * a.cap_i * a.d + h;
+  {
+    float x2[DT], x1v[DT];
+    dec_outer<TD, DT>(a, b, h0, lane, L0, wo, ub, x2, x1v);
+    TD* ring_w = a.inner_ring + static_cast<size_t>(b) * a.cap_i * a.d + h;
 #pragma unroll
-  for (int t = 0; t < DEC_T; ++t) {
-    hist[(H + t) * 32 + lane] = from_f32<TD>(x1v[t]);
-    if (t < T) ring_w[static_cast<size_t>((L0 + t) & (a.cap_i - 1)) * a.d] = from_f32<TD>(x1v[t]);
+    for (int t = 0; t < DT; ++t) {
+      // x1v is rounded to TD: its history copy holds it exactly; x2 waits in shared memory
+      hist[(H + t) * 32 + lane] = from_f32<TD>(x1v[t]);
+      x2s[t * 32 + lane] = x2[t];
+      if (t < T) ring_w[static_cast<size_t>((L0 + t) & (a.cap_i - 1)) * a.d] = from_f32<TD>(x1v[t]);
+    }
   }
   cp_async_wait<0>();
   __syncwarp();  // the history rows the other lanes copied
-  float acc[DEC_T];
+  float acc[DT];
 #pragma unroll
-  for (int t = 0; t < DEC_T; ++t) acc[t] = 0.f;
+  for (int t = 0; t < DT; ++t) acc[t] = 0.f;
   if (FLIP || a.prefill || L0 >= H) {
     // every position uses the full window (positions before 0 hold zeros, which add nothing):
     // acc[t] += w(age) * x(L0 + t - age) for age = H .. 0, the window rotating one position a step
-    float win[DEC_T];
+    float win[DT];
 #pragma unroll
-    for (int t = 0; t < DEC_T; ++t) win[t] = to_f32(hist[t * 32 + lane]);
+    for (int t = 0; t < DT; ++t) win[t] = to_f32(hist[t * 32 + lane]);
     const float* tp = taps + lane * KS;
 #pragma unroll
     for (int a4 = H / 4; a4 >= 0; --a4) {
@@ -543,11 +555,11 @@ __global__ void __launch_bounds__(32 * DEC_ROWS) hyena_fir_dec_kernel(HyArgs<TD>
         const int age = 4 * a4 + e;
         if (age > H) continue;
 #pragma unroll
-        for (int t = 0; t < DEC_T; ++t) acc[t] = fmaf(wv[e], win[t], acc[t]);
+        for (int t = 0; t < DT; ++t) acc[t] = fmaf(wv[e], win[t], acc[t]);
         if (age > 0) {
 #pragma unroll
-          for (int t = 0; t < DEC_T - 1; ++t) win[t] = win[t + 1];
-          win[DEC_T - 1] = to_f32(hist[(H + DEC_T - age) * 32 + lane]);
+          for (int t = 0; t < DT - 1; ++t) win[t] = win[t + 1];
+          win[DT - 1] = to_f32(hist[(H + DT - age) * 32 + lane]);
         }
       }
     }
@@ -556,7 +568,7 @@ __global__ void __launch_bounds__(32 * DEC_ROWS) hyena_fir_dec_kernel(HyArgs<TD>
     // prefill): position P weights age a by w[min(P, K-1) - a]
     const float* wr = a.inner_w + static_cast<size_t>(h) * KI;
 #pragma unroll
-    for (int t = 0; t < DEC_T; ++t) {
+    for (int t = 0; t < DT; ++t) {
       if (t < T) {
         const int P = L0 + t, cs = min(P, H);
         float z = 0.f;
@@ -566,11 +578,11 @@ __global__ void __launch_bounds__(32 * DEC_ROWS) hyena_fir_dec_kernel(HyArgs<TD>
     }
   }
 #pragma unroll
-  for (int t = 0; t < DEC_T; ++t) {
+  for (int t = 0; t < DT; ++t) {
     if (t < T) {
       float z = acc[t];
-      if (FLIP) z = fmaf(Dg, x1v[t], z);
-      const float yv = round_to<TD>(x2[t] * round_to<TD>(z));
+      if (FLIP) z = fmaf(Dg, to_f32(hist[(H + t) * 32 + lane]), z);
+      const float yv = round_to<TD>(x2s[t * 32 + lane] * round_to<TD>(z));
       a.y[static_cast<size_t>(b * T + t) * a.ld_y + h] = from_f32<TD>(yv);
     }
   }
@@ -795,27 +807,34 @@ int launch_hyena_t(const evs_model* m, evs_state* s, int layer, int B, int T, in
                          (L.kind == EVS_LAYER_HCL ? a.S == 16 : (a.K == 7 || a.K == 128));
   if (dec_shape) {
     const dim3 dgrid(d / 32, (B + DEC_ROWS - 1) / DEC_ROWS), dblock(32, DEC_ROWS);
-    const size_t ub_bytes = sizeof(TD) * DEC_ROWS * DEC_T * 96;
     if (L.kind == EVS_LAYER_HCL) {
       EVS_CHECK_ARG(d % 8 == 0, "IIR channels must be a multiple of 8");
       EVS_CUDA_TRY(evs_launch(hyena_iir_dec_kernel<TD>, dim3(d / 8, (B + DEC_ROWS - 1) / DEC_ROWS), dblock,
                               sizeof(TD) * DEC_ROWS * DEC_T * 24, st, s->use_pdl(), a));
     } else {
-      auto launch = [&](auto kern, int KI) -> int {
-        const size_t smem =
-            sizeof(float) * 32 * tap_stride(KI) + sizeof(TD) * DEC_ROWS * (KI - 1 + DEC_T) * 32 + ub_bytes;
+      auto launch = [&](auto kern, size_t smem) -> int {
         EVS_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
         EVS_CUDA_TRY(evs_launch(kern, dgrid, dblock, smem, st, s->use_pdl(), a));
         return EVS_OK;
       };
-      if (L.kind == EVS_LAYER_HCM && a.K == 128)
-        EVS_TRY(launch(hyena_fir_dec_kernel<TD, true, 128>, 128));
-      else if (L.kind == EVS_LAYER_HCM)
-        EVS_TRY(launch(hyena_fir_dec_kernel<TD, true, 7>, 7));
-      else if (a.K == 128)
-        EVS_TRY(launch(hyena_fir_dec_kernel<TD, false, 128>, 128));
-      else
-        EVS_TRY(launch(hyena_fir_dec_kernel<TD, false, 7>, 7));
+      // 13 positions (a verify block of gamma = 12) held exactly, else DEC_T with the tail unused
+      const bool t13 = T == 13;
+      const bool flip = L.kind == EVS_LAYER_HCM;
+      if (a.K == 128) {
+        if (flip)
+          EVS_TRY(t13 ? launch(hyena_fir_dec_kernel<TD, true, 128, 13>, fir_dec_smem<128, 13, TD>())
+                      : launch(hyena_fir_dec_kernel<TD, true, 128, DEC_T>, fir_dec_smem<128, DEC_T, TD>()));
+        else
+          EVS_TRY(t13 ? launch(hyena_fir_dec_kernel<TD, false, 128, 13>, fir_dec_smem<128, 13, TD>())
+                      : launch(hyena_fir_dec_kernel<TD, false, 128, DEC_T>, fir_dec_smem<128, DEC_T, TD>()));
+      } else {
+        if (flip)
+          EVS_TRY(t13 ? launch(hyena_fir_dec_kernel<TD, true, 7, 13>, fir_dec_smem<7, 13, TD>())
+                      : launch(hyena_fir_dec_kernel<TD, true, 7, DEC_T>, fir_dec_smem<7, DEC_T, TD>()));
+        else
+          EVS_TRY(t13 ? launch(hyena_fir_dec_kernel<TD, false, 7, 13>, fir_dec_smem<7, 13, TD>())
+                      : launch(hyena_fir_dec_kernel<TD, false, 7, DEC_T>, fir_dec_smem<7, DEC_T, TD>()));
+      }
     }
     EVS_CUDA_TRY(cudaGetLastError());
     evs_count_launch(1);

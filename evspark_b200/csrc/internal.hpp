@@ -22,8 +22,10 @@ inline int smem_attr_once(std::atomic<unsigned long long>& done, const void* ker
 constexpr int GEMM_BM = 128;
 constexpr int GEMM_BK = 64;
 constexpr int TOK_TILE = 16;  // token rows per decode tile (MMA N)
-// token tiles (MMA N) of the projection kernel, chosen from the token count M
-constexpr int GEMM_NT[3] = {16, 64, 128};
+// token tiles (MMA N) of the projection kernel, chosen from the token count M; index 3 is the
+// serial-split kernel's narrow tile (its wide tile is GEMM_NT[2])
+constexpr int GEMM_NT[4] = {16, 64, 128, 96};
+constexpr int GEMM_NMAPS = 4;  // activation maps per operand (box rows GEMM_NT[i])
 constexpr int ATTN_BLOCK = 64;  // keys per attention partial (aligned at absolute positions)
 constexpr int EVS_TP_MAX = 8;   // channel-sharding ranks
 constexpr int ATTN_TCAP = 16;   // split-KV attention handles chunks of at most this many queries
@@ -125,11 +127,11 @@ struct evs_state {
   bool tp_connected = false;
   long long tp_epoch = 0;  // row-parallel reductions issued so far (same count on every rank)
   // activation buffer as GEMM B operand, K = d, K = local F and K = local d, box rows GEMM_NT[i]
-  CUtensorMap tm_act_d[3], tm_act_f[3], tm_act_l[3];
+  CUtensorMap tm_act_d[GEMM_NMAPS], tm_act_f[GEMM_NMAPS], tm_act_l[GEMM_NMAPS];
   // bf16: the w1/w2 projection's fused SwiGLU output [m_cap][F] (its own buffer: the projection's
   // other CTAs still read act while one CTA's epilogue writes), read by w3 through tm_gate
   void* gate = nullptr;
-  CUtensorMap tm_gate[3];
+  CUtensorMap tm_gate[GEMM_NMAPS];
   // profiling (evs_profile_start / evs_profile_stop)
   struct ProfRec {
     int kind;

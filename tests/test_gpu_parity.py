@@ -419,17 +419,19 @@ def test_7b_width_bf16_block_vs_oracle(cuda):
     model.close()
 
 
-def test_serial_split_prefill_equals_split_k_bitwise(cuda):
+@pytest.mark.parametrize("n_prompt", [700, 832])
+def test_serial_split_prefill_equals_split_k_bitwise(cuda, n_prompt):
     """A prefill chunk of >= 512 tokens runs the large projections with every split of the fixed
-    split plan in one CTA, storing the splits' running sum as a single split.  Its logits at every
-    position, and the verify block after it, equal a prefill in 64-token chunks (per-split partial
-    sums added by the consumers) bit for bit."""
+    split plan in one CTA, storing the splits' running sum as a single split (96- and 128-token
+    tiles at 700 tokens, 96-token tiles at 832).  Its logits at every position, and the verify
+    block after it, equal a prefill in 64-token chunks (per-split partial sums added by the
+    consumers) bit for bit."""
     from evspark_b200.config import EVO2_7B_SLICE
     from evspark_b200.model import TargetModel
 
     model = TargetModel.random(EVO2_7B_SLICE, seed=13, device=cuda, init_on="cuda")
     rng = np.random.default_rng(31)
-    prompt = rng.choice([65, 67, 71, 84], size=700)
+    prompt = rng.choice([65, 67, 71, 84], size=n_prompt)
     chunk = rng.choice([65, 67, 71, 84], size=13)
     pre_one, blk_one = _prefill_then_block(model, prompt, chunk, 1024)
     pre64, blk64 = _prefill_then_block(model, prompt, chunk, 64)
