@@ -195,25 +195,140 @@ __global__ void __cluster_dims__(NORM_CL, 1, 1) __launch_bounds__(NORM_THREADS)
   }
 }
 
-// ws holds the dual GEMM: virtual row (f / 64) * 128 + j * 64 + f % 64 is w_{j+1} feature f.
-// Each thread gates four consecutive features (one float4 of each half).
+// Many token rows of one split without channel sharding (the serial-split projections): a cluster
+// walks NORM_RPC consecutive rows with the next row's residual and partial sums in flight while the
+// current row's sum of squares is reduced.  A row's arithmetic is res_add_norm_kernel's (0 + the
+// split, the residual added, the same reduction order), so both kernels give the same bits.
+constexpr int NORM_RPC = 4;
 template <typename TD>
+__global__ void __cluster_dims__(NORM_CL, 1, 1) __launch_bounds__(NORM_THREADS)
+    res_add_norm_rows_kernel(const float* __restrict__ part, int M, float* __restrict__ resid,
+                             const float* __restrict__ scale, TD* __restrict__ act, int ld_act, int d, float eps,
+                             float* __restrict__ ring, int ring_len, const int32_t* __restrict__ len, int T,
+                             unsigned long long* __restrict__ tags, const unsigned long long* __restrict__ fwd_seq,
+                             unsigned long long tag_hi) {
+  pdl_trigger();
+  cg::cluster_group cluster = cg::this_cluster();
+  const int rank = static_cast<int>(cluster.block_rank());
+  const int cpc = d / NORM_CL, n4 = cpc / 4;
+  const int c_base = rank * cpc;
+  float4 sc[NORM_VPT];
+#pragma unroll
+  for (int v = 0; v < NORM_VPT; ++v) {
+    const int c4 = threadIdx.x + v * NORM_THREADS;
+    if (c4 < n4) sc[v] = __ldg(reinterpret_cast<const float4*>(scale + c_base + c4 * 4));
+  }
+  pdl_wait();
+  __shared__ float red[NORM_THREADS / 32];
+  __shared__ float cta_ss;
+  const int row0 = blockIdx.y * NORM_RPC, row_end = min(M, row0 + NORM_RPC);
+  float4 xr[NORM_VPT], pv[NORM_VPT];
+  auto load_row = [&](int row, float4 (&x)[NORM_VPT], float4 (&q)[NORM_VPT]) {
+#pragma unroll
+    for (int v = 0; v < NORM_VPT; ++v) {
+      const int c4 = threadIdx.x + v * NORM_THREADS;
+      if (c4 < n4) {
+        const size_t o = static_cast<size_t>(row) * d + c_base + c4 * 4;
+        x[v] = *reinterpret_cast<const float4*>(resid + o);
+        q[v] = *reinterpret_cast<const float4*>(part + o);
+      }
+    }
+  };
+  load_row(row0, xr, pv);
+  for (int row = row0; row < row_end; ++row) {
+    float4 xn[NORM_VPT], pn[NORM_VPT];
+    if (row + 1 < row_end) load_row(row + 1, xn, pn);
+    const int b = row / T, t = row % T;
+    float* cap = nullptr;
+    if (ring != nullptr && t >= T - ring_len) {
+      const int P = len[b] + t;
+      cap = ring + (static_cast<size_t>(b) * ring_len + P % ring_len) * d;
+      if (tags != nullptr && rank == 0 && threadIdx.x == 0)
+        tags[static_cast<size_t>(b) * ring_len + P % ring_len] = evs_capture_tag(tag_hi, b, *fwd_seq);
+    }
+    float4 r[NORM_VPT];
+    float ss = 0.f;
+#pragma unroll
+    for (int v = 0; v < NORM_VPT; ++v) {
+      const int c4 = threadIdx.x + v * NORM_THREADS;
+      if (c4 < n4) {
+        const int c = c_base + c4 * 4;
+        float4 x = xr[v];
+        x.x += 0.f + pv[v].x;
+        x.y += 0.f + pv[v].y;
+        x.z += 0.f + pv[v].z;
+        x.w += 0.f + pv[v].w;
+        *reinterpret_cast<float4*>(resid + static_cast<size_t>(row) * d + c) = x;
+        if (cap != nullptr) *reinterpret_cast<float4*>(cap + c) = x;
+        ss = fmaf(x.x, x.x, ss);
+        ss = fmaf(x.y, x.y, ss);
+        ss = fmaf(x.z, x.z, ss);
+        ss = fmaf(x.w, x.w, ss);
+        r[v] = x;
+      }
+    }
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float a = 0.f;
+      for (int w = 0; w < NORM_THREADS / 32; ++w) a += red[w];
+      cta_ss = a;
+    }
+    cluster.sync();
+    float tot = 0.f;
+    for (int q = 0; q < NORM_CL; ++q) tot += *cluster.map_shared_rank(&cta_ss, q);
+    cluster.sync();  // peers stay resident (and cta_ss unchanged) until every CTA has read the sums
+    const float inv = 1.0f / sqrtf(tot / static_cast<float>(d) + eps);
+#pragma unroll
+    for (int v = 0; v < NORM_VPT; ++v) {
+      const int c4 = threadIdx.x + v * NORM_THREADS;
+      if (c4 < n4) {
+        const int c = c_base + c4 * 4;
+        const float4 x = r[v];
+        store4<TD>(act + static_cast<size_t>(row) * ld_act + c,
+                   make_float4(x.x * inv * sc[v].x, x.y * inv * sc[v].y, x.z * inv * sc[v].z, x.w * inv * sc[v].w));
+      }
+    }
+#pragma unroll
+    for (int v = 0; v < NORM_VPT; ++v) {
+      xr[v] = xn[v];
+      pv[v] = pn[v];
+    }
+  }
+}
+
+// ws holds the dual GEMM: virtual row (f / 64) * 128 + j * 64 + f % 64 is w_{j+1} feature f.
+// Each thread gates four consecutive features (one float4 of each half) of RPT token rows
+// (rows blockIdx.y * RPT ..; their loads in flight together when the projection left one split).
+template <typename TD, int RPT>
 __global__ void __launch_bounds__(ROW_THREADS) swiglu_kernel(const float* __restrict__ ws, int splits, int M, int F,
                                                             TD* __restrict__ act, int ld_act) {
   pdl_trigger();
   pdl_wait();
-  const int row = blockIdx.y;
   const int f = (blockIdx.x * ROW_THREADS + threadIdx.x) * 4;
   if (f >= F) return;
   const int N2 = 2 * F;
   const int v1 = (f / 64) * 128 + (f % 64), v2 = v1 + 64;
-  float4 g1 = make_float4(0.f, 0.f, 0.f, 0.f), g2 = g1;
-  const float* r = ws + static_cast<size_t>(row) * N2;
-  split_sum4<false>(g1, r + v1, static_cast<size_t>(M) * N2, splits);
-  split_sum4<false>(g2, r + v2, static_cast<size_t>(M) * N2, splits);
-  store4<TD>(act + static_cast<size_t>(row) * ld_act + f,
-             make_float4(swiglu_gate(g1.x, g2.x), swiglu_gate(g1.y, g2.y), swiglu_gate(g1.z, g2.z),
-                         swiglu_gate(g1.w, g2.w)));
+  float4 g1[RPT], g2[RPT];
+#pragma unroll
+  for (int i = 0; i < RPT; ++i) {
+    const int row = blockIdx.y * RPT + i;
+    g1[i] = g2[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (row < M) {
+      const float* r = ws + static_cast<size_t>(row) * N2;
+      split_sum4<false>(g1[i], r + v1, static_cast<size_t>(M) * N2, splits);
+      split_sum4<false>(g2[i], r + v2, static_cast<size_t>(M) * N2, splits);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < RPT; ++i) {
+    const int row = blockIdx.y * RPT + i;
+    if (row < M)
+      store4<TD>(act + static_cast<size_t>(row) * ld_act + f,
+                 make_float4(swiglu_gate(g1[i].x, g2[i].x), swiglu_gate(g1[i].y, g2[i].y),
+                             swiglu_gate(g1[i].z, g2[i].z), swiglu_gate(g1[i].w, g2[i].w)));
+  }
 }
 
 __global__ void logits_kernel(const float* __restrict__ ws, int splits, int M, int V, int T, int out_T, int t0,
@@ -309,6 +424,22 @@ int launch_res_add_norm(const evs_model* m, evs_state* s, int M, int splits, con
   EVS_CHECK_ARG(d % (NORM_CL * 4) == 0 && d <= NORM_CL * NORM_THREADS * 4 * NORM_VPT && s->ld_act % 4 == 0,
                 "d_model must be a multiple of 32 and at most 16384");
   EVS_CHECK_ARG(parts.R >= 1 && parts.R <= EVS_TP_MAX, "bad partial-sum ranks");
+  if (parts.R == 1 && splits == 1 && M >= 512) {
+    const dim3 grid(NORM_CL, (M + NORM_RPC - 1) / NORM_RPC);
+    const unsigned long long* seq = static_cast<const unsigned long long*>(s->d_fwd_seq);
+    unsigned long long* tg = ring ? s->cap_tag : nullptr;
+    const int32_t* ln = static_cast<const int32_t*>(s->d_len);
+    if (m->cfg.dtype == EVS_DTYPE_BF16)
+      EVS_CUDA_TRY(evs_launch(res_add_norm_rows_kernel<__nv_bfloat16>, grid, dim3(NORM_THREADS), 0, st, s->use_pdl(),
+                              parts.buf[0], M, s->resid, scale, static_cast<__nv_bfloat16*>(s->act), s->ld_act, d,
+                              m->cfg.eps, ring, s->ring_len, ln, T, tg, seq, s->tag_hi));
+    else
+      EVS_CUDA_TRY(evs_launch(res_add_norm_rows_kernel<float>, grid, dim3(NORM_THREADS), 0, st, s->use_pdl(),
+                              parts.buf[0], M, s->resid, scale, static_cast<float*>(s->act), s->ld_act, d, m->cfg.eps,
+                              ring, s->ring_len, ln, T, tg, seq, s->tag_hi));
+    evs_count_launch(1);
+    return EVS_OK;
+  }
   if (m->cfg.dtype == EVS_DTYPE_BF16)
     EVS_CUDA_TRY(evs_launch(res_add_norm_kernel<__nv_bfloat16>, dim3(NORM_CL, M), dim3(NORM_THREADS), 0, st,
                             s->use_pdl(), parts, splits, M, s->resid, scale, static_cast<__nv_bfloat16*>(s->act),
@@ -327,14 +458,18 @@ int launch_res_add_norm(const evs_model* m, evs_state* s, int M, int splits, con
 int launch_swiglu(const evs_model* m, evs_state* s, int M, int splits, cudaStream_t st) {
   const int F = m->Fl;  // this rank's MLP features
   EVS_CHECK_ARG(F % 64 == 0, "mlp_inner must be a multiple of 64");
-  dim3 grid((F / 4 + ROW_THREADS - 1) / ROW_THREADS, M);
+  // many rows of one split (the serial-split projection): four rows per thread, their loads in flight
+  const bool four = M >= 256 && splits == 1;
+  const int rpt = four ? 4 : 1;
+  dim3 grid((F / 4 + ROW_THREADS - 1) / ROW_THREADS, (M + rpt - 1) / rpt);
   if (m->cfg.dtype == EVS_DTYPE_BF16)
-    EVS_CUDA_TRY(evs_launch(swiglu_kernel<__nv_bfloat16>, grid, dim3(ROW_THREADS), 0, st, s->use_pdl(),
-                            static_cast<const float*>(s->ws), splits, M, F, static_cast<__nv_bfloat16*>(s->act),
-                            s->ld_act));
+    EVS_CUDA_TRY(evs_launch(four ? swiglu_kernel<__nv_bfloat16, 4> : swiglu_kernel<__nv_bfloat16, 1>, grid,
+                            dim3(ROW_THREADS), 0, st, s->use_pdl(), static_cast<const float*>(s->ws), splits, M, F,
+                            static_cast<__nv_bfloat16*>(s->act), s->ld_act));
   else
-    EVS_CUDA_TRY(evs_launch(swiglu_kernel<float>, grid, dim3(ROW_THREADS), 0, st, s->use_pdl(),
-                            static_cast<const float*>(s->ws), splits, M, F, static_cast<float*>(s->act), s->ld_act));
+    EVS_CUDA_TRY(evs_launch(four ? swiglu_kernel<float, 4> : swiglu_kernel<float, 1>, grid, dim3(ROW_THREADS), 0, st,
+                            s->use_pdl(), static_cast<const float*>(s->ws), splits, M, F,
+                            static_cast<float*>(s->act), s->ld_act));
   evs_count_launch(1);
   return EVS_OK;
 }
