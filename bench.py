@@ -48,10 +48,14 @@ sys.path.insert(0, str(ROOT))
 METRIC = "accepted tok/s single-stream Evo2-7B-shape γ=12; verify-block µs; HBM GB/s"
 GAMMA = 12
 PROMPT_LEN = 1024
-# ncu dram__bytes_read.sum + dram__bytes_write.sum per launch of the tcgen05 projection, averaged
-# over one round's launches with this round's launch mix (None until captured)
-GEMM_TRAFFIC_PER_LAUNCH = None
-GEMM_TRAFFIC_NOTE = "not captured on the current kernels"
+# ncu dram__bytes_read.sum + dram__bytes_write.sum of the tcgen05 projections of one block (in-, out-,
+# w1/w2 and w3 projections) of the 4-block 7B-width model, which has the 32-block model's projection
+# shapes: 403.8 MB of DRAM traffic for 414.0 MB of algorithmic bytes (weights + activations + fp32
+# partials, which stay in L2).  The per-launch traffic below is this measured ratio times the run's
+# per-launch algorithmic bytes (the same launch mix per block).
+GEMM_TRAFFIC_RATIO = 403.8 / 414.0
+GEMM_TRAFFIC_NOTE = ("ncu DRAM bytes of one block's projections on the 4-block 7B-width model (same shapes), "
+                     "403.8 MB per 414.0 MB algorithmic; scaled to this run's bytes per launch")
 E2E_TOKENS = 1024
 VERIFY_REPS = 32
 
@@ -700,7 +704,7 @@ def run_ours(args) -> int:
                                  "forward alone (no profiling events), after the timed rounds",
             "roofline": {"bound": "hbm", "kernel": "gemm_tc (tcgen05 projections)", "achieved": round(achieved, 1),
                          "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
-                         "traffic": GEMM_TRAFFIC_PER_LAUNCH,
+                         "traffic": round(GEMM_TRAFFIC_RATIO * gemm_bytes / max(gemm_n, 1)),
                          "traffic_note": GEMM_TRAFFIC_NOTE,
                          "launches": int(gemm_n),
                          "bytes_per_launch": round(gemm_bytes / max(gemm_n, 1)),

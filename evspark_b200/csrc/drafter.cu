@@ -174,8 +174,10 @@ __global__ void __launch_bounds__(EPI_THREADS) draft_epi_kernel(DraftEpiArgs a) 
   if constexpr (MODE == EPI_BIAS_NORM || MODE == EPI_IN_NORM || MODE == EPI_RESID_NORM || MODE == EPI_TOK_IN_NORM) {
     extern __shared__ float vrow[];  // the row before the norm
     __shared__ float red[33];
-    const int row = blockIdx.x, N = a.N;
-    if (a.m_dev != nullptr && row >= *a.m_dev) return;
+    const int N = a.N;
+    const int M_rows = a.m_dev != nullptr ? min(a.M, *a.m_dev) : a.M;
+    for (int row = blockIdx.x; row < M_rows; row += gridDim.x) {
+    if (row != static_cast<int>(blockIdx.x)) __syncthreads();  // the previous row's vrow and red are read
     const size_t r0 = static_cast<size_t>(row) * N;
     float ss = 0.f;
     // EPI_VPT columns c = tid + 256 j per pass; the split loads of all of them are in flight together
@@ -246,6 +248,7 @@ __global__ void __launch_bounds__(EPI_THREADS) draft_epi_kernel(DraftEpiArgs a) 
     const float rms = sqrtf(red[32] / static_cast<float>(N) + a.eps);
     float* o = a.out + r0;
     for (int c = threadIdx.x; c < N; c += EPI_THREADS) o[c] = a.scale[c] * (vrow[c] / rms);
+    }
   } else {
     const size_t i = static_cast<size_t>(blockIdx.x) * EPI_THREADS + threadIdx.x;
     if (i >= MN) return;
@@ -884,29 +887,33 @@ int64_t drafter_numel(const evs_drafter_config& c, int id) {
 
 // out[M][N] = X W^T (fp32, split-K partials reduced in split order); m_dev: optional device-side
 // row count at most M
+// m_hint: the row count the grids are sized for when m_dev is given (the kernels walk any rows
+// beyond it), so that a launch sized for the largest count does not carry idle CTAs
 int sgemm(evs_drafter* dr, const float* W, const float* X, int ldx, float* out, int N, int K, int M,
-          cudaStream_t st, const int32_t* m_dev = nullptr) {
+          cudaStream_t st, const int32_t* m_dev = nullptr, int m_hint = 0) {
   const GemmPlan p = gemm_plan_f32_drafter(N, K, M);
   EVS_CHECK_RANGE(static_cast<size_t>(p.splits) * M * N <= dr->ws_floats, "drafter workspace too small");
-  if (p.splits == 1) return launch_gemm_simt(W, nullptr, X, ldx, EVS_DTYPE_FP32, p, out, st, true, m_dev);
-  EVS_TRY(launch_gemm_simt(W, nullptr, X, ldx, EVS_DTYPE_FP32, p, dr->ws, st, true, m_dev));
-  return launch_reduce_splits(dr->ws, p.splits, M, N, nullptr, out, st, true, m_dev);
+  if (p.splits == 1) return launch_gemm_simt(W, nullptr, X, ldx, EVS_DTYPE_FP32, p, out, st, true, m_dev, m_hint);
+  EVS_TRY(launch_gemm_simt(W, nullptr, X, ldx, EVS_DTYPE_FP32, p, dr->ws, st, true, m_dev, m_hint));
+  return launch_reduce_splits(dr->ws, p.splits, M, N, nullptr, out, st, true, m_dev, m_hint);
 }
 
 inline unsigned blocks_for(size_t n, int t) { return static_cast<unsigned>((n + t - 1) / t); }
 
 // projection partials into the workspace (no reduction), then the fused epilogue `mode` over them
 int sgemm_epi(evs_drafter* dr, const float* W, const float* X, int ldx, int N, int K, int M, int mode,
-              DraftEpiArgs e, cudaStream_t st) {
+              DraftEpiArgs e, cudaStream_t st, int m_hint = 0) {
   const GemmPlan p = gemm_plan_f32_drafter(N, K, M);
   EVS_CHECK_RANGE(static_cast<size_t>(p.splits) * M * N <= dr->ws_floats, "drafter workspace too small");
-  EVS_TRY(launch_gemm_simt(W, nullptr, X, ldx, EVS_DTYPE_FP32, p, dr->ws, st, true, e.m_dev));
+  EVS_TRY(launch_gemm_simt(W, nullptr, X, ldx, EVS_DTYPE_FP32, p, dr->ws, st, true, e.m_dev, m_hint));
   e.ws = dr->ws;
   e.splits = p.splits;
   e.M = M;
   e.N = N;
   const bool norm = mode == EPI_BIAS_NORM || mode == EPI_IN_NORM || mode == EPI_RESID_NORM || mode == EPI_TOK_IN_NORM;
-  const dim3 grid = norm ? dim3(M) : dim3(blocks_for(static_cast<size_t>(M) * N, EPI_THREADS));
+  const int rows = e.m_dev != nullptr && m_hint > 0 ? std::min(M, m_hint) : M;  // (norm CTAs walk the rest)
+  EVS_CHECK_ARG(norm || e.m_dev == nullptr || m_hint <= 0, "a row hint needs a norm epilogue");
+  const dim3 grid = norm ? dim3(rows) : dim3(blocks_for(static_cast<size_t>(M) * N, EPI_THREADS));
   const size_t smem = norm ? sizeof(float) * N : 0;
   EVS_CHECK_ARG(smem <= 48 * 1024, "drafter width too large for the fused norm");
   switch (mode) {
@@ -1104,8 +1111,9 @@ int evs_draft_propose(evs_drafter* dr, const evs_state* s, const int64_t* anchor
                             dr->ctx_in));
     DraftEpiArgs e = epi(T[EVS_D_CTX_B], dr->ctx, T[EVS_D_CTX_NORM], nullptr, nullptr, 1, eps);
     e.m_dev = dr->ccount;
+    // grids for about two new context positions per row (a speculative round accepts k + 1)
     EVS_TRY(sgemm_epi(dr, T[EVS_D_CTX_W], dr->ctx_in, c.n_inject * H, d, c.n_inject * H, B * CW, EPI_BIAS_NORM, e,
-                      st));
+                      st, std::min(B * CW, 2 * B + 16)));
   }
   // ---- h = in_proj(embed([anchor, MASK...])) + pos (rows of the token table), and the first
   // layer's pre-norm of h into xb ----
@@ -1134,8 +1142,9 @@ int evs_draft_propose(evs_drafter* dr, const evs_state* s, const int64_t* anchor
     EVS_CUDA_TRY(evs_launch(build_kv_kernel, dim3(kv_rows), dim3(256), 0, st, true, static_cast<const float*>(dr->xb),
                             static_cast<const float*>(dr->ctx), Bg, ctxr ? static_cast<const int32_t*>(dr->ccount) : nullptr,
                             d, dr->kv_in));
-    EVS_TRY(sgemm(dr, L[EVS_D_K], dr->kv_in, d, dr->kb, d, d, kv_rows, st, kv_m));
-    EVS_TRY(sgemm(dr, L[EVS_D_V], dr->kv_in, d, dr->vb, d, d, kv_rows, st, kv_m));
+    const int kv_hint = ctxr ? std::min(kv_rows, Bg + 2 * B + 16) : 0;
+    EVS_TRY(sgemm(dr, L[EVS_D_K], dr->kv_in, d, dr->kb, d, d, kv_rows, st, kv_m, kv_hint));
+    EVS_TRY(sgemm(dr, L[EVS_D_V], dr->kv_in, d, dr->vb, d, d, kv_rows, st, kv_m, kv_hint));
     float* ckl = dr->ck + static_cast<size_t>(l) * B_cap * DR_CR * d;
     float* cvl = dr->cv + static_cast<size_t>(l) * B_cap * DR_CR * d;
     if (ctxr)

@@ -346,80 +346,83 @@ __global__ void __launch_bounds__(SK_WARPS * 32) gemm_skinny_f32_kernel(const fl
   pdl_trigger();
   pdl_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * SK_ROWS, sp = blockIdx.y, m0 = blockIdx.z * SK_TOK;
+  const int n0 = blockIdx.x * SK_ROWS, sp = blockIdx.y;
   // a device-side row count (rows decided by an earlier kernel): token groups past it have no work
-  // (M stays the partial buffers' row stride)
+  // (M stays the partial buffers' row stride).  The grid may hold fewer token groups than M: a CTA
+  // then takes groups blockIdx.z, blockIdx.z + gridDim.z, ... (the arithmetic of a group is the same)
   const int M_rows = m_dev != nullptr ? min(M, *m_dev) : M;
-  if (m0 >= M_rows) return;
-  const int mt = min(SK_TOK, M_rows - m0);
-  const int kb = sp * kc, ke = min(K, kb + kc);  // this CTA's K range, staged SK_KC_MAX columns at a time
-  const float* wr[SK_R];
+  for (int m0 = blockIdx.z * SK_TOK; m0 < M_rows; m0 += gridDim.z * SK_TOK) {
+    if (m0 != static_cast<int>(blockIdx.z) * SK_TOK) __syncthreads();  // the previous group's partials are read
+    const int mt = min(SK_TOK, M_rows - m0);
+    const int kb = sp * kc, ke = min(K, kb + kc);  // this CTA's K range, staged SK_KC_MAX columns at a time
+    const float* wr[SK_R];
 #pragma unroll
-  for (int i = 0; i < SK_R; ++i) {
-    const int v = n0 + warp * SK_R + i;
-    const int vr = v < N ? v : N - 1;
-    if (dual) {
-      const int f = (vr / 128) * 64 + (vr % 64);
-      wr[i] = ((vr % 128) < 64 ? W : W2) + static_cast<size_t>(f) * K;
-    } else {
-      wr[i] = W + static_cast<size_t>(vr) * K;
+    for (int i = 0; i < SK_R; ++i) {
+      const int v = n0 + warp * SK_R + i;
+      const int vr = v < N ? v : N - 1;
+      if (dual) {
+        const int f = (vr / 128) * 64 + (vr % 64);
+        wr[i] = ((vr % 128) < 64 ? W : W2) + static_cast<size_t>(f) * K;
+      } else {
+        wr[i] = W + static_cast<size_t>(vr) * K;
+      }
     }
-  }
-  float acc[SK_R][SK_TOK];
+    float acc[SK_R][SK_TOK];
 #pragma unroll
-  for (int i = 0; i < SK_R; ++i)
+    for (int i = 0; i < SK_R; ++i)
 #pragma unroll
-    for (int m = 0; m < SK_TOK; ++m) acc[i][m] = 0.f;
-  for (int cb = kb; cb < ke; cb += SK_KC_MAX) {
-    const int kw = min(SK_KC_MAX, ke - cb);  // multiple of 4
-    // stage X[m0 .. m0+mt)[cb .. cb+kw) as xs[m][k - cb] (row stride SK_KC_MAX)
-    const int c4 = kw / 4;
-    if (cb != kb) __syncthreads();  // every warp is done with the previous stage
-    for (int i = threadIdx.x; i < mt * c4; i += blockDim.x) {
-      const int m = i / c4, c = i - m * c4;
-      cp_async16(sk_sm + m * SK_KC_MAX + 4 * c, X + static_cast<size_t>(m0 + m) * ldx + cb + 4 * c);
-    }
-    cp_async_commit();
-    cp_async_wait<0>();
-    __syncthreads();
+      for (int m = 0; m < SK_TOK; ++m) acc[i][m] = 0.f;
+    for (int cb = kb; cb < ke; cb += SK_KC_MAX) {
+      const int kw = min(SK_KC_MAX, ke - cb);  // multiple of 4
+      // stage X[m0 .. m0+mt)[cb .. cb+kw) as xs[m][k - cb] (row stride SK_KC_MAX)
+      const int c4 = kw / 4;
+      if (cb != kb) __syncthreads();  // every warp is done with the previous stage
+      for (int i = threadIdx.x; i < mt * c4; i += blockDim.x) {
+        const int m = i / c4, c = i - m * c4;
+        cp_async16(sk_sm + m * SK_KC_MAX + 4 * c, X + static_cast<size_t>(m0 + m) * ldx + cb + 4 * c);
+      }
+      cp_async_commit();
+      cp_async_wait<0>();
+      __syncthreads();
 #pragma unroll 2
-    for (int k = 4 * lane; k < kw; k += 128) {
-      float4 w4[SK_R];
+      for (int k = 4 * lane; k < kw; k += 128) {
+        float4 w4[SK_R];
 #pragma unroll
-      for (int i = 0; i < SK_R; ++i) w4[i] = __ldg(reinterpret_cast<const float4*>(wr[i] + cb + k));
+        for (int i = 0; i < SK_R; ++i) w4[i] = __ldg(reinterpret_cast<const float4*>(wr[i] + cb + k));
 #pragma unroll
-      for (int m = 0; m < SK_TOK; ++m) {
-        if (m < mt) {
-          const float4 x4 = *reinterpret_cast<const float4*>(sk_sm + m * SK_KC_MAX + k);
+        for (int m = 0; m < SK_TOK; ++m) {
+          if (m < mt) {
+            const float4 x4 = *reinterpret_cast<const float4*>(sk_sm + m * SK_KC_MAX + k);
 #pragma unroll
-          for (int i = 0; i < SK_R; ++i) {
-            acc[i][m] = fmaf(w4[i].x, x4.x, acc[i][m]);
-            acc[i][m] = fmaf(w4[i].y, x4.y, acc[i][m]);
-            acc[i][m] = fmaf(w4[i].z, x4.z, acc[i][m]);
-            acc[i][m] = fmaf(w4[i].w, x4.w, acc[i][m]);
+            for (int i = 0; i < SK_R; ++i) {
+              acc[i][m] = fmaf(w4[i].x, x4.x, acc[i][m]);
+              acc[i][m] = fmaf(w4[i].y, x4.y, acc[i][m]);
+              acc[i][m] = fmaf(w4[i].z, x4.z, acc[i][m]);
+              acc[i][m] = fmaf(w4[i].w, x4.w, acc[i][m]);
+            }
           }
         }
       }
     }
-  }
-  __syncthreads();  // xs no longer needed: reuse it for the lane partials
-  float* red = sk_sm + warp * (SK_R * SK_TOK * 32);
+    __syncthreads();  // xs no longer needed: reuse it for the lane partials
+    float* red = sk_sm + warp * (SK_R * SK_TOK * 32);
 #pragma unroll
-  for (int i = 0; i < SK_R; ++i)
+    for (int i = 0; i < SK_R; ++i)
 #pragma unroll
-    for (int m = 0; m < SK_TOK; ++m) {
-      const int v = i * SK_TOK + m;
-      red[v * 32 + (lane ^ (v & 31))] = acc[i][m];
+      for (int m = 0; m < SK_TOK; ++m) {
+        const int v = i * SK_TOK + m;
+        red[v * 32 + (lane ^ (v & 31))] = acc[i][m];
+      }
+    __syncwarp();
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int v = lane + 32 * h;
+      const int i = v / SK_TOK, m = v % SK_TOK;
+      float sum = 0.f;
+      for (int j = 0; j < 32; ++j) sum += red[v * 32 + (j ^ (v & 31))];
+      const int n = n0 + warp * SK_R + i;
+      if (m < mt && n < N) ws[(static_cast<size_t>(sp) * M + m0 + m) * N + n] = sum;
     }
-  __syncwarp();
-#pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    const int v = lane + 32 * h;
-    const int i = v / SK_TOK, m = v % SK_TOK;
-    float sum = 0.f;
-    for (int j = 0; j < 32; ++j) sum += red[v * 32 + (j ^ (v & 31))];
-    const int n = n0 + warp * SK_R + i;
-    if (m < mt && n < N) ws[(static_cast<size_t>(sp) * M + m0 + m) * N + n] = sum;
   }
 }
 
@@ -427,10 +430,12 @@ __global__ void reduce_splits_kernel(const float* __restrict__ ws, int splits, i
                                      int N, float* __restrict__ out, const int32_t* __restrict__ m_dev) {
   pdl_trigger();
   pdl_wait();
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= MN || (m_dev != nullptr && i / N >= *m_dev)) return;
-  float acc = split_sum(ws + i, MN, splits);
-  out[i] = bias ? acc + bias[i % N] : acc;
+  // grid-stride over the rows below the device-side count (the grid may cover fewer)
+  const int lim = m_dev != nullptr ? min(MN, *m_dev * N) : MN;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < lim; i += gridDim.x * blockDim.x) {
+    float acc = split_sum(ws + i, MN, splits);
+    out[i] = bias ? acc + bias[i % N] : acc;
+  }
 }
 
 typedef CUresult (*PFN_encodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -577,7 +582,7 @@ int launch_gemm_tc(const CUtensorMap* tmA, const CUtensorMap* tmA2, const CUtens
 }
 
 int launch_gemm_simt(const void* W, const void* W2, const void* X, int ldx, int dtype, const GemmPlan& p, float* ws,
-                     cudaStream_t st, bool pdl, const int32_t* m_dev) {
+                     cudaStream_t st, bool pdl, const int32_t* m_dev, int m_hint) {
   if (p.M <= 0) return EVS_OK;
   EVS_CHECK_ARG(dtype == EVS_DTYPE_FP32, "CUDA-core projection is fp32 only");
   EVS_CHECK_ARG(p.K % 4 == 0 && ldx % 4 == 0 && reinterpret_cast<uintptr_t>(X) % 16 == 0 &&
@@ -587,7 +592,10 @@ int launch_gemm_simt(const void* W, const void* W2, const void* X, int ldx, int 
   static std::atomic<unsigned long long> attr_devs{0};
   EVS_TRY(smem_attr_once(attr_devs, reinterpret_cast<const void*>(gemm_skinny_f32_kernel), static_cast<int>(SK_SMEM)));
   const size_t smem = SK_SMEM;
-  dim3 grid((p.N + SK_ROWS - 1) / SK_ROWS, p.splits, (p.M + SK_TOK - 1) / SK_TOK);
+  // with a device-side row count, token groups for about m_hint rows (the CTAs walk the rest)
+  const int ngroups = (p.M + SK_TOK - 1) / SK_TOK;
+  const int zg = m_dev != nullptr && m_hint > 0 ? std::min(ngroups, (m_hint + SK_TOK - 1) / SK_TOK) : ngroups;
+  dim3 grid((p.N + SK_ROWS - 1) / SK_ROWS, p.splits, zg);
   EVS_CUDA_TRY(evs_launch(gemm_skinny_f32_kernel, grid, dim3(SK_WARPS * 32), smem, st, pdl,
                           static_cast<const float*>(W), static_cast<const float*>(W2 ? W2 : W),
                           static_cast<const float*>(X), ldx, ws, p.N, p.K, p.M, p.kchunk, p.dual, m_dev));
@@ -596,11 +604,12 @@ int launch_gemm_simt(const void* W, const void* W2, const void* X, int ldx, int 
 }
 
 int launch_reduce_splits(const float* ws, int splits, int M, int N, const float* bias, float* out, cudaStream_t st,
-                         bool pdl, const int32_t* m_dev) {
+                         bool pdl, const int32_t* m_dev, int m_hint) {
   const int MN = M * N;
   if (MN <= 0) return EVS_OK;
-  EVS_CUDA_TRY(evs_launch(reduce_splits_kernel, dim3((MN + 255) / 256), dim3(256), 0, st, pdl, ws, splits, MN, bias,
-                          N, out, m_dev));
+  const int rows = m_dev != nullptr && m_hint > 0 ? std::min(M, m_hint) : M;
+  EVS_CUDA_TRY(evs_launch(reduce_splits_kernel, dim3((rows * N + 255) / 256), dim3(256), 0, st, pdl, ws, splits, MN,
+                          bias, N, out, m_dev));
   evs_count_launch(1);
   return EVS_OK;
 }

@@ -159,7 +159,8 @@ GemmPlan gemm_plan_f32(int N, int K, int M, int dual);
 GemmPlan gemm_plan_f32_drafter(int N, int K, int M);
 // out[m][n] = sum of the split partials (in split order) + bias[n]
 int launch_reduce_splits(const float* ws, int splits, int M, int N, const float* bias, float* out, cudaStream_t st,
-                         bool pdl = false, const int32_t* m_dev = nullptr);
+                         bool pdl = false, const int32_t* m_dev = nullptr,
+                         int m_hint = 0);
 // pdl: launch with programmatic stream serialization (see pdl_wait)
 // tmB: three maps of the activations with box rows GEMM_NT[0..2]; the tile is chosen from p.M
 int gemm_tile_index(int M);
@@ -175,7 +176,7 @@ int launch_gemm_tc_serial(const CUtensorMap* tmA, const CUtensorMap* tmA2, const
                           float* ws, EvsDevErr* err, cudaStream_t st, bool pdl = false);
 // m_dev: optional device-side row count (at most p.M, which sizes the grid)
 int launch_gemm_simt(const void* W, const void* W2, const void* X, int ldx, int dtype, const GemmPlan& p, float* ws,
-                     cudaStream_t st, bool pdl = false, const int32_t* m_dev = nullptr);
+                     cudaStream_t st, bool pdl = false, const int32_t* m_dev = nullptr, int m_hint = 0);
 int make_tmap_2d_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t row_stride_bytes,
                       uint32_t box_inner, uint32_t box_outer);
 
