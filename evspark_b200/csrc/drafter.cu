@@ -55,6 +55,7 @@ struct RingPtrs {
 
 constexpr int DR_CR = 128;  // cache slots per row: covers the ctx_window (<= 64) positions a call reads
 constexpr int DRAFT_ATTN_ROWS_MIN_B = 4;  // rows from which one attention CTA per (head, row) serves all queries
+                                          // (fewer rows: one CTA per (head, row, query))
 
 // Which context rows of a call lack a current projection: row b reads positions L-n .. L-1
 // (n = min(CW, L)); position P is current when its slot holds P with the capture tag that the
@@ -369,13 +370,15 @@ __global__ void __launch_bounds__(128) draft_attn_kernel(const float* q, const f
 // thread, same reductions, same add order), so the two kernels give the same bits.
 __global__ void __launch_bounds__(128) draft_attn_rows_kernel(const float* q, const float* kd, const float* vd,
                                                               const float* ck, const float* cv, const int32_t* len,
-                                                              int with_ctx, int CW, int g, int d, int heads,
+                                                              int with_ctx, int CW, int g, int d, int heads, int qpc,
                                                               float* y) {
   pdl_trigger();
   pdl_wait();
   extern __shared__ __align__(16) float da_sm[];
   __shared__ float red[8];
   const int hh = blockIdx.x, b = blockIdx.y;
+  // this CTA's queries t0 .. t1-1 (blockIdx.z chunk of qpc); the draft keys up to t1-1 are staged
+  const int t0 = blockIdx.z * qpc, t1 = min(g, t0 + qpc);
   const int hd = d / heads;
   const int L = len[b];
   const int nctx = with_ctx ? min(CW, L) : 0;
@@ -391,7 +394,7 @@ __global__ void __launch_bounds__(128) draft_attn_rows_kernel(const float* q, co
   };
   // 16-byte loads, eight per thread in flight (context slots before position 0 are never visible
   // and never read)
-  const int h4 = hd / 4, n4 = nk * h4;
+  const int h4 = hd / 4, n4 = (CW + t1) * h4;
   for (int i0 = threadIdx.x; i0 < n4; i0 += 8 * blockDim.x) {
     float4 kx[8], vx[8];
 #pragma unroll
@@ -415,14 +418,14 @@ __global__ void __launch_bounds__(128) draft_attn_rows_kernel(const float* q, co
       }
     }
   }
-  for (int i = threadIdx.x; i < g * h4; i += blockDim.x) {
+  for (int i = threadIdx.x; i < (t1 - t0) * h4; i += blockDim.x) {
     const int t = i / h4, e4 = i - t * h4;
     *reinterpret_cast<float4*>(Qs + 4 * i) =
-        *reinterpret_cast<const float4*>(q + (static_cast<size_t>(b) * g + t) * d + hh * hd + 4 * e4);
+        *reinterpret_cast<const float4*>(q + (static_cast<size_t>(b) * g + t0 + t) * d + hh * hd + 4 * e4);
   }
   __syncthreads();
-  for (int t = 0; t < g; ++t) {
-    const float* qr = Qs + t * hd;
+  for (int t = t0; t < t1; ++t) {
+    const float* qr = Qs + (t - t0) * hd;
     for (int j = threadIdx.x; j < nk; j += blockDim.x) {
       const bool vis = j < CW ? j < nctx : (j - CW) <= t;
       float s = -CUDART_INF_F;
@@ -841,9 +844,21 @@ __global__ void conf_kernel(const float* h, const float* tok_in, const int64_t* 
   if (row >= rows) return;
   const float* pe = tok_in + static_cast<size_t>(prev[row]) * d;
   float acc = 0.f;
-  for (int c = lane; c < 2 * d; c += 32) {
-    const float x = c < d ? h[static_cast<size_t>(row) * d + c] : pe[c - d];
-    acc = fmaf(x, w[c], acc);
+  // lane's elements c = lane, lane + 32, ... in order; sixteen of them (and their weights) loaded
+  // at a time
+  for (int c0 = lane; c0 < 2 * d; c0 += 32 * 16) {
+    float x[16], wv[16];
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      const int c = c0 + 32 * k;
+      if (c < 2 * d) {
+        x[k] = c < d ? h[static_cast<size_t>(row) * d + c] : pe[c - d];
+        wv[k] = w[c];
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < 16; ++k)
+      if (c0 + 32 * k < 2 * d) acc = fmaf(x[k], wv[k], acc);
   }
   acc = warp_sum(acc);
   if (lane == 0) conf[row] = 1.0f / (1.0f + expf(-(acc + bias[0])));
@@ -1156,12 +1171,14 @@ int evs_draft_propose(evs_drafter* dr, const evs_state* s, const int64_t* anchor
     const int hd = d / c.n_heads, nk = CW + g;
     const size_t rows_smem =
         sizeof(float) * ((static_cast<size_t>(nk) * (hd + 1) + 3) / 4 * 4 + static_cast<size_t>(nk) * hd + g * hd + nk);
-    if (B >= DRAFT_ATTN_ROWS_MIN_B && rows_smem <= 48 * 1024 && hd % 4 == 0 && d % 4 == 0) {
-      EVS_CUDA_TRY(evs_launch(draft_attn_rows_kernel, dim3(c.n_heads, B), dim3(128), rows_smem, st, true,
-                              static_cast<const float*>(dr->q), static_cast<const float*>(dr->kb),
+    if (rows_smem <= 48 * 1024 && hd % 4 == 0 && d % 4 == 0) {
+      // few rows: one CTA per query as well (the staging is repeated, the CTAs run side by side)
+      const int qpc = B >= DRAFT_ATTN_ROWS_MIN_B ? g : 1;
+      EVS_CUDA_TRY(evs_launch(draft_attn_rows_kernel, dim3(c.n_heads, B, (g + qpc - 1) / qpc), dim3(128), rows_smem,
+                              st, true, static_cast<const float*>(dr->q), static_cast<const float*>(dr->kb),
                               static_cast<const float*>(dr->vb), static_cast<const float*>(ckl),
                               static_cast<const float*>(cvl), static_cast<const int32_t*>(s->d_len),
-                              static_cast<int>(ctxr), CW, g, d, c.n_heads, dr->y));
+                              static_cast<int>(ctxr), CW, g, d, c.n_heads, qpc, dr->y));
     } else {
       EVS_CUDA_TRY(evs_launch(draft_attn_kernel, dim3(dim3(g, c.n_heads, B)), dim3(128), 0, st, true,
                               static_cast<const float*>(dr->q), static_cast<const float*>(dr->kb),
