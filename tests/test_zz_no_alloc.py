@@ -93,3 +93,28 @@ def test_noalloc_rejects_sizes_beyond_the_fixed_scratch(cuda):
     with pytest.raises(ValueError, match="scratch"):
         N.call("evs_gemm_bf16_noalloc", W.data_ptr(), X.data_ptr(), out.data_ptr(), 12288, 4096, 512,
                N.stream_ptr())
+
+
+def test_noalloc_on_a_second_device(cuda):
+    """The shared-memory opt-in, the scratch array and the error word are per device: a call on a
+    second GPU after calls on the first gives the same bits as on the first."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two CUDA devices")
+    from evspark_b200 import _native as N
+
+    N_, K, M = 4096, 4096, 13
+    outs = []
+    for dev in (0, 1, 0):
+        d = torch.device("cuda", dev)
+        with torch.cuda.device(d):
+            g = torch.Generator(device=d).manual_seed(5)
+            W = torch.randn(N_, K, device=d, generator=g).to(torch.bfloat16)
+            X = torch.randn(M, K, device=d, generator=g).to(torch.bfloat16)
+            out = torch.full((M, N_), float("nan"), device=d)
+            N.call("evs_gemm_bf16_noalloc", W.data_ptr(), X.data_ptr(), out.data_ptr(), N_, K, M,
+                   torch.cuda.current_stream(d).cuda_stream)
+            torch.cuda.synchronize(d)
+            exact = X.float() @ W.float().T
+            assert (out - exact).abs().max().item() <= TOL_REL * exact.abs().max().item()
+            outs.append(out.cpu())
+    assert torch.equal(outs[0], outs[1]) and torch.equal(outs[0], outs[2])
