@@ -57,7 +57,7 @@ GEMM_TRAFFIC_RATIO = 403.8 / 414.0
 GEMM_TRAFFIC_NOTE = ("ncu DRAM bytes of one block's projections on the 4-block 7B-width model (same shapes), "
                      "403.8 MB per 414.0 MB algorithmic; scaled to this run's bytes per launch")
 E2E_TOKENS = 1024
-VERIFY_REPS = 32
+VERIFY_REPS = 200
 
 
 def peaks() -> tuple[float, str]:
@@ -389,7 +389,7 @@ def run_tp(args) -> int:
     nd = NeuralDraftModel(model, drafter, dcfg.inject_layers)
     prompt = markov_prompt(L, seed=20260821)  # the same stream on every rank
     rounds = args.warmup + args.steps
-    ip = model.initialize_inference_params(L + (rounds + 4) * (GAMMA + 1) + 64, max_chunk=args.prefill_chunk or None)
+    ip = model.initialize_inference_params(L + (rounds + 4) * (GAMMA + 1) + VERIFY_REPS + 64, max_chunk=args.prefill_chunk or None)
     nd.capture_begin()
     t0 = time.perf_counter()
     prefill(model, torch.as_tensor(prompt[:-1], device=device)[None], ip)
