@@ -501,6 +501,9 @@ __device__ __forceinline__ float fold_acc(float acc, float a, float accj, float 
 // block order, from an empty accumulator; then the groups in group order.  Folding one group's
 // result into the empty accumulator is exact, so contexts of one group fold block by block.
 constexpr int ATTN_GROUP = 16;
+// per-block partials of contexts up to this many blocks are folded on both levels by the combine
+// kernel alone (a sequential fold per query, as short as the group fold kernel's launch)
+constexpr int ATTN_COMBINE_BLOCKS = 64;
 
 // Split-KV (chunks of at most QT queries, i.e. one pass): grid (block ranges, H, B), ATTN_THREADS
 // threads.  A CTA walks bpc consecutive ATTN_BLOCK-key blocks of one head; for each it computes the
@@ -680,7 +683,10 @@ __global__ void attn_group_fold_kernel(float* __restrict__ part, const int32_t* 
 }
 
 // grid (M, H), Dh threads: the query's partial slots j = 0, jstep, 2 jstep, ... <= its last block
-// folded in order (jstep = 1: the blocks of a one-group context; ATTN_GROUP: the group results)
+// folded in order (jstep = 1: the blocks of a one-group context; ATTN_GROUP: the group results).
+// jstep = 0: per-block partials of a context of a few groups, both levels of the fold here (each
+// group's blocks from an empty accumulator, then the group into the total: attn_group_fold_kernel
+// followed by jstep = ATTN_GROUP, without its launch).
 template <typename TD>
 __global__ void attn_combine_kernel(const float* __restrict__ part, const int32_t* __restrict__ len, int T, int d,
                                     int H, int Dh, int nblk_cap, int tcap, int jstep, TD* __restrict__ out,
@@ -695,7 +701,18 @@ __global__ void attn_combine_kernel(const float* __restrict__ part, const int32_
   float m = -CUDART_INF_F, l = 0.f, acc = 0.f;
   const float* pb = part + ((static_cast<size_t>(b) * H + h) * nblk_cap * tcap + t) * (Dh + 2);
   const size_t jstride = static_cast<size_t>(tcap) * (Dh + 2);
-  fold_blocks(pb, jstride, Dh, dd, 0, jmax, jstep, m, l, acc);
+  if (jstep > 0) {
+    fold_blocks(pb, jstride, Dh, dd, 0, jmax, jstep, m, l, acc);
+  } else {
+    for (int jb = 0; jb <= jmax; jb += ATTN_GROUP) {
+      float gm = -CUDART_INF_F, gl = 0.f, ga = 0.f;
+      fold_blocks(pb, jstride, Dh, dd, jb, min(jmax, jb + ATTN_GROUP - 1), 1, gm, gl, ga);
+      if (gm == -CUDART_INF_F) continue;
+      float a, bg;
+      fold_stats(m, l, gm, gl, a, bg);
+      acc = fold_acc(acc, a, ga, bg);
+    }
+  }
   out[static_cast<size_t>(row) * ld_out + h * Dh + dd] = from_f32<TD>(acc / l);
 }
 
@@ -858,6 +875,8 @@ int launch_attention_t(const evs_model* m, evs_state* s, int layer, int B, int T
   int jstep = 1;
   if (group_fold) {
     jstep = ATTN_GROUP;
+  } else if (kv_blocks > ATTN_GROUP && kv_blocks <= ATTN_COMBINE_BLOCKS) {
+    jstep = 0;  // a few groups: both fold levels in the combine
   } else if (kv_blocks > ATTN_GROUP) {
     const int ngroups = (kv_blocks + ATTN_GROUP - 1) / ATTN_GROUP;
     EVS_CUDA_TRY(evs_launch(attn_group_fold_kernel, dim3(M, H, ngroups), dim3(Dh), 0, st, pdl, s->attn_part,

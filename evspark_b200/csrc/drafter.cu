@@ -629,14 +629,25 @@ __global__ void __launch_bounds__(128) serial_head_warp_kernel(const float* U, c
         for (int s2 = 0; s2 < PT; ++s2) row[tid + 128 * s2] = exp(row[tid + 128 * s2] - xm);
       }
       __syncthreads();
+      if (!onehot) {
+        // normalise: the pairwise sum in warp 0's layout, then every thread divides its elements
+        if (warp == 0) {
+#pragma unroll
+          for (int t = 0; t < 16; ++t) p[t] = act ? row[base + 8 * t] : 0.0;
+          const double z = warp_pw_sum<NL>(p, lane);
+          if (lane == 0) dsh[1] = z;
+        }
+        __syncthreads();
+        const double z = dsh[1];
+        const bool bad = !(z > 0.0) || !isfinite(z);
+#pragma unroll
+        for (int s2 = 0; s2 < PT; ++s2) row[tid + 128 * s2] = bad ? 1.0 / V : row[tid + 128 * s2] / z;
+        __syncthreads();
+      }
       if (warp == 0) {
 #pragma unroll
         for (int t = 0; t < 16; ++t) p[t] = act ? row[base + 8 * t] : 0.0;
         if (!onehot) {
-          const double z = warp_pw_sum<NL>(p, lane);
-          const bool bad = !(z > 0.0) || !isfinite(z);
-#pragma unroll
-          for (int t = 0; t < 16; ++t) p[t] = act ? (bad ? 1.0 / V : p[t] / z) : 0.0;
           if (top_k > 0 && top_k < V) {
             unsigned keep = 0;
             double m[16];
