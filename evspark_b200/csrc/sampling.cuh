@@ -24,6 +24,7 @@ struct SampScratch {
   int iv[32];
   double scal[2];
   int icount;
+  int cidx[VMAX];  // sampling: indices of the nonzero weights, in index order
 };
 
 // leaf ranges of the pairwise-summation tree of n values, left to right
@@ -164,39 +165,51 @@ __device__ inline int block_argmax(const double* row, int V, SampScratch* sc) {
   return out;
 }
 
-// w[i] <- w[0] + ... + w[i], added left to right (numpy cumsum order), one thread.  Loads are
-// batched 32 at a time so that only the add chain is serial, and zero entries are skipped: adding
-// +0 to a non-negative running sum never changes it, so the result is the same bits.
-__device__ inline void seq_cumsum(double* w, int V) {
-  double c = 0.0;
-  for (int i0 = 0; i0 < V; i0 += 32) {
-    double v[32];
-#pragma unroll
-    for (int k = 0; k < 32; ++k) v[k] = i0 + k < V ? w[i0 + k] : 0.0;
-#pragma unroll
-    for (int k = 0; k < 32; ++k) {
-      if (v[k] != 0.0) c += v[k];
-      if (i0 + k < V) w[i0 + k] = c;
-    }
-  }
-}
-
-// sample_categorical(w, u) with w already clipped at 0 (w is overwritten); whole block
+// sample_categorical(w, u) with w already clipped at 0 (w is overwritten); whole block.  numpy:
+// cumsum left to right, then the count of prefixes with prefix / total <= u.  Adding +0 leaves a
+// running sum unchanged, so the prefixes are those of the nonzero weights in index order: warp 0
+// compacts them (in place, a ballot per 32 indices), lane 0 sums them in order, and since the
+// prefixes never decrease the count is the index of the first nonzero whose prefix / total > u
+// (every index before it has a prefix at most the previous one's), or V if there is none.
 __device__ inline int block_sample_clipped(double* w, int V, double u, SampScratch* sc) {
   const double s = block_pairwise_sum(w, V, sc);
   const bool bad = !(s > 0.0) || !isfinite(s);
   for (int i = threadIdx.x; i < V; i += blockDim.x) w[i] = bad ? 1.0 / V : w[i] / s;
   __syncthreads();
-  if (threadIdx.x == 0) {  // left-to-right cumulative sum (numpy cumsum order)
-    seq_cumsum(w, V);
-    sc->icount = 0;
+  if (threadIdx.x < 32) {
+    const unsigned full = 0xffffffffu;
+    const int lane = threadIdx.x;
+    int nnz = 0;
+    for (int i0 = 0; i0 < V; i0 += 32) {
+      const int i = i0 + lane;
+      const double v = i < V ? w[i] : 0.0;
+      const unsigned m = __ballot_sync(full, v != 0.0);
+      if (v != 0.0) {
+        const int pos = nnz + __popc(m & ((1u << lane) - 1u));
+        w[pos] = v;  // pos <= i: this round's values were read above, later rounds read higher indices
+        sc->cidx[pos] = i;
+      }
+      nnz += __popc(m);
+    }
+    __syncwarp();
+    if (lane == 0) {
+      double c = 0.0;
+      for (int n = 0; n < nnz; ++n) {
+        c += w[n];
+        w[n] = c;
+      }
+    }
+    __syncwarp();
+    const double last = nnz > 0 ? w[nnz - 1] : 0.0;
+    int first = nnz;
+    for (int n = lane; n < nnz; n += 32)
+      if (!(w[n] / last <= u)) {
+        first = n;
+        break;
+      }
+    for (int o = 16; o > 0; o >>= 1) first = min(first, __shfl_xor_sync(full, first, o));
+    if (lane == 0) sc->icount = first < nnz ? sc->cidx[first] : V;
   }
-  __syncthreads();
-  const double last = w[V - 1];
-  int cnt = 0;
-  for (int i = threadIdx.x; i < V; i += blockDim.x) cnt += (w[i] / last <= u) ? 1 : 0;
-  for (int o = 16; o > 0; o >>= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, o);
-  if ((threadIdx.x & 31) == 0 && cnt) atomicAdd(&sc->icount, cnt);
   __syncthreads();
   const int idx = sc->icount;
   __syncthreads();
