@@ -465,51 +465,9 @@ __global__ void __launch_bounds__(128) draft_attn_rows_kernel(const float* q, co
   }
 }
 
-// serial Markov head, one warp per row, for V = 128 * NL (NL = 1, 2, 4).  Lane L holds the 16
-// elements leaf * 128 + j + 8t (leaf = L / 8, j = L % 8, t = 0..15) in registers: exactly the
-// slots of numpy's pairwise sum (8 running partials per 128-element leaf), so sums are formed as
-// lane-local partials in t order -> ((r0+r1)+(r2+r3))+((r4+r5)+(r6+r7)) over the 8 lanes of a leaf
-// -> the leaf tree, and equal numpy's.  Argmax and top-k are warp shuffles (lowest index on ties);
-// only the left-to-right cumulative sum of sampling runs sequentially, in shared memory.
-template <int NL>
-__device__ __forceinline__ double warp_pw_sum(const double (&v)[16], int lane) {
-  double r = 0.0;
-#pragma unroll
-  for (int t = 0; t < 16; ++t) r += v[t];
-  const unsigned full = 0xffffffffu;
-  r = r + __shfl_xor_sync(full, r, 1);
-  r = r + __shfl_xor_sync(full, r, 2);
-  r = r + __shfl_xor_sync(full, r, 4);  // every lane of a leaf: that leaf's sum
-  if (NL >= 2) r = r + __shfl_xor_sync(full, r, 8);
-  if (NL >= 4) r = r + __shfl_xor_sync(full, r, 16);
-  (void)lane;
-  return r;
-}
-
-// index of the max of the row (lowest index on ties); every lane gets it
-__device__ __forceinline__ int warp_argmax16(const double (&v)[16], int base, double* best_out) {
-  double best = v[0];
-  int bi = base;
-#pragma unroll
-  for (int t = 1; t < 16; ++t)
-    if (v[t] > best) {  // indices grow with t: ties keep the lower index
-      best = v[t];
-      bi = base + 8 * t;
-    }
-  const unsigned full = 0xffffffffu;
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const double ov = __shfl_xor_sync(full, best, o);
-    const int oi = __shfl_xor_sync(full, bi, o);
-    if (ov > best || (ov == best && oi < bi)) {
-      best = ov;
-      bi = oi;
-    }
-  }
-  if (best_out) *best_out = best;
-  return bi;
-}
-
+// serial Markov head for V = 128 * NL (NL = 1, 2, 4), with the warp-level layout of
+// warp_pw_sum / warp_argmax16 (sampling.cuh) for the sums, argmax and top-k; only the
+// left-to-right cumulative sum of sampling runs sequentially, in shared memory.
 // 4 warps: the elementwise fp32/fp64 math of a step is spread over 128 threads (element i on
 // thread i % 128), through shared memory; warp 0 gathers the row into the pairwise-sum layout
 // above (lane L: elements leaf*128 + j + 8t) for the sums, argmax and top-k.

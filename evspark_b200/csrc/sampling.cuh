@@ -216,6 +216,51 @@ __device__ inline int block_sample_clipped(double* w, int V, double u, SampScrat
   return idx < V ? idx : V - 1;
 }
 
+// Warp-level forms for V = 128 * NL (NL = 1, 2, 4): lane L holds the 16 elements
+// leaf * 128 + j + 8t (leaf = L / 8, j = L % 8, t = 0..15) in registers, exactly the slots of the
+// pairwise sum above (8 running partials per 128-element leaf), so a sum is formed as lane-local
+// partials in t order -> ((r0+r1)+(r2+r3))+((r4+r5)+(r6+r7)) over the 8 lanes of a leaf -> the leaf
+// tree, the same additions as block_pairwise_sum.  Argmax is by warp shuffles (lowest index on
+// ties), as block_argmax.
+template <int NL>
+__device__ __forceinline__ double warp_pw_sum(const double (&v)[16], int lane) {
+  double r = 0.0;
+#pragma unroll
+  for (int t = 0; t < 16; ++t) r += v[t];
+  const unsigned full = 0xffffffffu;
+  r = r + __shfl_xor_sync(full, r, 1);
+  r = r + __shfl_xor_sync(full, r, 2);
+  r = r + __shfl_xor_sync(full, r, 4);  // every lane of a leaf: that leaf's sum
+  if (NL >= 2) r = r + __shfl_xor_sync(full, r, 8);
+  if (NL >= 4) r = r + __shfl_xor_sync(full, r, 16);
+  (void)lane;
+  return r;
+}
+
+// index of the max of the row (lowest index on ties); every lane gets it
+__device__ __forceinline__ int warp_argmax16(const double (&v)[16], int base, double* best_out) {
+  double best = v[0];
+  int bi = base;
+#pragma unroll
+  for (int t = 1; t < 16; ++t)
+    if (v[t] > best) {  // indices grow with t: ties keep the lower index
+      best = v[t];
+      bi = base + 8 * t;
+    }
+  const unsigned full = 0xffffffffu;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const double ov = __shfl_xor_sync(full, best, o);
+    const int oi = __shfl_xor_sync(full, bi, o);
+    if (ov > best || (ov == best && oi < bi)) {
+      best = ov;
+      bi = oi;
+    }
+  }
+  if (best_out) *best_out = best;
+  return bi;
+}
+
 // apply_transform of the fp64 row e[0..V) (shared memory; overwritten) into out (global or
 // shared).  Whole block participates.  keep / masked: shared scratch of V.
 __device__ inline void transform_row(double* e, int V, double temperature, int top_k, double* out, int* keep,

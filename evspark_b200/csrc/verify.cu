@@ -37,6 +37,71 @@ __global__ void __launch_bounds__(256) transform_kernel(const void* __restrict__
   transform_row(e, V, temperature, top_k, probs + static_cast<size_t>(r) * V, keep, masked, &sc);
 }
 
+// V = 128 NL: one warp per row in the warp layout of warp_pw_sum (lane L holds elements
+// leaf * 128 + j + 8t), every reduction a warp shuffle, no block barrier; element by element the
+// operations of transform_row, and its sums and argmaxes in the same order, so the same bits.
+template <int NL>
+__global__ void __launch_bounds__(32) transform_warp_kernel(const void* __restrict__ logits, int f64,
+                                                            double temperature, int top_k,
+                                                            double* __restrict__ probs) {
+  constexpr int V = 128 * NL;
+  const int r = blockIdx.x, lane = threadIdx.x, leaf = lane >> 3, j = lane & 7;
+  const bool act = leaf < NL;
+  const int base = act ? leaf * 128 + j : 0;
+  double e[16];
+#pragma unroll
+  for (int t = 0; t < 16; ++t) {
+    const size_t i = static_cast<size_t>(r) * V + base + 8 * t;
+    e[t] = !act ? -CUDART_INF
+                : (f64 ? static_cast<const double*>(logits)[i] : static_cast<double>(static_cast<const float*>(logits)[i]));
+  }
+  double* out = probs + static_cast<size_t>(r) * V;
+  if (temperature <= 0.0) {
+    const int am = warp_argmax16(e, base, nullptr);
+#pragma unroll
+    for (int t = 0; t < 16; ++t)
+      if (act) out[base + 8 * t] = base + 8 * t == am ? 1.0 : 0.0;
+    return;
+  }
+#pragma unroll
+  for (int t = 0; t < 16; ++t)
+    if (act) e[t] = e[t] / temperature;
+  double mx;
+  warp_argmax16(e, base, &mx);
+#pragma unroll
+  for (int t = 0; t < 16; ++t) e[t] = act ? exp(e[t] - mx) : 0.0;
+  const double z = warp_pw_sum<NL>(e, lane);
+  const bool bad = !(z > 0.0) || !isfinite(z);
+#pragma unroll
+  for (int t = 0; t < 16; ++t) e[t] = act ? (bad ? 1.0 / V : e[t] / z) : 0.0;
+  if (top_k <= 0 || top_k >= V) {
+#pragma unroll
+    for (int t = 0; t < 16; ++t)
+      if (act) out[base + 8 * t] = e[t];
+    return;
+  }
+  unsigned keep = 0;
+  double m[16];
+#pragma unroll
+  for (int t = 0; t < 16; ++t) m[t] = act ? e[t] : -CUDART_INF;
+  for (int k = 0; k < top_k; ++k) {
+    const int am2 = warp_argmax16(m, base, nullptr);
+#pragma unroll
+    for (int t = 0; t < 16; ++t)
+      if (act && base + 8 * t == am2) {
+        keep |= 1u << t;
+        m[t] = -CUDART_INF;
+      }
+  }
+#pragma unroll
+  for (int t = 0; t < 16; ++t) m[t] = (keep >> t & 1u) ? e[t] : 0.0;
+  const double ms = warp_pw_sum<NL>(m, lane);
+  const bool bad2 = !(ms > 0.0) || !isfinite(ms);
+#pragma unroll
+  for (int t = 0; t < 16; ++t)
+    if (act) out[base + 8 * t] = (keep >> t & 1u) ? (bad2 ? 1.0 / top_k : m[t] / ms) : 0.0;
+}
+
 // one CTA per row b; every block-wide helper is called by all threads (uniform control flow)
 __global__ void __launch_bounds__(256) verify_kernel(const double* __restrict__ p, const double* __restrict__ q,
                                                      const int64_t* __restrict__ x, const double* __restrict__ u,
@@ -255,7 +320,14 @@ int launch_transform(const void* logits, int logits_fp64, int rows, int V, doubl
                      double* probs, cudaStream_t st) {
   EVS_CHECK_ARG(V > 0 && V <= VMAX, "vocabulary must be in [1, 1024]");
   if (rows <= 0) return EVS_OK;
-  transform_kernel<<<rows, 256, 0, st>>>(logits, logits_fp64, V, temperature, top_k, probs);
+  if (V == 512)
+    transform_warp_kernel<4><<<rows, 32, 0, st>>>(logits, logits_fp64, temperature, top_k, probs);
+  else if (V == 256)
+    transform_warp_kernel<2><<<rows, 32, 0, st>>>(logits, logits_fp64, temperature, top_k, probs);
+  else if (V == 128)
+    transform_warp_kernel<1><<<rows, 32, 0, st>>>(logits, logits_fp64, temperature, top_k, probs);
+  else
+    transform_kernel<<<rows, 256, 0, st>>>(logits, logits_fp64, V, temperature, top_k, probs);
   EVS_CUDA_TRY(cudaGetLastError());
   evs_count_launch(1);
   return EVS_OK;
