@@ -746,16 +746,25 @@ __global__ void __launch_bounds__(ATTN_THREADS, 4) attn_fused_kernel(const TD* _
 #pragma unroll
   for (int i = 0; i < ACC_N; ++i) cc[i] = gc[i] = 0.f;
   const int jlast = (L0 + tq0 + nq - 1) / ATTN_BLOCK;
+  // K and V of the next block in flight while this block computes (as in attn_block_kernel)
+  const TD* kvb = kv + static_cast<size_t>(b) * Lmax * 2 * HD + static_cast<size_t>(h) * Dh;
+  auto nk_of = [&](int j) { return min(ATTN_BLOCK, Lend - j * ATTN_BLOCK); };
+  stage_k(sm, kvb, HD, Dh, nk_of(0));
+  stage_v(sm, kvb, HD, Dh, nk_of(0));
   for (int j = 0; j <= jlast; ++j) {
     const int k0 = j * ATTN_BLOCK;
-    const int nk = min(ATTN_BLOCK, Lend - k0);
-    __syncthreads();  // the previous block's K/V/S are no longer read
-    stage_kv(sm, kv + (static_cast<size_t>(b) * Lmax + k0) * 2 * HD + static_cast<size_t>(h) * Dh, HD, Dh, nk);
-    cp_async_wait<0>();
+    const int nk = nk_of(j);
+    const bool more = j < jlast;
+    cp_async_wait<1>();  // K of block j (its V may still be in flight)
     __syncthreads();
     block_scores(sm, Dh, nk, nq, k0, L0 + tq0, scale);
-    __syncthreads();
+    __syncthreads();  // K of block j no longer read
+    if (more) stage_k(sm, kvb + static_cast<size_t>(j + 1) * ATTN_BLOCK * 2 * HD, HD, Dh, nk_of(j + 1));
     block_softmax(sm, nq);
+    if (more)
+      cp_async_wait<1>();  // V of block j (the next K may still be in flight)
+    else
+      cp_async_wait<0>();
     __syncthreads();
     for (int t = threadIdx.x; t < nq; t += ATTN_THREADS) {
       const float mj = sm.stt[2 * t];
@@ -775,6 +784,8 @@ __global__ void __launch_bounds__(ATTN_THREADS, 4) attn_fused_kernel(const TD* _
     __syncthreads();
     float acc[ACC_N];
     block_pv(sm, Dh, nk, nq, acc);
+    __syncthreads();  // V of block j no longer read
+    if (more) stage_v(sm, kvb + static_cast<size_t>(j + 1) * ATTN_BLOCK * 2 * HD, HD, Dh, nk_of(j + 1));
 #pragma unroll
     for (int i = 0; i < ACC_N; i += 2) {
       const int t = acc_row<TD>(i, Dh);
