@@ -82,7 +82,10 @@ __device__ inline void store4(TD* dst, float4 v) {
   }
 }
 
-template <typename TD>
+// TP: the partial sums come from parts.R ranks (channel sharding), one summed partial per rank.
+// Thread r polls rank r's flag and every rank's float4 of a column is loaded before the rank-order
+// adds, so a reduction costs one NVLink round trip for the flags and one for the data, not R each.
+template <typename TD, bool TP>
 __global__ void __cluster_dims__(NORM_CL, 1, 1) __launch_bounds__(NORM_THREADS)
     res_add_norm_kernel(TpPartials parts, int splits, int M, float* __restrict__ resid,
                         const float* __restrict__ scale, TD* __restrict__ act, int ld_act, int d, float eps,
@@ -102,25 +105,25 @@ __global__ void __cluster_dims__(NORM_CL, 1, 1) __launch_bounds__(NORM_THREADS)
     if (c4 < n4) sc[v] = __ldg(reinterpret_cast<const float4*>(scale + c_base + c4 * 4));
   }
   pdl_wait();
-  if (parts.R > 1) {
-    // every rank's partial sums of this reduction are published once its flag reaches the epoch
-    __shared__ int ok;
-    if (threadIdx.x == 0) {
-      ok = 1;
-      for (int r = 0; r < parts.R; ++r) {
-        if (ld_acquire_sys(parts.flag[r]) >= parts.epoch) continue;
-        const uint64_t t0 = globaltimer_ns();
-        while (ld_acquire_sys(parts.flag[r]) < parts.epoch) {
-          if (globaltimer_ns() - t0 > EVS_WAIT_LIMIT_NS) {
-            evs_record_error(err, EVS_ETIMEOUT, EVS_K_ROW, 1000 + r);
-            ok = 0;
-            break;
-          }
+  if constexpr (TP) {
+    // every rank's partial sums of this reduction are published once its flag reaches the epoch;
+    // thread r waits for rank r (on a timeout the sums below use whatever the buffers hold and the
+    // error word reports it)
+    const int r = threadIdx.x;
+    const long long* f = nullptr;
+#pragma unroll
+    for (int q = 0; q < EVS_TP_MAX; ++q)
+      if (q == r && q < parts.R) f = parts.flag[q];
+    if (f != nullptr && ld_acquire_sys(f) < parts.epoch) {
+      const uint64_t t0 = globaltimer_ns();
+      while (ld_acquire_sys(f) < parts.epoch) {
+        if (globaltimer_ns() - t0 > EVS_WAIT_LIMIT_NS) {
+          evs_record_error(err, EVS_ETIMEOUT, EVS_K_ROW, 1000 + r);
+          break;
         }
       }
     }
     __syncthreads();
-    (void)ok;  // on a timeout the sums below use whatever the buffers hold; the error word reports it
   }
   __shared__ float red[NORM_THREADS / 32];
   __shared__ float cta_ss;
@@ -142,18 +145,48 @@ __global__ void __cluster_dims__(NORM_CL, 1, 1) __launch_bounds__(NORM_THREADS)
     const int c4 = threadIdx.x + v * NORM_THREADS;
     if (c4 < n4) xr[v] = *reinterpret_cast<const float4*>(resid + static_cast<size_t>(row) * d + c_base + c4 * 4);
   }
+  // TP: every rank's partial (one summed split each) for two column groups at a time, all in flight
+  constexpr int TPV = 2;
+  float4 tp_acc[NORM_VPT];
+  if constexpr (TP) {
+#pragma unroll
+    for (int v0 = 0; v0 < NORM_VPT; v0 += TPV) {
+      float4 pv[TPV][EVS_TP_MAX];
+#pragma unroll
+      for (int v = v0; v < v0 + TPV; ++v) {
+        const int c4 = threadIdx.x + v * NORM_THREADS;
+#pragma unroll
+        for (int q = 0; q < EVS_TP_MAX; ++q)
+          if (c4 < n4 && q < parts.R)
+            pv[v - v0][q] = __ldcv(reinterpret_cast<const float4*>(parts.buf[q] + static_cast<size_t>(row) * d +
+                                                                    c_base + c4 * 4));
+      }
+#pragma unroll
+      for (int v = v0; v < v0 + TPV; ++v) {
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int q = 0; q < EVS_TP_MAX; ++q)  // ranks in rank order
+          if (q < parts.R) {
+            acc.x += pv[v - v0][q].x;
+            acc.y += pv[v - v0][q].y;
+            acc.z += pv[v - v0][q].z;
+            acc.w += pv[v - v0][q].w;
+          }
+        tp_acc[v] = acc;
+      }
+    }
+  }
 #pragma unroll
   for (int v = 0; v < NORM_VPT; ++v) {
     const int c4 = threadIdx.x + v * NORM_THREADS;
     if (c4 < n4) {
       const int c = c_base + c4 * 4;
       float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int r = 0; r < parts.R; ++r) {  // ranks in rank order, each rank's splits in split order
-        const float* src = parts.buf[r] + static_cast<size_t>(row) * d + c;
-        if (parts.R > 1)
-          split_sum4<true>(acc, src, static_cast<size_t>(M) * d, splits);
-        else
-          split_sum4<false>(acc, src, static_cast<size_t>(M) * d, splits);
+      if constexpr (TP) {
+        acc = tp_acc[v];
+      } else {
+        // one rank: its splits in split order
+        split_sum4<false>(acc, parts.buf[0] + static_cast<size_t>(row) * d + c, static_cast<size_t>(M) * d, splits);
       }
       float4* rp = reinterpret_cast<float4*>(resid + static_cast<size_t>(row) * d + c);
       float4 x = xr[v];
@@ -440,16 +473,19 @@ int launch_res_add_norm(const evs_model* m, evs_state* s, int M, int splits, con
     evs_count_launch(1);
     return EVS_OK;
   }
+  const bool tp = parts.R > 1;
+  EVS_CHECK_ARG(!tp || splits == 1, "channel-sharded partial sums must be pre-summed to one split per rank");
   if (m->cfg.dtype == EVS_DTYPE_BF16)
-    EVS_CUDA_TRY(evs_launch(res_add_norm_kernel<__nv_bfloat16>, dim3(NORM_CL, M), dim3(NORM_THREADS), 0, st,
-                            s->use_pdl(), parts, splits, M, s->resid, scale, static_cast<__nv_bfloat16*>(s->act),
-                            s->ld_act, d, m->cfg.eps, ring, s->ring_len, static_cast<const int32_t*>(s->d_len), T,
-                            ring ? s->cap_tag : nullptr, static_cast<const unsigned long long*>(s->d_fwd_seq),
-                            s->tag_hi, s->d_err));
+    EVS_CUDA_TRY(evs_launch(tp ? res_add_norm_kernel<__nv_bfloat16, true> : res_add_norm_kernel<__nv_bfloat16, false>,
+                            dim3(NORM_CL, M), dim3(NORM_THREADS), 0, st, s->use_pdl(), parts, splits, M, s->resid,
+                            scale, static_cast<__nv_bfloat16*>(s->act), s->ld_act, d, m->cfg.eps, ring, s->ring_len,
+                            static_cast<const int32_t*>(s->d_len), T, ring ? s->cap_tag : nullptr,
+                            static_cast<const unsigned long long*>(s->d_fwd_seq), s->tag_hi, s->d_err));
   else
-    EVS_CUDA_TRY(evs_launch(res_add_norm_kernel<float>, dim3(NORM_CL, M), dim3(NORM_THREADS), 0, st, s->use_pdl(),
-                            parts, splits, M, s->resid, scale, static_cast<float*>(s->act), s->ld_act, d, m->cfg.eps,
-                            ring, s->ring_len, static_cast<const int32_t*>(s->d_len), T, ring ? s->cap_tag : nullptr,
+    EVS_CUDA_TRY(evs_launch(tp ? res_add_norm_kernel<float, true> : res_add_norm_kernel<float, false>,
+                            dim3(NORM_CL, M), dim3(NORM_THREADS), 0, st, s->use_pdl(), parts, splits, M, s->resid,
+                            scale, static_cast<float*>(s->act), s->ld_act, d, m->cfg.eps, ring, s->ring_len,
+                            static_cast<const int32_t*>(s->d_len), T, ring ? s->cap_tag : nullptr,
                             static_cast<const unsigned long long*>(s->d_fwd_seq), s->tag_hi, s->d_err));
   evs_count_launch(1);
   return EVS_OK;
