@@ -25,7 +25,7 @@ struct evs_drafter {
   const float* t[EVS_D_LAYER0 + EVS_D_MAX_LAYERS * EVS_D_PER_LAYER] = {nullptr};
   int64_t numel[EVS_D_LAYER0 + EVS_D_MAX_LAYERS * EVS_D_PER_LAYER] = {0};
   float *ctx_in = nullptr, *ctx = nullptr, *h = nullptr, *xb = nullptr, *q = nullptr;
-  float *kv_in = nullptr, *kb = nullptr, *vb = nullptr, *y = nullptr, *tmp = nullptr, *m1 = nullptr;
+  float *kb = nullptr, *vb = nullptr, *y = nullptr, *tmp = nullptr, *m1 = nullptr;
   float *z = nullptr, *U = nullptr;
   // in_proj(embed[v]) + in_proj.bias for every token v [V][d], formed once at finalize by the same
   // projection and epilogue as a round's rows (a token's row does not depend on the other rows), so
@@ -266,43 +266,48 @@ __global__ void __launch_bounds__(EPI_THREADS) draft_epi_kernel(DraftEpiArgs a) 
 }
 
 // rows of the k / v projections: [the B*g draft rows (xb) ; the context rows to project]
-__global__ void build_kv_kernel(const float* __restrict__ xb, const float* __restrict__ ctx, int Bg,
-                                const int32_t* __restrict__ ccount, int d, float* __restrict__ out) {
+// The q, k and v partial sums of one layer, each added in split order (reduce_splits_kernel's
+// additions; blockIdx.y = 0, 1, 2 for q, k, v).  q and the draft rows (below Bg) of k and v go to
+// out[]; the context rows of k and v (row Bg + r is the r-th context row of this call, cmap) go
+// straight into their cache slots, and after the last layer the slots get the rows' positions and
+// capture tags, after which those rows are current for later calls.
+struct QkvRed {
+  const float* ws[3];  // [splits][M_j][N]
+  float* out[3];
+  int M[3];
+};
+__global__ void qkv_reduce_kernel(const __grid_constant__ QkvRed a, int splits, int N, int Bg,
+                                  const int32_t* __restrict__ ccount, const int32_t* __restrict__ cmap,
+                                  float* __restrict__ ck, float* __restrict__ cv, int last,
+                                  const unsigned long long* __restrict__ cap_tag, int ring_len,
+                                  int32_t* __restrict__ cpos, unsigned long long* __restrict__ ctag) {
   pdl_trigger();
   pdl_wait();
-  const int r = blockIdx.x;
-  const float* src;
-  if (r < Bg) {
-    src = xb + static_cast<size_t>(r) * d;
-  } else {
-    if (ccount == nullptr || r - Bg >= ccount[0]) return;
-    src = ctx + static_cast<size_t>(r - Bg) * d;
-  }
-  float* dst = out + static_cast<size_t>(r) * d;
-  for (int c = threadIdx.x; c < d; c += blockDim.x) dst[c] = src[c];
-}
-
-// the projected context rows of one layer into their cache slots; after the last layer, the slots'
-// positions and tags (the rows are then current for later calls)
-__global__ void ctx_kv_store_kernel(const float* __restrict__ kb, const float* __restrict__ vb, int Bg,
-                                    const int32_t* __restrict__ cmap, const int32_t* __restrict__ ccount, int d,
-                                    float* __restrict__ ck, float* __restrict__ cv, int last,
-                                    const unsigned long long* __restrict__ cap_tag, int ring_len,
-                                    int32_t* __restrict__ cpos, unsigned long long* __restrict__ ctag) {
-  pdl_trigger();
-  pdl_wait();
-  const int r = blockIdx.x;
-  if (r >= ccount[0]) return;
-  const int b = cmap[2 * r], P = cmap[2 * r + 1];
-  const int slot = P % DR_CR;
-  const size_t src = static_cast<size_t>(Bg + r) * d, dst = (static_cast<size_t>(b) * DR_CR + slot) * d;
-  for (int c = threadIdx.x; c < d; c += blockDim.x) {
-    ck[dst + c] = kb[src + c];
-    cv[dst + c] = vb[src + c];
-  }
-  if (last && threadIdx.x == 0) {
-    cpos[b * DR_CR + slot] = P;
-    ctag[b * DR_CR + slot] = cap_tag[static_cast<size_t>(b) * ring_len + P % ring_len];
+  const int j = static_cast<int>(blockIdx.y);
+  const int M = a.M[j];
+  const size_t MN = static_cast<size_t>(M) * N;
+  // rows with work: q's Bg; for k and v the draft rows and this call's context rows (ccount[1])
+  const int rows = (j == 0 || ccount == nullptr) ? M : min(M, ccount[1]);
+  const int lim = rows * N;
+  const float* ws = a.ws[j];
+  float* out = a.out[j];
+  float* cache = j == 1 ? ck : cv;
+  for (int i = static_cast<int>(blockIdx.x * blockDim.x + threadIdx.x); i < lim;
+       i += static_cast<int>(gridDim.x * blockDim.x)) {
+    const float acc = split_sum(ws + i, MN, splits);
+    const int row = i / N;
+    if (j == 0 || row < Bg) {
+      out[i] = acc;
+      continue;
+    }
+    const int r = row - Bg, col = i - row * N;
+    const int b = cmap[2 * r], P = cmap[2 * r + 1];
+    const int slot = P % DR_CR;
+    cache[(static_cast<size_t>(b) * DR_CR + slot) * N + col] = acc;
+    if (last && j == 2 && col == 0) {
+      cpos[b * DR_CR + slot] = P;
+      ctag[b * DR_CR + slot] = cap_tag[static_cast<size_t>(b) * ring_len + P % ring_len];
+    }
   }
 }
 
@@ -873,15 +878,6 @@ int64_t drafter_numel(const evs_drafter_config& c, int id) {
 // row count at most M
 // m_hint: the row count the grids are sized for when m_dev is given (the kernels walk any rows
 // beyond it), so that a launch sized for the largest count does not carry idle CTAs
-int sgemm(evs_drafter* dr, const float* W, const float* X, int ldx, float* out, int N, int K, int M,
-          cudaStream_t st, const int32_t* m_dev = nullptr, int m_hint = 0) {
-  const GemmPlan p = gemm_plan_f32_drafter(N, K, M);
-  EVS_CHECK_RANGE(static_cast<size_t>(p.splits) * M * N <= dr->ws_floats, "drafter workspace too small");
-  if (p.splits == 1) return launch_gemm_simt(W, nullptr, X, ldx, EVS_DTYPE_FP32, p, out, st, true, m_dev, m_hint);
-  EVS_TRY(launch_gemm_simt(W, nullptr, X, ldx, EVS_DTYPE_FP32, p, dr->ws, st, true, m_dev, m_hint));
-  return launch_reduce_splits(dr->ws, p.splits, M, N, nullptr, out, st, true, m_dev, m_hint);
-}
-
 inline unsigned blocks_for(size_t n, int t) { return static_cast<unsigned>((n + t - 1) / t); }
 
 // projection partials into the workspace (no reduction), then the fused epilogue `mode` over them
@@ -957,7 +953,7 @@ int evs_drafter_create(const evs_drafter_config* cfg, int max_batch, evs_drafter
   };
   const size_t o_ctx_in = take(4 * B * CW * nI * H), o_ctx = take(4 * B * CW * d);
   const size_t o_h = take(4 * B * g * d), o_xb = take(4 * B * g * d), o_q = take(4 * B * g * d);
-  const size_t o_kv = take(4 * B * (CW + g) * d), o_kb = take(4 * B * (CW + g) * d), o_vb = take(4 * B * (CW + g) * d);
+  const size_t o_kb = take(4 * B * (CW + g) * d), o_vb = take(4 * B * (CW + g) * d);
   const size_t o_y = take(4 * B * g * d), o_tmp = take(4 * B * g * d), o_m1 = take(4 * B * g * hid);
   const size_t o_z = take(4 * B * g * H), o_U = take(4 * B * g * V);
   const size_t o_prev = take(8 * B * g), o_tok = take(4 * V * d);
@@ -980,6 +976,11 @@ int evs_drafter_create(const evs_drafter_config* cfg, int max_batch, evs_drafter
   need(B * g, H, d);
   need(B * g, V, H);
   need(V, d, H);  // the token table
+  {
+    // q, k and v of one layer side by side: the draft rows, twice the draft + context rows
+    const GemmPlan p = gemm_plan_f32_drafter(static_cast<int>(d), static_cast<int>(d), static_cast<int>(B * (CW + g)));
+    wsf = std::max(wsf, static_cast<size_t>(p.splits) * (B * g + 2 * B * (CW + g)) * d);
+  }
   const size_t o_ws = take(4 * wsf);
   if (cudaMalloc(&dr->block, off) != cudaSuccess) {
     cudaGetLastError();
@@ -993,7 +994,6 @@ int evs_drafter_create(const evs_drafter_config* cfg, int max_batch, evs_drafter
   dr->h = reinterpret_cast<float*>(base + o_h);
   dr->xb = reinterpret_cast<float*>(base + o_xb);
   dr->q = reinterpret_cast<float*>(base + o_q);
-  dr->kv_in = reinterpret_cast<float*>(base + o_kv);
   dr->kb = reinterpret_cast<float*>(base + o_kb);
   dr->vb = reinterpret_cast<float*>(base + o_vb);
   dr->y = reinterpret_cast<float*>(base + o_y);
@@ -1117,26 +1117,40 @@ int evs_draft_propose(evs_drafter* dr, const evs_state* s, const int64_t* anchor
     const float* const* L = T + EVS_D_LAYER0 + l * EVS_D_PER_LAYER;
     // the norm after this layer's MLP: the next layer's pre-norm, or the final norm
     const float* next_ln = l + 1 < c.n_layers ? T[EVS_D_LAYER0 + (l + 1) * EVS_D_PER_LAYER + EVS_D_LN1] : T[EVS_D_FINAL_LN];
-    EVS_TRY(sgemm(dr, L[EVS_D_Q], dr->xb, d, dr->q, d, d, rows, st));
-    // k and v of [the draft rows ; the context rows to project], then those context rows' k/v
-    // into the cache
+    // q, k and v in one launch (each its own rows: q the draft rows; k and v the draft rows, then
+    // the context rows to project), then one reduction that also stores those context rows' k and
+    // v in the cache
     const bool ctxr = c.n_inject > 0;
     const int kv_rows = ctxr ? Bg + B * CW : Bg;
     const int32_t* kv_m = ctxr ? dr->ccount + 1 : nullptr;
-    EVS_CUDA_TRY(evs_launch(build_kv_kernel, dim3(kv_rows), dim3(256), 0, st, true, static_cast<const float*>(dr->xb),
-                            static_cast<const float*>(dr->ctx), Bg, ctxr ? static_cast<const int32_t*>(dr->ccount) : nullptr,
-                            d, dr->kv_in));
     const int kv_hint = ctxr ? std::min(kv_rows, Bg + 2 * B + 16) : 0;
-    EVS_TRY(sgemm(dr, L[EVS_D_K], dr->kv_in, d, dr->kb, d, d, kv_rows, st, kv_m, kv_hint));
-    EVS_TRY(sgemm(dr, L[EVS_D_V], dr->kv_in, d, dr->vb, d, d, kv_rows, st, kv_m, kv_hint));
     float* ckl = dr->ck + static_cast<size_t>(l) * B_cap * DR_CR * d;
     float* cvl = dr->cv + static_cast<size_t>(l) * B_cap * DR_CR * d;
-    if (ctxr)
-      EVS_CUDA_TRY(evs_launch(ctx_kv_store_kernel, dim3(B * CW), dim3(256), 0, st, true,
-                              static_cast<const float*>(dr->kb), static_cast<const float*>(dr->vb), Bg,
-                              static_cast<const int32_t*>(dr->cmap), static_cast<const int32_t*>(dr->ccount), d, ckl,
-                              cvl, static_cast<int>(l == c.n_layers - 1),
+    {
+      const GemmPlan p = gemm_plan_f32_drafter(d, d, kv_rows);
+      const size_t sq = static_cast<size_t>(p.splits) * Bg * d, skv = static_cast<size_t>(p.splits) * kv_rows * d;
+      EVS_CHECK_RANGE(sq + 2 * skv <= dr->ws_floats, "drafter workspace too small");
+      SkJobs jobs{};
+      jobs.j[0] = SkJob{L[EVS_D_Q], dr->xb, nullptr, dr->ws, nullptr, Bg, Bg};
+      jobs.j[1] = SkJob{L[EVS_D_K], dr->xb, dr->ctx, dr->ws + sq, kv_m, Bg, kv_rows};
+      jobs.j[2] = SkJob{L[EVS_D_V], dr->xb, dr->ctx, dr->ws + sq + skv, kv_m, Bg, kv_rows};
+      EVS_TRY(launch_gemm_simt_jobs(jobs, 3, d, p, st, true, kv_hint));
+      QkvRed qr{};
+      qr.ws[0] = dr->ws;
+      qr.ws[1] = dr->ws + sq;
+      qr.ws[2] = dr->ws + sq + skv;
+      qr.out[0] = dr->q;
+      qr.out[1] = dr->kb;
+      qr.out[2] = dr->vb;
+      qr.M[0] = Bg;
+      qr.M[1] = qr.M[2] = kv_rows;
+      const int red_rows = std::max(Bg, ctxr ? kv_hint : kv_rows);
+      EVS_CUDA_TRY(evs_launch(qkv_reduce_kernel, dim3(blocks_for(static_cast<size_t>(red_rows) * d, 256), 3), dim3(256),
+                              0, st, true, qr, p.splits, d, Bg, ctxr ? static_cast<const int32_t*>(dr->ccount) : nullptr,
+                              static_cast<const int32_t*>(dr->cmap), ckl, cvl, static_cast<int>(l == c.n_layers - 1),
                               static_cast<const unsigned long long*>(s->cap_tag), s->ring_len, dr->cpos, dr->ctag));
+      evs_count_launch(1);
+    }
     const int hd = d / c.n_heads, nk = CW + g;
     const size_t rows_smem =
         sizeof(float) * ((static_cast<size_t>(nk) * (hd + 1) + 3) / 4 * 4 + static_cast<size_t>(nk) * hd + g * hd + nk);
@@ -1179,10 +1193,10 @@ int evs_draft_propose(evs_drafter* dr, const evs_state* s, const int64_t* anchor
   // ---- confidence: σ(conf_w [final_ln(h) ; in_proj(embed(prev))]), the second half from the table ----
   EVS_CUDA_TRY(evs_launch(conf_kernel, dim3(blocks_for(rows, 4)), dim3(128), 0, st, true, dr->xb, dr->tok_in, dr->prev,
                           T[EVS_D_CONF_W], T[EVS_D_CONF_B], d, rows, conf));
-  // kernels of this call that count nowhere else (projections and their fused epilogues count
-  // themselves): context plan + gather, draft rows, kv build (+ cache store) + attention per layer,
-  // serial head, conf
-  evs_count_launch((c.n_inject > 0 ? 2 : 0) + 1 + (c.n_inject > 0 ? 3 : 2) * c.n_layers + 2);
+  // kernels of this call that count nowhere else (projections, their fused epilogues and the q/k/v
+  // reduction count themselves): context plan + gather, draft rows, attention per layer, serial
+  // head, conf
+  evs_count_launch((c.n_inject > 0 ? 2 : 0) + 1 + c.n_layers + 2);
   if (U_out != nullptr)
     EVS_CUDA_TRY(cudaMemcpyAsync(U_out, dr->U, sizeof(float) * rows * V, cudaMemcpyDeviceToDevice, st));
   EVS_CUDA_TRY(cudaGetLastError());

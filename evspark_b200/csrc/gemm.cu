@@ -336,23 +336,15 @@ __global__ void __launch_bounds__(192, 2)
 constexpr int SK_WARPS = 8, SK_R = 4, SK_ROWS = SK_WARPS * SK_R, SK_TOK = 16, SK_KC_MAX = 1024;
 constexpr size_t SK_SMEM = sizeof(float) * SK_TOK * SK_KC_MAX;  // also holds 8 x 64 x 32 lane partials
 
-__global__ void __launch_bounds__(SK_WARPS * 32) gemm_skinny_f32_kernel(const float* __restrict__ W,
-                                                                        const float* __restrict__ W2,
-                                                                        const float* __restrict__ X, int ldx,
-                                                                        float* __restrict__ ws, int N, int K, int M,
-                                                                        int kc, int dual,
-                                                                        const int32_t* __restrict__ m_dev) {
-  extern __shared__ __align__(16) float sk_sm[];
-  pdl_trigger();
-  pdl_wait();
+// One CTA's work: weight rows n0 .. n0+SK_ROWS-1, split sp, token groups z0, z0 + zs, ... below
+// M_rows.  xrow(m) is token row m of the activations.
+template <typename XRow>
+__device__ __forceinline__ void skinny_cta(const float* __restrict__ W, const float* __restrict__ W2, XRow xrow,
+                                           float* __restrict__ ws, int N, int K, int M, int kc, int dual, int M_rows,
+                                           int n0, int sp, int z0, int zs, float* sk_sm) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * SK_ROWS, sp = blockIdx.y;
-  // a device-side row count (rows decided by an earlier kernel): token groups past it have no work
-  // (M stays the partial buffers' row stride).  The grid may hold fewer token groups than M: a CTA
-  // then takes groups blockIdx.z, blockIdx.z + gridDim.z, ... (the arithmetic of a group is the same)
-  const int M_rows = m_dev != nullptr ? min(M, *m_dev) : M;
-  for (int m0 = blockIdx.z * SK_TOK; m0 < M_rows; m0 += gridDim.z * SK_TOK) {
-    if (m0 != static_cast<int>(blockIdx.z) * SK_TOK) __syncthreads();  // the previous group's partials are read
+  for (int m0 = z0 * SK_TOK; m0 < M_rows; m0 += zs * SK_TOK) {
+    if (m0 != z0 * SK_TOK) __syncthreads();  // the previous group's partials are read
     const int mt = min(SK_TOK, M_rows - m0);
     const int kb = sp * kc, ke = min(K, kb + kc);  // this CTA's K range, staged SK_KC_MAX columns at a time
     const float* wr[SK_R];
@@ -379,7 +371,7 @@ __global__ void __launch_bounds__(SK_WARPS * 32) gemm_skinny_f32_kernel(const fl
       if (cb != kb) __syncthreads();  // every warp is done with the previous stage
       for (int i = threadIdx.x; i < mt * c4; i += blockDim.x) {
         const int m = i / c4, c = i - m * c4;
-        cp_async16(sk_sm + m * SK_KC_MAX + 4 * c, X + static_cast<size_t>(m0 + m) * ldx + cb + 4 * c);
+        cp_async16(sk_sm + m * SK_KC_MAX + 4 * c, xrow(m0 + m) + cb + 4 * c);
       }
       cp_async_commit();
       cp_async_wait<0>();
@@ -424,6 +416,46 @@ __global__ void __launch_bounds__(SK_WARPS * 32) gemm_skinny_f32_kernel(const fl
       if (m < mt && n < N) ws[(static_cast<size_t>(sp) * M + m0 + m) * N + n] = sum;
     }
   }
+}
+
+
+__global__ void __launch_bounds__(SK_WARPS * 32) gemm_skinny_f32_kernel(const float* __restrict__ W,
+                                                                        const float* __restrict__ W2,
+                                                                        const float* __restrict__ X, int ldx,
+                                                                        float* __restrict__ ws, int N, int K, int M,
+                                                                        int kc, int dual,
+                                                                        const int32_t* __restrict__ m_dev) {
+  extern __shared__ __align__(16) float sk_sm[];
+  pdl_trigger();
+  pdl_wait();
+  // a device-side row count (rows decided by an earlier kernel): token groups past it have no work
+  // (M stays the partial buffers' row stride).  The grid may hold fewer token groups than M: a CTA
+  // then takes groups blockIdx.z, blockIdx.z + gridDim.z, ... (the arithmetic of a group is the same)
+  const int M_rows = m_dev != nullptr ? min(M, *m_dev) : M;
+  skinny_cta(W, W2, [&](int m) { return X + static_cast<size_t>(m) * ldx; }, ws, N, K, M, kc, dual, M_rows,
+             static_cast<int>(blockIdx.x) * SK_ROWS, static_cast<int>(blockIdx.y), static_cast<int>(blockIdx.z),
+             static_cast<int>(gridDim.z), sk_sm);
+}
+
+// Several projections of the same shape (N x K, one plan) in one launch: job j = blockIdx.x / tiles
+// runs gemm_skinny_f32_kernel's CTA on its own weights, rows and partial buffer.  Token row m of a
+// job is row m of X0 below msplit and row m - msplit of X1 from there.
+__global__ void __launch_bounds__(SK_WARPS * 32) gemm_skinny_f32_jobs_kernel(const __grid_constant__ SkJobs jobs,
+                                                                             int tiles, int N, int K, int ldx,
+                                                                             int kc) {
+  extern __shared__ __align__(16) float sk_sm[];
+  pdl_trigger();
+  pdl_wait();
+  const int j = static_cast<int>(blockIdx.x) / tiles, tile = static_cast<int>(blockIdx.x) - j * tiles;
+  const SkJob& J = jobs.j[j];
+  const int M_rows = J.m_dev != nullptr ? min(J.M, *J.m_dev) : J.M;
+  const float* X0 = J.X0;
+  const float* X1 = J.X1;
+  const int ms = J.msplit;
+  skinny_cta(J.W, J.W,
+             [&](int m) { return m < ms ? X0 + static_cast<size_t>(m) * ldx : X1 + static_cast<size_t>(m - ms) * ldx; },
+             J.ws, N, K, J.M, kc, 0, M_rows, tile * SK_ROWS, static_cast<int>(blockIdx.y),
+             static_cast<int>(blockIdx.z), static_cast<int>(gridDim.z), sk_sm);
 }
 
 __global__ void reduce_splits_kernel(const float* __restrict__ ws, int splits, int MN, const float* __restrict__ bias,
@@ -599,6 +631,33 @@ int launch_gemm_simt(const void* W, const void* W2, const void* X, int ldx, int 
   EVS_CUDA_TRY(evs_launch(gemm_skinny_f32_kernel, grid, dim3(SK_WARPS * 32), smem, st, pdl,
                           static_cast<const float*>(W), static_cast<const float*>(W2 ? W2 : W),
                           static_cast<const float*>(X), ldx, ws, p.N, p.K, p.M, p.kchunk, p.dual, m_dev));
+  evs_count_launch(1);
+  return EVS_OK;
+}
+
+int launch_gemm_simt_jobs(const SkJobs& jobs, int n_jobs, int ldx, const GemmPlan& p, cudaStream_t st, bool pdl,
+                          int m_hint) {
+  EVS_CHECK_ARG(n_jobs >= 1 && n_jobs <= SK_MAX_JOBS, "1 to 3 projection jobs");
+  EVS_CHECK_ARG(p.K % 4 == 0 && ldx % 4 == 0 && p.N % SK_ROWS == 0, "fp32 projection jobs need K, ldx % 4 and N % 32");
+  EVS_CHECK_ARG(p.kchunk > 0 && p.kchunk % 128 == 0 && p.splits * p.kchunk >= p.K, "bad fp32 projection plan");
+  int groups = 0;
+  for (int j = 0; j < n_jobs; ++j) {
+    const SkJob& J = jobs.j[j];
+    EVS_CHECK_ARG(J.W && J.X0 && J.ws && J.M >= 0 && (J.X1 || J.msplit >= J.M), "bad projection job");
+    EVS_CHECK_ARG(reinterpret_cast<uintptr_t>(J.W) % 16 == 0 && reinterpret_cast<uintptr_t>(J.X0) % 16 == 0 &&
+                      reinterpret_cast<uintptr_t>(J.X1) % 16 == 0,
+                  "fp32 projection jobs need 16-byte aligned operands");
+    const int rows = J.m_dev != nullptr && m_hint > 0 ? std::min(J.M, m_hint) : J.M;
+    groups = std::max(groups, (rows + SK_TOK - 1) / SK_TOK);
+  }
+  if (groups == 0) return EVS_OK;
+  static std::atomic<unsigned long long> attr_devs{0};
+  EVS_TRY(smem_attr_once(attr_devs, reinterpret_cast<const void*>(gemm_skinny_f32_jobs_kernel),
+                         static_cast<int>(SK_SMEM)));
+  const int tiles = p.N / SK_ROWS;
+  dim3 grid(tiles * n_jobs, p.splits, groups);
+  EVS_CUDA_TRY(evs_launch(gemm_skinny_f32_jobs_kernel, grid, dim3(SK_WARPS * 32), SK_SMEM, st, pdl, jobs, tiles, p.N,
+                          p.K, ldx, p.kchunk));
   evs_count_launch(1);
   return EVS_OK;
 }

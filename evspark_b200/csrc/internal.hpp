@@ -177,6 +177,23 @@ int launch_gemm_tc_serial(const CUtensorMap* tmA, const CUtensorMap* tmA2, const
 // m_dev: optional device-side row count (at most p.M, which sizes the grid)
 int launch_gemm_simt(const void* W, const void* W2, const void* X, int ldx, int dtype, const GemmPlan& p, float* ws,
                      cudaStream_t st, bool pdl = false, const int32_t* m_dev = nullptr, int m_hint = 0);
+// several fp32 projections of one shape and plan in one launch (at most SK_MAX_JOBS): job j
+// computes the partials of W_j x row m into its own ws_j[split][M_j][N], row m being X0[m] below
+// msplit and X1[m - msplit] from there; each CTA does gemm_skinny_f32_kernel's arithmetic
+constexpr int SK_MAX_JOBS = 3;
+struct SkJob {
+  const float* W;
+  const float* X0;
+  const float* X1;
+  float* ws;
+  const int32_t* m_dev;  // optional device-side row count
+  int msplit, M;
+};
+struct SkJobs {
+  SkJob j[SK_MAX_JOBS];
+};
+int launch_gemm_simt_jobs(const SkJobs& jobs, int n_jobs, int ldx, const GemmPlan& p, cudaStream_t st, bool pdl,
+                          int m_hint = 0);
 int make_tmap_2d_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t row_stride_bytes,
                       uint32_t box_inner, uint32_t box_outer);
 
