@@ -193,6 +193,13 @@ __device__ __forceinline__ uint64_t l2_policy_evict_first() {
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
+// split cluster barrier: arrive without ordering memory, then wait (cluster.sync() is both, with
+// release / acquire)
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.aligned;" ::: "memory"); }
+
 // system-scope flag access for peers that read this GPU's memory (and for reading theirs)
 __device__ __forceinline__ long long ld_acquire_sys(const long long* p) {
   long long v;

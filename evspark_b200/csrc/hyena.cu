@@ -89,19 +89,86 @@ __device__ void outer_stage(const HyArgs<TD>& a, int b, int L0, int h0, float* u
   batched_copy(C3 * a.K0, [&](int i) { return __ldg(sw + i); }, [&](int i, float v) { wo[i] = v; });
 }
 
+// The in-projection partials of a pass loaded ahead of the state lengths, which they do not
+// depend on: the thread's float4 chunks i = tid + k * blockDim (k < PK) of every split (at most
+// PS).  ok is false when the pass has more splits or chunks; outer_pass then loads them itself.
+constexpr int PS = 4;
+template <int PK>
+struct OuterPre {
+  float4 v[PS][PK];
+  bool ok;
+};
+template <typename TD, int PK>
+__device__ __forceinline__ void outer_preload(const HyArgs<TD>& a, int b, int h0, int t0, int ns, OuterPre<PK>& pre) {
+  constexpr int Q = C3 / 4;
+  const int n4 = ns * Q;
+  pre.ok = a.splits <= PS && n4 <= PK * static_cast<int>(blockDim.x);
+  if (!pre.ok) return;
+  const size_t N3 = 3 * static_cast<size_t>(a.d);
+  const size_t split_stride = static_cast<size_t>(a.M) * N3;
+#pragma unroll
+  for (int u = 0; u < PS; ++u)
+#pragma unroll
+    for (int k = 0; k < PK; ++k) {
+      const int i = threadIdx.x + k * blockDim.x;
+      if (u < a.splits && i < n4) {
+        const int t = i / Q, q4 = i - t * Q;
+        pre.v[u][k] = __ldg(reinterpret_cast<const float4*>(a.ws + u * split_stride +
+                                                            static_cast<size_t>(b * a.T + t0 + t) * N3 + 3 * h0) + q4);
+      }
+    }
+}
+
+// u of chunk i (float4 q4 of position t) into the outer ring and the window uw
+template <typename TD>
+__device__ __forceinline__ void outer_store_u(const HyArgs<TD>& a, int b, int L0, int h0, int t0, int i, float4 acc,
+                                              float* uw) {
+  constexpr int Q = C3 / 4;
+  const size_t N3 = 3 * static_cast<size_t>(a.d);
+  const int t = i / Q, q4 = i - t * Q;
+  const int P = L0 + t0 + t;
+  const float4 un = make_float4(round_to<TD>(acc.x), round_to<TD>(acc.y), round_to<TD>(acc.z), round_to<TD>(acc.w));
+  *reinterpret_cast<float4*>(uw + (P & (UW - 1)) * C3 + 4 * q4) = un;
+  TD* dst = a.outer_ring + (static_cast<size_t>(b) * a.cap_o + (P % a.cap_o)) * N3 + 3 * h0 + 4 * q4;
+  dst[0] = from_f32<TD>(un.x);
+  dst[1] = from_f32<TD>(un.y);
+  dst[2] = from_f32<TD>(un.z);
+  dst[3] = from_f32<TD>(un.w);
+}
+
 // One pass over chunk positions t0 .. t0+ns-1 of row b: in-projection values u (sum of the
 // split partials in split order, rounded to the data dtype) into the outer ring and the window uw,
 // then the outer FIR outputs z (rounded) into zs[ns][96].  Starts and ends with a block barrier.
-template <typename TD>
+// pre: this pass's partials loaded by outer_preload (the same chunks per thread, the same order
+// of additions), or null.
+template <typename TD, int PK = 1>
 __device__ void outer_pass(const HyArgs<TD>& a, int b, int L0, int h0, int t0, int ns, float* uw, const float* wo,
-                           float* zs) {
+                           float* zs, const OuterPre<PK>* pre = nullptr) {
   const size_t N3 = 3 * static_cast<size_t>(a.d);
   const size_t split_stride = static_cast<size_t>(a.M) * N3;
   const int c0 = 3 * h0;
   constexpr int Q = C3 / 4;  // float4s per position
   const int n4 = ns * Q;
   __syncthreads();  // the previous pass has finished reading uw / zs
-  for (int i0 = threadIdx.x; i0 < n4; i0 += 4 * blockDim.x) {
+  if (pre != nullptr && pre->ok) {
+#pragma unroll
+    for (int k = 0; k < PK; ++k) {
+      const int i = threadIdx.x + k * blockDim.x;
+      if (i < n4) {
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int u = 0; u < PS; ++u)
+          if (u < a.splits) {
+            acc.x += pre->v[u][k].x;
+            acc.y += pre->v[u][k].y;
+            acc.z += pre->v[u][k].z;
+            acc.w += pre->v[u][k].w;
+          }
+        outer_store_u(a, b, L0, h0, t0, i, acc, uw);
+      }
+    }
+  }
+  for (int i0 = threadIdx.x; i0 < ((pre != nullptr && pre->ok) ? 0 : n4); i0 += 4 * blockDim.x) {
     float4 acc[4];
 #pragma unroll
     for (int k = 0; k < 4; ++k) acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -133,18 +200,7 @@ __device__ void outer_pass(const HyArgs<TD>& a, int b, int L0, int h0, int t0, i
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
       const int i = i0 + k * blockDim.x;
-      if (i < n4) {
-        const int t = i / Q, q4 = i - t * Q;
-        const int P = L0 + t0 + t;
-        const float4 un = make_float4(round_to<TD>(acc[k].x), round_to<TD>(acc[k].y), round_to<TD>(acc[k].z),
-                                      round_to<TD>(acc[k].w));
-        *reinterpret_cast<float4*>(uw + (P & (UW - 1)) * C3 + 4 * q4) = un;
-        TD* dst = a.outer_ring + (static_cast<size_t>(b) * a.cap_o + (P % a.cap_o)) * N3 + c0 + 4 * q4;
-        dst[0] = from_f32<TD>(un.x);
-        dst[1] = from_f32<TD>(un.y);
-        dst[2] = from_f32<TD>(un.z);
-        dst[3] = from_f32<TD>(un.w);
-      }
+      if (i < n4) outer_store_u(a, b, L0, h0, t0, i, acc[k], uw);
     }
   }
   __syncthreads();
@@ -201,6 +257,8 @@ __global__ void __launch_bounds__(HY_FIR_THREADS) hyena_fir_kernel(HyArgs<TD> a,
   }
   cp_async_commit();
   pdl_wait();
+  OuterPre<1> pre;
+  outer_preload(a, b, h0, 0, min(TS, T), pre);
   const int L0 = a.len[b];
   // inner-FIR history rows, asynchronously
   constexpr int EPC = 16 / sizeof(TD);
@@ -218,7 +276,7 @@ __global__ void __launch_bounds__(HY_FIR_THREADS) hyena_fir_kernel(HyArgs<TD> a,
   const float* tp = taps + lane * KS;
   for (int t0 = 0; t0 < T; t0 += TS) {
     const int ns = min(TS, T - t0);
-    outer_pass(a, b, L0, h0, t0, ns, uw, wo, zs);
+    outer_pass(a, b, L0, h0, t0, ns, uw, wo, zs, t0 == 0 ? &pre : nullptr);
     if (t0 == 0) {
       cp_async_wait<0>();
       __syncthreads();
@@ -308,6 +366,8 @@ __global__ void __launch_bounds__(HY_THREADS) hyena_iir_kernel(HyArgs<TD> a) {
   load_vec<SPT>(a.residues + static_cast<size_t>(h) * S + q * SPT, r);
   const float Dg = a.D[h];
   pdl_wait();
+  OuterPre<3> pre;
+  outer_preload(a, b, h0, 0, min(TS, T), pre);
   const int L0 = a.len[b];
   outer_stage(a, b, L0, h0, uw, wo);
   if (L0 > 0) {
@@ -319,7 +379,7 @@ __global__ void __launch_bounds__(HY_THREADS) hyena_iir_kernel(HyArgs<TD> a) {
   __syncthreads();
   for (int t0 = 0; t0 < T; t0 += TS) {
     const int ns = min(TS, T - t0);
-    outer_pass(a, b, L0, h0, t0, ns, uw, wo, zs);
+    outer_pass(a, b, L0, h0, t0, ns, uw, wo, zs, t0 == 0 ? &pre : nullptr);
     for (int t = 0; t < ns; ++t) {
       const float* zr = zs + t * C3 + 3 * hl;
       const float x1v = round_to<TD>(zr[1] * zr[2]);

@@ -94,6 +94,9 @@ __global__ void __cluster_dims__(NORM_CL, 1, 1) __launch_bounds__(NORM_THREADS)
                         unsigned long long tag_hi, EvsDevErr* err) {
   pdl_trigger();
   cg::cluster_group cluster = cg::this_cluster();
+  // first phase of a cluster barrier: its wait (before the first store into a peer's shared memory)
+  // guarantees that every CTA of the cluster has started
+  cluster_arrive_relaxed();
   const int rank = static_cast<int>(cluster.block_rank());
   const int cpc = d / NORM_CL, n4 = cpc / 4;
   const int c_base = rank * cpc;
@@ -126,7 +129,7 @@ __global__ void __cluster_dims__(NORM_CL, 1, 1) __launch_bounds__(NORM_THREADS)
     __syncthreads();
   }
   __shared__ float red[NORM_THREADS / 32];
-  __shared__ float cta_ss;
+  __shared__ float ss_all[NORM_CL];  // every CTA's sum of squares, stored here by its owner
   const int row = blockIdx.y;
   const int b = row / T, t = row % T;
   float* cap = nullptr;
@@ -206,15 +209,17 @@ __global__ void __cluster_dims__(NORM_CL, 1, 1) __launch_bounds__(NORM_THREADS)
   ss = warp_sum(ss);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
   __syncthreads();
+  cluster_wait();  // every CTA of the cluster has started
   if (threadIdx.x == 0) {
     float a = 0.f;
     for (int w = 0; w < NORM_THREADS / 32; ++w) a += red[w];
-    cta_ss = a;
+    // this CTA's sum into slot `rank` of every CTA's ss_all (its own included)
+#pragma unroll
+    for (int q = 0; q < NORM_CL; ++q) *cluster.map_shared_rank(&ss_all[rank], q) = a;
   }
-  cluster.sync();
+  cluster.sync();  // every CTA's sums have arrived; no shared memory of a peer is touched after this
   float tot = 0.f;
-  for (int q = 0; q < NORM_CL; ++q) tot += *cluster.map_shared_rank(&cta_ss, q);
-  cluster.sync();  // peers stay resident until every CTA has read their sums
+  for (int q = 0; q < NORM_CL; ++q) tot += ss_all[q];
   const float inv = 1.0f / sqrtf(tot / static_cast<float>(d) + eps);
 #pragma unroll
   for (int v = 0; v < NORM_VPT; ++v) {
