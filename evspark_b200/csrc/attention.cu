@@ -26,16 +26,13 @@ __global__ void rope_append_kernel(const float* __restrict__ ws, int splits, int
                                    double log_base, const int32_t* __restrict__ len, int Lmax, TD* __restrict__ qrot,
                                    TD* __restrict__ kv, EvsDevErr* err) {
   pdl_trigger();
-  pdl_wait();
   const int row = blockIdx.x, h = blockIdx.y, j = threadIdx.x;
   const int half = Dh / 2;
   if (j >= half) return;
+  const double inv_freq = exp(-(2.0 * j / Dh) * log_base);  // depends on no earlier kernel
+  pdl_wait();
   const int b = row / T, t = row % T;
-  const int P = len[b] + t;
-  if (P >= Lmax) {
-    if (j == 0) evs_record_error(err, EVS_ERANGE, EVS_K_ATTN, row);
-    return;
-  }
+  // the projection's partial sums do not depend on the state length: their loads go first
   const int N = 3 * d;
   auto val = [&](int c) {
     return round_to<TD>(split_sum(ws + static_cast<size_t>(row) * N + c, static_cast<size_t>(M) * N, splits));
@@ -44,7 +41,11 @@ __global__ void rope_append_kernel(const float* __restrict__ ws, int splits, int
   const float q1 = val(c1), q2 = val(c2);
   const float k1 = val(d + c1), k2 = val(d + c2);
   const float v1 = val(2 * d + c1), v2 = val(2 * d + c2);
-  const double inv_freq = exp(-(2.0 * j / Dh) * log_base);
+  const int P = len[b] + t;
+  if (P >= Lmax) {
+    if (j == 0) evs_record_error(err, EVS_ERANGE, EVS_K_ATTN, row);
+    return;
+  }
   double sn, cs;
   sincos(static_cast<double>(P) * inv_freq, &sn, &cs);
   const float c = static_cast<float>(cs), s = static_cast<float>(sn);

@@ -369,13 +369,14 @@ __global__ void __launch_bounds__(HY_THREADS) hyena_iir_kernel(HyArgs<TD> a) {
   OuterPre<3> pre;
   outer_preload(a, b, h0, 0, min(TS, T), pre);
   const int L0 = a.len[b];
-  outer_stage(a, b, L0, h0, uw, wo);
+  const int cur = a.iir_cur[b];  // loaded with the length: the state load below waits for one round trip
   if (L0 > 0) {
-    load_vec<SPT>(a.s_all + ((static_cast<size_t>(b) * a.slots + a.iir_cur[b]) * d + h) * S + q * SPT, s);
+    load_vec<SPT>(a.s_all + ((static_cast<size_t>(b) * a.slots + cur) * d + h) * S + q * SPT, s);
   } else {
 #pragma unroll
     for (int j = 0; j < SPT; ++j) s[j] = 0.f;
   }
+  outer_stage(a, b, L0, h0, uw, wo);
   __syncthreads();
   for (int t0 = 0; t0 < T; t0 += TS) {
     const int ns = min(TS, T - t0);
