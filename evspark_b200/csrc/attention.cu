@@ -637,10 +637,11 @@ __global__ void __launch_bounds__(ATTN_THREADS, 5) attn_block_kernel(const TD* _
 // in flight); blocks with max -inf (past the query) are skipped
 __device__ __forceinline__ void fold_blocks(const float* pb, size_t jstride, int Dh, int dd, int jb, int jend,
                                             int jstep, float& m, float& l, float& acc) {
-  for (int j0 = jb; j0 <= jend; j0 += 8 * jstep) {
-    float mj[8], lj[8], aj[8];
+  constexpr int FB = 16;  // block partials loaded per batch (folded in block order)
+  for (int j0 = jb; j0 <= jend; j0 += FB * jstep) {
+    float mj[FB], lj[FB], aj[FB];
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
+    for (int k = 0; k < FB; ++k) {
       const int j = j0 + k * jstep;
       if (j <= jend) {
         const float* pj = pb + j * jstride;
@@ -650,7 +651,7 @@ __device__ __forceinline__ void fold_blocks(const float* pb, size_t jstride, int
       }
     }
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
+    for (int k = 0; k < FB; ++k) {
       if (j0 + k * jstep > jend || mj[k] == -CUDART_INF_F) continue;
       float a, bj;
       fold_stats(m, l, mj[k], lj[k], a, bj);

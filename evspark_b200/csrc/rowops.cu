@@ -247,6 +247,7 @@ __global__ void __cluster_dims__(NORM_CL, 1, 1) __launch_bounds__(NORM_THREADS)
                              unsigned long long tag_hi) {
   pdl_trigger();
   cg::cluster_group cluster = cg::this_cluster();
+  cluster_arrive_relaxed();  // its wait, before the first remote store: every peer has started
   const int rank = static_cast<int>(cluster.block_rank());
   const int cpc = d / NORM_CL, n4 = cpc / 4;
   const int c_base = rank * cpc;
@@ -258,7 +259,9 @@ __global__ void __cluster_dims__(NORM_CL, 1, 1) __launch_bounds__(NORM_THREADS)
   }
   pdl_wait();
   __shared__ float red[NORM_THREADS / 32];
-  __shared__ float cta_ss;
+  // every CTA's sum of squares, stored here by its owner; rows alternate between the two halves, so
+  // a peer's store for row i + 2 (after row i + 1's barrier) never meets this CTA's reads of row i
+  __shared__ float ss_all[2][NORM_CL];
   const int row0 = blockIdx.y * NORM_RPC, row_end = min(M, row0 + NORM_RPC);
   float4 xr[NORM_VPT], pv[NORM_VPT];
   auto load_row = [&](int row, float4 (&x)[NORM_VPT], float4 (&q)[NORM_VPT]) {
@@ -308,15 +311,17 @@ __global__ void __cluster_dims__(NORM_CL, 1, 1) __launch_bounds__(NORM_THREADS)
     ss = warp_sum(ss);
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
     __syncthreads();
+    if (row == row0) cluster_wait();
+    float* slots = ss_all[(row - row0) & 1];
     if (threadIdx.x == 0) {
       float a = 0.f;
       for (int w = 0; w < NORM_THREADS / 32; ++w) a += red[w];
-      cta_ss = a;
+#pragma unroll
+      for (int q = 0; q < NORM_CL; ++q) *cluster.map_shared_rank(&slots[rank], q) = a;
     }
-    cluster.sync();
+    cluster.sync();  // every CTA's sum of this row has arrived
     float tot = 0.f;
-    for (int q = 0; q < NORM_CL; ++q) tot += *cluster.map_shared_rank(&cta_ss, q);
-    cluster.sync();  // peers stay resident (and cta_ss unchanged) until every CTA has read the sums
+    for (int q = 0; q < NORM_CL; ++q) tot += slots[q];
     const float inv = 1.0f / sqrtf(tot / static_cast<float>(d) + eps);
 #pragma unroll
     for (int v = 0; v < NORM_VPT; ++v) {
