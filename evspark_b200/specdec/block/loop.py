@@ -135,10 +135,15 @@ class _RoundBuffers:
 
     def __init__(self, device, gamma: int):
         self.gamma = gamma
-        self.chunk = torch.empty(1, gamma + 1, dtype=torch.int64, device=device)
-        self.u_draft_h = torch.empty(gamma, dtype=torch.float64, pin_memory=True)
+        # one device buffer [draft uniforms (γ fp64) | anchor | draft tokens (γ)]: the chunk the
+        # verify forward reads is its last γ+1 slots, so one host copy of the first γ+1 slots sends a
+        # round's uniforms and anchor, and the drafter writes its tokens straight into the chunk
+        self.stage = torch.empty(2 * gamma + 1, dtype=torch.int64, device=device)
+        self.stage_h = torch.empty(gamma + 1, dtype=torch.int64, pin_memory=True)
+        self.chunk = self.stage[gamma:].view(1, gamma + 1)
+        self.u_draft = self.stage[:gamma].view(torch.float64)
+        self.u_draft_h = self.stage_h[:gamma].view(torch.float64)
         self.u_ver_h = torch.empty(gamma + 1, dtype=torch.float64, pin_memory=True)
-        self.u_draft = torch.empty(gamma, dtype=torch.float64, device=device)
         self.u_ver = torch.empty(gamma + 1, dtype=torch.float64, device=device)
         self.res_h = torch.empty(4 + gamma + 1, dtype=torch.int64, pin_memory=True)
         self.conf_h = torch.empty(gamma, dtype=torch.float32, pin_memory=True)
@@ -159,18 +164,21 @@ def _spec_round_device(model, draft, ip, y: int, gamma: int, greedy: bool, rng, 
         bufs = ip._round_bufs = _RoundBuffers(model.device, gamma)
     draft._check_gamma(gamma)
     chunk = bufs.chunk
-    chunk[0, 0] = int(y)  # the anchor travels as a kernel argument
-    h2d = chunk.element_size()
+    # the anchor (and, sampling, the drafter's uniforms before it) in one copy from pinned memory
+    bufs.stage_h.numpy()[gamma] = int(y)
     u = None
-    if not greedy:
+    if greedy:
+        bufs.stage[gamma:gamma + 1].copy_(bufs.stage_h[gamma:], non_blocking=True)
+        h2d = chunk.element_size()
+    else:
         bufs.u_draft_h.numpy()[:] = rng.random(int(gamma))
-        bufs.u_draft.copy_(bufs.u_draft_h, non_blocking=True)
-        h2d += bufs.u_draft_h.nbytes
+        bufs.stage[:gamma + 1].copy_(bufs.stage_h, non_blocking=True)
+        h2d = bufs.stage_h.nbytes
         u = bufs.u_draft[None]
     dr = draft.drafter
     if bufs.toks is None:
         V = dr.cfg.vocab_size
-        bufs.toks = torch.empty(1, gamma, dtype=torch.int64, device=model.device)
+        bufs.toks = chunk[:, 1:]  # the drafter's tokens land in the verify chunk
         bufs.q = torch.empty(1, gamma, V, dtype=torch.float64, device=model.device)
         bufs.conf = torch.empty(1, gamma, dtype=torch.float32, device=model.device)
     key = (ip.handle.value, dr._h.value, bool(greedy), float(temperature), None if top_k is None else int(top_k))
@@ -190,8 +198,7 @@ def _spec_round_device(model, draft, ip, y: int, gamma: int, greedy: bool, rng, 
         graph, n_calls = entry
         graph.replay()
         N.note_replayed(n_calls)
-    toks_d, q_rows, conf_d = bufs.toks, bufs.q, bufs.conf
-    chunk[0, 1:] = toks_d[0]
+    q_rows, conf_d = bufs.q, bufs.conf
     draft.capture_begin()
     logits = ip.forward(chunk, retain=True)
     x = chunk[:, 1:]
