@@ -145,8 +145,14 @@ class _RoundBuffers:
         self.u_draft_h = self.stage_h[:gamma].view(torch.float64)
         self.u_ver_h = torch.empty(gamma + 1, dtype=torch.float64, pin_memory=True)
         self.u_ver = torch.empty(gamma + 1, dtype=torch.float64, device=device)
-        self.res_h = torch.empty(4 + gamma + 1, dtype=torch.int64, pin_memory=True)
-        self.conf_h = torch.empty(gamma, dtype=torch.float32, pin_memory=True)
+        # the round's results in one device buffer read back by one copy, in 8-byte slots:
+        # [accepted (int32) | from_residual, fallback, consumed (int32) | γ+1 tokens | γ confidences (fp32)]
+        self.res = torch.empty(4 + gamma + (gamma + 1) // 2, dtype=torch.int64, device=device)
+        self.res_h = torch.empty(self.res.numel(), dtype=torch.int64, pin_memory=True)
+        self.acc = self.res[0:1].view(torch.int32)[:1]
+        self.info = self.res[1:3].view(torch.int32)[:3].view(1, 3)
+        self.toks_v = self.res[3:4 + gamma].view(1, gamma + 1)
+        self.conf_all = self.res[4 + gamma:].view(torch.float32)[:gamma].view(1, gamma)
         # drafter outputs of the round, and the drafter call captured as a CUDA graph per
         # (state, sampling settings): the same launches, issued by one graph launch
         self.toks = self.q = self.conf = None
@@ -180,7 +186,7 @@ def _spec_round_device(model, draft, ip, y: int, gamma: int, greedy: bool, rng, 
         V = dr.cfg.vocab_size
         bufs.toks = chunk[:, 1:]  # the drafter's tokens land in the verify chunk
         bufs.q = torch.empty(1, gamma, V, dtype=torch.float64, device=model.device)
-        bufs.conf = torch.empty(1, gamma, dtype=torch.float32, device=model.device)
+        bufs.conf = bufs.conf_all  # the drafter's confidences land in the result buffer
     key = (ip.handle.value, dr._h.value, bool(greedy), float(temperature), None if top_k is None else int(top_k))
     entry = bufs.draft_graphs.get(key)
     call = lambda: dr.propose_into(ip, chunk[:, 0], int(gamma), greedy, bufs.toks, bufs.q, bufs.conf,
@@ -198,29 +204,31 @@ def _spec_round_device(model, draft, ip, y: int, gamma: int, greedy: bool, rng, 
         graph, n_calls = entry
         graph.replay()
         N.note_replayed(n_calls)
-    q_rows, conf_d = bufs.q, bufs.conf
+    q_rows = bufs.q
     draft.capture_begin()
     logits = ip.forward(chunk, retain=True)
     x = chunk[:, 1:]
     state = None
+    out = (bufs.acc, bufs.toks_v, bufs.info)
     if greedy:
-        acc, toks_v, info = verify_device(logits.double(), None, x, None, greedy=True)
+        verify_device(logits.double(), None, x, None, greedy=True, out=out)
     else:
         p = transform_rows(logits[0], temperature, top_k)[None]
         uv, state = draw_uniforms(rng, gamma + 1)
         bufs.u_ver_h.numpy()[:] = uv
         bufs.u_ver.copy_(bufs.u_ver_h, non_blocking=True)
         h2d += bufs.u_ver_h.nbytes
-        acc, toks_v, info = verify_device(p, q_rows, x, bufs.u_ver[None], greedy=False)
-    ip.rollback_launch(torch.clamp(acc, max=int(remaining) - 1))
-    bufs.res_h.copy_(torch.cat([acc.to(torch.int64), info[0].to(torch.int64), toks_v[0]]), non_blocking=True)
-    bufs.conf_h.copy_(conf_d[0], non_blocking=True)
-    N.note_transfer(h2d=h2d, d2h=bufs.res_h.nbytes + bufs.conf_h.nbytes)
+        verify_device(p, q_rows, x, bufs.u_ver[None], greedy=False, out=out)
+    # j* = min(k, remaining - 1); k <= γ, so the clamp only matters near the end of a generation
+    ip.rollback_launch(bufs.acc if int(remaining) - 1 >= gamma else torch.clamp(bufs.acc, max=int(remaining) - 1))
+    bufs.res_h.copy_(bufs.res, non_blocking=True)
+    N.note_transfer(h2d=h2d, d2h=bufs.res_h.nbytes)
     torch.cuda.current_stream(model.device).synchronize()
     res = bufs.res_h.numpy()
-    k = int(res[0])
-    from_residual, fallback, consumed = bool(res[1]), bool(res[2]), int(res[3])
-    tokens = res[4:4 + k + 1].copy()
+    k = int(res[:1].view(np.int32)[0])
+    info = res[1:3].view(np.int32)
+    from_residual, fallback, consumed = bool(info[0]), bool(info[1]), int(info[2])
+    tokens = res[3:3 + k + 1].copy()
     if state is not None:
         rewind_uniforms(rng, state, consumed)
     take = min(k + 1, remaining)
@@ -229,7 +237,7 @@ def _spec_round_device(model, draft, ip, y: int, gamma: int, greedy: bool, rng, 
     draft.capture_commit(j_star + 1)
     log = RoundLog(k=k, replay_len=0, t_draft=0.0, t_block=0.0, t_verify=0.0, t_restore_replay=0.0,
                    from_residual=from_residual, fallback=fallback, n_emitted=take,
-                   conf=[float(c) for c in bufs.conf_h.numpy()])
+                   conf=res[4 + gamma:].view(np.float32)[:gamma].tolist())
     return RoundOutcome(taken=tokens[:take].astype(np.int64), log=log, ip=ip)
 
 

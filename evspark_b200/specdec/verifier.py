@@ -58,15 +58,24 @@ def rewind_uniforms(rng: np.random.Generator, state, consumed: int) -> None:
         rng.random(int(consumed))
 
 
-def verify_device(p: torch.Tensor, q: torch.Tensor | None, x: torch.Tensor, u: torch.Tensor | None, greedy: bool):
+def verify_device(p: torch.Tensor, q: torch.Tensor | None, x: torch.Tensor, u: torch.Tensor | None, greedy: bool,
+                  out: tuple | None = None):
     """Batched device verification: p [B, γ+1, V] fp64, q [B, γ, V] fp64, x [B, γ] int64,
-    u [B, γ+1] fp64.  Returns device (accepted [B], tokens [B, γ+1], info [B, 3])."""
+    u [B, γ+1] fp64.  Returns device (accepted [B], tokens [B, γ+1], info [B, 3]), written into
+    ``out`` = (int32 [B], int64 [B, γ+1], int32 [B, 3]) contiguous tensors when given."""
     B, g1, V = p.shape
     g = g1 - 1
     dev = p.device
-    acc = torch.empty(B, dtype=torch.int32, device=dev)
-    toks = torch.empty(B, g + 1, dtype=torch.int64, device=dev)
-    info = torch.empty(B, 3, dtype=torch.int32, device=dev)
+    if out is not None:
+        acc, toks, info = out
+        if (acc.dtype != torch.int32 or toks.dtype != torch.int64 or info.dtype != torch.int32
+                or acc.numel() != B or toks.shape != (B, g + 1) or info.shape != (B, 3)
+                or not (acc.is_contiguous() and toks.is_contiguous() and info.is_contiguous())):
+            raise ValueError("verify_device: out must be contiguous int32 [B], int64 [B, γ+1] and int32 [B, 3]")
+    else:
+        acc = torch.empty(B, dtype=torch.int32, device=dev)
+        toks = torch.empty(B, g + 1, dtype=torch.int64, device=dev)
+        info = torch.empty(B, 3, dtype=torch.int32, device=dev)
     N.check(N.lib().evs_verify(p.data_ptr(), N.ptr(q), x.data_ptr(), N.ptr(u), B, g, V, int(greedy),
                                acc.data_ptr(), toks.data_ptr(), info.data_ptr(), N.stream_ptr()), "evs_verify")
     return acc, toks, info
