@@ -58,3 +58,26 @@ def test_product_fails_loudly_without_gpu():
 
     with pytest.raises(RuntimeError, match="CUDA|device"):
         TargetModel.random(TINY, device="cuda:0")
+
+
+def test_verify_device_rejects_mismatched_result_buffers():
+    """The device round hands verify_device views of one result buffer; a view of the wrong dtype,
+    shape or layout is refused on the host, before any device call."""
+    import torch
+
+    from evspark_b200.specdec.verifier import verify_device
+
+    B, g, V = 1, 12, 512
+    p = torch.zeros(B, g + 1, V, dtype=torch.float64)
+    x = torch.zeros(B, g, dtype=torch.int64)
+    good = (torch.zeros(B, dtype=torch.int32), torch.zeros(B, g + 1, dtype=torch.int64),
+            torch.zeros(B, 3, dtype=torch.int32))
+    bad = [
+        (good[0].long(), good[1], good[2]),                                   # accepted not int32
+        (good[0], torch.zeros(B, g, dtype=torch.int64), good[2]),             # tokens one short
+        (good[0], good[1], torch.zeros(B, 4, dtype=torch.int32)),             # flags of the wrong width
+        (good[0], torch.zeros(g + 1, 2, dtype=torch.int64).t()[:1], good[2]),  # tokens not contiguous
+    ]
+    for out in bad:
+        with pytest.raises(ValueError, match="out must be"):
+            verify_device(p, None, x, None, greedy=True, out=out)
